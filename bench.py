@@ -1,0 +1,566 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 DFA hot path (Sparse4D v3 DeformableFeatureAggregation).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N ...
+
+One step = six stacked DFA layers (different weights, anchors refined between layers, each
+layer's output feeding the next) over a batch of 32 frames per GPU at the Sparse4D v3 R50
+shape: 900 anchors x 13 keypoints x 6 cameras x 4 levels x 256 channels, bf16 channels-last
+maps of a 704x256 image, fp32 accumulation.  Each layer runs through the drop-in
+``DeformableFeatureAggregation.run`` (cuBLAS linears + the keypoint kernel + the fused
+softmax/gather kernel).  Frames shard across GPUs with no collective in the timed region
+(weak scaling: 32 frames per GPU).
+
+Printed (rank 0, one JSON line): DFA calls/s for the whole job (calls = frames x layers),
+the gather kernel's roofline (algorithmic bytes per launch over its CUDA-event duration,
+against the measured HBM peak), the CPU baseline (the oracle's torch port of the reference
+DFA on this host), end-to-end calls/s through the module with host buffers, and a bs=1
+latency figure with L2 flushed between iterations.
+
+``--impl reference`` times the reference algorithm on the host CPU instead (the oracle port:
+the reference is a Tenstorrent TT-NN program and its PyTorch DFA is the CPU implementation),
+one single-frame DFA layer per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+METRIC = "DFA calls/s and keypoint-samples/s per B200 (bf16) at 1/2/4/8 GPUs; % HBM roofline"
+UNIT = "DFA calls/s"
+SAMPLES_PER_CALL = 900 * 13 * 6 * 4  # logical keypoint samples of one frame through one layer
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--frames", type=int, default=32, help="frames per GPU")
+    ap.add_argument("--layers", type=int, default=6)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-bs1", action="store_true")
+    return ap.parse_args()
+
+
+def env_dist():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def measured_hbm():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def workload_config(frames, layers, world):
+    return {
+        "workload": f"{layers} stacked DFA layers x {frames} frames per GPU; 900 anchors x 13 pts x 6 cams x "
+                    f"4 levels x 256 ch; 704x256 image (maps 64x176, 32x88, 16x44, 8x22); bf16 maps",
+        "frames_per_gpu": frames, "layers": layers, "global_batch": frames * world,
+        "anchors": 900, "num_pts": 13, "num_cams": 6, "num_levels": 4, "embed_dims": 256, "num_groups": 8,
+        "accumulate": "f32", "logits": "split (per-anchor + per-camera terms, summed in the gather kernel)",
+        "parallelism": f"dp{world} (frames)",
+        "l2": "inputs larger than L2 (1.47 GB of maps per GPU, re-read by every layer)",
+    }
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        self.lines = []
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            gid = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", gid, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax.append(float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------------------------
+class Workload:
+    """Device-resident inputs of one step on one GPU."""
+
+    def __init__(self, frames, layers, device, seed):
+        from sparse4d_tt_b200 import DeformableFeatureAggregation, ops
+        from sparse4d_tt_b200 import synthetic as syn
+
+        self.cfg = syn.DFAConfig(bs=frames)
+        cfg = self.cfg
+        self.frames, self.layers, self.device = frames, layers, device
+        gen = torch.Generator().manual_seed(seed)
+        self.shape, self.start, self.num_feat = ops.level_tables(cfg.spatial_shapes, cfg.num_cams, device=device)
+        dgen = torch.Generator(device=device).manual_seed(seed)
+        self.feat = torch.randn(frames, self.num_feat, cfg.embed_dims, device=device, generator=dgen,
+                                dtype=torch.bfloat16)
+        self.packed = (self.feat, self.shape, self.start)
+        self.inst0 = torch.randn(frames, cfg.num_anchor, cfg.embed_dims, generator=gen).to(device)
+        a = syn.make_anchors(frames, cfg.num_anchor, gen)
+        self.anchors, self.embeds, self.mods = [], [], []
+        for layer in range(layers):
+            self.anchors.append(a.to(device))
+            self.embeds.append(torch.randn(frames, cfg.num_anchor, cfg.embed_dims, generator=gen).to(device))
+            params = syn.make_params(cfg, torch.Generator().manual_seed(seed * 100 + layer))
+            self.mods.append(DeformableFeatureAggregation(device, params, {"FEATURE_DTYPE": torch.bfloat16},
+                                                          split_logits=True))
+            a = syn.refine_anchors(a, gen)
+        self.proj = syn.camera_ring(cfg.num_cams, cfg.image_wh)[None].expand(frames, -1, -1, -1).contiguous().to(device)
+        self.wh = torch.tensor(cfg.image_wh, dtype=torch.float32).expand(frames, cfg.num_cams, 2).contiguous().to(device)
+
+    def step(self, inst=None, anchors=None, embeds=None, packed=None, proj=None, wh=None):
+        inst = self.inst0 if inst is None else inst
+        anchors = self.anchors if anchors is None else anchors
+        embeds = self.embeds if embeds is None else embeds
+        packed = self.packed if packed is None else packed
+        proj = self.proj if proj is None else proj
+        wh = self.wh if wh is None else wh
+        out = None
+        for layer, mod in enumerate(self.mods):
+            out = mod.run(inst, anchors[layer], embeds[layer], packed, proj, wh, self.cfg.spatial_shapes,
+                          self.frames, self.cfg.num_anchor)
+            inst = out[..., : self.cfg.embed_dims]
+        return out
+
+    def set_event_logs(self, on):
+        for m in self.mods:
+            m.event_log = [] if on else None
+
+    def gather_ms(self):
+        ts = []
+        for m in self.mods:
+            ts += [s.elapsed_time(e) for s, e in (m.event_log or [])]
+        return ts
+
+    @torch.no_grad()
+    def algorithmic_bytes_per_layer(self):
+        """Compulsory HBM bytes of each layer's gather launch: unique in-bounds tap pixels x
+        256 ch x 2 B + split logits + sample locations + output.  Computed from the sample
+        locations of an untimed pass (replaying the module's own keypoint step)."""
+        import torch.nn.functional as F
+
+        from sparse4d_tt_b200 import ops
+
+        cfg, dev = self.cfg, self.device
+        inst = self.inst0
+        out_bytes = []
+        for layer, mod in enumerate(self.mods):
+            learn = F.linear(inst, mod.learnable_fc_weight, mod.learnable_fc_bias).contiguous()
+            loc = torch.empty(self.frames, cfg.num_anchor, cfg.num_cams, cfg.num_pts, 2, device=dev)
+            ops.kps_project_into(self.anchors[layer], learn, mod.fix_scale, self.proj, self.wh, sample_location=loc)
+            touched = unique_tap_pixels(loc, cfg.spatial_shapes, self.start, self.num_feat)
+            lpg = cfg.num_levels * cfg.num_pts * cfg.num_groups
+            b = (touched * cfg.embed_dims * 2
+                 + self.frames * cfg.num_anchor * lpg * 4 + self.frames * cfg.num_cams * lpg * 4
+                 + loc.numel() * 4 + self.frames * cfg.num_anchor * cfg.embed_dims * 4)
+            out_bytes.append((b, touched))
+            out = mod.run(inst, self.anchors[layer], self.embeds[layer], self.packed, self.proj, self.wh,
+                          cfg.spatial_shapes, self.frames, cfg.num_anchor)
+            inst = out[..., : cfg.embed_dims]
+        return out_bytes
+
+
+def unique_tap_pixels(loc, spatial_shapes, start, num_feat):
+    """Number of distinct feature rows (batch, camera, level, y, x) that the in-bounds bilinear
+    taps of ``loc [bs, A, Ncam, P, 2]`` touch (grid_sample, align_corners=False)."""
+    bs, A, nc, P, _ = loc.shape
+    dev = loc.device
+    mark = torch.zeros(bs * num_feat, dtype=torch.bool, device=dev)
+    b_idx = torch.arange(bs, device=dev).view(bs, 1, 1, 1)
+    starts = start.to(torch.int64)
+    for l, (h, w) in enumerate(spatial_shapes):
+        ix = ((loc[..., 0] * 2 - 1 + 1) * w - 1) * 0.5
+        iy = ((loc[..., 1] * 2 - 1 + 1) * h - 1) * 0.5
+        x0, y0 = ix.floor(), iy.floor()
+        cam_start = starts[:, l].view(1, 1, nc, 1)
+        for dx in (0, 1):
+            for dy in (0, 1):
+                x, y = x0 + dx, y0 + dy
+                ok = (x >= 0) & (x < w) & (y >= 0) & (y < h)
+                pix = b_idx * num_feat + cam_start + y.clamp(0, h - 1).long() * w + x.clamp(0, w - 1).long()
+                mark[pix[ok]] = True
+    return int(mark.sum())
+
+
+# ---------------------------------------------------------------------------------------------
+# legs
+# ---------------------------------------------------------------------------------------------
+def time_steps(fn, steps, sync_barrier):
+    sync_barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    sync_barrier()
+    return e0.elapsed_time(e1)
+
+
+def e2e_leg(w, steps, warmup, sync_barrier):
+    """Same step through the module with every input copied from pinned host memory inside
+    the timed region and the final output read back to the host."""
+    dev = w.device
+    host = {
+        "feat": w.feat.cpu().pin_memory(), "inst": w.inst0.cpu().pin_memory(),
+        "anchors": [a.cpu().pin_memory() for a in w.anchors], "embeds": [e.cpu().pin_memory() for e in w.embeds],
+        "proj": w.proj.cpu().pin_memory(), "wh": w.wh.cpu().pin_memory(),
+    }
+    dbuf = {
+        "feat": torch.empty_like(w.feat), "inst": torch.empty_like(w.inst0),
+        "anchors": [torch.empty_like(a) for a in w.anchors], "embeds": [torch.empty_like(e) for e in w.embeds],
+        "proj": torch.empty_like(w.proj), "wh": torch.empty_like(w.wh),
+    }
+    out_host = torch.empty(w.frames, w.cfg.num_anchor, 2 * w.cfg.embed_dims, pin_memory=True)
+    h2d = (host["feat"].numel() * 2 + host["inst"].numel() * 4 + sum(a.numel() * 4 for a in host["anchors"])
+           + sum(e.numel() * 4 for e in host["embeds"]) + host["proj"].numel() * 4 + host["wh"].numel() * 4)
+    d2h = out_host.numel() * 4
+
+    def step():
+        dbuf["feat"].copy_(host["feat"], non_blocking=True)
+        dbuf["inst"].copy_(host["inst"], non_blocking=True)
+        for d, h in zip(dbuf["anchors"], host["anchors"]):
+            d.copy_(h, non_blocking=True)
+        for d, h in zip(dbuf["embeds"], host["embeds"]):
+            d.copy_(h, non_blocking=True)
+        dbuf["proj"].copy_(host["proj"], non_blocking=True)
+        dbuf["wh"].copy_(host["wh"], non_blocking=True)
+        out = w.step(dbuf["inst"], dbuf["anchors"], dbuf["embeds"], (dbuf["feat"], w.shape, w.start), dbuf["proj"],
+                     dbuf["wh"])
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    ms = time_steps(step, steps, sync_barrier)
+    return ms, h2d, d2h
+
+
+def bs1_leg(device, iters=200):
+    """Single frame, single layer (the Sparse4D bs=1 inference shape): the gather kernel timed
+    alone with a >= 2x L2 write between iterations, and the whole layer (eager) timed the same
+    way."""
+    import torch.nn.functional as F
+
+    from sparse4d_tt_b200 import DeformableFeatureAggregation, ops
+    from sparse4d_tt_b200 import synthetic as syn
+
+    cfg = syn.config_standard(1)
+    ins = syn.make_inputs(cfg, 0, feature_dtype=torch.bfloat16)
+    params = syn.make_params(cfg, torch.Generator().manual_seed(100))
+    mod = DeformableFeatureAggregation(device, params, {"FEATURE_DTYPE": torch.bfloat16}, split_logits=True)
+    packed = ops.pack_feature_maps([m.to(device) for m in ins.feature_maps], dtype=torch.bfloat16)
+    inst, anchor, embed = (t.to(device) for t in (ins.instance_feature, ins.anchor, ins.anchor_embed))
+    proj, wh = ins.projection_mat.to(device), ins.image_wh.to(device)
+    wa, wc = mod._get_weights(inst, embed, proj, 1, 900)
+    wa, wc = wa.contiguous(), wc.contiguous()
+    learn = F.linear(inst, mod.learnable_fc_weight, mod.learnable_fc_bias).contiguous()
+    loc = torch.empty(1, 900, 6, 13, 2, device=device)
+    ops.kps_project_into(anchor, learn, mod.fix_scale, proj, wh, sample_location=loc)
+    out = torch.empty(1, 900, 256, device=device)
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    flush = torch.empty(max(2 * l2, 256 << 20) // 4, dtype=torch.float32, device=device)
+    touched = unique_tap_pixels(loc, cfg.spatial_shapes, packed[2], packed[0].shape[1])
+    lpg = 4 * 13 * 8
+    alg = touched * 512 + 900 * lpg * 4 + 6 * lpg * 4 + loc.numel() * 4 + out.numel() * 4
+
+    def gather():
+        ops.deformable_aggregation_into(out, packed[0], packed[1], packed[2], loc, wa, True, wc)
+
+    def layer():
+        mod.run(inst, anchor, embed, packed, proj, wh, cfg.spatial_shapes, 1, 900)
+
+    res = {}
+    for name, fn in (("gather", gather), ("layer", layer)):
+        for _ in range(10):
+            fn()
+        times = []
+        for _ in range(iters):
+            flush.fill_(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            times.append((e0, e1))
+        torch.cuda.synchronize()
+        ms = sorted(s.elapsed_time(e) for s, e in times)
+        res[name] = {"median_us": 1000 * ms[len(ms) // 2], "p10_us": 1000 * ms[len(ms) // 10],
+                     "p90_us": 1000 * ms[(9 * len(ms)) // 10]}
+    peak, src = measured_hbm()
+    g_s = res["gather"]["median_us"] * 1e-6
+    return {
+        "workload": "1 frame, 1 DFA layer, 900 anchors, bf16 maps (704x256 image); L2 written (>= 2x L2) "
+                    "before every iteration",
+        "gather_kernel_us": res["gather"], "layer_us": res["layer"],
+        "layer_calls_per_s": 1e6 / res["layer"]["median_us"],
+        "algorithmic_bytes": alg, "unique_tap_pixels": touched,
+        "gather_achieved_gbs": alg / g_s / 1e9, "gather_frac_of_hbm": alg / g_s / 1e9 / peak,
+        "peak_gbs": peak, "peak_source": src,
+    }
+
+
+def cpu_baseline(seconds=12.0, max_calls=40):
+    """The oracle's torch port of the reference DFA layer on the host CPU (all threads), at the
+    single-frame 900-anchor shape, fp32."""
+    from oracle import dfa_torch as oto
+    from sparse4d_tt_b200 import synthetic as syn
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    cfg = syn.config_standard(1)
+    ins = syn.make_inputs(cfg, 0, feature_dtype=torch.bfloat16)
+    params = syn.make_params(cfg, torch.Generator().manual_seed(100))
+
+    def call():
+        with torch.no_grad():
+            oto.dfa_layer(params, ins.instance_feature, ins.anchor, ins.anchor_embed, ins.feature_maps,
+                          ins.projection_mat, ins.image_wh)
+
+    for _ in range(2):
+        call()
+    times = []
+    t_end = time.perf_counter() + seconds
+    while len(times) < max_calls and (time.perf_counter() < t_end or len(times) < 5):
+        t0 = time.perf_counter()
+        call()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": 1.0 / med, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{len(times)} single-frame DFA layer calls (900 anchors, 704x256 maps as fp32, all linears "
+                      f"included) after 2 warm-ups; median {med * 1e3:.1f} ms/call; torch {torch.__version__} CPU",
+            "median_ms": med * 1e3, "cpu": _cpu_model()}
+
+
+def _cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def read_profile_traffic():
+    """DRAM bytes per gather launch from the committed ncu summary, if present."""
+    path = os.path.join(REPO, "profiles", "dfa_gather_stacked_bs32.md")
+    try:
+        with open(path) as f:
+            for ln in f:
+                if ln.startswith("traffic_bytes_per_launch:"):
+                    return float(ln.split(":", 1)[1].strip())
+    except Exception:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------------------------
+def run_reference(args):
+    rank, world, _ = env_dist()
+    if rank != 0:
+        return
+    res = cpu_baseline_steps(args.steps, args.warmup)
+    cfg = workload_config(args.frames, args.layers, world)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded camera ring, Xavier init)",
+        "config": cfg,
+        "cpu_baseline": {"value": res["value"], "unit": UNIT, "cores": res["cores"], "kind": "port",
+                         "sample": res["sample"]},
+        "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_steps(steps, warmup):
+    from oracle import dfa_torch as oto
+    from sparse4d_tt_b200 import synthetic as syn
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    cfg = syn.config_standard(1)
+    ins = syn.make_inputs(cfg, 0, feature_dtype=torch.bfloat16)
+    params = syn.make_params(cfg, torch.Generator().manual_seed(100))
+
+    def call():
+        with torch.no_grad():
+            oto.dfa_layer(params, ins.instance_feature, ins.anchor, ins.anchor_embed, ins.feature_maps,
+                          ins.projection_mat, ins.image_wh)
+
+    for _ in range(warmup):
+        call()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        call()
+    dt = time.perf_counter() - t0
+    return {"value": steps / dt, "ms_per_step": dt / steps * 1e3, "cores": threads,
+            "sample": f"each step = 1 single-frame DFA layer call (900 anchors, 704x256 maps as fp32) of the "
+                      f"workload, oracle torch port of the reference DFA on {threads} host threads "
+                      f"({_cpu_model()})"}
+
+
+def run_ours(args):
+    rank, world, local_rank = env_dist()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py: no CUDA device")
+    device = torch.device(f"cuda:{local_rank}")
+    torch.cuda.set_device(device)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        pg = dist
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    w = Workload(args.frames, args.layers, device, seed=1 + rank)
+    for _ in range(args.warmup):
+        w.step()
+    torch.cuda.synchronize()
+    bytes_per_layer = w.algorithmic_bytes_per_layer()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(device)
+    w.set_event_logs(True)
+    ms = time_steps(w.step, args.steps, barrier)
+    clock_info = clocks.stop()
+    g_ms = w.gather_ms()
+    w.set_event_logs(False)
+
+    t = torch.tensor([ms], device=device)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms_max = float(t.item())
+    calls = args.frames * args.layers * args.steps * world
+    value = calls / (ms_max / 1e3)
+
+    e2e = None
+    if not args.no_e2e:
+        e_steps = max(3, args.steps // 4)
+        e_ms, h2d, d2h = e2e_leg(w, e_steps, 1, barrier)
+        te = torch.tensor([e_ms], device=device)
+        if pg is not None:
+            pg.all_reduce(te, op=pg.ReduceOp.MAX)
+        e2e = {"value": args.frames * args.layers * e_steps * world / (float(te.item()) / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e_steps,
+               "path": "DeformableFeatureAggregation.run x layers, inputs from pinned host memory"}
+
+    bs1 = None
+    if rank == 0 and not args.no_bs1:
+        bs1 = bs1_leg(device)
+    barrier()
+
+    if rank == 0:
+        peak, src = measured_hbm()
+        alg = statistics.mean(b for b, _ in bytes_per_layer)
+        g_avg_ms = statistics.mean(g_ms)
+        achieved = alg / (g_avg_ms / 1e3) / 1e9
+        traffic = read_profile_traffic()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded camera ring, Xavier init)",
+            "config": workload_config(args.frames, args.layers, world),
+            "keypoint_samples_per_s": value * SAMPLES_PER_CALL,
+            "roofline": {
+                "kernel": "dfa_gather_kernel<bf16>", "bound": "hbm", "achieved": achieved, "peak": peak,
+                "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)",
+                "traffic": traffic, "algorithmic_bytes_per_launch": alg,
+                "unique_tap_pixels_per_launch": statistics.mean(t for _, t in bytes_per_layer),
+                "avg_launch_us": g_avg_ms * 1e3, "launches_timed": len(g_ms),
+                "share_of_step": sum(g_ms) / ms,
+            },
+            "gpu_launches": 2 * args.layers * args.steps,
+            "clocks": clock_info,
+            "e2e": e2e,
+            "bs1": bs1,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

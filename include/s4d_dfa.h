@@ -1,0 +1,168 @@
+/*
+ * s4d_dfa.h -- C ABI of the B200 (sm_100a) DeformableFeatureAggregation hot path.
+ *
+ * Two operators, each a set of hand-written CUDA kernels:
+ *
+ *   s4d_kps_project            anchor decode -> 7 fixed + N learnable keypoints -> yaw rotation
+ *                              -> per-camera lidar2img projection -> depth clamp and
+ *                              normalisation -> depth mask, frustum mask and the compacted
+ *                              list of visible (batch, anchor, camera, point) indices.
+ *   s4d_deformable_aggregation softmax of the weight logits over camera x level x point per
+ *                              group, fused with the multi-camera, multi-scale bilinear gather
+ *                              (zeros padding, align_corners=False) and the weighted sum over
+ *                              cameras, levels and points.
+ *
+ * Conventions
+ *   - Every pointer is a DEVICE pointer of the current CUDA device unless stated otherwise.
+ *     The library never allocates or frees: the caller owns every input, output and workspace.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).  Calls are
+ *     asynchronous and stream-ordered; nothing here synchronises the host.  Calls on different
+ *     streams from different host threads are safe.
+ *   - Every entry point returns an s4d_status; nothing throws and no kernel traps.  Shapes are
+ *     checked on the host before any launch.  The text of the last failure on the calling
+ *     thread is returned by s4d_last_error().
+ *   - Integer sizes are int64_t; element counts of one call must stay below 2^31.
+ */
+#ifndef S4D_DFA_H_
+#define S4D_DFA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define S4D_API __attribute__((visibility("default")))
+#else
+#define S4D_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum s4d_status {
+  S4D_OK = 0,
+  S4D_ERR_INVALID_ARG = 1,       /* null pointer, negative size, bad enum value */
+  S4D_ERR_UNSUPPORTED_SHAPE = 2, /* valid but outside what the kernels implement */
+  S4D_ERR_CUDA = 3,              /* a CUDA runtime call or launch failed */
+  S4D_ERR_DEVICE_FAULT = 4       /* a kernel reported bad device-side data via error_flag */
+} s4d_status;
+
+/* Feature element types of mc_ms_feat. */
+enum { S4D_DTYPE_F32 = 0, S4D_DTYPE_BF16 = 1 };
+
+/* Index layouts of sample_location and weights.
+ *   CAM_MAJOR (native):  sample_location [bs, A, Ncam, P, 2]; weights [bs, A, Ncam, L, P, G]
+ *                        (the order weights_fc produces, test/dfa_pcc.py:314-318).
+ *   PT_MAJOR (upstream Sparse4D deformable_aggregation op order):
+ *                        sample_location [bs, A, P, Ncam, 2]; weights [bs, A, P, Ncam, L, G].
+ *   GRID (s4d_kps_project output only): grid [Ncam, bs*A, P, 2] holding 2*uv - 1 clamped to
+ *                        [-2, 2], the output page order of ttnn.kps_project_fused
+ *                        (tt-metal/ops/kps_project_fused/device/kernels/dataflow/
+ *                        writer_kps_project.cpp:43-45). */
+enum { S4D_LAYOUT_CAM_MAJOR = 0, S4D_LAYOUT_PT_MAJOR = 1, S4D_LAYOUT_GRID = 2 };
+
+/* Bits of the optional device error_flag (OR-ed by kernels, never cleared by them). */
+enum { S4D_FLAG_BAD_LEVEL = 1 /* a (camera, level) spatial_shape / scale_start_index entry
+                                 lies outside mc_ms_feat; its samples were skipped */ };
+
+/* Human-readable name of a status code. */
+S4D_API const char* s4d_status_string(int status);
+
+/* Text of the last non-OK status returned on the calling thread ("" if none). */
+S4D_API const char* s4d_last_error(void);
+
+/* Version of this ABI (major * 100 + minor). */
+S4D_API int s4d_abi_version(void);
+
+/* Bytes of device workspace s4d_kps_project needs when it compacts visible indices
+ * (visible_idx or visible_count non-NULL).  Host-only, launches nothing. */
+S4D_API size_t s4d_kps_workspace_bytes(int64_t bs, int64_t num_anchor, int64_t num_cams, int64_t num_pts);
+
+/*
+ * Keypoint generation + projection + visibility compaction.
+ *
+ * Replaces ttnn.kps_project_fused (tt-metal/ops/kps_project_fused/kps_project_fused.hpp:12-22)
+ * together with the keypoint generator it consumes (model/deformable_feature_aggregation.py:
+ * 651-677) and the reference's PyTorch _KPSGenerator + project_points
+ * (test/dfa_pcc.py:225-247,322-333).
+ *
+ * Inputs
+ *   anchor          [bs, A, anchor_dim] f32, anchor_dim >= 8: x y z log(w) log(l) log(h) sin cos ...
+ *   fix_scale       [num_fix, 3] f32 fixed keypoint scales (may be NULL when num_fix == 0)
+ *   learnable       [bs, A, num_learnable * 3] f32 learnable_fc outputs BEFORE the sigmoid
+ *                   (may be NULL when num_learnable == 0)
+ *   projection_mat  [bs, Ncam, 4, 4] f32 lidar2img
+ *   image_wh        [bs, Ncam, 2] f32 (width, height)
+ *   P = num_fix + num_learnable keypoints per anchor.
+ * Outputs (each may be NULL to skip it)
+ *   key_points      [bs, A, P, 3] f32
+ *   sample_location CAM_MAJOR [bs, A, Ncam, P, 2] / PT_MAJOR [bs, A, P, Ncam, 2]: (u, v) =
+ *                   xy / max(z, 1e-5) / image_wh, unclamped; or GRID layout (see above)
+ *   depth_mask      [bs, A, Ncam, P] u8: 1 where z > 1e-5
+ *   visible_idx     [bs*A*Ncam*P, 4] i32 rows (b, a, cam, pt) of every visible point
+ *                   (z > 1e-5 and 0 <= u, v <= 1), lexicographic like torch.nonzero; only the
+ *                   first *visible_count rows are written
+ *   visible_count   [1] i32
+ *   workspace       >= s4d_kps_workspace_bytes(...) bytes, 16-byte aligned; required when
+ *                   visible_idx or visible_count is non-NULL, otherwise may be NULL
+ */
+S4D_API int s4d_kps_project(const float* anchor, int64_t anchor_dim, const float* fix_scale, int64_t num_fix,
+                    const float* learnable, int64_t num_learnable, const float* projection_mat,
+                    const float* image_wh, int64_t bs, int64_t num_anchor, int64_t num_cams, int layout,
+                    float* key_points, float* sample_location, uint8_t* depth_mask, int32_t* visible_idx,
+                    int32_t* visible_count, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Drop-in of ttnn.kps_project_fused in its standard mode
+ * (tt-metal/ops/kps_project_fused/kps_project_fused.hpp:12-22, kernel
+ * .../dataflow/reader_kps_project.cpp:255-289): pre-rotation keypoints in, normalised grid out.
+ *
+ *   key_points      [n, P, 3] f32 pre-rotation keypoints (fixed and learnable, times size)
+ *   anchor          [n, anchor_dim] f32 (yaw and centre are read from it)
+ *   projection_mat  [Ncam, 4, 4] f32, image_wh [Ncam, 2] f32
+ *   grid            [Ncam, n, P, 2] f32 = clamp(2 * uv - 1, -2, 2)
+ * The reference reads keypoints and anchors as bf16; this reads and computes in f32.
+ */
+S4D_API int s4d_kps_project_fused(const float* key_points, const float* anchor, int64_t anchor_dim,
+                          const float* projection_mat, const float* image_wh, int64_t n, int64_t num_cams,
+                          int64_t num_pts, float* grid, void* stream);
+
+/*
+ * Fused softmax + multi-camera multi-scale bilinear gather + weighted sum.
+ *
+ * Replaces ttnn.grid_sample + ttnn.transposed_s2i
+ * (tt-metal/ops/transposed_s2i/transposed_s2i.hpp:10-13) + ttnn.grouped_weighted_sum
+ * (tt-metal/ops/grouped_weighted_sum/grouped_weighted_sum.hpp:11-16) + the ttnn.softmax of
+ * model/deformable_feature_aggregation.py:791-796, i.e. the reference's PyTorch
+ * feature_sampling + multi_view_level_fusion + sum over points (test/dfa_pcc.py:298,335-358).
+ * Argument meaning follows upstream Sparse4D's deformable_aggregation(mc_ms_feat,
+ * spatial_shape, scale_start_index, sample_location, weights).
+ *
+ *   mc_ms_feat        [bs, num_feat, C] channels-last features, f32 or bf16 (feat_dtype);
+ *                     pixel (y, x) of camera c, level l is row scale_start_index[c, l] + y*W + x
+ *   spatial_shape     [Ncam, L, 2] i32 (H, W)
+ *   scale_start_index [Ncam, L] i32
+ *   sample_location   see layout; (u, v) in [0, 1] inside the image
+ *   weights           see layout.  With weights_cam != NULL (CAM_MAJOR only) the logits are
+ *                     split: weights [bs, A, L, P, G] is the per-anchor term and weights_cam
+ *                     [bs, Ncam, L, P, G] the per-camera term; logit = weights + weights_cam.
+ *   weights_are_logits 1: softmax over (cam, level, pt) per group first (over ALL Ncam cameras
+ *                     even when [cam_begin, cam_end) is a sub-range); 0: use as given
+ *   cam_begin/cam_end only cameras in [cam_begin, cam_end) are sampled (camera sharding)
+ *   out               [bs, A, C] f32, summed over points
+ *   error_flag        optional [1] i32, OR-ed with S4D_FLAG_* bits
+ * Implemented: C == 256, G in {1, 2, 4, 8, 16, 32}, Ncam*L*P*G <= 12288.
+ */
+S4D_API int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, int64_t num_feat,
+                               const int32_t* spatial_shape, const int32_t* scale_start_index,
+                               const float* sample_location, const float* weights, const float* weights_cam,
+                               int weights_are_logits, int layout, int64_t bs, int64_t num_anchor,
+                               int64_t num_cams, int64_t num_levels, int64_t num_pts, int64_t num_groups,
+                               int64_t embed_dims, int64_t cam_begin, int64_t cam_end, float* out,
+                               int32_t* error_flag, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* S4D_DFA_H_ */

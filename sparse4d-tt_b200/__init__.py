@@ -1,0 +1,21 @@
+"""B200-native DeformableFeatureAggregation (DFA) hot path of Sparse4D v3.
+
+Public API:
+  DeformableFeatureAggregation, preprocess_dfa_parameters   -- drop-in module (dfa.py)
+  deformable_aggregation, kps_project, kps_project_fused,
+  pack_feature_maps, level_tables                           -- operators (ops.py)
+The operators run hand-written sm_100a CUDA kernels from lib/libs4d_dfa.so through the C ABI
+of include/s4d_dfa.h; the library is loaded on first use and its absence raises.
+"""
+from . import synthetic  # noqa: F401
+from .dfa import DeformableFeatureAggregation, preprocess_dfa_parameters  # noqa: F401
+from .ops import (  # noqa: F401
+    deformable_aggregation,
+    deformable_aggregation_into,
+    kps_project,
+    kps_project_fused,
+    kps_project_into,
+    level_tables,
+    pack_feature_maps,
+    visible_indices,
+)

@@ -1,0 +1,85 @@
+"""ctypes binding of ``lib/libs4d_dfa.so`` (the C ABI declared in ``include/s4d_dfa.h``).
+
+The library is loaded on first use.  If it is missing, every operator raises instead of
+falling back to another implementation.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "lib", "libs4d_dfa.so")
+
+S4D_OK = 0
+S4D_ERR_INVALID_ARG = 1
+S4D_ERR_UNSUPPORTED_SHAPE = 2
+S4D_ERR_CUDA = 3
+S4D_ERR_DEVICE_FAULT = 4
+
+S4D_DTYPE_F32 = 0
+S4D_DTYPE_BF16 = 1
+
+S4D_LAYOUT_CAM_MAJOR = 0
+S4D_LAYOUT_PT_MAJOR = 1
+S4D_LAYOUT_GRID = 2
+
+S4D_FLAG_BAD_LEVEL = 1
+
+_i64, _int, _p, _sz = C.c_int64, C.c_int, C.c_void_p, C.c_size_t
+
+# name -> (restype, argtypes); one entry per function of include/s4d_dfa.h
+SIGNATURES = {
+    "s4d_status_string": (C.c_char_p, [_int]),
+    "s4d_last_error": (C.c_char_p, []),
+    "s4d_abi_version": (_int, []),
+    "s4d_kps_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
+    "s4d_kps_project": (_int, [_p, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _int,
+                               _p, _p, _p, _p, _p, _p, _sz, _p]),
+    "s4d_kps_project_fused": (_int, [_p, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _p]),
+    "s4d_deformable_aggregation": (_int, [_p, _int, _i64, _p, _p, _p, _p, _p, _int, _int,
+                                          _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                          _p, _p, _p]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class S4DError(RuntimeError):
+    """A non-OK status from the C ABI."""
+
+    def __init__(self, fn: str, status: int, msg: str):
+        self.status = status
+        super().__init__(f"{fn}: {status_string(status)}: {msg}")
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"CUDA library {LIB_PATH} is not built; run `python __graft_entry__.py build` "
+                        "(or python sparse4d-tt_b200/build.py).  There is no CPU fallback.")
+                handle = C.CDLL(LIB_PATH)
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(handle, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = handle
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return lib().s4d_status_string(status).decode()
+
+
+def check(fn: str, status: int) -> None:
+    if status != S4D_OK:
+        msg = lib().s4d_last_error().decode()
+        if status in (S4D_ERR_INVALID_ARG, S4D_ERR_UNSUPPORTED_SHAPE):
+            raise ValueError(f"{fn}: {status_string(status)}: {msg}")
+        raise S4DError(fn, status, msg)

@@ -1,0 +1,206 @@
+// extern "C" entry points of include/s4d_dfa.h: argument validation on the host, then the
+// launches of kps_project.cu and dfa_gather.cu.  Nothing here allocates, frees or
+// synchronises.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "params.cuh"
+
+namespace s4d {
+
+static thread_local char g_last_error[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+}  // namespace s4d
+
+using namespace s4d;
+
+namespace {
+
+constexpr int64_t kMaxElems = (int64_t)1 << 31;
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+const char* s4d_status_string(int status) {
+  switch (status) {
+    case S4D_OK: return "S4D_OK";
+    case S4D_ERR_INVALID_ARG: return "S4D_ERR_INVALID_ARG";
+    case S4D_ERR_UNSUPPORTED_SHAPE: return "S4D_ERR_UNSUPPORTED_SHAPE";
+    case S4D_ERR_CUDA: return "S4D_ERR_CUDA";
+    case S4D_ERR_DEVICE_FAULT: return "S4D_ERR_DEVICE_FAULT";
+    default: return "S4D_ERR_UNKNOWN";
+  }
+}
+
+const char* s4d_last_error(void) { return g_last_error; }
+
+int s4d_abi_version(void) { return 100; }
+
+size_t s4d_kps_workspace_bytes(int64_t bs, int64_t num_anchor, int64_t num_cams, int64_t num_pts) {
+  if (bs <= 0 || num_anchor <= 0 || num_cams <= 0 || num_pts <= 0) return 0;
+  return kps_workspace_bytes(bs * num_anchor * num_cams * num_pts);
+}
+
+int s4d_kps_project(const float* anchor, int64_t anchor_dim, const float* fix_scale, int64_t num_fix,
+                    const float* learnable, int64_t num_learnable, const float* projection_mat,
+                    const float* image_wh, int64_t bs, int64_t num_anchor, int64_t num_cams, int layout,
+                    float* key_points, float* sample_location, uint8_t* depth_mask, int32_t* visible_idx,
+                    int32_t* visible_count, void* workspace, size_t workspace_bytes, void* stream) {
+  set_error("%s", "");
+  if (bs < 0 || num_anchor < 0 || num_cams < 0 || num_fix < 0 || num_learnable < 0)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: negative size");
+  if (layout != S4D_LAYOUT_CAM_MAJOR && layout != S4D_LAYOUT_PT_MAJOR && layout != S4D_LAYOUT_GRID)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: unknown layout");
+  if (anchor_dim < 8) return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: anchor_dim must be >= 8");
+  const int64_t num_pts = num_fix + num_learnable;
+  if (num_pts == 0) return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: no keypoints");
+  const int64_t total = bs * num_anchor * num_cams * num_pts;
+  if (total >= kMaxElems || num_cams * num_pts >= (1 << 24))
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project: bs*A*Ncam*P must be < 2^31");
+  const bool compact = visible_idx != nullptr || visible_count != nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (total == 0) {
+    if (visible_count != nullptr)
+      return cuda_check(cudaMemsetAsync(visible_count, 0, sizeof(int32_t), st), "cudaMemsetAsync(visible_count)");
+    return S4D_OK;
+  }
+  if (anchor == nullptr || projection_mat == nullptr || image_wh == nullptr)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: null input pointer");
+  if ((num_fix > 0 && fix_scale == nullptr) || (num_learnable > 0 && learnable == nullptr))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: null fix_scale / learnable with a non-zero count");
+  if (sample_location != nullptr && !aligned(sample_location, 8))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: sample_location must be 8-byte aligned");
+  if (visible_idx != nullptr && !aligned(visible_idx, 16))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: visible_idx must be 16-byte aligned");
+  if (compact) {
+    if (workspace == nullptr || !aligned(workspace, 16))
+      return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: compaction needs a 16-byte aligned workspace");
+    if (workspace_bytes < kps_workspace_bytes(total))
+      return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: workspace smaller than s4d_kps_workspace_bytes()");
+  }
+  KpsParams k{};
+  k.anchor = anchor;
+  k.anchor_dim = (int)anchor_dim;
+  k.fix_scale = fix_scale;
+  k.num_fix = (int)num_fix;
+  k.learnable = learnable;
+  k.num_learnable = (int)num_learnable;
+  k.kp_pre = nullptr;
+  k.proj = projection_mat;
+  k.wh = image_wh;
+  k.bs = (int)bs;
+  k.num_anchor = (int)num_anchor;
+  k.num_cams = (int)num_cams;
+  k.num_pts = (int)num_pts;
+  k.layout = layout;
+  k.total = total;
+  k.key_points = key_points;
+  k.loc = sample_location;
+  k.mask = depth_mask;
+  return launch_kps_project(k, visible_idx, visible_count, workspace, st);
+}
+
+int s4d_kps_project_fused(const float* key_points, const float* anchor, int64_t anchor_dim,
+                          const float* projection_mat, const float* image_wh, int64_t n, int64_t num_cams,
+                          int64_t num_pts, float* grid, void* stream) {
+  set_error("%s", "");
+  if (n < 0 || num_cams < 0 || num_pts < 0) return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project_fused: negative size");
+  if (anchor_dim < 8) return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project_fused: anchor_dim must be >= 8");
+  const int64_t total = n * num_cams * num_pts;
+  if (total >= kMaxElems) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project_fused: n*Ncam*P must be < 2^31");
+  if (total == 0) return S4D_OK;
+  if (key_points == nullptr || anchor == nullptr || projection_mat == nullptr || image_wh == nullptr ||
+      grid == nullptr)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project_fused: null pointer");
+  if (!aligned(grid, 8)) return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project_fused: grid must be 8-byte aligned");
+  KpsParams k{};
+  k.anchor = anchor;
+  k.anchor_dim = (int)anchor_dim;
+  k.kp_pre = key_points;
+  k.proj = projection_mat;
+  k.wh = image_wh;
+  k.bs = 1;
+  k.num_anchor = (int)n;
+  k.num_cams = (int)num_cams;
+  k.num_pts = (int)num_pts;
+  k.layout = S4D_LAYOUT_GRID;
+  k.total = total;
+  k.loc = grid;
+  return launch_kps_project(k, nullptr, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, int64_t num_feat,
+                               const int32_t* spatial_shape, const int32_t* scale_start_index,
+                               const float* sample_location, const float* weights, const float* weights_cam,
+                               int weights_are_logits, int layout, int64_t bs, int64_t num_anchor,
+                               int64_t num_cams, int64_t num_levels, int64_t num_pts, int64_t num_groups,
+                               int64_t embed_dims, int64_t cam_begin, int64_t cam_end, float* out,
+                               int32_t* error_flag, void* stream) {
+  set_error("%s", "");
+  if (bs < 0 || num_anchor < 0 || num_cams <= 0 || num_levels <= 0 || num_pts <= 0 || num_groups <= 0 ||
+      embed_dims <= 0 || num_feat < 0)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: sizes must be positive");
+  if (feat_dtype != S4D_DTYPE_F32 && feat_dtype != S4D_DTYPE_BF16)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: unknown feat_dtype");
+  if (layout != S4D_LAYOUT_CAM_MAJOR && layout != S4D_LAYOUT_PT_MAJOR)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: layout must be CAM_MAJOR or PT_MAJOR");
+  if (cam_begin < 0 || cam_end > num_cams || cam_begin > cam_end)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: need 0 <= cam_begin <= cam_end <= num_cams");
+  if (weights_cam != nullptr && layout != S4D_LAYOUT_CAM_MAJOR)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: split logits (weights_cam) need CAM_MAJOR");
+  if (weights_cam != nullptr && !weights_are_logits)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: split weights are only defined for logits");
+  if (embed_dims != 256)
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: embed_dims must be 256");
+  if (num_groups > 32 || (num_groups & (num_groups - 1)) != 0)
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: num_groups must be 1, 2, 4, 8, 16 or 32");
+  if (num_cams * num_levels * num_pts * num_groups > kGatherMaxWeights)
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: Ncam*L*P*G must be <= 12288");
+  if (bs * num_anchor >= kMaxElems || bs * num_feat >= ((int64_t)1 << 40))
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: too many anchors or feature rows");
+  if (num_feat >= kMaxElems)
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: num_feat must be < 2^31");
+  if (bs * num_anchor == 0) return S4D_OK;
+  if (mc_ms_feat == nullptr || spatial_shape == nullptr || scale_start_index == nullptr ||
+      sample_location == nullptr || weights == nullptr || out == nullptr)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: null pointer");
+  if (!aligned(mc_ms_feat, 16))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: mc_ms_feat must be 16-byte aligned");
+  if (!aligned(sample_location, 8) || !aligned(weights, 4) || !aligned(out, 4))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: misaligned sample_location/weights/out");
+  GatherParams p{};
+  p.feat = mc_ms_feat;
+  p.num_feat = num_feat;
+  p.spatial_shape = spatial_shape;
+  p.scale_start = scale_start_index;
+  p.loc = sample_location;
+  p.weights = weights;
+  p.weights_cam = weights_cam;
+  p.out = out;
+  p.error_flag = error_flag;
+  p.bs = (int)bs;
+  p.num_anchor = (int)num_anchor;
+  p.num_cams = (int)num_cams;
+  p.num_levels = (int)num_levels;
+  p.num_pts = (int)num_pts;
+  p.num_groups = (int)num_groups;
+  p.cam_begin = (int)cam_begin;
+  p.cam_end = (int)cam_end;
+  p.logits = weights_are_logits ? 1 : 0;
+  p.layout = layout;
+  if (gather_smem_bytes(p.num_cams, p.num_levels, p.num_pts, p.num_groups, p.cam_begin, p.cam_end) > 200 * 1024)
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: per-anchor staging exceeds shared memory");
+  return launch_gather(p, feat_dtype, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,53 @@
+// Shared helpers of the DFA kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "s4d_dfa.h"
+
+namespace s4d {
+
+// Records the text of the last failure on this host thread (read by s4d_last_error()).
+void set_error(const char* fmt, ...);
+
+inline int fail(int status, const char* msg) {
+  set_error("%s", msg);
+  return status;
+}
+
+inline int cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return S4D_OK;
+  set_error("%s: %s", what, cudaGetErrorString(e));
+  return S4D_ERR_CUDA;
+}
+
+// 8 consecutive bf16 channels (one 16-byte vector) widened to fp32.
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // bf16 is the top half of an fp32: shifting the bits into place is exact.
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float4 ldg_nc_f4(const void* p) {
+  float4 r;
+  asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p));
+  return r;
+}
+
+}  // namespace s4d

@@ -1,0 +1,222 @@
+// Kernel (a): keypoint generation, projection, depth/frustum masks and lexicographic
+// compaction of the visible (batch, anchor, camera, point) indices.
+//
+// Follows the reference's _KPSGenerator.forward (test/dfa_pcc.py:225-247) and project_points
+// (test/dfa_pcc.py:322-333); in TT-NN the same work is ttnn.kps_project_fused
+// (tt-metal/ops/kps_project_fused/device/kernels/dataflow/reader_kps_project.cpp:255-289)
+// fed by _kps_generator_pre_rotation (model/deformable_feature_aggregation.py:651-677).
+//
+// Work split: one thread per (batch, anchor, camera, point) element, elements in
+// lexicographic order, so every output store is coalesced and the visibility bits of a warp
+// are 32 consecutive elements.  A block owns kElemsPerBlock consecutive elements (4 rounds of
+// 256).  Compaction is count -> scatter with no inter-block waits: the project kernel writes
+// one ballot word per 32 elements and one visible count per block; the scatter kernel sums the
+// counts of the blocks before it, scans its own 32 words and writes the rows.
+//
+// Arithmetic order is fixed and fused multiply-add is disabled on every line that decides a
+// mask bit (the __f*_rn intrinsics), so the integer outputs reproduce a CPU evaluation of the
+// same expression order bit for bit:
+//   X_r = ((P[r][0]*px + P[r][1]*py) + P[r][2]*pz) + P[r][3];   z = X_2 < 1e-5 ? 1e-5 : X_2
+//   u = (X_0 / z) / w;   v = (X_1 / z) / h
+#include "params.cuh"
+
+namespace s4d {
+
+constexpr int kKpsThreads = 256;
+constexpr int kKpsRounds = 4;
+constexpr int kElemsPerBlock = kKpsThreads * kKpsRounds;  // 1024
+constexpr int kWordsPerBlock = kElemsPerBlock / 32;        // 32
+
+
+__device__ __forceinline__ float sigmoid_rn(float x) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+}
+
+// Rotated + translated keypoint p of anchor n (fp32, fixed order).
+__device__ __forceinline__ void keypoint(const KpsParams& k, int64_t n, int p, float& px, float& py, float& pz) {
+  const float* a = k.anchor + n * k.anchor_dim;
+  float kx, ky, kz;
+  if (k.kp_pre != nullptr) {
+    const float* q = k.kp_pre + (n * k.num_pts + p) * 3;
+    kx = q[0];
+    ky = q[1];
+    kz = q[2];
+  } else {
+    const float sx = expf(a[3]), sy = expf(a[4]), sz = expf(a[5]);
+    if (p < k.num_fix) {
+      const float* fs = k.fix_scale + p * 3;
+      kx = __fmul_rn(fs[0], sx);
+      ky = __fmul_rn(fs[1], sy);
+      kz = __fmul_rn(fs[2], sz);
+    } else {
+      const float* lg = k.learnable + n * (int64_t)(k.num_learnable * 3) + (p - k.num_fix) * 3;
+      kx = __fmul_rn(__fsub_rn(sigmoid_rn(lg[0]), 0.5f), sx);
+      ky = __fmul_rn(__fsub_rn(sigmoid_rn(lg[1]), 0.5f), sy);
+      kz = __fmul_rn(__fsub_rn(sigmoid_rn(lg[2]), 0.5f), sz);
+    }
+  }
+  const float s = a[6], c = a[7];
+  const float rx = __fsub_rn(__fmul_rn(c, kx), __fmul_rn(s, ky));
+  const float ry = __fadd_rn(__fmul_rn(s, kx), __fmul_rn(c, ky));
+  px = __fadd_rn(rx, a[0]);
+  py = __fadd_rn(ry, a[1]);
+  pz = __fadd_rn(kz, a[2]);
+}
+
+__device__ __forceinline__ float proj_row(const float* r, float px, float py, float pz) {
+  return __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(r[0], px), __fmul_rn(r[1], py)), __fmul_rn(r[2], pz)), r[3]);
+}
+
+__global__ void __launch_bounds__(kKpsThreads) kps_project_kernel(KpsParams k) {
+  const int lane = threadIdx.x & 31;
+  const int64_t block_base = (int64_t)blockIdx.x * kElemsPerBlock;
+  const int per_anchor = k.num_cams * k.num_pts;
+  int count = 0;
+#pragma unroll
+  for (int r = 0; r < kKpsRounds; ++r) {
+    const int64_t e = block_base + r * kKpsThreads + threadIdx.x;
+    bool vis = false;
+    if (e < k.total) {
+      const int64_t n = e / per_anchor;  // linear anchor index b * A + a
+      const int rem = (int)(e - n * per_anchor);
+      const int c = rem / k.num_pts;
+      const int p = rem - c * k.num_pts;
+      const int b = (int)(n / k.num_anchor);
+      float px, py, pz;
+      keypoint(k, n, p, px, py, pz);
+      if (k.key_points != nullptr && c == 0) {
+        float* kp = k.key_points + (n * k.num_pts + p) * 3;
+        kp[0] = px;
+        kp[1] = py;
+        kp[2] = pz;
+      }
+      const float* P = k.proj + ((int64_t)b * k.num_cams + c) * 16;
+      const float X0 = proj_row(P, px, py, pz);
+      const float X1 = proj_row(P + 4, px, py, pz);
+      const float X2 = proj_row(P + 8, px, py, pz);
+      const bool in_front = X2 > 1e-5f;
+      const float z = X2 < 1e-5f ? 1e-5f : X2;  // torch.clamp(min=1e-5): NaN stays NaN
+      const float* wh = k.wh + ((int64_t)b * k.num_cams + c) * 2;
+      const float u = __fdiv_rn(__fdiv_rn(X0, z), wh[0]);
+      const float v = __fdiv_rn(__fdiv_rn(X1, z), wh[1]);
+      vis = in_front && u >= 0.0f && u <= 1.0f && v >= 0.0f && v <= 1.0f;
+      if (k.mask != nullptr) k.mask[e] = in_front ? 1 : 0;
+      if (k.loc != nullptr) {
+        if (k.layout == S4D_LAYOUT_CAM_MAJOR) {
+          reinterpret_cast<float2*>(k.loc)[e] = make_float2(u, v);
+        } else if (k.layout == S4D_LAYOUT_PT_MAJOR) {
+          reinterpret_cast<float2*>(k.loc)[(n * k.num_pts + p) * k.num_cams + c] = make_float2(u, v);
+        } else {  // GRID: [ncam, n_total, P, 2], 2*uv - 1 clamped to [-2, 2]
+          const int64_t n_total = (int64_t)k.bs * k.num_anchor;
+          const float gx = fminf(fmaxf(__fsub_rn(__fmul_rn(u, 2.0f), 1.0f), -2.0f), 2.0f);
+          const float gy = fminf(fmaxf(__fsub_rn(__fmul_rn(v, 2.0f), 1.0f), -2.0f), 2.0f);
+          reinterpret_cast<float2*>(k.loc)[((int64_t)c * n_total + n) * k.num_pts + p] = make_float2(gx, gy);
+        }
+      }
+    }
+    if (k.vis_words != nullptr) {
+      const uint32_t word = __ballot_sync(0xffffffffu, vis);
+      if (lane == 0) {
+        k.vis_words[(int64_t)blockIdx.x * kWordsPerBlock + r * (kKpsThreads / 32) + (threadIdx.x >> 5)] = word;
+        count += __popc(word);
+      }
+    }
+  }
+  if (k.block_counts != nullptr) {
+    __shared__ int s_cnt[kKpsThreads / 32];
+    if (lane == 0) s_cnt[threadIdx.x >> 5] = count;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int t = 0;
+#pragma unroll
+      for (int w = 0; w < kKpsThreads / 32; ++w) t += s_cnt[w];
+      k.block_counts[blockIdx.x] = t;
+    }
+  }
+}
+
+// Writes the (b, a, cam, pt) rows of the visible elements of this block at their global
+// lexicographic position.  The block's offset is the sum of the counts of all earlier blocks,
+// read directly (no inter-block waiting; the project kernel has finished in stream order).
+__global__ void __launch_bounds__(kKpsThreads) kps_compact_kernel(const int32_t* __restrict__ block_counts,
+                                                                  const uint32_t* __restrict__ vis_words,
+                                                                  int num_blocks, int64_t total, int num_anchor,
+                                                                  int num_cams, int num_pts, int4* __restrict__ idx,
+                                                                  int32_t* __restrict__ count_out) {
+  __shared__ int s_part[kKpsThreads / 32];
+  __shared__ int s_word_off[kWordsPerBlock];
+  __shared__ uint32_t s_words[kWordsPerBlock];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  int part = 0;
+  for (int j = threadIdx.x; j < (int)blockIdx.x; j += kKpsThreads) part += block_counts[j];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if (lane == 0) s_part[warp] = part;
+  if (warp == 0) {
+    const uint32_t w = vis_words[(int64_t)blockIdx.x * kWordsPerBlock + lane];
+    s_words[lane] = w;
+    int c = __popc(w);
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    s_word_off[lane] = incl - c;
+  }
+  __syncthreads();
+  int block_off = 0;
+#pragma unroll
+  for (int w = 0; w < kKpsThreads / 32; ++w) block_off += s_part[w];
+  if (count_out != nullptr && blockIdx.x == num_blocks - 1 && threadIdx.x == 0) {
+    *count_out = block_off + s_word_off[kWordsPerBlock - 1] + __popc(s_words[kWordsPerBlock - 1]);
+  }
+  if (idx == nullptr) return;
+  const int per_anchor = num_cams * num_pts;
+#pragma unroll
+  for (int r = 0; r < kKpsRounds; ++r) {
+    const int word_id = r * (kKpsThreads / 32) + warp;
+    const uint32_t w = s_words[word_id];
+    if ((w >> lane) & 1u) {
+      const int64_t e = (int64_t)blockIdx.x * kElemsPerBlock + r * kKpsThreads + threadIdx.x;
+      const int pos = block_off + s_word_off[word_id] + __popc(w & ((1u << lane) - 1u));
+      const int64_t n = e / per_anchor;
+      const int rem = (int)(e - n * per_anchor);
+      const int c = rem / num_pts;
+      idx[pos] = make_int4((int)(n / num_anchor), (int)(n % num_anchor), c, rem - c * num_pts);
+    }
+  }
+  (void)total;
+}
+
+int64_t kps_num_blocks(int64_t total) { return (total + kElemsPerBlock - 1) / kElemsPerBlock; }
+
+size_t kps_workspace_bytes(int64_t total) {
+  const int64_t nb = kps_num_blocks(total);
+  const size_t counts = ((size_t)nb * sizeof(int32_t) + 255) & ~(size_t)255;
+  return counts + (size_t)nb * kWordsPerBlock * sizeof(uint32_t);
+}
+
+int launch_kps_project(KpsParams k, int32_t* visible_idx, int32_t* visible_count, void* workspace,
+                       cudaStream_t stream) {
+  const int64_t nb = kps_num_blocks(k.total);
+  const bool compact = visible_idx != nullptr || visible_count != nullptr;
+  if (compact) {
+    k.block_counts = static_cast<int32_t*>(workspace);
+    const size_t counts = ((size_t)nb * sizeof(int32_t) + 255) & ~(size_t)255;
+    k.vis_words = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + counts);
+  } else {
+    k.block_counts = nullptr;
+    k.vis_words = nullptr;
+  }
+  kps_project_kernel<<<(unsigned)nb, kKpsThreads, 0, stream>>>(k);
+  int st = cuda_check(cudaGetLastError(), "kps_project_kernel launch");
+  if (st != S4D_OK || !compact) return st;
+  kps_compact_kernel<<<(unsigned)nb, kKpsThreads, 0, stream>>>(
+      k.block_counts, k.vis_words, (int)nb, k.total, k.num_anchor, k.num_cams, k.num_pts,
+      reinterpret_cast<int4*>(visible_idx), visible_count);
+  return cuda_check(cudaGetLastError(), "kps_compact_kernel launch");
+}
+
+}  // namespace s4d

@@ -1,0 +1,55 @@
+// Launch parameters and launcher declarations shared by the kernel translation units and the
+// C-ABI layer (capi.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace s4d {
+
+struct KpsParams {
+  const float* anchor;
+  int anchor_dim;
+  const float* fix_scale;
+  int num_fix;
+  const float* learnable;  // [n, num_learnable*3] logits, or null
+  int num_learnable;
+  const float* kp_pre;  // [n, P, 3] pre-rotation keypoints (kps_project_fused mode), or null
+  const float* proj;    // [bs, ncam, 4, 4]
+  const float* wh;      // [bs, ncam, 2]
+  int bs, num_anchor, num_cams, num_pts;
+  int layout;
+  int64_t total;  // bs * A * ncam * P
+  float* key_points;
+  float* loc;
+  uint8_t* mask;
+  int32_t* block_counts;  // [num_blocks] (compaction only)
+  uint32_t* vis_words;    // [num_blocks * 32] (compaction only)
+};
+
+// Largest Ncam*L*P*G the gather stages per anchor in shared memory (48 KiB of fp32).
+constexpr int kGatherMaxWeights = 12288;
+
+struct GatherParams {
+  const void* feat;
+  int64_t num_feat;  // pixel rows per batch item
+  const int32_t* spatial_shape;
+  const int32_t* scale_start;
+  const float* loc;
+  const float* weights;
+  const float* weights_cam;
+  float* out;
+  int32_t* error_flag;
+  int bs, num_anchor, num_cams, num_levels, num_pts, num_groups;
+  int cam_begin, cam_end;
+  int logits;
+  int layout;
+};
+
+int launch_kps_project(KpsParams k, int32_t* visible_idx, int32_t* visible_count, void* workspace,
+                       cudaStream_t stream);
+size_t kps_workspace_bytes(int64_t total);
+
+int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream);
+size_t gather_smem_bytes(int ncam, int nl, int np, int G, int cam_begin, int cam_end);
+
+}  // namespace s4d

@@ -1,0 +1,237 @@
+"""Drop-in ``DeformableFeatureAggregation`` for Sparse4D v3 on B200.
+
+Same constructor arguments, parameter-dictionary keys and ``run`` signature as the reference
+module (``model/deformable_feature_aggregation.py:42-57,800-811,954-995``), called the same
+way by the decoder head (``model/sparse4d_head.py:405-411``).  What runs:
+
+* the dense layers stay on cuBLAS through torch: camera encoder
+  (``model/deformable_feature_aggregation.py:679-717``), ``weights_fc``, the keypoint
+  ``learnable_fc`` and ``output_proj`` (``:934-950``);
+* kernel (a) ``s4d_kps_project`` replaces ``_kps_generator_pre_rotation`` +
+  ``ttnn.kps_project_fused`` (``:651-677,855-860``);
+* kernel (b)+(c) ``s4d_deformable_aggregation`` replaces the softmax, the per-level
+  ``ttnn.grid_sample`` + ``ttnn.transposed_s2i`` loop and ``ttnn.grouped_weighted_sum``
+  (``:791-796,864-899``).
+
+Camera sharding (the reference's ``mesh_device`` mode, ``:172-176,925-931``) is available by
+passing a ``torch.distributed`` process group as ``mesh_device``: each rank samples only its
+own cameras, with the softmax taken over ALL cameras, and the partial sums are all-reduced
+(the reference softmaxes over each device's cameras only; see ``camera_shard``).
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Optional, Sequence, Tuple, Union
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+
+Tensor = torch.Tensor
+
+X, Y, Z = 0, 1, 2
+W, L, H = 3, 4, 5
+SIN_YAW, COS_YAW = 6, 7
+
+PARAM_KEYS = (
+    "kps_fix_scale", "kps_learnable_fc_weight", "kps_learnable_fc_bias",
+    "cam_linear1_weight", "cam_linear1_bias", "cam_ln1_weight", "cam_ln1_bias",
+    "cam_linear2_weight", "cam_linear2_bias", "cam_ln2_weight", "cam_ln2_bias",
+    "weights_fc_weight", "weights_fc_bias", "output_proj_weight", "output_proj_bias",
+)
+
+
+def preprocess_dfa_parameters(pt_model) -> Dict[str, Tensor]:
+    """Parameter dictionary of a PyTorch DFA module, keyed as
+    ``model/deformable_feature_aggregation.py:954-995`` keys it (works for the mmdet3d
+    module and for the reference's standalone ``_PTDeformableFeatureAggregation``)."""
+    p = {
+        "kps_fix_scale": pt_model.kps_generator.fix_scale.data.clone(),
+        "kps_learnable_fc_weight": pt_model.kps_generator.learnable_fc.weight.data.clone(),
+        "kps_learnable_fc_bias": pt_model.kps_generator.learnable_fc.bias.data.clone(),
+    }
+    if getattr(pt_model, "camera_encoder", None) is not None:
+        enc = pt_model.camera_encoder
+        for idx, key in ((0, "cam_linear1"), (2, "cam_ln1"), (3, "cam_linear2"), (5, "cam_ln2")):
+            p[key + "_weight"] = enc[idx].weight.data.clone()
+            p[key + "_bias"] = enc[idx].bias.data.clone()
+    p["weights_fc_weight"] = pt_model.weights_fc.weight.data.clone()
+    p["weights_fc_bias"] = pt_model.weights_fc.bias.data.clone()
+    p["output_proj_weight"] = pt_model.output_proj.weight.data.clone()
+    p["output_proj_bias"] = pt_model.output_proj.bias.data.clone()
+    return p
+
+
+FeatureMaps = Union[List[Tensor], Tuple[Tensor, Tensor, Tensor]]
+
+
+class DeformableFeatureAggregation:
+    """B200 DFA layer.  ``device`` is a CUDA device (``"cuda:0"``, ``torch.device`` or index).
+
+    ``model_config`` may carry ``"FEATURE_DTYPE"`` (``torch.bfloat16`` default, or
+    ``torch.float32``): the dtype feature maps are packed to when ``run`` receives a list.
+    ``split_logits=True`` evaluates ``weights_fc(f + cam) = weights_fc(f) + W cam`` as two
+    smaller GEMMs and adds the two terms inside the gather kernel instead of materialising the
+    ``[bs, A, Ncam, L*P*G]`` logits (same result up to fp32 rounding)."""
+
+    def __init__(self, device, parameters: Dict[str, Tensor], model_config: Optional[Dict] = None,
+                 embed_dims: int = 256, num_groups: int = 8, num_levels: int = 4, num_cams: int = 6,
+                 num_pts: int = 13, num_learnable_pts: int = 6, use_camera_embed: bool = True,
+                 residual_mode: str = "cat", mesh_device=None, split_logits: bool = False) -> None:
+        self.device = torch.device(device if not isinstance(device, int) else f"cuda:{device}")
+        if self.device.type != "cuda":
+            raise ValueError("DeformableFeatureAggregation runs on a CUDA device only")
+        self.embed_dims = embed_dims
+        self.num_groups = num_groups
+        self.group_dims = embed_dims // num_groups
+        self.num_levels = num_levels
+        self.num_cams = num_cams
+        self.num_pts = num_pts
+        self.num_learnable_pts = num_learnable_pts
+        self.use_camera_embed = use_camera_embed
+        self.residual_mode = residual_mode
+        self.model_config = dict(model_config or {})
+        self.feature_dtype = self.model_config.get("FEATURE_DTYPE", torch.bfloat16)
+        self.split_logits = bool(split_logits and use_camera_embed)
+        self.process_group = mesh_device if _is_process_group(mesh_device) else None
+        if mesh_device is not None and self.process_group is None:
+            raise ValueError("mesh_device must be a torch.distributed ProcessGroup (camera sharding)")
+        missing = [k for k in PARAM_KEYS if k not in parameters and (use_camera_embed or not k.startswith("cam_"))]
+        if missing:
+            raise KeyError(f"parameters missing {missing}")
+        dev = self.device
+
+        def t(k):
+            return parameters[k].detach().to(dev, torch.float32).contiguous()
+
+        self.fix_scale = t("kps_fix_scale")
+        if self.fix_scale.shape[0] + num_learnable_pts != num_pts:
+            raise ValueError("num_pts must equal len(kps_fix_scale) + num_learnable_pts")
+        self.learnable_fc_weight = t("kps_learnable_fc_weight")
+        self.learnable_fc_bias = t("kps_learnable_fc_bias")
+        if use_camera_embed:
+            self.cam_linear1_weight, self.cam_linear1_bias = t("cam_linear1_weight"), t("cam_linear1_bias")
+            self.cam_ln1_weight, self.cam_ln1_bias = t("cam_ln1_weight"), t("cam_ln1_bias")
+            self.cam_linear2_weight, self.cam_linear2_bias = t("cam_linear2_weight"), t("cam_linear2_bias")
+            self.cam_ln2_weight, self.cam_ln2_bias = t("cam_ln2_weight"), t("cam_ln2_bias")
+        self.weights_fc_weight = t("weights_fc_weight")
+        self.weights_fc_bias = t("weights_fc_bias")
+        self.output_proj_weight = t("output_proj_weight")
+        self.output_proj_bias = t("output_proj_bias")
+        # Per-frame caches, cleared by the head at the start of a frame
+        # (model/sparse4d_head.py:290-296 resets the same attribute names).
+        self._cached_camera_embed = None
+        self._cached_proj_rm = None
+        self._cached_wh_rm = None
+        self._cam_key = None
+        # When a list, every run() appends a (start, end) pair of CUDA events recorded on the
+        # launching stream around the gather kernel (used to time that kernel in place).
+        self.event_log: Optional[List[Tuple[torch.cuda.Event, torch.cuda.Event]]] = None
+
+    # ---- dense parts (cuBLAS through torch) -----------------------------------------------
+    def _camera_encoder(self, projection_mat: Tensor, bs: int) -> Tensor:
+        """``[bs, Ncam, C]`` (``model/deformable_feature_aggregation.py:679-717``)."""
+        x = projection_mat[:, :, :3].reshape(bs, self.num_cams, 12)
+        C = self.embed_dims
+        x = F.relu(F.linear(x, self.cam_linear1_weight, self.cam_linear1_bias))
+        x = F.layer_norm(x, (C,), self.cam_ln1_weight, self.cam_ln1_bias, 1e-5)
+        x = F.relu(F.linear(x, self.cam_linear2_weight, self.cam_linear2_bias))
+        return F.layer_norm(x, (C,), self.cam_ln2_weight, self.cam_ln2_bias, 1e-5)
+
+    def _camera_embed(self, projection_mat: Tensor, bs: int) -> Tensor:
+        key = (projection_mat.data_ptr(), projection_mat._version, tuple(projection_mat.shape))
+        if self._cached_camera_embed is None or self._cam_key != key:
+            self._cached_camera_embed = self._camera_encoder(projection_mat, bs)
+            self._cam_key = key
+        return self._cached_camera_embed
+
+    def _get_weights(self, instance_feature: Tensor, anchor_embed: Tensor, projection_mat: Tensor, bs: int,
+                     num_anchor: int):
+        """Weight logits: ``[bs, A, Ncam, L, P, G]``, or with ``split_logits`` the pair
+        (``[bs, A, L, P, G]``, ``[bs, Ncam, L, P, G]``) whose sum is the same logit
+        (``model/deformable_feature_aggregation.py:719-798`` before its softmax)."""
+        feature = instance_feature + anchor_embed
+        lpg = (self.num_levels, self.num_pts, self.num_groups)
+        if not self.use_camera_embed:
+            w = F.linear(feature, self.weights_fc_weight, self.weights_fc_bias)
+            return w.reshape(bs, num_anchor, self.num_cams, *lpg), None
+        cam = self._camera_embed(projection_mat, bs)
+        if self.split_logits:
+            wa = F.linear(feature, self.weights_fc_weight).reshape(bs, num_anchor, *lpg)
+            wc = F.linear(cam, self.weights_fc_weight, self.weights_fc_bias).reshape(bs, self.num_cams, *lpg)
+            return wa, wc
+        w = F.linear(feature[:, :, None] + cam[:, None], self.weights_fc_weight, self.weights_fc_bias)
+        return w.reshape(bs, num_anchor, self.num_cams, *lpg), None
+
+    # ---- features ---------------------------------------------------------------------------
+    def _features(self, feature_maps: FeatureMaps, spatial_shapes, bs: int):
+        if isinstance(feature_maps, (tuple, list)) and len(feature_maps) == 3 and feature_maps[1].dtype == torch.int32 \
+                and feature_maps[1].dim() == 3:
+            return feature_maps  # already packed (mc_ms_feat, spatial_shape, scale_start_index)
+        maps = list(feature_maps)
+        if maps[0].dim() == 5:  # [bs, Ncam, C, H, W]
+            return ops.pack_feature_maps(maps, dtype=self.feature_dtype)
+        # reference TT layout: per level [1, 1, bs*Ncam*H*W, C] channels-last
+        cl = [m.reshape(bs, self.num_cams, h, w, self.embed_dims) for m, (h, w) in zip(maps, spatial_shapes)]
+        return ops.pack_feature_maps(cl, dtype=self.feature_dtype, channels_last=True)
+
+    # ---- forward ----------------------------------------------------------------------------
+    def run(self, instance_feature: Tensor, anchor: Tensor, anchor_embed: Tensor, feature_maps: FeatureMaps,
+            projection_mat: Tensor, image_wh: Tensor, spatial_shapes: Sequence[Tuple[int, int]], bs: int,
+            num_anchor: int) -> Tensor:
+        """``[bs, A, 2C]`` (residual ``cat``) or ``[bs, A, C]`` (``add``), fp32."""
+        dev = self.device
+        instance_feature = instance_feature.reshape(bs, num_anchor, self.embed_dims)
+        anchor = anchor.reshape(bs, num_anchor, -1).float().contiguous()
+        anchor_embed = anchor_embed.reshape(bs, num_anchor, self.embed_dims)
+        projection_mat = projection_mat.reshape(bs, self.num_cams, 4, 4).float().contiguous()
+        image_wh = image_wh.reshape(bs, self.num_cams, 2).float().contiguous()
+        mc_ms_feat, spatial_shape, scale_start = self._features(feature_maps, spatial_shapes, bs)
+
+        logits, logits_cam = self._get_weights(instance_feature, anchor_embed, projection_mat, bs, num_anchor)
+        learn = F.linear(instance_feature, self.learnable_fc_weight, self.learnable_fc_bias).contiguous()
+        loc = torch.empty(bs, num_anchor, self.num_cams, self.num_pts, 2, dtype=torch.float32, device=dev)
+        ops.kps_project_into(anchor, learn, self.fix_scale, projection_mat, image_wh, sample_location=loc)
+
+        cam_begin, cam_end = 0, self.num_cams
+        if self.process_group is not None:
+            from .camera_shard import rank_camera_range
+
+            cam_begin, cam_end = rank_camera_range(self.num_cams, self.process_group)
+        feats = torch.empty(bs, num_anchor, self.embed_dims, dtype=torch.float32, device=dev)
+        logits = logits.contiguous()
+        logits_cam = None if logits_cam is None else logits_cam.contiguous()
+        log = self.event_log
+        if log is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        ops.deformable_aggregation_into(feats, mc_ms_feat, spatial_shape, scale_start, loc, logits, True,
+                                        logits_cam, cam_begin, cam_end)
+        if log is not None:
+            ev[1].record()
+            log.append(ev)
+        if self.process_group is not None:
+            import torch.distributed as dist
+
+            dist.all_reduce(feats, group=self.process_group)
+
+        out = F.linear(feats, self.output_proj_weight, self.output_proj_bias)
+        inst = instance_feature.to(out.dtype)
+        if self.residual_mode == "add":
+            return out + inst
+        if self.residual_mode == "cat":
+            return torch.cat([out, inst], dim=-1)
+        return out
+
+    __call__ = run
+
+
+def _is_process_group(obj) -> bool:
+    if obj is None:
+        return False
+    try:
+        import torch.distributed as dist
+
+        return isinstance(obj, dist.ProcessGroup)
+    except Exception:  # pragma: no cover - torch built without distributed
+        return False

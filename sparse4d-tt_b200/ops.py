@@ -1,0 +1,325 @@
+"""Torch operators of the DFA hot path, each a thin wrapper over the C ABI.
+
+* ``deformable_aggregation(mc_ms_feat, spatial_shape, scale_start_index, sample_location,
+  weights, ...)`` -- fused softmax + multi-camera multi-scale bilinear gather + weighted sum;
+  the argument meaning of upstream Sparse4D's op of the same name, and the replacement of
+  ``ttnn.grid_sample`` + ``ttnn.transposed_s2i`` + ``ttnn.grouped_weighted_sum`` + softmax
+  (``model/deformable_feature_aggregation.py:791-796,877-899``).
+* ``kps_project(anchor, learnable_logits, fix_scale, projection_mat, image_wh, ...)`` --
+  keypoints, projection, depth / frustum masks and the compacted visible indices
+  (``test/dfa_pcc.py:225-247,322-333``).
+* ``kps_project_fused(key_points, anchor, projection_mat, image_wh, num_cams, num_pts)`` --
+  same arguments and output layout as ``ttnn.kps_project_fused``
+  (``tt-metal/ops/kps_project_fused/kps_project_fused_nanobind.cpp:69-91``).
+* ``pack_feature_maps(feature_maps)`` -- per-level maps to the packed channels-last
+  ``mc_ms_feat`` layout.
+
+The ``*_into`` variants write into caller-provided tensors and are what the drop-in module
+uses (no allocation, CUDA-graph capturable).  All of them validate dtype, device, shape and
+contiguity and raise ``ValueError`` / ``TypeError``; a non-OK status from the library raises.
+There is no CPU path: CPU tensors are rejected.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence, Tuple, Union
+
+import torch
+
+from . import _lib as L
+
+Tensor = torch.Tensor
+
+LAYOUTS = {"cam_major": L.S4D_LAYOUT_CAM_MAJOR, "pt_major": L.S4D_LAYOUT_PT_MAJOR}
+
+
+def _ptr(t: Optional[Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(name: str, *ts: Optional[Tensor]) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError(f"{name}: every tensor must be on a CUDA device (got {t.device}); no CPU path exists")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"{name}: tensors on different devices ({dev} and {t.device})")
+    return dev
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _check_contig(name: str, **ts: Optional[Tensor]) -> None:
+    for k, t in ts.items():
+        if t is not None and not t.is_contiguous():
+            raise ValueError(f"{name}: {k} must be contiguous")
+
+
+def _check_dtype(name: str, t: Optional[Tensor], dtypes: Sequence[torch.dtype], what: str) -> None:
+    if t is not None and t.dtype not in dtypes:
+        raise TypeError(f"{name}: {what} must be one of {list(dtypes)}, got {t.dtype}")
+
+
+# ---------------------------------------------------------------------------------------------
+# deformable_aggregation
+# ---------------------------------------------------------------------------------------------
+
+def _dfa_dims(sample_location: Tensor, weights: Tensor, weights_cam: Optional[Tensor], layout: int):
+    if layout == L.S4D_LAYOUT_CAM_MAJOR:
+        _require(sample_location.dim() == 5 and sample_location.shape[-1] == 2,
+                 "sample_location must be [bs, A, Ncam, P, 2] (cam_major)")
+        bs, A, nc, P = sample_location.shape[:4]
+        if weights_cam is None:
+            _require(weights.dim() == 6 and tuple(weights.shape[:3]) == (bs, A, nc) and weights.shape[4] == P,
+                     "weights must be [bs, A, Ncam, L, P, G] (cam_major)")
+            nl, G = weights.shape[3], weights.shape[5]
+        else:
+            _require(weights.dim() == 5 and tuple(weights.shape[:2]) == (bs, A) and weights.shape[3] == P,
+                     "split weights must be [bs, A, L, P, G]")
+            nl, G = weights.shape[2], weights.shape[4]
+            _require(tuple(weights_cam.shape) == (bs, nc, nl, P, G), "weights_cam must be [bs, Ncam, L, P, G]")
+    else:
+        _require(sample_location.dim() == 5 and sample_location.shape[-1] == 2,
+                 "sample_location must be [bs, A, P, Ncam, 2] (pt_major)")
+        bs, A, P, nc = sample_location.shape[:4]
+        _require(weights.dim() == 6 and tuple(weights.shape[:4]) == (bs, A, P, nc),
+                 "weights must be [bs, A, P, Ncam, L, G] (pt_major)")
+        nl, G = weights.shape[4], weights.shape[5]
+    return int(bs), int(A), int(nc), int(nl), int(P), int(G)
+
+
+def deformable_aggregation_into(out: Tensor, mc_ms_feat: Tensor, spatial_shape: Tensor, scale_start_index: Tensor,
+                                sample_location: Tensor, weights: Tensor, weights_are_logits: bool = True,
+                                weights_cam: Optional[Tensor] = None, cam_begin: int = 0, cam_end: int = -1,
+                                layout: Union[int, str] = "cam_major", error_flag: Optional[Tensor] = None) -> Tensor:
+    """Writes the fused gather into ``out [bs, A, C]`` (fp32) and returns it."""
+    name = "deformable_aggregation"
+    lay = LAYOUTS[layout] if isinstance(layout, str) else int(layout)
+    dev = _require_cuda(name, out, mc_ms_feat, spatial_shape, scale_start_index, sample_location, weights,
+                        weights_cam, error_flag)
+    _check_contig(name, out=out, mc_ms_feat=mc_ms_feat, spatial_shape=spatial_shape,
+                  scale_start_index=scale_start_index, sample_location=sample_location, weights=weights,
+                  weights_cam=weights_cam)
+    _check_dtype(name, mc_ms_feat, (torch.float32, torch.bfloat16), "mc_ms_feat")
+    _check_dtype(name, spatial_shape, (torch.int32,), "spatial_shape")
+    _check_dtype(name, scale_start_index, (torch.int32,), "scale_start_index")
+    for k, t in (("sample_location", sample_location), ("weights", weights), ("weights_cam", weights_cam),
+                 ("out", out)):
+        _check_dtype(name, t, (torch.float32,), k)
+    _check_dtype(name, error_flag, (torch.int32,), "error_flag")
+    _require(mc_ms_feat.dim() == 3, "mc_ms_feat must be [bs, num_feat, C]")
+    bs, A, nc, nl, P, G = _dfa_dims(sample_location, weights, weights_cam, lay)
+    C = int(mc_ms_feat.shape[2])
+    _require(int(mc_ms_feat.shape[0]) == bs, "mc_ms_feat batch must match sample_location")
+    _require(tuple(spatial_shape.shape) == (nc, nl, 2), f"spatial_shape must be [{nc}, {nl}, 2]")
+    _require(tuple(scale_start_index.shape) == (nc, nl), f"scale_start_index must be [{nc}, {nl}]")
+    _require(tuple(out.shape) == (bs, A, C), f"out must be [{bs}, {A}, {C}]")
+    ce = nc if cam_end is None or cam_end < 0 else int(cam_end)
+    st = L.lib().s4d_deformable_aggregation(
+        mc_ms_feat.data_ptr(), L.S4D_DTYPE_BF16 if mc_ms_feat.dtype == torch.bfloat16 else L.S4D_DTYPE_F32,
+        int(mc_ms_feat.shape[1]), spatial_shape.data_ptr(), scale_start_index.data_ptr(),
+        sample_location.data_ptr(), weights.data_ptr(), _ptr(weights_cam), 1 if weights_are_logits else 0, lay,
+        bs, A, nc, nl, P, G, C, int(cam_begin), ce, out.data_ptr(), _ptr(error_flag), _stream_ptr(dev))
+    L.check(name, st)
+    return out
+
+
+@torch.library.custom_op("s4d::deformable_aggregation", mutates_args=())
+def deformable_aggregation(mc_ms_feat: Tensor, spatial_shape: Tensor, scale_start_index: Tensor,
+                           sample_location: Tensor, weights: Tensor, weights_are_logits: bool = True,
+                           weights_cam: Optional[Tensor] = None, cam_begin: int = 0, cam_end: int = -1,
+                           layout: int = 0) -> Tensor:
+    """Fused softmax (when ``weights_are_logits``) + bilinear gather + weighted sum.
+
+    ``mc_ms_feat [bs, num_feat, C]`` channels-last (f32 or bf16); ``spatial_shape [Ncam, L, 2]``
+    and ``scale_start_index [Ncam, L]`` int32; ``sample_location`` / ``weights`` in
+    ``layout`` 0 (cam-major, native: ``[bs, A, Ncam, P, 2]`` / ``[bs, A, Ncam, L, P, G]``) or 1
+    (pt-major, upstream Sparse4D: ``[bs, A, P, Ncam, 2]`` / ``[bs, A, P, Ncam, L, G]``).
+    Returns ``[bs, A, C]`` fp32 summed over points."""
+    bs, A = sample_location.shape[:2]
+    out = torch.empty(bs, A, mc_ms_feat.shape[2], dtype=torch.float32, device=mc_ms_feat.device)
+    return deformable_aggregation_into(out, mc_ms_feat, spatial_shape, scale_start_index, sample_location, weights,
+                                       weights_are_logits, weights_cam, cam_begin, cam_end, layout)
+
+
+@deformable_aggregation.register_fake
+def _(mc_ms_feat, spatial_shape, scale_start_index, sample_location, weights, weights_are_logits=True,
+      weights_cam=None, cam_begin=0, cam_end=-1, layout=0):
+    bs, A = sample_location.shape[:2]
+    return mc_ms_feat.new_empty(bs, A, mc_ms_feat.shape[2], dtype=torch.float32)
+
+
+# ---------------------------------------------------------------------------------------------
+# kps_project
+# ---------------------------------------------------------------------------------------------
+
+def kps_workspace_bytes(bs: int, num_anchor: int, num_cams: int, num_pts: int) -> int:
+    return int(L.lib().s4d_kps_workspace_bytes(bs, num_anchor, num_cams, num_pts))
+
+
+def kps_project_into(anchor: Tensor, learnable_logits: Optional[Tensor], fix_scale: Optional[Tensor],
+                     projection_mat: Tensor, image_wh: Tensor, sample_location: Optional[Tensor] = None,
+                     depth_mask: Optional[Tensor] = None, visible_idx: Optional[Tensor] = None,
+                     visible_count: Optional[Tensor] = None, key_points: Optional[Tensor] = None,
+                     workspace: Optional[Tensor] = None, layout: Union[int, str] = "cam_major") -> None:
+    """Runs the keypoint kernel into caller-provided outputs (any may be None)."""
+    name = "kps_project"
+    lay = LAYOUTS[layout] if isinstance(layout, str) else int(layout)
+    dev = _require_cuda(name, anchor, learnable_logits, fix_scale, projection_mat, image_wh, sample_location,
+                        depth_mask, visible_idx, visible_count, key_points, workspace)
+    _check_contig(name, anchor=anchor, learnable_logits=learnable_logits, fix_scale=fix_scale,
+                  projection_mat=projection_mat, image_wh=image_wh, sample_location=sample_location,
+                  depth_mask=depth_mask, visible_idx=visible_idx, key_points=key_points)
+    for k, t in (("anchor", anchor), ("learnable_logits", learnable_logits), ("fix_scale", fix_scale),
+                 ("projection_mat", projection_mat), ("image_wh", image_wh), ("sample_location", sample_location),
+                 ("key_points", key_points)):
+        _check_dtype(name, t, (torch.float32,), k)
+    _check_dtype(name, depth_mask, (torch.uint8, torch.bool), "depth_mask")
+    _check_dtype(name, visible_idx, (torch.int32,), "visible_idx")
+    _check_dtype(name, visible_count, (torch.int32,), "visible_count")
+    _require(anchor.dim() == 3 and anchor.shape[-1] >= 8, "anchor must be [bs, A, >=8]")
+    bs, A = int(anchor.shape[0]), int(anchor.shape[1])
+    _require(projection_mat.dim() == 4 and projection_mat.shape[0] == bs and tuple(projection_mat.shape[2:]) == (4, 4),
+             "projection_mat must be [bs, Ncam, 4, 4]")
+    nc = int(projection_mat.shape[1])
+    _require(tuple(image_wh.shape) == (bs, nc, 2), "image_wh must be [bs, Ncam, 2]")
+    n_fix = 0 if fix_scale is None else int(fix_scale.shape[0])
+    if fix_scale is not None:
+        _require(fix_scale.dim() == 2 and fix_scale.shape[1] == 3, "fix_scale must be [num_fix, 3]")
+    n_learn = 0
+    if learnable_logits is not None:
+        _require(learnable_logits.dim() == 3 and tuple(learnable_logits.shape[:2]) == (bs, A)
+                 and learnable_logits.shape[2] % 3 == 0, "learnable_logits must be [bs, A, 3 * num_learnable]")
+        n_learn = int(learnable_logits.shape[2]) // 3
+    P = n_fix + n_learn
+    if sample_location is not None:
+        exp = (bs, A, nc, P, 2) if lay == L.S4D_LAYOUT_CAM_MAJOR else (bs, A, P, nc, 2)
+        _require(tuple(sample_location.shape) == exp, f"sample_location must be {list(exp)}")
+    if depth_mask is not None:
+        _require(tuple(depth_mask.shape) == (bs, A, nc, P), f"depth_mask must be [{bs}, {A}, {nc}, {P}]")
+    if key_points is not None:
+        _require(tuple(key_points.shape) == (bs, A, P, 3), f"key_points must be [{bs}, {A}, {P}, 3]")
+    if visible_idx is not None:
+        _require(tuple(visible_idx.shape) == (bs * A * nc * P, 4), "visible_idx must be [bs*A*Ncam*P, 4]")
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    st = L.lib().s4d_kps_project(
+        anchor.data_ptr(), int(anchor.shape[2]), _ptr(fix_scale), n_fix, _ptr(learnable_logits), n_learn,
+        projection_mat.data_ptr(), image_wh.data_ptr(), bs, A, nc, lay, _ptr(key_points), _ptr(sample_location),
+        _ptr(depth_mask), _ptr(visible_idx), _ptr(visible_count), _ptr(workspace), ws_bytes, _stream_ptr(dev))
+    L.check(name, st)
+
+
+@torch.library.custom_op("s4d::kps_project", mutates_args=())
+def kps_project(anchor: Tensor, learnable_logits: Optional[Tensor], fix_scale: Tensor, projection_mat: Tensor,
+                image_wh: Tensor, layout: int = 0) -> Tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Keypoints + projection + masks + compaction.
+
+    Returns ``(sample_location, depth_mask, visible_idx, visible_count, key_points)``:
+    ``sample_location [bs, A, Ncam, P, 2]`` (layout 0) or ``[bs, A, P, Ncam, 2]`` (layout 1),
+    ``depth_mask [bs, A, Ncam, P]`` uint8, ``visible_idx [bs*A*Ncam*P, 4]`` int32 whose first
+    ``visible_count[0]`` rows are the visible (b, a, cam, pt) in lexicographic order, and
+    ``key_points [bs, A, P, 3]``."""
+    bs, A = anchor.shape[:2]
+    nc = projection_mat.shape[1]
+    P = fix_scale.shape[0] + (0 if learnable_logits is None else learnable_logits.shape[2] // 3)
+    dev = anchor.device
+    loc_shape = (bs, A, nc, P, 2) if layout == L.S4D_LAYOUT_CAM_MAJOR else (bs, A, P, nc, 2)
+    loc = torch.empty(loc_shape, dtype=torch.float32, device=dev)
+    mask = torch.empty(bs, A, nc, P, dtype=torch.uint8, device=dev)
+    idx = torch.empty(bs * A * nc * P, 4, dtype=torch.int32, device=dev)
+    cnt = torch.zeros(1, dtype=torch.int32, device=dev)
+    kp = torch.empty(bs, A, P, 3, dtype=torch.float32, device=dev)
+    ws = torch.empty(max(kps_workspace_bytes(bs, A, nc, P), 16), dtype=torch.uint8, device=dev)
+    kps_project_into(anchor, learnable_logits, fix_scale, projection_mat, image_wh, loc, mask, idx, cnt, kp, ws,
+                     layout)
+    return loc, mask, idx, cnt, kp
+
+
+@kps_project.register_fake
+def _(anchor, learnable_logits, fix_scale, projection_mat, image_wh, layout=0):
+    bs, A = anchor.shape[:2]
+    nc = projection_mat.shape[1]
+    P = fix_scale.shape[0] + (0 if learnable_logits is None else learnable_logits.shape[2] // 3)
+    loc_shape = (bs, A, nc, P, 2) if layout == 0 else (bs, A, P, nc, 2)
+    return (anchor.new_empty(loc_shape), anchor.new_empty(bs, A, nc, P, dtype=torch.uint8),
+            anchor.new_empty(bs * A * nc * P, 4, dtype=torch.int32), anchor.new_empty(1, dtype=torch.int32),
+            anchor.new_empty(bs, A, P, 3))
+
+
+def visible_indices(visible_idx: Tensor, visible_count: Tensor) -> Tensor:
+    """The valid rows of ``visible_idx`` (synchronises to read the count)."""
+    return visible_idx[: int(visible_count.item())]
+
+
+def kps_project_fused(key_points: Tensor, anchor: Tensor, projection_mat: Tensor, image_wh: Tensor, num_cams: int,
+                      num_pts: int) -> Tensor:
+    """``ttnn.kps_project_fused`` standard mode: ``key_points [n, P, 3]`` pre-rotation,
+    ``anchor [n, 1, 11]``, ``projection_mat [Ncam, 4, 4]``, ``image_wh [Ncam, 1, 2]`` ->
+    ``[Ncam, n, 1, 2P]`` holding ``clamp(2 * uv - 1, -2, 2)``."""
+    name = "kps_project_fused"
+    dev = _require_cuda(name, key_points, anchor, projection_mat, image_wh)
+    for k, t in (("key_points", key_points), ("anchor", anchor), ("projection_mat", projection_mat),
+                 ("image_wh", image_wh)):
+        _check_dtype(name, t, (torch.float32,), k)
+    _require(key_points.dim() == 3 and key_points.shape[1] == num_pts and key_points.shape[2] == 3,
+             "key_points must be [n, num_pts, 3]")
+    n = int(key_points.shape[0])
+    anchor2 = anchor.reshape(n, -1).contiguous()
+    proj = projection_mat.reshape(num_cams, 4, 4).contiguous()
+    wh = image_wh.reshape(num_cams, 2).contiguous()
+    kp = key_points.contiguous()
+    out = torch.empty(num_cams, n, 1, num_pts * 2, dtype=torch.float32, device=dev)
+    st = L.lib().s4d_kps_project_fused(kp.data_ptr(), anchor2.data_ptr(), int(anchor2.shape[1]), proj.data_ptr(),
+                                       wh.data_ptr(), n, int(num_cams), int(num_pts), out.data_ptr(),
+                                       _stream_ptr(dev))
+    L.check(name, st)
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
+# feature-map packing
+# ---------------------------------------------------------------------------------------------
+
+def level_tables(spatial_shapes: Sequence[Tuple[int, int]], num_cams: int, device=None):
+    """``spatial_shape [Ncam, L, 2]`` and ``scale_start_index [Ncam, L]`` (int32) of the packed
+    camera-major layout, plus ``num_feat`` (rows per batch item)."""
+    hw = [int(h) * int(w) for h, w in spatial_shapes]
+    per_cam = sum(hw)
+    starts, acc = [], 0
+    for v in hw:
+        starts.append(acc)
+        acc += v
+    shape = torch.tensor([[list(s) for s in spatial_shapes]] * num_cams, dtype=torch.int32)
+    start = torch.tensor([[c * per_cam + s for s in starts] for c in range(num_cams)], dtype=torch.int32)
+    if device is not None:
+        shape, start = shape.to(device), start.to(device)
+    return shape, start, per_cam * num_cams
+
+
+def pack_feature_maps(feature_maps: List[Tensor], dtype: Optional[torch.dtype] = None, channels_last: bool = False):
+    """Pack per-level maps into ``(mc_ms_feat [bs, Ncam*sum(HW), C], spatial_shape,
+    scale_start_index)``.  Maps are NCHW ``[bs, Ncam, C, H, W]`` (the oracle's format), or with
+    ``channels_last=True`` ``[bs, Ncam, H, W, C]``.  This is one copy of the maps; producers
+    that can write the packed layout directly skip it."""
+    if channels_last:
+        bs, nc = feature_maps[0].shape[:2]
+        shapes = [(int(f.shape[2]), int(f.shape[3])) for f in feature_maps]
+        cols = [f.reshape(bs, nc, -1, f.shape[-1]) for f in feature_maps]
+    else:
+        bs, nc = feature_maps[0].shape[:2]
+        shapes = [(int(f.shape[3]), int(f.shape[4])) for f in feature_maps]
+        cols = [f.flatten(3).transpose(2, 3) for f in feature_maps]
+    packed = torch.cat(cols, dim=2).reshape(bs, -1, cols[0].shape[-1])
+    packed = packed.to(dtype).contiguous() if dtype is not None else packed.contiguous()
+    shape, start, _ = level_tables(shapes, nc, device=packed.device)
+    return packed, shape, start

@@ -1,0 +1,97 @@
+"""Helpers shared by the golden-fixture generator and the tests that read the fixtures.
+
+The fixtures hold the reference's outputs on seeded inputs.  Inputs are not stored; they are
+regenerated from their seed (torch's CPU generator is deterministic for a given torch build),
+and the fixture stores checksums of every input so a regeneration that drifts fails loudly
+instead of comparing against the wrong case.
+"""
+from __future__ import annotations
+
+import os
+from typing import Dict, List, Tuple
+
+import numpy as np
+import torch
+
+GOLDEN_DIR = os.path.dirname(os.path.abspath(__file__))
+
+
+def checksum(t) -> np.ndarray:
+    """(sum, position-weighted sum, sum of squares) in float64; order-sensitive."""
+    a = np.asarray(t.detach().cpu().double().numpy() if isinstance(t, torch.Tensor) else t, dtype=np.float64).ravel()
+    w = (np.arange(a.size) % 97 + 1).astype(np.float64)
+    return np.array([a.sum(), (a * w).sum(), (a * a).sum()])
+
+
+def pack_bits(mask) -> np.ndarray:
+    m = np.asarray(mask.cpu().numpy() if isinstance(mask, torch.Tensor) else mask, dtype=bool).ravel()
+    return np.packbits(m)
+
+
+def unpack_bits(bits: np.ndarray, shape) -> np.ndarray:
+    n = int(np.prod(shape))
+    return np.unpackbits(bits)[:n].astype(bool).reshape(shape)
+
+
+def load(name: str) -> Dict[str, np.ndarray]:
+    path = os.path.join(GOLDEN_DIR, name + ".npz")
+    with np.load(path, allow_pickle=False) as z:
+        return {k: z[k] for k in z.files}
+
+
+# Rows of the large cases whose full values are stored (the rest is pinned by per-row
+# checksums).
+def sample_rows(n: int, k: int = 32, seed: int = 1234) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    return np.sort(rng.choice(n, size=min(k, n), replace=False))
+
+
+# ---------------------------------------------------------------------------------------
+# Replay of the reference's own test case: ``create_dummy_inputs`` (seed 42) followed by
+# ``build_pt_dfa()`` with torch's default Linear init (``test/dfa_pcc.py:170-204,361-371``,
+# as ``test_e2e_pcc`` calls them at ``:496-519``).  The replay draws from the global RNG in
+# the same order so that the case can be rebuilt where the reference is not installed; the
+# fixture's checksums of inputs and parameters prove that it matches.
+# ---------------------------------------------------------------------------------------
+
+def reference_dummy_case(bs: int, num_anchor: int = 900, num_cams: int = 6, embed_dims: int = 256,
+                         spatial_shapes: List[Tuple[int, int]] = ((64, 176), (32, 88), (16, 44), (8, 22)),
+                         num_groups: int = 8, num_pts: int = 13, num_learnable_pts: int = 6):
+    torch.manual_seed(42)
+    inst = torch.randn(bs, num_anchor, embed_dims)
+    anchor = torch.randn(bs, num_anchor, 11)
+    anchor[..., 3:6] = torch.randn(bs, num_anchor, 3) * 0.5
+    yaw = torch.randn(bs, num_anchor, 1)
+    anchor[..., 6] = torch.sin(yaw).squeeze(-1)
+    anchor[..., 7] = torch.cos(yaw).squeeze(-1)
+    embed = torch.randn(bs, num_anchor, embed_dims)
+    proj = torch.randn(bs, num_cams, 4, 4)
+    wh = torch.tensor([[704.0, 256.0]]).unsqueeze(0).expand(bs, num_cams, 2).contiguous()
+    maps = [torch.randn(bs, num_cams, embed_dims, h, w) for h, w in spatial_shapes]
+    # Module construction order of the reference DFA: keypoint fc, output projection,
+    # camera encoder (Linear, ReLU, LN, Linear, ReLU, LN), weights fc.
+    learn = torch.nn.Linear(embed_dims, num_learnable_pts * 3)
+    out_proj = torch.nn.Linear(embed_dims, embed_dims)
+    cam1 = torch.nn.Linear(12, embed_dims)
+    cam2 = torch.nn.Linear(embed_dims, embed_dims)
+    wfc = torch.nn.Linear(embed_dims, num_groups * len(spatial_shapes) * num_pts)
+    from sparse4d_tt_b200.synthetic import FIX_SCALE
+
+    params = {
+        "kps_fix_scale": torch.tensor(FIX_SCALE, dtype=torch.float32),
+        "kps_learnable_fc_weight": learn.weight.data.clone(),
+        "kps_learnable_fc_bias": learn.bias.data.clone(),
+        "cam_linear1_weight": cam1.weight.data.clone(),
+        "cam_linear1_bias": cam1.bias.data.clone(),
+        "cam_ln1_weight": torch.ones(embed_dims),
+        "cam_ln1_bias": torch.zeros(embed_dims),
+        "cam_linear2_weight": cam2.weight.data.clone(),
+        "cam_linear2_bias": cam2.bias.data.clone(),
+        "cam_ln2_weight": torch.ones(embed_dims),
+        "cam_ln2_bias": torch.zeros(embed_dims),
+        "weights_fc_weight": wfc.weight.data.clone(),
+        "weights_fc_bias": wfc.bias.data.clone(),
+        "output_proj_weight": out_proj.weight.data.clone(),
+        "output_proj_bias": out_proj.bias.data.clone(),
+    }
+    return (inst, anchor, embed, maps, proj, wh), params

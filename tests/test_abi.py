@@ -1,0 +1,171 @@
+"""The C-ABI library: it loads, exports every function that include/s4d_dfa.h declares, and
+rejects bad arguments on the host with a status code (no GPU needed: none of these calls
+reaches a launch)."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from sparse4d_tt_b200 import _lib as L
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "s4d_dfa.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(s4d_[a-z_0-9]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(L.LIB_PATH):
+        import importlib.util
+
+        spec = importlib.util.spec_from_file_location("s4d_build", os.path.join(REPO, "sparse4d-tt_b200", "build.py"))
+        b = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(b)
+        b.build()
+    return L.lib()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_functions()
+    assert len(names) == 7, names
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in L.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_no_extra_exports(lib):
+    """Hidden visibility: only the declared API is exported."""
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", L.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    assert {n for n in exported if n.startswith("s4d_")} == set(declared_functions())
+
+
+def test_status_strings_and_version(lib):
+    assert L.status_string(0) == "S4D_OK"
+    assert L.status_string(2) == "S4D_ERR_UNSUPPORTED_SHAPE"
+    assert L.status_string(99) == "S4D_ERR_UNKNOWN"
+    assert lib.s4d_abi_version() == 100
+
+
+def test_workspace_bytes(lib):
+    assert lib.s4d_kps_workspace_bytes(1, 900, 6, 13) >= 4 * 69 + 4 * 69 * 32
+    assert lib.s4d_kps_workspace_bytes(0, 900, 6, 13) == 0
+    assert lib.s4d_kps_workspace_bytes(2, 900, 6, 13) > lib.s4d_kps_workspace_bytes(1, 900, 6, 13)
+
+
+def _gather(lib, **kw):
+    args = dict(feat=8, dtype=1, num_feat=100, shape=8, start=8, loc=8, w=8, wc=None, logits=1, layout=0, bs=1,
+                A=4, nc=6, nl=4, np=13, G=8, C=256, cb=0, ce=6, out=8, flag=None)
+    args.update(kw)
+    st = lib.s4d_deformable_aggregation(
+        args["feat"], args["dtype"], args["num_feat"], args["shape"], args["start"], args["loc"], args["w"],
+        args["wc"], args["logits"], args["layout"], args["bs"], args["A"], args["nc"], args["nl"], args["np"],
+        args["G"], args["C"], args["cb"], args["ce"], args["out"], args["flag"], None)
+    return st, lib.s4d_last_error().decode()
+
+
+@pytest.mark.parametrize("kw,status,text", [
+    (dict(C=128), L.S4D_ERR_UNSUPPORTED_SHAPE, "embed_dims"),
+    (dict(G=3), L.S4D_ERR_UNSUPPORTED_SHAPE, "num_groups"),
+    (dict(G=64), L.S4D_ERR_UNSUPPORTED_SHAPE, "num_groups"),
+    (dict(np=200, nl=4), L.S4D_ERR_UNSUPPORTED_SHAPE, "12288"),
+    (dict(dtype=7), L.S4D_ERR_INVALID_ARG, "feat_dtype"),
+    (dict(layout=2), L.S4D_ERR_INVALID_ARG, "layout"),
+    (dict(cb=4, ce=2), L.S4D_ERR_INVALID_ARG, "cam_begin"),
+    (dict(ce=7), L.S4D_ERR_INVALID_ARG, "cam_begin"),
+    (dict(wc=8, layout=1), L.S4D_ERR_INVALID_ARG, "weights_cam"),
+    (dict(wc=8, logits=0), L.S4D_ERR_INVALID_ARG, "split"),
+    (dict(feat=None), L.S4D_ERR_INVALID_ARG, "null"),
+    (dict(feat=24), L.S4D_ERR_INVALID_ARG, "16-byte"),
+    (dict(bs=-1), L.S4D_ERR_INVALID_ARG, "positive"),
+])
+def test_gather_rejects_on_host(lib, kw, status, text):
+    st, msg = _gather(lib, **kw)
+    assert st == status, (st, msg)
+    assert text in msg
+
+
+def test_gather_empty_batch_is_a_noop(lib):
+    st, msg = _gather(lib, bs=0, feat=None, out=None)
+    assert st == L.S4D_OK, msg
+
+
+def _kps(lib, **kw):
+    a = dict(anchor=16, adim=11, fix=16, nfix=7, learn=16, nlearn=6, proj=16, wh=16, bs=1, A=4, nc=6, layout=0,
+             kp=None, loc=16, mask=None, idx=16, cnt=16, ws=16, wsb=1 << 20)
+    a.update(kw)
+    st = lib.s4d_kps_project(a["anchor"], a["adim"], a["fix"], a["nfix"], a["learn"], a["nlearn"], a["proj"],
+                             a["wh"], a["bs"], a["A"], a["nc"], a["layout"], a["kp"], a["loc"], a["mask"], a["idx"],
+                             a["cnt"], a["ws"], a["wsb"], None)
+    return st, lib.s4d_last_error().decode()
+
+
+@pytest.mark.parametrize("kw,status,text", [
+    (dict(adim=7), L.S4D_ERR_INVALID_ARG, "anchor_dim"),
+    (dict(layout=5), L.S4D_ERR_INVALID_ARG, "layout"),
+    (dict(nfix=-1), L.S4D_ERR_INVALID_ARG, "negative"),
+    (dict(anchor=None), L.S4D_ERR_INVALID_ARG, "null"),
+    (dict(learn=None), L.S4D_ERR_INVALID_ARG, "learnable"),
+    (dict(idx=20), L.S4D_ERR_INVALID_ARG, "visible_idx"),
+    (dict(loc=20), L.S4D_ERR_INVALID_ARG, "sample_location"),
+    (dict(ws=None), L.S4D_ERR_INVALID_ARG, "workspace"),
+    (dict(wsb=8), L.S4D_ERR_INVALID_ARG, "workspace"),
+    (dict(A=1 << 30), L.S4D_ERR_UNSUPPORTED_SHAPE, "2^31"),
+    (dict(nfix=0, nlearn=0), L.S4D_ERR_INVALID_ARG, "keypoints"),
+])
+def test_kps_rejects_on_host(lib, kw, status, text):
+    st, msg = _kps(lib, **kw)
+    assert st == status, (st, msg)
+    assert text in msg
+
+
+def test_kps_fused_rejects_on_host(lib):
+    st = lib.s4d_kps_project_fused(16, 16, 5, 16, 16, 4, 6, 13, 16, None)
+    assert st == L.S4D_ERR_INVALID_ARG
+    st = lib.s4d_kps_project_fused(None, 16, 11, 16, 16, 4, 6, 13, 16, None)
+    assert st == L.S4D_ERR_INVALID_ARG
+    st = lib.s4d_kps_project_fused(16, 16, 11, 16, 16, 0, 6, 13, 16, None)
+    assert st == L.S4D_OK  # nothing to do
+
+
+def test_last_error_is_per_thread(lib):
+    import threading
+
+    st, msg = _gather(lib, C=128)
+    assert "embed_dims" in msg
+    seen = {}
+
+    def other():
+        seen["msg"] = lib.s4d_last_error().decode()
+
+    t = threading.Thread(target=other)
+    t.start()
+    t.join()
+    assert seen["msg"] == ""
+    assert "embed_dims" in lib.s4d_last_error().decode()
+
+
+def test_ops_reject_cpu_tensors():
+    """No CPU fallback: the operators refuse host tensors."""
+    import torch
+
+    from sparse4d_tt_b200 import ops
+
+    feat = torch.zeros(1, 10, 256)
+    shape = torch.zeros(6, 4, 2, dtype=torch.int32)
+    start = torch.zeros(6, 4, dtype=torch.int32)
+    loc = torch.zeros(1, 2, 6, 13, 2)
+    w = torch.zeros(1, 2, 6, 4, 13, 8)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.deformable_aggregation_into(torch.zeros(1, 2, 256), feat, shape, start, loc, w)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.kps_project_into(torch.zeros(1, 2, 11), torch.zeros(1, 2, 18), torch.zeros(7, 3),
+                             torch.zeros(1, 6, 4, 4), torch.zeros(1, 6, 2))

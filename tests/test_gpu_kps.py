@@ -1,0 +1,145 @@
+"""Kernel (a) on the GPU against the oracle and the reference's fixtures: projected points
+within float tolerance, depth mask / frustum mask / compacted (b, a, cam, pt) indices bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+import fixtures as fx
+from helpers import regen
+from oracle import dfa_numpy as onp
+from oracle import dfa_torch as oto
+from sparse4d_tt_b200 import ops
+from sparse4d_tt_b200 import synthetic as syn
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(anchor, learn, fix, proj, wh, layout=0):
+    d = torch.device("cuda:0")
+    out = ops.kps_project(anchor.to(d), None if learn is None else learn.to(d), fix.to(d), proj.to(d), wh.to(d),
+                          layout)
+    torch.cuda.synchronize()
+    loc, mask, idx, cnt, kp = [t.cpu() for t in out]
+    return loc, mask, idx[: int(cnt[0])], int(cnt[0]), kp
+
+
+def _margins(uv, depth):
+    """Distance of the nearest sample to a mask threshold (explains any flip)."""
+    u, v = uv[..., 0].abs(), uv[..., 1].abs()
+    return {
+        "depth": float((depth - 1e-5).abs().min()),
+        "u0": float(u.min()), "u1": float((1 - uv[..., 0]).abs().min()),
+        "v0": float(v.min()), "v1": float((1 - uv[..., 1]).abs().min()),
+    }
+
+
+@pytest.mark.parametrize("name", ["standard_s0_fp32", "highres_s2_bf16", "small_b2_s3", "small_b1_s4_cam3"])
+def test_kps_bit_exact_masks_and_indices(cuda_device, name):
+    g, cfg, ins, params = regen(name)
+    learn = oto.learnable_logits(ins.instance_feature, params)  # the oracle's own fp32 logits
+    loc, mask, idx, cnt, kp = _run(ins.anchor, learn, params["kps_fix_scale"], ins.projection_mat, ins.image_wh)
+    bs, A, nc, P = cfg.bs, cfg.num_anchor, cfg.num_cams, cfg.num_pts
+    ref_mask = fx.unpack_bits(g["mask_bits"], (bs, A, nc, P))
+    ref_vis = fx.unpack_bits(g["vis_bits"], (bs, A, nc, P))
+    assert np.array_equal(mask.numpy().astype(bool), ref_mask)
+    assert cnt == int(ref_vis.sum())
+    assert np.array_equal(idx.numpy(), np.argwhere(ref_vis).astype(np.int32))
+    # the numpy oracle evaluates the same fixed order: identical masks
+    kp_np = onp.key_points(ins.anchor.numpy(), learn.numpy(), params["kps_fix_scale"].numpy())
+    uv_np, mask_np, vis_np = onp.project(kp_np, ins.projection_mat.numpy(), ins.image_wh.numpy())
+    assert np.array_equal(mask.numpy().astype(bool), mask_np)
+    np.testing.assert_allclose(kp.numpy(), kp_np, rtol=1e-5, atol=1e-5)
+    finite = np.isfinite(uv_np) & (np.abs(uv_np) < 1e3)
+    np.testing.assert_allclose(loc.numpy()[finite], uv_np[finite], rtol=1e-4, atol=1e-6)
+    kps_t = oto.key_points(ins.anchor, ins.instance_feature, params)
+    uv_t, depth_t = oto.project_points_with_depth(kps_t, ins.projection_mat, ins.image_wh)
+    m = _margins(uv_t, depth_t)
+    print(f"{name}: visible={cnt} margins={m}")
+
+
+@pytest.mark.parametrize("bs", [1, 2])
+def test_kps_reference_dummy_inputs(cuda_device, bs):
+    """The reference's own e2e inputs (random N(0,1) projection matrices)."""
+    g = fx.load(f"refdummy_bs{bs}")
+    (inst, anchor, embed, maps, proj, wh), params = fx.reference_dummy_case(bs)
+    learn = oto.learnable_logits(inst, params)
+    loc, mask, idx, cnt, kp = _run(anchor, learn, params["kps_fix_scale"], proj, wh)
+    ref_vis = fx.unpack_bits(g["vis_bits"], (bs, 900, 6, 13))
+    assert cnt == int(ref_vis.sum())
+    assert np.array_equal(idx.numpy(), np.argwhere(ref_vis).astype(np.int32))
+    rows = g["rows"]
+    np.testing.assert_allclose(kp.reshape(bs * 900, 13, 3).numpy()[rows], g["kp_rows"], rtol=1e-5, atol=1e-5)
+
+
+def test_kps_layouts_agree(cuda_device):
+    cfg = syn.DFAConfig(bs=2, num_anchor=77)
+    ins = syn.make_inputs(cfg, 11)
+    params = syn.make_params(cfg, torch.Generator().manual_seed(5))
+    learn = oto.learnable_logits(ins.instance_feature, params)
+    a = _run(ins.anchor, learn, params["kps_fix_scale"], ins.projection_mat, ins.image_wh, 0)
+    b = _run(ins.anchor, learn, params["kps_fix_scale"], ins.projection_mat, ins.image_wh, 1)
+    assert torch.equal(a[0], b[0].permute(0, 1, 3, 2, 4))
+    assert torch.equal(a[1], b[1]) and torch.equal(a[2], b[2])
+
+
+def test_kps_edge_cases(cuda_device):
+    d = torch.device("cuda:0")
+    fix = torch.tensor(syn.FIX_SCALE)
+    proj = syn.camera_ring(6, (704, 256))[None]
+    wh = torch.tensor([[704.0, 256.0]]).expand(1, 6, 2).contiguous()
+    # no anchors: count is 0
+    loc, mask, idx, cnt, kp = _run(torch.zeros(1, 0, 11), torch.zeros(1, 0, 18), fix, proj, wh)
+    assert cnt == 0 and loc.numel() == 0
+    # one anchor straight ahead of camera 0 at 20 m: its centre is visible in camera 0
+    a = torch.zeros(1, 1, 11)
+    a[0, 0, 0] = 20.0
+    a[0, 0, 2] = 1.5
+    a[0, 0, 7] = 1.0
+    loc, mask, idx, cnt, kp = _run(a, torch.zeros(1, 1, 18), fix, proj, wh)
+    assert cnt > 0 and idx[0].tolist() == [0, 0, 0, 0]
+    np.testing.assert_allclose(loc[0, 0, 0, 0].numpy(), [0.5, 0.5], atol=1e-6)
+    # anchors behind every camera plane of a forward-only rig: nothing in front
+    proj1 = proj[:, :1].contiguous()
+    a2 = a.clone()
+    a2[0, 0, 0] = -20.0
+    loc, mask, idx, cnt, kp = _run(a2, torch.zeros(1, 1, 18), fix, proj1, wh[:, :1].contiguous())
+    assert cnt == 0 and int(mask.sum()) == 0
+    # no learnable points; extra anchor fields beyond the 11 are ignored
+    cfg = syn.DFAConfig(bs=1, num_anchor=50)
+    ins = syn.make_inputs(cfg, 3)
+    wide = torch.cat([ins.anchor, torch.randn(1, 50, 5)], dim=-1).contiguous()
+    r1 = _run(ins.anchor, None, fix, ins.projection_mat, ins.image_wh)
+    r2 = _run(wide, None, fix, ins.projection_mat, ins.image_wh)
+    assert torch.equal(r1[0], r2[0]) and torch.equal(r1[2], r2[2])
+    assert r1[0].shape == (1, 50, 6, 7, 2)
+
+
+def test_kps_project_fused_dropin(cuda_device):
+    """``ttnn.kps_project_fused`` arguments and output: grid = clamp(2 uv - 1, -2, 2)."""
+    cfg = syn.DFAConfig(bs=1, num_anchor=64)
+    ins = syn.make_inputs(cfg, 21)
+    params = syn.make_params(cfg, torch.Generator().manual_seed(2))
+    learn = oto.learnable_logits(ins.instance_feature, params)
+    n = 64
+    size = ins.anchor[0, :, 3:6].exp()[:, None]
+    pre = torch.cat([params["kps_fix_scale"][None] * size,
+                     (learn[0].reshape(n, 6, 3).sigmoid() - 0.5) * size], dim=1).contiguous()
+    d = torch.device("cuda:0")
+    grid = ops.kps_project_fused(pre.to(d), ins.anchor[0].reshape(n, 1, 11).to(d),
+                                 ins.projection_mat[0].to(d), ins.image_wh[0].reshape(6, 1, 2).to(d), 6, 13)
+    torch.cuda.synchronize()
+    assert grid.shape == (6, n, 1, 26)
+    kps = oto.key_points(ins.anchor, ins.instance_feature, params)
+    uv, _ = oto.project_points_with_depth(kps, ins.projection_mat, ins.image_wh)
+    ref = (uv[0] * 2 - 1).clamp(-2, 2).reshape(6, n, 1, 26)
+    np.testing.assert_allclose(grid.cpu().numpy(), ref.numpy(), rtol=1e-4, atol=1e-5)
+
+
+def test_kps_deterministic(cuda_device):
+    g, cfg, ins, params = regen("standard_s0_fp32")
+    learn = oto.learnable_logits(ins.instance_feature, params)
+    a = _run(ins.anchor, learn, params["kps_fix_scale"], ins.projection_mat, ins.image_wh)
+    b = _run(ins.anchor, learn, params["kps_fix_scale"], ins.projection_mat, ins.image_wh)
+    for x, y in zip(a, b):
+        if isinstance(x, torch.Tensor):
+            assert torch.equal(x, y)
