@@ -251,10 +251,12 @@ def time_steps(fn, steps, sync_barrier):
     sync_barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     e0.record()
     for _ in range(steps):
         fn()
     e1.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     sync_barrier()
     return e0.elapsed_time(e1)
