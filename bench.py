@@ -87,13 +87,37 @@ def workload_config(frames, layers, world):
 # clocks
 # ---------------------------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock and clock-event reasons sampled during the timed region: NVML polled every
+    20 ms from a thread (read-only queries), or nvidia-smi at 200 ms when NVML is missing."""
+
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, device):
         self.proc = None
         self.lines = []
+        self.nvml = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            gid = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            h = pynvml.nvmlDeviceGetHandleByUUID(gid)
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.nvml = (pynvml, h, reasons)
+            self.samples = []
+            self.stop_flag = threading.Event()
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return
+        except Exception:
+            self.nvml = None
         try:
             uuid = str(torch.cuda.get_device_properties(device).uuid)
             gid = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
@@ -109,7 +133,26 @@ class ClockSampler:
         for ln in self.proc.stdout:
             self.lines.append(ln.strip())
 
+    def _poll(self):
+        pynvml, h, reasons = self.nvml
+        while not self.stop_flag.is_set():
+            try:
+                self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                     pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), int(reasons(h))))
+            except Exception:
+                pass
+            self.stop_flag.wait(0.02)
+
     def stop(self):
+        if self.nvml is not None:
+            self.stop_flag.set()
+            self.t.join(timeout=2)
+            if not self.samples:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "source": "nvml"}
+            found = sorted({n for _, _, r in self.samples for n, bit in self.REASON_BITS.items() if r & bit})
+            return {"sm_mhz": statistics.median(s for s, _, _ in self.samples),
+                    "sm_max_mhz": max(m for _, m, _ in self.samples), "reasons": found,
+                    "samples": len(self.samples), "source": "nvml, 20 ms"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()

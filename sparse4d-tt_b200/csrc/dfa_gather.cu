@@ -313,6 +313,304 @@ __global__ void __launch_bounds__(kGatherThreads, 4) dfa_gather_kernel(GatherPar
   }
 }
 
+// -----------------------------------------------------------------------------------------------
+// Shape-specialised kernel for the Sparse4D v3 layout (compile-time Ncam, L, P, G; cam-major
+// logits, full or split).  Same five phases as dfa_gather_kernel, with the fixed per-anchor
+// work cut down so that the kernel is bound by memory rather than by instruction issue:
+//   * logits staged as float4 (split logits: per-anchor row + per-camera row, both float4)
+//     with the running max fused into the staging loop.  Element 4i+k of the staged row
+//     belongs to group (4i + k) % G, and with a 256-thread stride i = t (mod 256), so every
+//     thread only ever sees the 4 groups (4t + k) % G: 4 register "slots" per thread, reduced
+//     across lanes with equal t mod G/4 by xor shuffles and across warps in shared memory;
+//   * exp as ex2.approx of a fused (x - max) * log2(e), unnormalised; 1/sum applied once per
+//     output channel at the end;
+//   * candidate (camera, level, point) indices decoded with compile-time divisors; both
+//     candidates of a thread compacted with one block prefix;
+//   * taps widened bf16 -> fp32 by shift/mask and accumulated with packed fp32x2 FMA
+//     (__ffma2_rn), 4 instructions per 8 channels.
+// -----------------------------------------------------------------------------------------------
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T>
+struct TapFma;
+
+template <>
+struct TapFma<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* fb, int pix, int lane, uint4& v) {
+    v = ldg_nc_v4(fb + (int64_t)pix * kChannels + lane * 8);
+  }
+  static __device__ __forceinline__ void fma(const uint4& v, float w, float2 (&acc)[4]) {
+    const float2 ww = make_float2(w, w);
+    const uint32_t q[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = make_float2(__uint_as_float(q[i] << 16), __uint_as_float(q[i] & 0xffff0000u));
+      acc[i] = __ffma2_rn(ww, f, acc[i]);
+    }
+  }
+};
+
+template <>
+struct TapFma<float> {
+  struct V {
+    float4 a, b;
+  };
+  static __device__ __forceinline__ void load(const float* fb, int pix, int lane, V& v) {
+    const float* row = fb + (int64_t)pix * kChannels + lane * 8;
+    v.a = ldg_nc_f4(row);
+    v.b = ldg_nc_f4(row + 4);
+  }
+  static __device__ __forceinline__ void fma(const V& v, float w, float2 (&acc)[4]) {
+    const float2 ww = make_float2(w, w);
+    acc[0] = __ffma2_rn(ww, make_float2(v.a.x, v.a.y), acc[0]);
+    acc[1] = __ffma2_rn(ww, make_float2(v.a.z, v.a.w), acc[1]);
+    acc[2] = __ffma2_rn(ww, make_float2(v.b.x, v.b.y), acc[2]);
+    acc[3] = __ffma2_rn(ww, make_float2(v.b.z, v.b.w), acc[3]);
+  }
+};
+
+template <typename T>
+struct TapVec {
+  using type = uint4;
+};
+template <>
+struct TapVec<float> {
+  using type = TapFma<float>::V;
+};
+
+// Slot reduction: after it, s_out[g] holds the max (kMax) or sum over every thread's slot
+// values of group g, where slot k of thread t belongs to group (4t + k) % G.
+template <int G, bool kMax>
+__device__ __forceinline__ void slot_reduce(float (&v)[4], float (*s_part)[8][4], float* s_out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = G / 4; o < 32; o <<= 1) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float t = __shfl_xor_sync(0xffffffffu, v[k], o);
+      v[k] = kMax ? fmaxf(v[k], t) : v[k] + t;
+    }
+  }
+  if (lane < G / 4) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) s_part[warp][lane][k] = v[k];
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int l = threadIdx.x >> 2, k = threadIdx.x & 3;
+    float r = s_part[0][l][k];
+#pragma unroll
+    for (int w = 1; w < kGatherWarps; ++w) r = kMax ? fmaxf(r, s_part[w][l][k]) : r + s_part[w][l][k];
+    s_out[threadIdx.x] = r;
+  }
+  __syncthreads();
+}
+
+template <typename T, int NC, int NL, int NP, int G>
+__global__ void __launch_bounds__(kGatherThreads, 4) dfa_gather_fast_kernel(GatherParams p) {
+  constexpr int NCLP = NC * NL * NP;
+  constexpr int LPG = NL * NP * G;
+  constexpr int NW4 = NC * LPG / 4;
+  constexpr int LPG4 = LPG / 4;
+  constexpr int D = kChannels / G;
+  constexpr float kLog2e = 1.4426950408889634f;
+  static_assert(LPG % 4 == 0 && G >= 4 && G <= 32 && (G & (G - 1)) == 0, "fast gather shape");
+  static_assert(NCLP <= 2 * kGatherThreads, "two candidates per thread");
+  static_assert(NCLP * 32 >= kGatherWarps * kChannels * 4, "reduction buffer aliases the sample list");
+
+  __shared__ __align__(16) float4 s_w4[NW4];
+  __shared__ __align__(16) float2 s_loc[NC * NP];
+  __shared__ __align__(16) int4 s_lvl[NC * NL];  // (H, W, start, ok)
+  __shared__ __align__(16) unsigned char s_list[NCLP * 32];
+  __shared__ int s_clp[NCLP];
+  __shared__ float s_part[kGatherWarps][8][4];
+  __shared__ float s_gmax[G];
+  __shared__ float s_ginv[G];
+  __shared__ int s_wcnt[2][kGatherWarps];
+
+  int4* s_pix = reinterpret_cast<int4*>(s_list);
+  float4* s_bw = reinterpret_cast<float4*>(s_list + NCLP * 16);
+  float* s_red = reinterpret_cast<float*>(s_list);
+  const float* s_w = reinterpret_cast<const float*>(s_w4);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t anchor_lin = blockIdx.x;
+  const int b = (int)(anchor_lin / p.num_anchor);
+
+  // ---- 1. stage levels, locations and logits (running max in 4 slots) --------------------
+  if (tid < NC * NL) {
+    const int H = p.spatial_shape[2 * tid], W = p.spatial_shape[2 * tid + 1], st = p.scale_start[tid];
+    const bool ok = H > 0 && W > 0 && st >= 0 && (int64_t)st + (int64_t)H * W <= p.num_feat;
+    const int c = tid / NL;
+    if (!ok && c >= p.cam_begin && c < p.cam_end && p.error_flag != nullptr && blockIdx.x == 0)
+      atomicOr(p.error_flag, S4D_FLAG_BAD_LEVEL);
+    s_lvl[tid] = make_int4(H, W, st, ok ? 1 : 0);
+  }
+  if (tid < NC * NP) s_loc[tid] = __ldg(reinterpret_cast<const float2*>(p.loc) + anchor_lin * (NC * NP) + tid);
+  float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  if (p.weights_cam != nullptr) {
+    const float4* wa = reinterpret_cast<const float4*>(p.weights) + anchor_lin * LPG4;
+    const float4* wc = reinterpret_cast<const float4*>(p.weights_cam) + (int64_t)b * NW4;
+#pragma unroll
+    for (int i = tid; i < NW4; i += kGatherThreads) {
+      const int c = i / LPG4;
+      const float4 x = __ldg(wa + (i - c * LPG4)), y = __ldg(wc + i);
+      const float4 v = make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+      s_w4[i] = v;
+      m[0] = fmaxf(m[0], v.x);
+      m[1] = fmaxf(m[1], v.y);
+      m[2] = fmaxf(m[2], v.z);
+      m[3] = fmaxf(m[3], v.w);
+    }
+  } else {
+    const float4* src = reinterpret_cast<const float4*>(p.weights) + anchor_lin * NW4;
+#pragma unroll
+    for (int i = tid; i < NW4; i += kGatherThreads) {
+      const float4 v = ldg_nc_f4(src + i);
+      s_w4[i] = v;
+      m[0] = fmaxf(m[0], v.x);
+      m[1] = fmaxf(m[1], v.y);
+      m[2] = fmaxf(m[2], v.z);
+      m[3] = fmaxf(m[3], v.w);
+    }
+  }
+  slot_reduce<G, true>(m, s_part, s_gmax);  // its barriers also publish s_w4 / s_loc / s_lvl
+
+  // ---- 2. unnormalised exp + 3. candidate validity -----------------------------------------
+  float sum[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    float mg[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) mg[k] = s_gmax[(4 * tid + k) % G] * kLog2e;
+#pragma unroll
+    for (int i = tid; i < NW4; i += kGatherThreads) {
+      const float4 v = s_w4[i];
+      const float4 e = make_float4(ex2_approx(fmaf(v.x, kLog2e, -mg[0])), ex2_approx(fmaf(v.y, kLog2e, -mg[1])),
+                                   ex2_approx(fmaf(v.z, kLog2e, -mg[2])), ex2_approx(fmaf(v.w, kLog2e, -mg[3])));
+      s_w4[i] = e;
+      sum[0] += e.x;
+      sum[1] += e.y;
+      sum[2] += e.z;
+      sum[3] += e.w;
+    }
+  }
+  bool valid[2];
+  int4 pix[2];
+  float4 bw[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int i = tid + r * kGatherThreads;
+    valid[r] = false;
+    pix[r] = make_int4(-1, -1, -1, -1);
+    bw[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < NCLP) {
+      const int c = i / (NL * NP);
+      const int rem = i - c * (NL * NP);
+      const int l = rem / NP, pt = rem - l * NP;
+      if (c >= p.cam_begin && c < p.cam_end) {
+        const int4 lv = s_lvl[c * NL + l];
+        const float2 uv = s_loc[c * NP + pt];
+        const float Wf = (float)lv.y, Hf = (float)lv.x;
+        const float ix = ((uv.x * 2.0f - 1.0f + 1.0f) * Wf - 1.0f) * 0.5f;
+        const float iy = ((uv.y * 2.0f - 1.0f + 1.0f) * Hf - 1.0f) * 0.5f;
+        if (lv.w && ix > -1.0f && ix < Wf && iy > -1.0f && iy < Hf) {
+          const float x0f = floorf(ix), y0f = floorf(iy);
+          const int x0 = (int)x0f, y0 = (int)y0f;
+          const float x1f = x0f + 1.0f, y1f = y0f + 1.0f;
+          const bool vx0 = x0 >= 0, vx1 = x0 + 1 < lv.y, vy0 = y0 >= 0, vy1 = y0 + 1 < lv.x;
+          const int p00 = lv.z + y0 * lv.y + x0;
+          pix[r] = make_int4(vx0 && vy0 ? p00 : -1, vx1 && vy0 ? p00 + 1 : -1, vx0 && vy1 ? p00 + lv.y : -1,
+                             vx1 && vy1 ? p00 + lv.y + 1 : -1);
+          bw[r] = make_float4((x1f - ix) * (y1f - iy), (ix - x0f) * (y1f - iy), (x1f - ix) * (iy - y0f),
+                              (ix - x0f) * (iy - y0f));
+          valid[r] = true;
+        }
+      }
+    }
+  }
+  const uint32_t ball0 = __ballot_sync(0xffffffffu, valid[0]);
+  const uint32_t ball1 = __ballot_sync(0xffffffffu, valid[1]);
+  if (lane == 0) {
+    s_wcnt[0][warp] = __popc(ball0);
+    s_wcnt[1][warp] = __popc(ball1);
+  }
+  slot_reduce<G, false>(sum, s_part, s_gmax);  // s_gmax now holds the sums; barriers publish s_wcnt
+  if (tid < G) s_ginv[tid] = 1.0f / s_gmax[tid];
+  int n_valid = 0, off0 = 0, off1 = 0;
+#pragma unroll
+  for (int w = 0; w < kGatherWarps; ++w) {
+    off0 += w < warp ? s_wcnt[0][w] : 0;
+    n_valid += s_wcnt[0][w];
+  }
+  off1 = n_valid;
+#pragma unroll
+  for (int w = 0; w < kGatherWarps; ++w) {
+    off1 += w < warp ? s_wcnt[1][w] : 0;
+    n_valid += s_wcnt[1][w];
+  }
+  const uint32_t lt = (1u << lane) - 1u;
+  if (valid[0]) {
+    const int pos = off0 + __popc(ball0 & lt);
+    s_pix[pos] = pix[0];
+    s_bw[pos] = bw[0];
+    s_clp[pos] = tid;
+  }
+  if (valid[1]) {
+    const int pos = off1 + __popc(ball1 & lt);
+    s_pix[pos] = pix[1];
+    s_bw[pos] = bw[1];
+    s_clp[pos] = tid + kGatherThreads;
+  }
+  __syncthreads();
+
+  // ---- 4. weighted gather -------------------------------------------------------------------
+  const int g = lane / (D / 8);
+  const T* fb = static_cast<const T*>(p.feat) + (int64_t)b * p.num_feat * kChannels;
+  float2 acc[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.f, 0.f);
+  using V = typename TapVec<T>::type;
+  for (int s = warp; s < n_valid; s += kGatherWarps) {
+    const int4 px = s_pix[s];
+    const float4 w4 = s_bw[s];
+    const float sw = s_w[s_clp[s] * G + g];
+    V v0, v1, v2, v3;
+    if (px.x >= 0) TapFma<T>::load(fb, px.x, lane, v0);
+    if (px.y >= 0) TapFma<T>::load(fb, px.y, lane, v1);
+    if (px.z >= 0) TapFma<T>::load(fb, px.z, lane, v2);
+    if (px.w >= 0) TapFma<T>::load(fb, px.w, lane, v3);
+    if (px.x >= 0) TapFma<T>::fma(v0, w4.x * sw, acc);
+    if (px.y >= 0) TapFma<T>::fma(v1, w4.y * sw, acc);
+    if (px.z >= 0) TapFma<T>::fma(v2, w4.z * sw, acc);
+    if (px.w >= 0) TapFma<T>::fma(v3, w4.w * sw, acc);
+  }
+
+  // ---- 5. cross-warp reduction -------------------------------------------------------------
+  __syncthreads();
+  float4* r4 = reinterpret_cast<float4*>(s_red + warp * kChannels + lane * 8);
+  r4[0] = make_float4(acc[0].x, acc[0].y, acc[1].x, acc[1].y);
+  r4[1] = make_float4(acc[2].x, acc[2].y, acc[3].x, acc[3].y);
+  __syncthreads();
+  float v = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kGatherWarps; ++w) v += s_red[w * kChannels + tid];
+  p.out[anchor_lin * kChannels + tid] = v * s_ginv[tid / D];
+}
+
+// The Sparse4D v3 shape the fast kernel is compiled for.
+constexpr int kFastNC = 6, kFastNL = 4, kFastNP = 13, kFastG = 8;
+
+static bool fast_path_ok(const GatherParams& p) {
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  return p.layout == S4D_LAYOUT_CAM_MAJOR && p.logits && p.num_cams == kFastNC && p.num_levels == kFastNL &&
+         p.num_pts == kFastNP && p.num_groups == kFastG && al16(p.weights) &&
+         (p.weights_cam == nullptr || al16(p.weights_cam));
+}
+
 size_t gather_smem_bytes(int ncam, int nl, int np, int G, int cam_begin, int cam_end) {
   return gather_smem_layout(ncam, nl, np, G, cam_begin, cam_end).bytes;
 }
@@ -320,6 +618,13 @@ size_t gather_smem_bytes(int ncam, int nl, int np, int G, int cam_begin, int cam
 int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream) {
   const size_t smem = gather_smem_bytes(p.num_cams, p.num_levels, p.num_pts, p.num_groups, p.cam_begin, p.cam_end);
   const unsigned grid = (unsigned)((int64_t)p.bs * p.num_anchor);
+  if (fast_path_ok(p)) {
+    if (feat_dtype == S4D_DTYPE_BF16)
+      dfa_gather_fast_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG><<<grid, kGatherThreads, 0, stream>>>(p);
+    else
+      dfa_gather_fast_kernel<float, kFastNC, kFastNL, kFastNP, kFastG><<<grid, kGatherThreads, 0, stream>>>(p);
+    return cuda_check(cudaGetLastError(), "dfa_gather_fast_kernel launch");
+  }
   if (feat_dtype == S4D_DTYPE_BF16) {
     auto k = dfa_gather_kernel<__nv_bfloat16>;
     if (smem > 48 * 1024) {
