@@ -151,7 +151,12 @@ S4D_API int s4d_kps_project_fused(const float* key_points, const float* anchor, 
  *   cam_begin/cam_end only cameras in [cam_begin, cam_end) are sampled (camera sharding)
  *   out               [bs, A, C] f32, summed over points
  *   error_flag        optional [1] i32, OR-ed with S4D_FLAG_* bits
- * Implemented: C == 256, G in {1, 2, 4, 8, 16, 32}, Ncam*L*P*G <= 12288.
+ *   workspace         optional, >= s4d_dfa_workspace_bytes(...) bytes, 16-byte aligned.  With
+ *                     split logits it holds the per-frame camera softmax factors, which lets the
+ *                     kernel factorise the softmax (fewer exps per anchor); without it (NULL)
+ *                     the result is the same up to fp32 rounding, computed without that saving.
+ * Implemented: C == 256, G in {1, 2, 4, 8, 16, 32}, Ncam*L*P*G <= 12288.  The Sparse4D v3
+ * shape (Ncam 6, L 4, P 13, G 8, cam-major logits) runs shape-specialised kernels.
  */
 S4D_API int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, int64_t num_feat,
                                const int32_t* spatial_shape, const int32_t* scale_start_index,
@@ -159,7 +164,13 @@ S4D_API int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, i
                                int weights_are_logits, int layout, int64_t bs, int64_t num_anchor,
                                int64_t num_cams, int64_t num_levels, int64_t num_pts, int64_t num_groups,
                                int64_t embed_dims, int64_t cam_begin, int64_t cam_end, float* out,
-                               int32_t* error_flag, void* stream);
+                               int32_t* error_flag, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of the optional workspace of s4d_deformable_aggregation (split logits only: the
+ * per-frame camera softmax factors, bs * (Ncam + 1) * L * P * G floats; 0 otherwise).
+ * Host-only, launches nothing. */
+S4D_API size_t s4d_dfa_workspace_bytes(int64_t bs, int64_t num_cams, int64_t num_levels, int64_t num_pts,
+                                       int64_t num_groups, int split_logits);
 
 #ifdef __cplusplus
 }

@@ -44,11 +44,17 @@ const char* s4d_status_string(int status) {
 
 const char* s4d_last_error(void) { return g_last_error; }
 
-int s4d_abi_version(void) { return 100; }
+int s4d_abi_version(void) { return 101; }
 
 size_t s4d_kps_workspace_bytes(int64_t bs, int64_t num_anchor, int64_t num_cams, int64_t num_pts) {
   if (bs <= 0 || num_anchor <= 0 || num_cams <= 0 || num_pts <= 0) return 0;
   return kps_workspace_bytes(bs * num_anchor * num_cams * num_pts);
+}
+
+size_t s4d_dfa_workspace_bytes(int64_t bs, int64_t num_cams, int64_t num_levels, int64_t num_pts,
+                               int64_t num_groups, int split_logits) {
+  if (!split_logits || bs <= 0 || num_cams <= 0 || num_levels <= 0 || num_pts <= 0 || num_groups <= 0) return 0;
+  return gather_workspace_bytes(bs, (int)num_cams, (int)num_levels, (int)num_pts, (int)num_groups);
 }
 
 int s4d_kps_project(const float* anchor, int64_t anchor_dim, const float* fix_scale, int64_t num_fix,
@@ -145,7 +151,7 @@ int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, int64_t n
                                int weights_are_logits, int layout, int64_t bs, int64_t num_anchor,
                                int64_t num_cams, int64_t num_levels, int64_t num_pts, int64_t num_groups,
                                int64_t embed_dims, int64_t cam_begin, int64_t cam_end, float* out,
-                               int32_t* error_flag, void* stream) {
+                               int32_t* error_flag, void* workspace, size_t workspace_bytes, void* stream) {
   set_error("%s", "");
   if (bs < 0 || num_anchor < 0 || num_cams <= 0 || num_levels <= 0 || num_pts <= 0 || num_groups <= 0 ||
       embed_dims <= 0 || num_feat < 0)
@@ -198,6 +204,14 @@ int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, int64_t n
   p.cam_end = (int)cam_end;
   p.logits = weights_are_logits ? 1 : 0;
   p.layout = layout;
+  p.cam_ws = nullptr;
+  if (weights_cam != nullptr && workspace != nullptr) {
+    if (!aligned(workspace, 16))
+      return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: workspace must be 16-byte aligned");
+    if (workspace_bytes < gather_workspace_bytes(bs, (int)num_cams, (int)num_levels, (int)num_pts, (int)num_groups))
+      return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: workspace smaller than s4d_dfa_workspace_bytes()");
+    p.cam_ws = static_cast<float*>(workspace);
+  }
   if (gather_smem_bytes(p.num_cams, p.num_levels, p.num_pts, p.num_groups, p.cam_begin, p.cam_end) > 200 * 1024)
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: per-anchor staging exceeds shared memory");
   return launch_gather(p, feat_dtype, static_cast<cudaStream_t>(stream));

@@ -601,8 +601,251 @@ __global__ void __launch_bounds__(kGatherThreads, 4) dfa_gather_fast_kernel(Gath
   p.out[anchor_lin * kChannels + tid] = v * s_ginv[tid / D];
 }
 
-// The Sparse4D v3 shape the fast kernel is compiled for.
+// -----------------------------------------------------------------------------------------------
+// Split logits, factorised softmax.  With logit[c, lp, g] = wa[lp, g] + wc[c, lp, g] (anchor
+// term + camera term, lp = (level, point)):
+//   exp(logit - M) = exp(wa - M1[g]) * exp(wc - M2[g])      (M = M1 + M2 cancels in the ratio)
+//   sum_{c,lp} exp(logit - M) = sum_lp ea[lp, g] * EC[lp, g],  EC = sum_c exp(wc - M2)
+// The camera factors (ec, EC) depend only on the frame, so cam_softmax_prep_kernel computes
+// them once per frame into the workspace; each anchor then needs LPG exps and an LPG-term dot
+// product (one warp, while the other warps build the sample list) instead of Ncam*LPG exps.
+// M1 and M2 are the per-group maxima of each term, so every factor is <= 1.  When a group's
+// sum falls below 1e-20 (the largest logit sits > ~46 below M1 + M2, where factors could
+// underflow) the anchor switches to the exact two-pass softmax over wa + wc.
+// -----------------------------------------------------------------------------------------------
+template <int NC, int LPG, int G>
+__global__ void __launch_bounds__(kGatherThreads) cam_softmax_prep_kernel(const float* __restrict__ wc,
+                                                                          float* __restrict__ ws) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  static_assert(kGatherThreads % G == 0, "thread t only sees group t % G");
+  __shared__ float s_tmp[kGatherWarps * 32];
+  __shared__ float s_m[32];
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const float* w = wc + (int64_t)b * NC * LPG;
+  float* ec = ws + (int64_t)b * (NC + 1) * LPG;
+  float m = -INFINITY;
+  for (int e = tid; e < NC * LPG; e += kGatherThreads) m = fmaxf(m, w[e]);
+  group_reduce<true>(m, G, s_tmp, s_m);
+  const float mg = s_m[tid % G] * kLog2e;
+  for (int j = tid; j < LPG; j += kGatherThreads) {
+    float s = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const float e = ex2_approx(fmaf(w[c * LPG + j], kLog2e, -mg));
+      ec[c * LPG + j] = e;
+      s += e;
+    }
+    ec[NC * LPG + j] = s;
+  }
+}
+
+template <typename T, int NC, int NL, int NP, int G>
+__global__ void __launch_bounds__(kGatherThreads, 4) dfa_gather_split_kernel(GatherParams p) {
+  constexpr int NLP = NL * NP;
+  constexpr int NCLP = NC * NLP;
+  constexpr int LPG = NLP * G;
+  constexpr int D = kChannels / G;
+  constexpr int kCandThreads = kGatherThreads - 32;  // warps 1..7 build the sample list
+  constexpr float kLog2e = 1.4426950408889634f;
+  static_assert(LPG % 4 == 0 && LPG % 32 == 0 && G >= 4 && G <= 32 && (G & (G - 1)) == 0, "split gather shape");
+  static_assert(NCLP <= 2 * kCandThreads, "two candidates per list-building thread");
+  static_assert(NCLP * 32 >= kGatherWarps * kChannels * 4, "reduction buffer aliases the sample list");
+
+  __shared__ __align__(16) float s_wa[LPG];
+  __shared__ __align__(16) float s_ea[LPG];
+  __shared__ __align__(16) float2 s_loc[NC * NP];
+  __shared__ __align__(16) int4 s_lvl[NC * NL];
+  __shared__ __align__(16) unsigned char s_list[NCLP * 32];
+  __shared__ int2 s_off[NCLP];  // (lp * G, c * LPG + lp * G) of each listed sample
+  __shared__ float s_tmp[kGatherWarps * 32];
+  __shared__ float s_gm[32];
+  __shared__ float s_ginv[32];
+  __shared__ int s_wcnt[2][kGatherWarps];
+  __shared__ int s_exact;
+
+  int4* s_pix = reinterpret_cast<int4*>(s_list);
+  float4* s_bw = reinterpret_cast<float4*>(s_list + NCLP * 16);
+  float* s_red = reinterpret_cast<float*>(s_list);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t anchor_lin = blockIdx.x;
+  const int b = (int)(anchor_lin / p.num_anchor);
+  const float* ec_tab = p.cam_ws + (int64_t)b * (NC + 1) * LPG;
+  const float* wc_raw = p.weights_cam + (int64_t)b * NC * LPG;
+
+  // ---- 1. stage levels, locations and the anchor's logit row -------------------------------
+  if (tid < NC * NL) {
+    const int H = p.spatial_shape[2 * tid], W = p.spatial_shape[2 * tid + 1], st = p.scale_start[tid];
+    const bool ok = H > 0 && W > 0 && st >= 0 && (int64_t)st + (int64_t)H * W <= p.num_feat;
+    const int c = tid / NL;
+    if (!ok && c >= p.cam_begin && c < p.cam_end && p.error_flag != nullptr && blockIdx.x == 0)
+      atomicOr(p.error_flag, S4D_FLAG_BAD_LEVEL);
+    s_lvl[tid] = make_int4(H, W, st, ok ? 1 : 0);
+  }
+  if (tid < NC * NP) s_loc[tid] = __ldg(reinterpret_cast<const float2*>(p.loc) + anchor_lin * (NC * NP) + tid);
+  if (tid < LPG / 4)
+    reinterpret_cast<float4*>(s_wa)[tid] = ldg_nc_f4(reinterpret_cast<const float4*>(p.weights) + anchor_lin * (LPG / 4) + tid);
+  __syncthreads();
+
+  // ---- 2. warp 0: factorised softmax; warps 1..7: candidate samples ------------------------
+  bool valid[2] = {false, false};
+  int4 pix[2];
+  float4 bw[2];
+  int2 off[2];
+  uint32_t ball0 = 0, ball1 = 0;
+  if (warp == 0) {
+    // lane owns elements lane + 32k of the row: always group lane % G
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < LPG / 32; ++k) m = fmaxf(m, s_wa[lane + 32 * k]);
+#pragma unroll
+    for (int o = G; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float ml = m * kLog2e;
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < LPG / 32; ++k) {
+      const int e = lane + 32 * k;
+      const float ea = ex2_approx(fmaf(s_wa[e], kLog2e, -ml));
+      s_ea[e] = ea;
+      s = fmaf(ea, __ldg(ec_tab + NC * LPG + e), s);
+    }
+#pragma unroll
+    for (int o = G; o < 32; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const bool ok = s >= 1e-20f;
+    const uint32_t all_ok = __ballot_sync(0xffffffffu, ok || lane >= G);
+    if (lane < G) s_ginv[lane] = 1.0f / s;
+    if (lane == 0) s_exact = all_ok == 0xffffffffu ? 0 : 1;
+  } else {
+    const int ct = tid - 32;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int i = ct + r * kCandThreads;
+      pix[r] = make_int4(-1, -1, -1, -1);
+      bw[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+      off[r] = make_int2(0, 0);
+      if (i < NCLP) {
+        const int c = i / NLP;
+        const int lp = i - c * NLP;
+        const int l = lp / NP, pt = lp - l * NP;
+        if (c >= p.cam_begin && c < p.cam_end) {
+          const int4 lv = s_lvl[c * NL + l];
+          const float2 uv = s_loc[c * NP + pt];
+          const float Wf = (float)lv.y, Hf = (float)lv.x;
+          const float ix = ((uv.x * 2.0f - 1.0f + 1.0f) * Wf - 1.0f) * 0.5f;
+          const float iy = ((uv.y * 2.0f - 1.0f + 1.0f) * Hf - 1.0f) * 0.5f;
+          if (lv.w && ix > -1.0f && ix < Wf && iy > -1.0f && iy < Hf) {
+            const float x0f = floorf(ix), y0f = floorf(iy);
+            const int x0 = (int)x0f, y0 = (int)y0f;
+            const float x1f = x0f + 1.0f, y1f = y0f + 1.0f;
+            const bool vx0 = x0 >= 0, vx1 = x0 + 1 < lv.y, vy0 = y0 >= 0, vy1 = y0 + 1 < lv.x;
+            const int p00 = lv.z + y0 * lv.y + x0;
+            pix[r] = make_int4(vx0 && vy0 ? p00 : -1, vx1 && vy0 ? p00 + 1 : -1, vx0 && vy1 ? p00 + lv.y : -1,
+                               vx1 && vy1 ? p00 + lv.y + 1 : -1);
+            bw[r] = make_float4((x1f - ix) * (y1f - iy), (ix - x0f) * (y1f - iy), (x1f - ix) * (iy - y0f),
+                                (ix - x0f) * (iy - y0f));
+            off[r] = make_int2(lp * G, c * LPG + lp * G);
+            valid[r] = true;
+          }
+        }
+      }
+    }
+    ball0 = __ballot_sync(0xffffffffu, valid[0]);
+    ball1 = __ballot_sync(0xffffffffu, valid[1]);
+    if (lane == 0) {
+      s_wcnt[0][warp] = __popc(ball0);
+      s_wcnt[1][warp] = __popc(ball1);
+    }
+  }
+  __syncthreads();
+  const bool exact = s_exact != 0;
+
+  // ---- 2b. rare exact softmax over wa + wc ---------------------------------------------------
+  if (exact) {
+    float m = -INFINITY;
+    for (int e = tid; e < NC * LPG; e += kGatherThreads) m = fmaxf(m, s_wa[e % LPG] + __ldg(wc_raw + e));
+    group_reduce<true>(m, G, s_tmp, s_gm);
+    const float mg = s_gm[tid % G] * kLog2e;
+    float s = 0.0f;
+    for (int e = tid; e < NC * LPG; e += kGatherThreads)
+      s += ex2_approx(fmaf(s_wa[e % LPG] + __ldg(wc_raw + e), kLog2e, -mg));
+    group_reduce<false>(s, G, s_tmp, s_ginv);
+    if (tid < G) s_ginv[tid] = 1.0f / s_ginv[tid];
+  }
+
+  // ---- 3. sample list ------------------------------------------------------------------------
+  int n_valid = 0;
+  if (warp > 0) {
+    int off0 = 0, off1 = 0;
+#pragma unroll
+    for (int w = 1; w < kGatherWarps; ++w) {
+      off0 += w < warp ? s_wcnt[0][w] : 0;
+      n_valid += s_wcnt[0][w];
+    }
+    off1 = n_valid;
+#pragma unroll
+    for (int w = 1; w < kGatherWarps; ++w) off1 += w < warp ? s_wcnt[1][w] : 0;
+    const uint32_t lt = (1u << lane) - 1u;
+    if (valid[0]) {
+      const int pos = off0 + __popc(ball0 & lt);
+      s_pix[pos] = pix[0];
+      s_bw[pos] = bw[0];
+      s_off[pos] = off[0];
+    }
+    if (valid[1]) {
+      const int pos = off1 + __popc(ball1 & lt);
+      s_pix[pos] = pix[1];
+      s_bw[pos] = bw[1];
+      s_off[pos] = off[1];
+    }
+  }
+  n_valid = 0;
+#pragma unroll
+  for (int w = 1; w < kGatherWarps; ++w) n_valid += s_wcnt[0][w] + s_wcnt[1][w];
+  __syncthreads();
+
+  // ---- 4. weighted gather -------------------------------------------------------------------
+  const int g = lane / (D / 8);
+  const float gml = exact ? s_gm[g] * kLog2e : 0.0f;
+  const T* fb = static_cast<const T*>(p.feat) + (int64_t)b * p.num_feat * kChannels;
+  float2 acc[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.f, 0.f);
+  using V = typename TapVec<T>::type;
+  for (int s = warp; s < n_valid; s += kGatherWarps) {
+    const int4 px = s_pix[s];
+    const float4 w4 = s_bw[s];
+    const int2 of = s_off[s];
+    V v0, v1, v2, v3;
+    if (px.x >= 0) TapFma<T>::load(fb, px.x, lane, v0);
+    if (px.y >= 0) TapFma<T>::load(fb, px.y, lane, v1);
+    if (px.z >= 0) TapFma<T>::load(fb, px.z, lane, v2);
+    if (px.w >= 0) TapFma<T>::load(fb, px.w, lane, v3);
+    const float sw = exact ? ex2_approx(fmaf(s_wa[of.x + g] + __ldg(wc_raw + of.y + g), kLog2e, -gml))
+                           : s_ea[of.x + g] * __ldg(ec_tab + of.y + g);
+    if (px.x >= 0) TapFma<T>::fma(v0, w4.x * sw, acc);
+    if (px.y >= 0) TapFma<T>::fma(v1, w4.y * sw, acc);
+    if (px.z >= 0) TapFma<T>::fma(v2, w4.z * sw, acc);
+    if (px.w >= 0) TapFma<T>::fma(v3, w4.w * sw, acc);
+  }
+
+  // ---- 5. cross-warp reduction -------------------------------------------------------------
+  __syncthreads();
+  float4* r4 = reinterpret_cast<float4*>(s_red + warp * kChannels + lane * 8);
+  r4[0] = make_float4(acc[0].x, acc[0].y, acc[1].x, acc[1].y);
+  r4[1] = make_float4(acc[2].x, acc[2].y, acc[3].x, acc[3].y);
+  __syncthreads();
+  float v = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kGatherWarps; ++w) v += s_red[w * kChannels + tid];
+  p.out[anchor_lin * kChannels + tid] = v * s_ginv[tid / D];
+}
+
+// The Sparse4D v3 shape the fast kernels are compiled for.
 constexpr int kFastNC = 6, kFastNL = 4, kFastNP = 13, kFastG = 8;
+
+size_t gather_workspace_bytes(int64_t bs, int ncam, int nl, int np, int G) {
+  return (size_t)bs * (ncam + 1) * nl * np * G * sizeof(float);
+}
 
 static bool fast_path_ok(const GatherParams& p) {
   auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
@@ -618,6 +861,17 @@ size_t gather_smem_bytes(int ncam, int nl, int np, int G, int cam_begin, int cam
 int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream) {
   const size_t smem = gather_smem_bytes(p.num_cams, p.num_levels, p.num_pts, p.num_groups, p.cam_begin, p.cam_end);
   const unsigned grid = (unsigned)((int64_t)p.bs * p.num_anchor);
+  if (fast_path_ok(p) && p.weights_cam != nullptr && p.cam_ws != nullptr) {
+    constexpr int LPG = kFastNL * kFastNP * kFastG;
+    cam_softmax_prep_kernel<kFastNC, LPG, kFastG><<<(unsigned)p.bs, kGatherThreads, 0, stream>>>(p.weights_cam, p.cam_ws);
+    int st = cuda_check(cudaGetLastError(), "cam_softmax_prep_kernel launch");
+    if (st) return st;
+    if (feat_dtype == S4D_DTYPE_BF16)
+      dfa_gather_split_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG><<<grid, kGatherThreads, 0, stream>>>(p);
+    else
+      dfa_gather_split_kernel<float, kFastNC, kFastNL, kFastNP, kFastG><<<grid, kGatherThreads, 0, stream>>>(p);
+    return cuda_check(cudaGetLastError(), "dfa_gather_split_kernel launch");
+  }
   if (fast_path_ok(p)) {
     if (feat_dtype == S4D_DTYPE_BF16)
       dfa_gather_fast_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG><<<grid, kGatherThreads, 0, stream>>>(p);

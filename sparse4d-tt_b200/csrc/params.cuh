@@ -39,6 +39,7 @@ struct GatherParams {
   const float* weights_cam;
   float* out;
   int32_t* error_flag;
+  float* cam_ws;  // split logits: per-frame camera softmax factors, or null
   int bs, num_anchor, num_cams, num_levels, num_pts, num_groups;
   int cam_begin, cam_end;
   int logits;
@@ -50,6 +51,7 @@ int launch_kps_project(KpsParams k, int32_t* visible_idx, int32_t* visible_count
 size_t kps_workspace_bytes(int64_t total);
 
 int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream);
+size_t gather_workspace_bytes(int64_t bs, int ncam, int nl, int np, int G);
 size_t gather_smem_bytes(int ncam, int nl, int np, int G, int cam_begin, int cam_end);
 
 }  // namespace s4d

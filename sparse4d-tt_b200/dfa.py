@@ -205,8 +205,11 @@ class DeformableFeatureAggregation:
         if log is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
+        ws = None
+        if logits_cam is not None:
+            ws = ops.dfa_workspace(bs, self.num_cams, self.num_levels, self.num_pts, self.num_groups, dev)
         ops.deformable_aggregation_into(feats, mc_ms_feat, spatial_shape, scale_start, loc, logits, True,
-                                        logits_cam, cam_begin, cam_end)
+                                        logits_cam, cam_begin, cam_end, workspace=ws)
         if log is not None:
             ev[1].record()
             log.append(ev)

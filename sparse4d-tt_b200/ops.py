@@ -101,8 +101,11 @@ def _dfa_dims(sample_location: Tensor, weights: Tensor, weights_cam: Optional[Te
 def deformable_aggregation_into(out: Tensor, mc_ms_feat: Tensor, spatial_shape: Tensor, scale_start_index: Tensor,
                                 sample_location: Tensor, weights: Tensor, weights_are_logits: bool = True,
                                 weights_cam: Optional[Tensor] = None, cam_begin: int = 0, cam_end: int = -1,
-                                layout: Union[int, str] = "cam_major", error_flag: Optional[Tensor] = None) -> Tensor:
-    """Writes the fused gather into ``out [bs, A, C]`` (fp32) and returns it."""
+                                layout: Union[int, str] = "cam_major", error_flag: Optional[Tensor] = None,
+                                workspace: Optional[Tensor] = None) -> Tensor:
+    """Writes the fused gather into ``out [bs, A, C]`` (fp32) and returns it.  With split
+    logits (``weights_cam``) an optional ``workspace`` of ``dfa_workspace_bytes(...)`` bytes
+    lets the kernel factorise the softmax."""
     name = "deformable_aggregation"
     lay = LAYOUTS[layout] if isinstance(layout, str) else int(layout)
     dev = _require_cuda(name, out, mc_ms_feat, spatial_shape, scale_start_index, sample_location, weights,
@@ -125,13 +128,29 @@ def deformable_aggregation_into(out: Tensor, mc_ms_feat: Tensor, spatial_shape: 
     _require(tuple(scale_start_index.shape) == (nc, nl), f"scale_start_index must be [{nc}, {nl}]")
     _require(tuple(out.shape) == (bs, A, C), f"out must be [{bs}, {A}, {C}]")
     ce = nc if cam_end is None or cam_end < 0 else int(cam_end)
+    _require_cuda(name, workspace)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     st = L.lib().s4d_deformable_aggregation(
         mc_ms_feat.data_ptr(), L.S4D_DTYPE_BF16 if mc_ms_feat.dtype == torch.bfloat16 else L.S4D_DTYPE_F32,
         int(mc_ms_feat.shape[1]), spatial_shape.data_ptr(), scale_start_index.data_ptr(),
         sample_location.data_ptr(), weights.data_ptr(), _ptr(weights_cam), 1 if weights_are_logits else 0, lay,
-        bs, A, nc, nl, P, G, C, int(cam_begin), ce, out.data_ptr(), _ptr(error_flag), _stream_ptr(dev))
+        bs, A, nc, nl, P, G, C, int(cam_begin), ce, out.data_ptr(), _ptr(error_flag), _ptr(workspace), ws_bytes,
+        _stream_ptr(dev))
     L.check(name, st)
     return out
+
+
+def dfa_workspace_bytes(bs: int, num_cams: int, num_levels: int, num_pts: int, num_groups: int,
+                        split_logits: bool) -> int:
+    return int(L.lib().s4d_dfa_workspace_bytes(bs, num_cams, num_levels, num_pts, num_groups,
+                                               1 if split_logits else 0))
+
+
+def dfa_workspace(bs: int, num_cams: int, num_levels: int, num_pts: int, num_groups: int,
+                  device) -> Optional[Tensor]:
+    """A workspace tensor for split-logit calls (None when no workspace is needed)."""
+    n = dfa_workspace_bytes(bs, num_cams, num_levels, num_pts, num_groups, True)
+    return torch.empty(n // 4, dtype=torch.float32, device=device) if n else None
 
 
 @torch.library.custom_op("s4d::deformable_aggregation", mutates_args=())
@@ -148,8 +167,12 @@ def deformable_aggregation(mc_ms_feat: Tensor, spatial_shape: Tensor, scale_star
     Returns ``[bs, A, C]`` fp32 summed over points."""
     bs, A = sample_location.shape[:2]
     out = torch.empty(bs, A, mc_ms_feat.shape[2], dtype=torch.float32, device=mc_ms_feat.device)
+    ws = None
+    if weights_cam is not None:
+        nc, nl, P, G = weights_cam.shape[1:5]
+        ws = dfa_workspace(bs, nc, nl, P, G, mc_ms_feat.device)
     return deformable_aggregation_into(out, mc_ms_feat, spatial_shape, scale_start_index, sample_location, weights,
-                                       weights_are_logits, weights_cam, cam_begin, cam_end, layout)
+                                       weights_are_logits, weights_cam, cam_begin, cam_end, layout, workspace=ws)
 
 
 @deformable_aggregation.register_fake

@@ -33,7 +33,7 @@ def lib():
 
 def test_every_declared_symbol_is_exported(lib):
     names = declared_functions()
-    assert len(names) == 7, names
+    assert len(names) == 8, names
     for n in names:
         assert hasattr(lib, n), n
         assert n in L.SIGNATURES, f"{n} has no ctypes signature"
@@ -52,7 +52,12 @@ def test_status_strings_and_version(lib):
     assert L.status_string(0) == "S4D_OK"
     assert L.status_string(2) == "S4D_ERR_UNSUPPORTED_SHAPE"
     assert L.status_string(99) == "S4D_ERR_UNKNOWN"
-    assert lib.s4d_abi_version() == 100
+    assert lib.s4d_abi_version() == 101
+
+
+def test_dfa_workspace_bytes(lib):
+    assert lib.s4d_dfa_workspace_bytes(2, 6, 4, 13, 8, 1) == 2 * 7 * 416 * 4
+    assert lib.s4d_dfa_workspace_bytes(2, 6, 4, 13, 8, 0) == 0
 
 
 def test_workspace_bytes(lib):
@@ -68,7 +73,8 @@ def _gather(lib, **kw):
     st = lib.s4d_deformable_aggregation(
         args["feat"], args["dtype"], args["num_feat"], args["shape"], args["start"], args["loc"], args["w"],
         args["wc"], args["logits"], args["layout"], args["bs"], args["A"], args["nc"], args["nl"], args["np"],
-        args["G"], args["C"], args["cb"], args["ce"], args["out"], args["flag"], None)
+        args["G"], args["C"], args["cb"], args["ce"], args["out"], args["flag"], args.get("ws"), args.get("wsb", 0),
+        None)
     return st, lib.s4d_last_error().decode()
 
 
@@ -86,6 +92,8 @@ def _gather(lib, **kw):
     (dict(feat=None), L.S4D_ERR_INVALID_ARG, "null"),
     (dict(feat=24), L.S4D_ERR_INVALID_ARG, "16-byte"),
     (dict(bs=-1), L.S4D_ERR_INVALID_ARG, "positive"),
+    (dict(feat=16, wc=16, ws=24, wsb=1 << 20), L.S4D_ERR_INVALID_ARG, "workspace"),
+    (dict(feat=16, wc=16, ws=16, wsb=64), L.S4D_ERR_INVALID_ARG, "workspace"),
 ])
 def test_gather_rejects_on_host(lib, kw, status, text):
     st, msg = _gather(lib, **kw)

@@ -97,12 +97,36 @@ def _oracle(maps, uv_bacp, logits, logits_flag=True, cam_range=None):
                                                        logits=logits_flag, cam_range=cam_range))
 
 
-def test_gather_pt_major_layout_is_identical(cuda_device):
+def test_gather_pt_major_layout(cuda_device):
+    """Upstream (pt-major) layout.  At the Sparse4D shape cam-major runs the shape-specialised
+    kernel and pt-major the generic one: both against the oracle and against each other."""
     maps, uv, logits = _small_case(1)
     a = _gpu_gather(maps, uv, logits)
     b = _gpu_gather(maps, uv.permute(0, 1, 3, 2, 4), logits.permute(0, 1, 4, 2, 3, 5), layout=1)
-    assert torch.equal(a, b)
-    assert (a - _oracle(maps, uv, logits)).abs().max().item() <= FP32_ATOL
+    ref = _oracle(maps, uv, logits)
+    assert (a - ref).abs().max().item() <= FP32_ATOL
+    assert (b - ref).abs().max().item() <= FP32_ATOL
+    assert (a - b).abs().max().item() <= 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fast_and_generic_kernels_agree(cuda_device, dtype):
+    """Force the generic kernel at the Sparse4D shape by misaligning the logits by one float
+    (the fast kernel needs 16-byte aligned rows) and compare with the fast kernel."""
+    d = torch.device("cuda:0")
+    maps, uv, logits = _small_case(11, bs=2, A=65)
+    feat, shape, start = ops.pack_feature_maps([m.to(d) for m in maps], dtype=dtype)
+    uv_d = uv.to(d).contiguous()
+    w = logits.to(d).contiguous()
+    store = torch.empty(w.numel() + 1, device=d)
+    w_mis = store[1:].view_as(w)
+    w_mis.copy_(w)
+    fast = ops.deformable_aggregation(feat, shape, start, uv_d, w)
+    generic = ops.deformable_aggregation(feat, shape, start, uv_d, w_mis)
+    torch.cuda.synchronize()
+    assert (fast - generic).abs().max().item() <= 1e-5
+    if dtype == torch.float32:
+        assert (fast.cpu() - _oracle(maps, uv, logits)).abs().max().item() <= FP32_ATOL
 
 
 def test_gather_split_logits(cuda_device):
@@ -115,6 +139,53 @@ def test_gather_split_logits(cuda_device):
     b = _gpu_gather(maps, uv, full)
     assert (a - b).abs().max().item() <= 1e-6
     assert (a - _oracle(maps, uv, full)).abs().max().item() <= FP32_ATOL
+
+
+def _split_gather(maps, uv, wa, wc, dtype=torch.float32, with_ws=True, cam_range=None):
+    d = torch.device("cuda:0")
+    feat, shape, start = ops.pack_feature_maps([m.to(d) for m in maps], dtype=dtype)
+    bs, A = uv.shape[:2]
+    nc = shape.shape[0]
+    cb, ce = (0, nc) if cam_range is None else cam_range
+    out = torch.empty(bs, A, 256, device=d)
+    ws = ops.dfa_workspace(bs, *wc.shape[1:5], d) if with_ws else None
+    ops.deformable_aggregation_into(out, feat, shape, start, uv.contiguous().to(d), wa.contiguous().to(d), True,
+                                    wc.contiguous().to(d), cb, ce, workspace=ws)
+    torch.cuda.synchronize()
+    return out.cpu()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gather_split_factorised_softmax(cuda_device, dtype):
+    """Split logits with a workspace (per-frame camera factors, factorised softmax) against
+    the same call without a workspace and against the oracle."""
+    maps, uv, _ = _small_case(12, bs=3, A=70)
+    gen = torch.Generator().manual_seed(19)
+    wa = torch.randn(3, 70, 4, 13, 8, generator=gen) * 2
+    wc = torch.randn(3, 6, 4, 13, 8, generator=gen) * 2
+    a = _split_gather(maps, uv, wa, wc, dtype, True)
+    b = _split_gather(maps, uv, wa, wc, dtype, False)
+    assert (a - b).abs().max().item() <= 1e-5
+    if dtype == torch.float32:
+        ref = _oracle(maps, uv, wa[:, :, None] + wc[:, None])
+        assert (a - ref).abs().max().item() <= FP32_ATOL
+    parts = [_split_gather(maps, uv, wa, wc, dtype, True, r) for r in ((0, 2), (2, 6))]
+    assert (parts[0] + parts[1] - a).abs().max().item() <= 1e-5
+
+
+def test_gather_split_exact_fallback(cuda_device):
+    """Logits whose largest sum sits far below max(wa) + max(wc): the factorised sum
+    underflows and the kernel switches to the exact softmax."""
+    maps, uv, _ = _small_case(13, bs=1, A=8)
+    wa = torch.zeros(1, 8, 4, 13, 8)
+    wc = torch.zeros(1, 6, 4, 13, 8)
+    wa[:, :, 1, 3] = 100.0  # max(wa) at (level 1, point 3) ...
+    wc[:, :, 1, 3] = -200.0  # ... where every camera term is very negative
+    wa[:, 5] += torch.randn(4, 13, 8, generator=torch.Generator().manual_seed(3))
+    a = _split_gather(maps, uv, wa, wc, torch.float32, True)
+    ref = _oracle(maps, uv, wa[:, :, None] + wc[:, None])
+    assert torch.isfinite(a).all()
+    assert (a - ref).abs().max().item() <= FP32_ATOL
 
 
 def test_gather_given_weights(cuda_device):
