@@ -10,7 +10,15 @@
 // (model/deformable_feature_aggregation.py:791-796,877-899).  The [cams*levels*pts, A, C]
 // intermediate of the reference is never materialised.
 //
-// One CTA of 256 threads (8 warps) per anchor:
+// Kernels, chosen by launch_gather():
+//   dfa_gather_warp_kernel   Sparse4D v3 shape (6 cams, 4 levels, 13 points, 8 groups), split
+//                            logits with the per-frame camera factors (cam_softmax_prep_kernel)
+//                            in the workspace: one warp per anchor, factorised softmax.
+//   dfa_gather_fast_kernel   Sparse4D v3 shape, cam-major logits (full or split, no workspace):
+//                            one CTA per anchor with compile-time dimensions.
+//   dfa_gather_kernel        every other shape / layout (generic, described below).
+//
+// dfa_gather_kernel -- one CTA of 256 threads (8 warps) per anchor:
 //   1. stage the anchor's logits (Ncam*L*P*G fp32) and sample locations in shared memory,
 //      together with the (H, W, start) of every (camera, level);
 //   2. per-group max and sum of exp over the Ncam*L*P entries: block reductions in which
@@ -639,41 +647,40 @@ __global__ void __launch_bounds__(kGatherThreads) cam_softmax_prep_kernel(const 
   }
 }
 
-template <typename T, int NC, int NL, int NP, int G>
-__global__ void __launch_bounds__(kGatherThreads, 4) dfa_gather_split_kernel(GatherParams p) {
+// -----------------------------------------------------------------------------------------------
+// One warp per anchor.  The per-anchor work is short (a few hundred instructions of softmax and
+// candidate bookkeeping, then ~50 in-bounds samples of 4 taps), so the kernel is limited by
+// latency unless many anchors are in flight per SM.  A warp per anchor needs no block barrier,
+// keeps the per-anchor state in registers (plus LPG floats of shared memory for the anchor's
+// softmax factors), and lets 40 anchors share an SM.
+//
+//   softmax   each lane owns the logits lane + 32k of the anchor row: always group lane % G.
+//             MODE 1 (split logits + per-frame camera factors in the workspace): factorised,
+//             LPG exps per anchor (see cam_softmax_prep_kernel).  MODE 0 (full logits) and
+//             MODE 2 (split logits, no workspace), and MODE 1 when its guard trips: exact
+//             two-pass max / sum over the full Ncam*LPG logits, read from L1.
+//   samples   the (camera, point) pairs whose (u, v) can touch a map ((u, v) in (-0.5, 1.5)) are
+//             kept, each expanded to its NL levels across the lanes; the in-bounds ones are
+//             broadcast by shuffle, one at a time, to the whole warp, which gathers the 4 taps
+//             (lane l: channels 8l..8l+7) and accumulates with packed fp32x2 FMA.
+//   output    normalised in registers (1 / sum of the lane's group) and stored by each lane.
+// -----------------------------------------------------------------------------------------------
+template <typename T, int NC, int NL, int NP, int G, int MODE>
+__global__ void __launch_bounds__(kGatherThreads, 4) dfa_gather_warp_kernel(GatherParams p) {
   constexpr int NLP = NL * NP;
-  constexpr int NCLP = NC * NLP;
   constexpr int LPG = NLP * G;
+  constexpr int NW = NC * LPG;
+  constexpr int NPAIR = NC * NP;
   constexpr int D = kChannels / G;
-  constexpr int kCandThreads = kGatherThreads - 32;  // warps 1..7 build the sample list
   constexpr float kLog2e = 1.4426950408889634f;
-  static_assert(LPG % 4 == 0 && LPG % 32 == 0 && G >= 4 && G <= 32 && (G & (G - 1)) == 0, "split gather shape");
-  static_assert(NCLP <= 2 * kCandThreads, "two candidates per list-building thread");
-  static_assert(NCLP * 32 >= kGatherWarps * kChannels * 4, "reduction buffer aliases the sample list");
+  static_assert(LPG % 32 == 0 && 32 % G == 0 && G >= 4 && (G & (G - 1)) == 0, "warp gather shape");
+  static_assert(NC * NL <= kGatherThreads, "level table staged by one pass");
 
-  __shared__ __align__(16) float s_wa[LPG];
-  __shared__ __align__(16) float s_ea[LPG];
-  __shared__ __align__(16) float2 s_loc[NC * NP];
-  __shared__ __align__(16) int4 s_lvl[NC * NL];
-  __shared__ __align__(16) unsigned char s_list[NCLP * 32];
-  __shared__ int2 s_off[NCLP];  // (lp * G, c * LPG + lp * G) of each listed sample
-  __shared__ float s_tmp[kGatherWarps * 32];
-  __shared__ float s_gm[32];
-  __shared__ float s_ginv[32];
-  __shared__ int s_wcnt[2][kGatherWarps];
-  __shared__ int s_exact;
-
-  int4* s_pix = reinterpret_cast<int4*>(s_list);
-  float4* s_bw = reinterpret_cast<float4*>(s_list + NCLP * 16);
-  float* s_red = reinterpret_cast<float*>(s_list);
+  __shared__ __align__(16) int4 s_lvl[NC * NL];  // (H, W, start, ok)
+  __shared__ __align__(16) float s_ea[MODE == 1 ? kGatherWarps * LPG : 1];
+  __shared__ unsigned char s_surv[kGatherWarps][32];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t anchor_lin = blockIdx.x;
-  const int b = (int)(anchor_lin / p.num_anchor);
-  const float* ec_tab = p.cam_ws + (int64_t)b * (NC + 1) * LPG;
-  const float* wc_raw = p.weights_cam + (int64_t)b * NC * LPG;
-
-  // ---- 1. stage levels, locations and the anchor's logit row -------------------------------
   if (tid < NC * NL) {
     const int H = p.spatial_shape[2 * tid], W = p.spatial_shape[2 * tid + 1], st = p.scale_start[tid];
     const bool ok = H > 0 && W > 0 && st >= 0 && (int64_t)st + (int64_t)H * W <= p.num_feat;
@@ -682,162 +689,145 @@ __global__ void __launch_bounds__(kGatherThreads, 4) dfa_gather_split_kernel(Gat
       atomicOr(p.error_flag, S4D_FLAG_BAD_LEVEL);
     s_lvl[tid] = make_int4(H, W, st, ok ? 1 : 0);
   }
-  if (tid < NC * NP) s_loc[tid] = __ldg(reinterpret_cast<const float2*>(p.loc) + anchor_lin * (NC * NP) + tid);
-  if (tid < LPG / 4)
-    reinterpret_cast<float4*>(s_wa)[tid] = ldg_nc_f4(reinterpret_cast<const float4*>(p.weights) + anchor_lin * (LPG / 4) + tid);
-  __syncthreads();
+  __syncthreads();  // the only block barrier: every thread reaches it before any warp leaves
+  const int64_t anchor_lin = (int64_t)blockIdx.x * kGatherWarps + warp;
+  if (anchor_lin >= (int64_t)p.bs * p.num_anchor) return;
+  const int b = (int)(anchor_lin / p.num_anchor);
+  const int gch = lane / (D / 8);  // group of this lane's output channels
 
-  // ---- 2. warp 0: factorised softmax; warps 1..7: candidate samples ------------------------
-  bool valid[2] = {false, false};
-  int4 pix[2];
-  float4 bw[2];
-  int2 off[2];
-  uint32_t ball0 = 0, ball1 = 0;
-  if (warp == 0) {
-    // lane owns elements lane + 32k of the row: always group lane % G
-    float m = -INFINITY;
+  const float* wrow = p.weights + anchor_lin * (MODE == 0 ? NW : LPG);
+  const float* wcam = MODE == 0 ? nullptr : p.weights_cam + (int64_t)b * NW;
+  const float* ec_tab = MODE == 1 ? p.cam_ws + (int64_t)b * (NC + 1) * LPG : nullptr;
+  float* ea = s_ea + (MODE == 1 ? warp * LPG : 0);
+
+  // ---- 1. softmax statistics of group lane % G ----------------------------------------------
+  float m_l = -INFINITY, s_l = 0.0f;
+  bool exact = MODE != 1;
+  if (MODE == 1) {
+    float x[LPG / 32];
 #pragma unroll
-    for (int k = 0; k < LPG / 32; ++k) m = fmaxf(m, s_wa[lane + 32 * k]);
+    for (int k = 0; k < LPG / 32; ++k) x[k] = __ldg(wrow + lane + 32 * k);
 #pragma unroll
-    for (int o = G; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float ml = m * kLog2e;
-    float s = 0.0f;
+    for (int k = 0; k < LPG / 32; ++k) m_l = fmaxf(m_l, x[k]);
+#pragma unroll
+    for (int o = G; o < 32; o <<= 1) m_l = fmaxf(m_l, __shfl_xor_sync(0xffffffffu, m_l, o));
+    const float ml = m_l * kLog2e;
 #pragma unroll
     for (int k = 0; k < LPG / 32; ++k) {
-      const int e = lane + 32 * k;
-      const float ea = ex2_approx(fmaf(s_wa[e], kLog2e, -ml));
-      s_ea[e] = ea;
-      s = fmaf(ea, __ldg(ec_tab + NC * LPG + e), s);
+      const float e = ex2_approx(fmaf(x[k], kLog2e, -ml));
+      ea[lane + 32 * k] = e;
+      s_l = fmaf(e, __ldg(ec_tab + NW + lane + 32 * k), s_l);
     }
 #pragma unroll
-    for (int o = G; o < 32; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const bool ok = s >= 1e-20f;
-    const uint32_t all_ok = __ballot_sync(0xffffffffu, ok || lane >= G);
-    if (lane < G) s_ginv[lane] = 1.0f / s;
-    if (lane == 0) s_exact = all_ok == 0xffffffffu ? 0 : 1;
-  } else {
-    const int ct = tid - 32;
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int i = ct + r * kCandThreads;
-      pix[r] = make_int4(-1, -1, -1, -1);
-      bw[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-      off[r] = make_int2(0, 0);
-      if (i < NCLP) {
-        const int c = i / NLP;
-        const int lp = i - c * NLP;
-        const int l = lp / NP, pt = lp - l * NP;
-        if (c >= p.cam_begin && c < p.cam_end) {
-          const int4 lv = s_lvl[c * NL + l];
-          const float2 uv = s_loc[c * NP + pt];
-          const float Wf = (float)lv.y, Hf = (float)lv.x;
-          const float ix = ((uv.x * 2.0f - 1.0f + 1.0f) * Wf - 1.0f) * 0.5f;
-          const float iy = ((uv.y * 2.0f - 1.0f + 1.0f) * Hf - 1.0f) * 0.5f;
-          if (lv.w && ix > -1.0f && ix < Wf && iy > -1.0f && iy < Hf) {
-            const float x0f = floorf(ix), y0f = floorf(iy);
-            const int x0 = (int)x0f, y0 = (int)y0f;
-            const float x1f = x0f + 1.0f, y1f = y0f + 1.0f;
-            const bool vx0 = x0 >= 0, vx1 = x0 + 1 < lv.y, vy0 = y0 >= 0, vy1 = y0 + 1 < lv.x;
-            const int p00 = lv.z + y0 * lv.y + x0;
-            pix[r] = make_int4(vx0 && vy0 ? p00 : -1, vx1 && vy0 ? p00 + 1 : -1, vx0 && vy1 ? p00 + lv.y : -1,
-                               vx1 && vy1 ? p00 + lv.y + 1 : -1);
-            bw[r] = make_float4((x1f - ix) * (y1f - iy), (ix - x0f) * (y1f - iy), (x1f - ix) * (iy - y0f),
-                                (ix - x0f) * (iy - y0f));
-            off[r] = make_int2(lp * G, c * LPG + lp * G);
-            valid[r] = true;
-          }
-        }
-      }
-    }
-    ball0 = __ballot_sync(0xffffffffu, valid[0]);
-    ball1 = __ballot_sync(0xffffffffu, valid[1]);
-    if (lane == 0) {
-      s_wcnt[0][warp] = __popc(ball0);
-      s_wcnt[1][warp] = __popc(ball1);
-    }
+    for (int o = G; o < 32; o <<= 1) s_l += __shfl_xor_sync(0xffffffffu, s_l, o);
+    exact = __any_sync(0xffffffffu, !(s_l >= 1e-20f));
+    __syncwarp();
   }
-  __syncthreads();
-  const bool exact = s_exact != 0;
-
-  // ---- 2b. rare exact softmax over wa + wc ---------------------------------------------------
   if (exact) {
-    float m = -INFINITY;
-    for (int e = tid; e < NC * LPG; e += kGatherThreads) m = fmaxf(m, s_wa[e % LPG] + __ldg(wc_raw + e));
-    group_reduce<true>(m, G, s_tmp, s_gm);
-    const float mg = s_gm[tid % G] * kLog2e;
-    float s = 0.0f;
-    for (int e = tid; e < NC * LPG; e += kGatherThreads)
-      s += ex2_approx(fmaf(s_wa[e % LPG] + __ldg(wc_raw + e), kLog2e, -mg));
-    group_reduce<false>(s, G, s_tmp, s_ginv);
-    if (tid < G) s_ginv[tid] = 1.0f / s_ginv[tid];
+    auto logit = [&](int e) { return MODE == 0 ? __ldg(wrow + e) : __ldg(wrow + e % LPG) + __ldg(wcam + e); };
+    m_l = -INFINITY;
+    for (int e = lane; e < NW; e += 32) m_l = fmaxf(m_l, logit(e));
+#pragma unroll
+    for (int o = G; o < 32; o <<= 1) m_l = fmaxf(m_l, __shfl_xor_sync(0xffffffffu, m_l, o));
+    const float ml = m_l * kLog2e;
+    s_l = 0.0f;
+    for (int e = lane; e < NW; e += 32) s_l += ex2_approx(fmaf(logit(e), kLog2e, -ml));
+#pragma unroll
+    for (int o = G; o < 32; o <<= 1) s_l += __shfl_xor_sync(0xffffffffu, s_l, o);
   }
+  // lanes 0..G-1 hold the statistics of groups 0..G-1
+  const float inv = __shfl_sync(0xffffffffu, 1.0f / s_l, gch);
+  const float mlg = __shfl_sync(0xffffffffu, m_l, gch) * kLog2e;
 
-  // ---- 3. sample list ------------------------------------------------------------------------
-  int n_valid = 0;
-  if (warp > 0) {
-    int off0 = 0, off1 = 0;
-#pragma unroll
-    for (int w = 1; w < kGatherWarps; ++w) {
-      off0 += w < warp ? s_wcnt[0][w] : 0;
-      n_valid += s_wcnt[0][w];
-    }
-    off1 = n_valid;
-#pragma unroll
-    for (int w = 1; w < kGatherWarps; ++w) off1 += w < warp ? s_wcnt[1][w] : 0;
-    const uint32_t lt = (1u << lane) - 1u;
-    if (valid[0]) {
-      const int pos = off0 + __popc(ball0 & lt);
-      s_pix[pos] = pix[0];
-      s_bw[pos] = bw[0];
-      s_off[pos] = off[0];
-    }
-    if (valid[1]) {
-      const int pos = off1 + __popc(ball1 & lt);
-      s_pix[pos] = pix[1];
-      s_bw[pos] = bw[1];
-      s_off[pos] = off[1];
-    }
-  }
-  n_valid = 0;
-#pragma unroll
-  for (int w = 1; w < kGatherWarps; ++w) n_valid += s_wcnt[0][w] + s_wcnt[1][w];
-  __syncthreads();
-
-  // ---- 4. weighted gather -------------------------------------------------------------------
-  const int g = lane / (D / 8);
-  const float gml = exact ? s_gm[g] * kLog2e : 0.0f;
+  // ---- 2. candidates and weighted gather -----------------------------------------------------
+  const float2* locp = reinterpret_cast<const float2*>(p.loc) + anchor_lin * NPAIR;
   const T* fb = static_cast<const T*>(p.feat) + (int64_t)b * p.num_feat * kChannels;
+  const uint32_t lt = (1u << lane) - 1u;
   float2 acc[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.f, 0.f);
   using V = typename TapVec<T>::type;
-  for (int s = warp; s < n_valid; s += kGatherWarps) {
-    const int4 px = s_pix[s];
-    const float4 w4 = s_bw[s];
-    const int2 of = s_off[s];
-    V v0, v1, v2, v3;
-    if (px.x >= 0) TapFma<T>::load(fb, px.x, lane, v0);
-    if (px.y >= 0) TapFma<T>::load(fb, px.y, lane, v1);
-    if (px.z >= 0) TapFma<T>::load(fb, px.z, lane, v2);
-    if (px.w >= 0) TapFma<T>::load(fb, px.w, lane, v3);
-    const float sw = exact ? ex2_approx(fmaf(s_wa[of.x + g] + __ldg(wc_raw + of.y + g), kLog2e, -gml))
-                           : s_ea[of.x + g] * __ldg(ec_tab + of.y + g);
-    if (px.x >= 0) TapFma<T>::fma(v0, w4.x * sw, acc);
-    if (px.y >= 0) TapFma<T>::fma(v1, w4.y * sw, acc);
-    if (px.z >= 0) TapFma<T>::fma(v2, w4.z * sw, acc);
-    if (px.w >= 0) TapFma<T>::fma(v3, w4.w * sw, acc);
+
+#pragma unroll 1
+  for (int base = 0; base < NPAIR; base += 32) {
+    const int q = base + lane;
+    const int cq = q / NP;
+    float2 uv = make_float2(-4.0f, -4.0f);
+    if (q < NPAIR) uv = __ldg(locp + q);
+    const bool maybe = q < NPAIR && cq >= p.cam_begin && cq < p.cam_end && uv.x > -0.5f && uv.x < 1.5f &&
+                       uv.y > -0.5f && uv.y < 1.5f;
+    const uint32_t keep = __ballot_sync(0xffffffffu, maybe);
+    if (keep == 0u) continue;
+    if (maybe) s_surv[warp][__popc(keep & lt)] = (unsigned char)lane;
+    __syncwarp();
+    const int n = __popc(keep) * NL;
+#pragma unroll 1
+    for (int sub = 0; sub < n; sub += 32) {
+      const int idx = sub + lane;
+      const int k = idx / NL, l = idx - (idx / NL) * NL;
+      const int src = idx < n ? s_surv[warp][k] : 0;
+      const float2 uvs = make_float2(__shfl_sync(0xffffffffu, uv.x, src), __shfl_sync(0xffffffffu, uv.y, src));
+      const int qs = base + src;
+      const int cs = qs / NP, ps = qs - (qs / NP) * NP;
+      int4 pix = make_int4(-1, -1, -1, -1);
+      float4 bw = make_float4(0.f, 0.f, 0.f, 0.f);
+      int e1 = 0, e2 = 0;
+      bool valid = false;
+      if (idx < n) {
+        const int4 lv = s_lvl[cs * NL + l];
+        const float Wf = (float)lv.y, Hf = (float)lv.x;
+        const float ix = ((uvs.x * 2.0f - 1.0f + 1.0f) * Wf - 1.0f) * 0.5f;
+        const float iy = ((uvs.y * 2.0f - 1.0f + 1.0f) * Hf - 1.0f) * 0.5f;
+        if (lv.w && ix > -1.0f && ix < Wf && iy > -1.0f && iy < Hf) {
+          const float x0f = floorf(ix), y0f = floorf(iy);
+          const int x0 = (int)x0f, y0 = (int)y0f;
+          const float x1f = x0f + 1.0f, y1f = y0f + 1.0f;
+          const bool vx0 = x0 >= 0, vx1 = x0 + 1 < lv.y, vy0 = y0 >= 0, vy1 = y0 + 1 < lv.x;
+          const int p00 = lv.z + y0 * lv.y + x0;
+          pix = make_int4(vx0 && vy0 ? p00 : -1, vx1 && vy0 ? p00 + 1 : -1, vx0 && vy1 ? p00 + lv.y : -1,
+                          vx1 && vy1 ? p00 + lv.y + 1 : -1);
+          bw = make_float4((x1f - ix) * (y1f - iy), (ix - x0f) * (y1f - iy), (x1f - ix) * (iy - y0f),
+                           (ix - x0f) * (iy - y0f));
+          const int lp = l * NP + ps;
+          e1 = lp * G;
+          e2 = cs * LPG + lp * G;
+          valid = true;
+        }
+      }
+      uint32_t vm = __ballot_sync(0xffffffffu, valid);
+      while (vm != 0u) {
+        const int sl = __ffs(vm) - 1;
+        vm &= vm - 1u;
+        const int4 px = make_int4(__shfl_sync(0xffffffffu, pix.x, sl), __shfl_sync(0xffffffffu, pix.y, sl),
+                                  __shfl_sync(0xffffffffu, pix.z, sl), __shfl_sync(0xffffffffu, pix.w, sl));
+        V v0, v1, v2, v3;
+        if (px.x >= 0) TapFma<T>::load(fb, px.x, lane, v0);
+        if (px.y >= 0) TapFma<T>::load(fb, px.y, lane, v1);
+        if (px.z >= 0) TapFma<T>::load(fb, px.z, lane, v2);
+        if (px.w >= 0) TapFma<T>::load(fb, px.w, lane, v3);
+        const float4 w4 = make_float4(__shfl_sync(0xffffffffu, bw.x, sl), __shfl_sync(0xffffffffu, bw.y, sl),
+                                      __shfl_sync(0xffffffffu, bw.z, sl), __shfl_sync(0xffffffffu, bw.w, sl));
+        const int i1 = __shfl_sync(0xffffffffu, e1, sl) + gch, i2 = __shfl_sync(0xffffffffu, e2, sl) + gch;
+        float sw;
+        if (!exact) {
+          sw = ea[i1] * __ldg(ec_tab + i2);
+        } else {
+          const float lg = MODE == 0 ? __ldg(wrow + i2) : __ldg(wrow + i1) + __ldg(wcam + i2);
+          sw = ex2_approx(fmaf(lg, kLog2e, -mlg));
+        }
+        if (px.x >= 0) TapFma<T>::fma(v0, w4.x * sw, acc);
+        if (px.y >= 0) TapFma<T>::fma(v1, w4.y * sw, acc);
+        if (px.z >= 0) TapFma<T>::fma(v2, w4.z * sw, acc);
+        if (px.w >= 0) TapFma<T>::fma(v3, w4.w * sw, acc);
+      }
+    }
+    __syncwarp();  // s_surv is rewritten by the next pair round
   }
 
-  // ---- 5. cross-warp reduction -------------------------------------------------------------
-  __syncthreads();
-  float4* r4 = reinterpret_cast<float4*>(s_red + warp * kChannels + lane * 8);
-  r4[0] = make_float4(acc[0].x, acc[0].y, acc[1].x, acc[1].y);
-  r4[1] = make_float4(acc[2].x, acc[2].y, acc[3].x, acc[3].y);
-  __syncthreads();
-  float v = 0.0f;
-#pragma unroll
-  for (int w = 0; w < kGatherWarps; ++w) v += s_red[w * kChannels + tid];
-  p.out[anchor_lin * kChannels + tid] = v * s_ginv[tid / D];
+  // ---- 3. normalise and store ------------------------------------------------------------------
+  float4* o = reinterpret_cast<float4*>(p.out + anchor_lin * kChannels + lane * 8);
+  o[0] = make_float4(acc[0].x * inv, acc[0].y * inv, acc[1].x * inv, acc[1].y * inv);
+  o[1] = make_float4(acc[2].x * inv, acc[2].y * inv, acc[3].x * inv, acc[3].y * inv);
 }
 
 // The Sparse4D v3 shape the fast kernels are compiled for.
@@ -862,15 +852,17 @@ int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream) {
   const size_t smem = gather_smem_bytes(p.num_cams, p.num_levels, p.num_pts, p.num_groups, p.cam_begin, p.cam_end);
   const unsigned grid = (unsigned)((int64_t)p.bs * p.num_anchor);
   if (fast_path_ok(p) && p.weights_cam != nullptr && p.cam_ws != nullptr) {
+    // split logits with a workspace: per-frame camera factors, then one warp per anchor
     constexpr int LPG = kFastNL * kFastNP * kFastG;
     cam_softmax_prep_kernel<kFastNC, LPG, kFastG><<<(unsigned)p.bs, kGatherThreads, 0, stream>>>(p.weights_cam, p.cam_ws);
     int st = cuda_check(cudaGetLastError(), "cam_softmax_prep_kernel launch");
     if (st) return st;
+    const unsigned wgrid = (unsigned)(((int64_t)p.bs * p.num_anchor + kGatherWarps - 1) / kGatherWarps);
     if (feat_dtype == S4D_DTYPE_BF16)
-      dfa_gather_split_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG><<<grid, kGatherThreads, 0, stream>>>(p);
+      dfa_gather_warp_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG, 1><<<wgrid, kGatherThreads, 0, stream>>>(p);
     else
-      dfa_gather_split_kernel<float, kFastNC, kFastNL, kFastNP, kFastG><<<grid, kGatherThreads, 0, stream>>>(p);
-    return cuda_check(cudaGetLastError(), "dfa_gather_split_kernel launch");
+      dfa_gather_warp_kernel<float, kFastNC, kFastNL, kFastNP, kFastG, 1><<<wgrid, kGatherThreads, 0, stream>>>(p);
+    return cuda_check(cudaGetLastError(), "dfa_gather_warp_kernel launch");
   }
   if (fast_path_ok(p)) {
     if (feat_dtype == S4D_DTYPE_BF16)

@@ -70,14 +70,15 @@ class DeformableFeatureAggregation:
 
     ``model_config`` may carry ``"FEATURE_DTYPE"`` (``torch.bfloat16`` default, or
     ``torch.float32``): the dtype feature maps are packed to when ``run`` receives a list.
-    ``split_logits=True`` evaluates ``weights_fc(f + cam) = weights_fc(f) + W cam`` as two
-    smaller GEMMs and adds the two terms inside the gather kernel instead of materialising the
-    ``[bs, A, Ncam, L*P*G]`` logits (same result up to fp32 rounding)."""
+    ``split_logits=True`` (default) evaluates ``weights_fc(f + cam) = weights_fc(f) + W cam``
+    as two smaller GEMMs (Ncam times fewer FLOPs) and combines the two terms inside the gather
+    kernel instead of materialising the ``[bs, A, Ncam, L*P*G]`` logits (same result up to
+    fp32 rounding); ``split_logits=False`` evaluates the linear exactly as the reference does."""
 
     def __init__(self, device, parameters: Dict[str, Tensor], model_config: Optional[Dict] = None,
                  embed_dims: int = 256, num_groups: int = 8, num_levels: int = 4, num_cams: int = 6,
                  num_pts: int = 13, num_learnable_pts: int = 6, use_camera_embed: bool = True,
-                 residual_mode: str = "cat", mesh_device=None, split_logits: bool = False) -> None:
+                 residual_mode: str = "cat", mesh_device=None, split_logits: bool = True) -> None:
         self.device = torch.device(device if not isinstance(device, int) else f"cuda:{device}")
         if self.device.type != "cuda":
             raise ValueError("DeformableFeatureAggregation runs on a CUDA device only")
