@@ -1,0 +1,116 @@
+"""Host-side logic that needs no GPU: synthetic inputs, packing, level tables, parameter
+extraction and the drop-in module's argument checks."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import dfa_numpy as onp
+from sparse4d_tt_b200 import DeformableFeatureAggregation, ops, preprocess_dfa_parameters
+from sparse4d_tt_b200 import synthetic as syn
+
+
+def test_synthetic_inputs_are_deterministic():
+    cfg = syn.DFAConfig(bs=2, num_anchor=16)
+    a, b = syn.make_inputs(cfg, 5), syn.make_inputs(cfg, 5)
+    for x, y in zip((a.instance_feature, a.anchor, a.projection_mat), (b.instance_feature, b.anchor, b.projection_mat)):
+        assert torch.equal(x, y)
+    assert not torch.equal(a.anchor, syn.make_inputs(cfg, 6).anchor)
+
+
+def test_camera_ring_projects_forward_points_to_image_centre():
+    proj = syn.camera_ring(6, (704, 256))
+    for c, yaw in enumerate(syn.CAMERA_YAWS_DEG):
+        r = np.radians(yaw)
+        p = torch.tensor([20 * np.cos(r), 20 * np.sin(r), 1.5, 1.0], dtype=torch.float32)
+        q = proj[c] @ p
+        assert q[2] > 0
+        np.testing.assert_allclose((q[:2] / q[2]).numpy(), [352, 128], atol=1e-3)
+
+
+def test_synthetic_visibility_fraction():
+    """About 15 % of the point samples land in front of a camera and inside its image."""
+    from oracle import dfa_torch as oto
+
+    cfg = syn.config_standard(1)
+    ins = syn.make_inputs(cfg, 0)
+    params = syn.make_params(cfg, torch.Generator().manual_seed(100))
+    kps = oto.key_points(ins.anchor, ins.instance_feature, params)
+    uv, depth = oto.project_points_with_depth(kps, ins.projection_mat, ins.image_wh)
+    _, vis = oto.visibility(uv, depth)
+    assert 0.10 < vis.float().mean().item() < 0.22
+
+
+@pytest.mark.parametrize("channels_last", [False, True])
+def test_pack_feature_maps_matches_numpy(channels_last):
+    rng = np.random.default_rng(1)
+    maps = [rng.standard_normal((2, 3, 256, h, w)).astype(np.float32) for h, w in ((4, 6), (2, 3))]
+    feat_np, shape_np, start_np = onp.pack_feature_maps(maps)
+    tm = [torch.from_numpy(m) for m in maps]
+    if channels_last:
+        tm = [m.permute(0, 1, 3, 4, 2).contiguous() for m in tm]
+    feat, shape, start = ops.pack_feature_maps(tm, channels_last=channels_last)
+    assert np.array_equal(feat.numpy(), feat_np)
+    assert np.array_equal(shape.numpy(), shape_np) and np.array_equal(start.numpy(), start_np)
+    assert feat.shape == (2, 3 * (24 + 6), 256)
+
+
+def test_level_tables():
+    shape, start, nf = ops.level_tables([(64, 176), (32, 88), (16, 44), (8, 22)], 6)
+    assert nf == 6 * 14960
+    assert start[1, 0].item() == 14960 and start[0, 3].item() == 64 * 176 + 32 * 88 + 16 * 44
+    assert shape.dtype == torch.int32 and tuple(shape.shape) == (6, 4, 2)
+
+
+def test_preprocess_parameters_matches_reference_keys():
+    """The keys of model/deformable_feature_aggregation.py:954-995, from a module with the
+    reference DFA's attribute structure."""
+    cfg = syn.DFAConfig()
+    p = syn.make_params(cfg, torch.Generator().manual_seed(0))
+
+    class Lin(torch.nn.Module):
+        def __init__(self, w, b):
+            super().__init__()
+            self.weight = torch.nn.Parameter(w)
+            self.bias = torch.nn.Parameter(b)
+
+    class KPS(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.fix_scale = torch.nn.Parameter(p["kps_fix_scale"], requires_grad=False)
+            self.learnable_fc = Lin(p["kps_learnable_fc_weight"], p["kps_learnable_fc_bias"])
+
+    class M(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.kps_generator = KPS()
+            self.camera_encoder = torch.nn.Sequential(
+                Lin(p["cam_linear1_weight"], p["cam_linear1_bias"]), torch.nn.ReLU(),
+                Lin(p["cam_ln1_weight"], p["cam_ln1_bias"]),
+                Lin(p["cam_linear2_weight"], p["cam_linear2_bias"]), torch.nn.ReLU(),
+                Lin(p["cam_ln2_weight"], p["cam_ln2_bias"]))
+            self.weights_fc = Lin(p["weights_fc_weight"], p["weights_fc_bias"])
+            self.output_proj = Lin(p["output_proj_weight"], p["output_proj_bias"])
+
+    got = preprocess_dfa_parameters(M())
+    assert set(got) == set(p)
+    for k in p:
+        assert torch.equal(got[k], p[k]), k
+
+
+def test_module_rejects_cpu_device_and_missing_params():
+    p = syn.make_params(syn.DFAConfig(), torch.Generator().manual_seed(0))
+    with pytest.raises(ValueError, match="CUDA"):
+        DeformableFeatureAggregation("cpu", p)
+    bad = dict(p)
+    del bad["weights_fc_bias"]
+    with pytest.raises(KeyError):
+        DeformableFeatureAggregation("cuda:0", bad)
+
+
+def test_refine_anchors_keeps_unit_yaw():
+    gen = torch.Generator().manual_seed(0)
+    a = syn.make_anchors(1, 100, gen)
+    r = syn.refine_anchors(a, gen)
+    n = r[..., 6:8].norm(dim=-1)
+    np.testing.assert_allclose(n.numpy(), 1.0, atol=1e-5)
+    assert (r[..., 0:3] - a[..., 0:3]).abs().max() < 1.0
