@@ -113,6 +113,25 @@ S4D_API int s4d_kps_project(const float* anchor, int64_t anchor_dim, const float
                     int32_t* visible_count, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * s4d_kps_project without a workspace, for callers that cannot allocate device memory (an FFI
+ * host without a CUDA allocator, a fixed device-memory budget, a loop that must not allocate
+ * after start-up).  No counterpart in the reference.
+ *
+ * Same arguments and results as s4d_kps_project minus workspace/workspace_bytes.  The
+ * compaction scratch is a 528 KiB array compiled into the library (held on every GPU that
+ * loads the library until exit), so bs*A*Ncam*P is limited to 4,194,304 elements; larger calls
+ * return S4D_ERR_UNSUPPORTED_SHAPE.  The first call on a device looks the array's device
+ * address up (cudaGetSymbolAddress) with that device current; make it before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race.  Allocates nothing.
+ */
+S4D_API int s4d_kps_project_noalloc(const float* anchor, int64_t anchor_dim, const float* fix_scale,
+                                    int64_t num_fix, const float* learnable, int64_t num_learnable,
+                                    const float* projection_mat, const float* image_wh, int64_t bs,
+                                    int64_t num_anchor, int64_t num_cams, int layout, float* key_points,
+                                    float* sample_location, uint8_t* depth_mask, int32_t* visible_idx,
+                                    int32_t* visible_count, void* stream);
+
+/*
  * Drop-in of ttnn.kps_project_fused in its standard mode
  * (tt-metal/ops/kps_project_fused/kps_project_fused.hpp:12-22, kernel
  * .../dataflow/reader_kps_project.cpp:255-289): pre-rotation keypoints in, normalised grid out.
