@@ -42,6 +42,10 @@ METRIC = "DFA calls/s and keypoint-samples/s per B200 (bf16) at 1/2/4/8 GPUs; % 
 UNIT = "DFA calls/s"
 SAMPLES_PER_CALL = 900 * 13 * 6 * 4  # logical keypoint samples of one frame through one layer
 FALLBACK_HBM_GBS = 6650.0
+# bf16 maps (fp32 accumulation); the layer's linears on TF32 tensor cores with fp32
+# accumulation (the reference's TT path runs them in bf16); parity of exactly this
+# configuration: tests/test_gpu_dfa_layer.py::test_layer_bf16_tf32_linears
+MODEL_CONFIG = {"FEATURE_DTYPE": torch.bfloat16, "MATMUL_PRECISION": "tf32"}
 
 
 def parse_args():
@@ -78,6 +82,7 @@ def workload_config(frames, layers, world):
         "frames_per_gpu": frames, "layers": layers, "global_batch": frames * world,
         "anchors": 900, "num_pts": 13, "num_cams": 6, "num_levels": 4, "embed_dims": 256, "num_groups": 8,
         "accumulate": "f32", "logits": "split (per-anchor + per-camera terms, summed in the gather kernel)",
+        "linears": "TF32 tensor cores, fp32 accumulation (cuBLAS through torch)",
         "parallelism": f"dp{world} (frames)",
         "l2": "inputs larger than L2 (1.47 GB of maps per GPU, re-read by every layer)",
     }
@@ -207,8 +212,7 @@ class Workload:
             self.anchors.append(a.to(device))
             self.embeds.append(torch.randn(frames, cfg.num_anchor, cfg.embed_dims, generator=gen).to(device))
             params = syn.make_params(cfg, torch.Generator().manual_seed(seed * 100 + layer))
-            self.mods.append(DeformableFeatureAggregation(device, params, {"FEATURE_DTYPE": torch.bfloat16},
-                                                          split_logits=True))
+            self.mods.append(DeformableFeatureAggregation(device, params, MODEL_CONFIG, split_logits=True))
             a = syn.refine_anchors(a, gen)
         self.proj = syn.camera_ring(cfg.num_cams, cfg.image_wh)[None].expand(frames, -1, -1, -1).contiguous().to(device)
         self.wh = torch.tensor(cfg.image_wh, dtype=torch.float32).expand(frames, cfg.num_cams, 2).contiguous().to(device)
@@ -355,7 +359,7 @@ def bs1_leg(device, iters=200):
     cfg = syn.config_standard(1)
     ins = syn.make_inputs(cfg, 0, feature_dtype=torch.bfloat16)
     params = syn.make_params(cfg, torch.Generator().manual_seed(100))
-    mod = DeformableFeatureAggregation(device, params, {"FEATURE_DTYPE": torch.bfloat16}, split_logits=True)
+    mod = DeformableFeatureAggregation(device, params, MODEL_CONFIG, split_logits=True)
     packed = ops.pack_feature_maps([m.to(device) for m in ins.feature_maps], dtype=torch.bfloat16)
     inst, anchor, embed = (t.to(device) for t in (ins.instance_feature, ins.anchor, ins.anchor_embed))
     proj, wh = ins.projection_mat.to(device), ins.image_wh.to(device)

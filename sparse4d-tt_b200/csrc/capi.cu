@@ -70,6 +70,7 @@ int s4d_kps_project(const float* anchor, int64_t anchor_dim, const float* fix_sc
   if (anchor_dim < 8) return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: anchor_dim must be >= 8");
   const int64_t num_pts = num_fix + num_learnable;
   if (num_pts == 0) return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: no keypoints");
+  if (num_pts > 64) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project: at most 64 keypoints per anchor");
   const int64_t total = bs * num_anchor * num_cams * num_pts;
   if (total >= kMaxElems || num_cams * num_pts >= (1 << 24))
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project: bs*A*Ncam*P must be < 2^31");
@@ -121,6 +122,7 @@ int s4d_kps_project_fused(const float* key_points, const float* anchor, int64_t 
                           int64_t num_pts, float* grid, void* stream) {
   set_error("%s", "");
   if (n < 0 || num_cams < 0 || num_pts < 0) return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project_fused: negative size");
+  if (num_pts > 64) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project_fused: at most 64 keypoints per anchor");
   if (anchor_dim < 8) return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project_fused: anchor_dim must be >= 8");
   const int64_t total = n * num_cams * num_pts;
   if (total >= kMaxElems) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project_fused: n*Ncam*P must be < 2^31");

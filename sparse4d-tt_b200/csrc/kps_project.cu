@@ -26,6 +26,9 @@ constexpr int kKpsThreads = 256;
 constexpr int kKpsRounds = 4;
 constexpr int kElemsPerBlock = kKpsThreads * kKpsRounds;  // 1024
 constexpr int kWordsPerBlock = kElemsPerBlock / 32;        // 32
+constexpr int kMaxPts = 64;                                // keypoints per anchor supported
+// anchors touched by one block's elements x keypoints: <= (1024 / (Ncam*P) + 2) * P
+constexpr int kMaxBlockKeypoints = kElemsPerBlock + 2 * kMaxPts;
 
 
 __device__ __forceinline__ float sigmoid_rn(float x) {
@@ -68,9 +71,31 @@ __device__ __forceinline__ float proj_row(const float* r, float px, float py, fl
 }
 
 __global__ void __launch_bounds__(kKpsThreads) kps_project_kernel(KpsParams k) {
+  // Keypoints of the anchors this block's elements belong to, computed once each (not once per
+  // camera) and shared through shared memory.
+  __shared__ float s_kp[kMaxBlockKeypoints * 3];
   const int lane = threadIdx.x & 31;
   const int64_t block_base = (int64_t)blockIdx.x * kElemsPerBlock;
   const int per_anchor = k.num_cams * k.num_pts;
+  const int64_t n0 = block_base / per_anchor;
+  const int64_t last = block_base + kElemsPerBlock - 1 < k.total ? block_base + kElemsPerBlock - 1 : k.total - 1;
+  const int nkp = (int)(last / per_anchor - n0 + 1) * k.num_pts;
+  for (int i = threadIdx.x; i < nkp; i += kKpsThreads) {
+    const int64_t n = n0 + i / k.num_pts;
+    const int p = i % k.num_pts;
+    float px, py, pz;
+    keypoint(k, n, p, px, py, pz);
+    s_kp[3 * i] = px;
+    s_kp[3 * i + 1] = py;
+    s_kp[3 * i + 2] = pz;
+    if (k.key_points != nullptr) {  // anchors shared by two blocks are written twice, identically
+      float* kp = k.key_points + (n * k.num_pts + p) * 3;
+      kp[0] = px;
+      kp[1] = py;
+      kp[2] = pz;
+    }
+  }
+  __syncthreads();
   int count = 0;
 #pragma unroll
   for (int r = 0; r < kKpsRounds; ++r) {
@@ -82,14 +107,8 @@ __global__ void __launch_bounds__(kKpsThreads) kps_project_kernel(KpsParams k) {
       const int c = rem / k.num_pts;
       const int p = rem - c * k.num_pts;
       const int b = (int)(n / k.num_anchor);
-      float px, py, pz;
-      keypoint(k, n, p, px, py, pz);
-      if (k.key_points != nullptr && c == 0) {
-        float* kp = k.key_points + (n * k.num_pts + p) * 3;
-        kp[0] = px;
-        kp[1] = py;
-        kp[2] = pz;
-      }
+      const int ik = (int)(n - n0) * k.num_pts + p;
+      const float px = s_kp[3 * ik], py = s_kp[3 * ik + 1], pz = s_kp[3 * ik + 2];
       const float* P = k.proj + ((int64_t)b * k.num_cams + c) * 16;
       const float X0 = proj_row(P, px, py, pz);
       const float X1 = proj_row(P + 4, px, py, pz);

@@ -20,6 +20,7 @@ own cameras, with the softmax taken over ALL cameras, and the partial sums are a
 """
 from __future__ import annotations
 
+import contextlib
 from typing import Dict, List, Optional, Sequence, Tuple, Union
 
 import torch
@@ -64,12 +65,31 @@ def preprocess_dfa_parameters(pt_model) -> Dict[str, Tensor]:
 
 FeatureMaps = Union[List[Tensor], Tuple[Tensor, Tensor, Tensor]]
 
+MATMUL_PRECISIONS = {"fp32": "highest", "tf32": "high"}
+
+
+@contextlib.contextmanager
+def _matmul_precision(precision: str):
+    """torch's fp32 matmul precision for the duration of the block ("highest": fp32 GEMMs;
+    "high": TF32 tensor-core GEMMs with fp32 accumulation), restored afterwards."""
+    old = torch.get_float32_matmul_precision()
+    if old == precision:
+        yield
+        return
+    torch.set_float32_matmul_precision(precision)
+    try:
+        yield
+    finally:
+        torch.set_float32_matmul_precision(old)
+
 
 class DeformableFeatureAggregation:
     """B200 DFA layer.  ``device`` is a CUDA device (``"cuda:0"``, ``torch.device`` or index).
 
     ``model_config`` may carry ``"FEATURE_DTYPE"`` (``torch.bfloat16`` default, or
-    ``torch.float32``): the dtype feature maps are packed to when ``run`` receives a list.
+    ``torch.float32``): the dtype feature maps are packed to when ``run`` receives a list; and
+    ``"MATMUL_PRECISION"``: ``"fp32"`` (default) or ``"tf32"`` for the layer's linears
+    (TF32 tensor cores, fp32 accumulation; the reference's TT path runs them in bf16).
     ``split_logits=True`` (default) evaluates ``weights_fc(f + cam) = weights_fc(f) + W cam``
     as two smaller GEMMs (Ncam times fewer FLOPs) and combines the two terms inside the gather
     kernel instead of materialising the ``[bs, A, Ncam, L*P*G]`` logits (same result up to
@@ -93,6 +113,10 @@ class DeformableFeatureAggregation:
         self.residual_mode = residual_mode
         self.model_config = dict(model_config or {})
         self.feature_dtype = self.model_config.get("FEATURE_DTYPE", torch.bfloat16)
+        prec = self.model_config.get("MATMUL_PRECISION", "fp32")
+        if prec not in MATMUL_PRECISIONS:
+            raise ValueError(f"MATMUL_PRECISION must be one of {sorted(MATMUL_PRECISIONS)}")
+        self.matmul_precision = MATMUL_PRECISIONS[prec]
         self.split_logits = bool(split_logits and use_camera_embed)
         self.process_group = mesh_device if _is_process_group(mesh_device) else None
         if mesh_device is not None and self.process_group is None:
@@ -189,8 +213,9 @@ class DeformableFeatureAggregation:
         image_wh = image_wh.reshape(bs, self.num_cams, 2).float().contiguous()
         mc_ms_feat, spatial_shape, scale_start = self._features(feature_maps, spatial_shapes, bs)
 
-        logits, logits_cam = self._get_weights(instance_feature, anchor_embed, projection_mat, bs, num_anchor)
-        learn = F.linear(instance_feature, self.learnable_fc_weight, self.learnable_fc_bias).contiguous()
+        with _matmul_precision(self.matmul_precision):
+            logits, logits_cam = self._get_weights(instance_feature, anchor_embed, projection_mat, bs, num_anchor)
+            learn = F.linear(instance_feature, self.learnable_fc_weight, self.learnable_fc_bias).contiguous()
         loc = torch.empty(bs, num_anchor, self.num_cams, self.num_pts, 2, dtype=torch.float32, device=dev)
         ops.kps_project_into(anchor, learn, self.fix_scale, projection_mat, image_wh, sample_location=loc)
 
@@ -219,7 +244,8 @@ class DeformableFeatureAggregation:
 
             dist.all_reduce(feats, group=self.process_group)
 
-        out = F.linear(feats, self.output_proj_weight, self.output_proj_bias)
+        with _matmul_precision(self.matmul_precision):
+            out = F.linear(feats, self.output_proj_weight, self.output_proj_bias)
         inst = instance_feature.to(out.dtype)
         if self.residual_mode == "add":
             return out + inst

@@ -23,8 +23,9 @@ def _fp32_matmul():
     assert not torch.backends.cuda.matmul.allow_tf32
 
 
-def _module(params, cfg, dtype=torch.float32, split=False):
-    return DeformableFeatureAggregation("cuda:0", params, {"FEATURE_DTYPE": dtype}, embed_dims=cfg.embed_dims,
+def _module(params, cfg, dtype=torch.float32, split=False, matmul="fp32"):
+    return DeformableFeatureAggregation("cuda:0", params, {"FEATURE_DTYPE": dtype, "MATMUL_PRECISION": matmul},
+                                        embed_dims=cfg.embed_dims,
                                         num_groups=cfg.num_groups, num_levels=cfg.num_levels,
                                         num_cams=cfg.num_cams, num_pts=cfg.num_pts,
                                         num_learnable_pts=cfg.num_learnable_pts, split_logits=split)
@@ -63,6 +64,21 @@ def test_layer_bf16_against_reference(cuda_device, split):
     sel = out[..., :256].reshape(900, 256).numpy()[g["rows"]]
     p, mre, xre = pcc(sel, g["out_rows"]), mean_rel_err(sel, g["out_rows"]), max_rel_err(sel, g["out_rows"])
     print(f"layer bf16 split={split}: pcc={p:.7f} mean_rel={mre:.2e} max_rel={xre:.2e}")
+    assert p >= BF16_PCC and mre <= BF16_REL and xre <= BF16_REL
+    ref = oto.dfa_layer(params, ins.instance_feature, ins.anchor, ins.anchor_embed, ins.feature_maps,
+                        ins.projection_mat, ins.image_wh)
+    assert pcc(out, ref) >= BF16_PCC and max_rel_err(out, ref) <= BF16_REL
+
+
+def test_layer_bf16_tf32_linears(cuda_device):
+    """The benchmark's configuration: bf16 maps, split logits, TF32 linears; against the
+    reference's rows and the fp32 oracle at the bf16 tolerance."""
+    g, cfg, ins, params = regen("standard_s1_bf16")
+    out = _run(_module(params, cfg, torch.bfloat16, True, "tf32"), ins, cfg)
+    assert torch.get_float32_matmul_precision() == "highest"  # restored after the layer
+    sel = out[..., :256].reshape(900, 256).numpy()[g["rows"]]
+    p, mre, xre = pcc(sel, g["out_rows"]), mean_rel_err(sel, g["out_rows"]), max_rel_err(sel, g["out_rows"])
+    print(f"layer bf16 + tf32 linears: pcc={p:.7f} mean_rel={mre:.2e} max_rel={xre:.2e}")
     assert p >= BF16_PCC and mre <= BF16_REL and xre <= BF16_REL
     ref = oto.dfa_layer(params, ins.instance_feature, ins.anchor, ins.anchor_embed, ins.feature_maps,
                         ins.projection_mat, ins.image_wh)
