@@ -59,6 +59,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-bs1", action="store_true")
+    ap.add_argument("--profile-gather", action="store_true",
+                    help="profiling case: one layer over --frames frames, one warm-up call then one call "
+                         "inside the NVTX range 'profile' (few launches before the profiled gather)")
     return ap.parse_args()
 
 
@@ -626,8 +629,25 @@ def run_ours(args):
         pg.destroy_process_group()
 
 
+def run_profile_case(args):
+    """A small, quiet case for ncu: the layer of bench.py's workload, run twice."""
+    device = torch.device("cuda:0")
+    torch.cuda.set_device(device)
+    w = Workload(args.frames, 1, device, seed=1)
+    w.step()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("profile")
+    w.step()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": f"1 DFA layer x {args.frames} frames", "ok": True}), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.profile_gather:
+        run_profile_case(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

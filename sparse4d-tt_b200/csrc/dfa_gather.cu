@@ -665,8 +665,16 @@ __global__ void __launch_bounds__(kGatherThreads) cam_softmax_prep_kernel(const 
 //             (lane l: channels 8l..8l+7) and accumulates with packed fp32x2 FMA.
 //   output    normalised in registers (1 / sum of the lane's group) and stored by each lane.
 // -----------------------------------------------------------------------------------------------
-template <typename T, int NC, int NL, int NP, int G, int MODE>
-__global__ void __launch_bounds__(kGatherThreads, 4) dfa_gather_warp_kernel(GatherParams p) {
+// One in-bounds sample of a warp's anchor, as the merging step shares it between lanes.
+struct SampleRec {
+  int4 pix;    // the 4 taps' feature rows (-1: outside the map)
+  float4 bw;   // their bilinear weights
+  int e1, e2;  // logit offsets: anchor term lp*G, camera term c*LPG + lp*G
+  int pad0, pad1;
+};
+
+template <typename T, int NC, int NL, int NP, int G, int MODE, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 32 / WARPS) dfa_gather_warp_kernel(GatherParams p) {
   constexpr int NLP = NL * NP;
   constexpr int LPG = NLP * G;
   constexpr int NW = NC * LPG;
@@ -674,23 +682,22 @@ __global__ void __launch_bounds__(kGatherThreads, 4) dfa_gather_warp_kernel(Gath
   constexpr int D = kChannels / G;
   constexpr float kLog2e = 1.4426950408889634f;
   static_assert(LPG % 32 == 0 && 32 % G == 0 && G >= 4 && (G & (G - 1)) == 0, "warp gather shape");
-  static_assert(NC * NL <= kGatherThreads, "level table staged by one pass");
-
   __shared__ __align__(16) int4 s_lvl[NC * NL];  // (H, W, start, ok)
-  __shared__ __align__(16) float s_ea[MODE == 1 ? kGatherWarps * LPG : 1];
-  __shared__ unsigned char s_surv[kGatherWarps][32];
+  __shared__ __align__(16) float s_ea[MODE == 1 ? WARPS * LPG : 1];
+  __shared__ unsigned char s_surv[WARPS][32];
+  __shared__ SampleRec s_rec[WARPS][32];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid < NC * NL) {
-    const int H = p.spatial_shape[2 * tid], W = p.spatial_shape[2 * tid + 1], st = p.scale_start[tid];
+  for (int i = tid; i < NC * NL; i += WARPS * 32) {
+    const int H = p.spatial_shape[2 * i], W = p.spatial_shape[2 * i + 1], st = p.scale_start[i];
     const bool ok = H > 0 && W > 0 && st >= 0 && (int64_t)st + (int64_t)H * W <= p.num_feat;
-    const int c = tid / NL;
+    const int c = i / NL;
     if (!ok && c >= p.cam_begin && c < p.cam_end && p.error_flag != nullptr && blockIdx.x == 0)
       atomicOr(p.error_flag, S4D_FLAG_BAD_LEVEL);
-    s_lvl[tid] = make_int4(H, W, st, ok ? 1 : 0);
+    s_lvl[i] = make_int4(H, W, st, ok ? 1 : 0);
   }
   __syncthreads();  // the only block barrier: every thread reaches it before any warp leaves
-  const int64_t anchor_lin = (int64_t)blockIdx.x * kGatherWarps + warp;
+  const int64_t anchor_lin = (int64_t)blockIdx.x * WARPS + warp;
   if (anchor_lin >= (int64_t)p.bs * p.num_anchor) return;
   const int b = (int)(anchor_lin / p.num_anchor);
   const int gch = lane / (D / 8);  // group of this lane's output channels
@@ -760,19 +767,21 @@ __global__ void __launch_bounds__(kGatherThreads, 4) dfa_gather_warp_kernel(Gath
     if (keep == 0u) continue;
     if (maybe) s_surv[warp][__popc(keep & lt)] = (unsigned char)lane;
     __syncwarp();
-    const int n = __popc(keep) * NL;
+    // Candidates (survivor, level), level-major so that one camera's points at one level sit in
+    // the same 32-lane sub-round: samples whose 2x2 tap block coincides are merged there.
+    const int nsurv = __popc(keep);
+    const int n = nsurv * NL;
 #pragma unroll 1
     for (int sub = 0; sub < n; sub += 32) {
       const int idx = sub + lane;
-      const int k = idx / NL, l = idx - (idx / NL) * NL;
+      const int l = idx / nsurv, k = idx - (idx / nsurv) * nsurv;
       const int src = idx < n ? s_surv[warp][k] : 0;
       const float2 uvs = make_float2(__shfl_sync(0xffffffffu, uv.x, src), __shfl_sync(0xffffffffu, uv.y, src));
       const int qs = base + src;
       const int cs = qs / NP, ps = qs - (qs / NP) * NP;
-      int4 pix = make_int4(-1, -1, -1, -1);
-      float4 bw = make_float4(0.f, 0.f, 0.f, 0.f);
-      int e1 = 0, e2 = 0;
+      uint64_t key = 0xffffffff00000000ull | (uint32_t)lane;  // invalid lanes only match themselves
       bool valid = false;
+      SampleRec rec;
       if (idx < n) {
         const int4 lv = s_lvl[cs * NL + l];
         const float Wf = (float)lv.y, Hf = (float)lv.x;
@@ -784,41 +793,57 @@ __global__ void __launch_bounds__(kGatherThreads, 4) dfa_gather_warp_kernel(Gath
           const float x1f = x0f + 1.0f, y1f = y0f + 1.0f;
           const bool vx0 = x0 >= 0, vx1 = x0 + 1 < lv.y, vy0 = y0 >= 0, vy1 = y0 + 1 < lv.x;
           const int p00 = lv.z + y0 * lv.y + x0;
-          pix = make_int4(vx0 && vy0 ? p00 : -1, vx1 && vy0 ? p00 + 1 : -1, vx0 && vy1 ? p00 + lv.y : -1,
-                          vx1 && vy1 ? p00 + lv.y + 1 : -1);
-          bw = make_float4((x1f - ix) * (y1f - iy), (ix - x0f) * (y1f - iy), (x1f - ix) * (iy - y0f),
-                           (ix - x0f) * (iy - y0f));
+          rec.pix = make_int4(vx0 && vy0 ? p00 : -1, vx1 && vy0 ? p00 + 1 : -1, vx0 && vy1 ? p00 + lv.y : -1,
+                              vx1 && vy1 ? p00 + lv.y + 1 : -1);
+          rec.bw = make_float4((x1f - ix) * (y1f - iy), (ix - x0f) * (y1f - iy), (x1f - ix) * (iy - y0f),
+                               (ix - x0f) * (iy - y0f));
           const int lp = l * NP + ps;
-          e1 = lp * G;
-          e2 = cs * LPG + lp * G;
+          rec.e1 = lp * G;
+          rec.e2 = cs * LPG + lp * G;
+          // (camera, level) and the top-left tap (x0, y0 >= -1) identify the 2x2 block
+          key = ((uint64_t)(cs * NL + l) << 32) | (uint32_t)((y0 + 1) * (lv.y + 1) + (x0 + 1));
           valid = true;
         }
       }
-      uint32_t vm = __ballot_sync(0xffffffffu, valid);
-      while (vm != 0u) {
-        const int sl = __ffs(vm) - 1;
-        vm &= vm - 1u;
-        const int4 px = make_int4(__shfl_sync(0xffffffffu, pix.x, sl), __shfl_sync(0xffffffffu, pix.y, sl),
-                                  __shfl_sync(0xffffffffu, pix.z, sl), __shfl_sync(0xffffffffu, pix.w, sl));
+      const uint32_t grp = __match_any_sync(0xffffffffu, key);
+      uint32_t leaders = __ballot_sync(0xffffffffu, valid && lane == __ffs(grp) - 1);
+      __syncwarp();  // the previous sub-round's records have been read
+      if (valid) s_rec[warp][lane] = rec;
+      __syncwarp();
+      while (leaders != 0u) {
+        const int ld = __ffs(leaders) - 1;
+        leaders &= leaders - 1u;
+        uint32_t mem = __shfl_sync(0xffffffffu, grp, ld);
+        const int4 px = s_rec[warp][ld].pix;
         V v0, v1, v2, v3;
         if (px.x >= 0) TapFma<T>::load(fb, px.x, lane, v0);
         if (px.y >= 0) TapFma<T>::load(fb, px.y, lane, v1);
         if (px.z >= 0) TapFma<T>::load(fb, px.z, lane, v2);
         if (px.w >= 0) TapFma<T>::load(fb, px.w, lane, v3);
-        const float4 w4 = make_float4(__shfl_sync(0xffffffffu, bw.x, sl), __shfl_sync(0xffffffffu, bw.y, sl),
-                                      __shfl_sync(0xffffffffu, bw.z, sl), __shfl_sync(0xffffffffu, bw.w, sl));
-        const int i1 = __shfl_sync(0xffffffffu, e1, sl) + gch, i2 = __shfl_sync(0xffffffffu, e2, sl) + gch;
-        float sw;
-        if (!exact) {
-          sw = ea[i1] * __ldg(ec_tab + i2);
-        } else {
-          const float lg = MODE == 0 ? __ldg(wrow + i2) : __ldg(wrow + i1) + __ldg(wcam + i2);
-          sw = ex2_approx(fmaf(lg, kLog2e, -mlg));
+        // the block's weight for this lane's group: sum over its member samples of bilinear
+        // weight x unnormalised softmax weight
+        float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        while (mem != 0u) {
+          const int j = __ffs(mem) - 1;
+          mem &= mem - 1u;
+          const float4 bw = s_rec[warp][j].bw;
+          const int i1 = s_rec[warp][j].e1 + gch, i2 = s_rec[warp][j].e2 + gch;
+          float sw;
+          if (!exact) {
+            sw = ea[i1] * __ldg(ec_tab + i2);
+          } else {
+            const float lg = MODE == 0 ? __ldg(wrow + i2) : __ldg(wrow + i1) + __ldg(wcam + i2);
+            sw = ex2_approx(fmaf(lg, kLog2e, -mlg));
+          }
+          w4.x = fmaf(bw.x, sw, w4.x);
+          w4.y = fmaf(bw.y, sw, w4.y);
+          w4.z = fmaf(bw.z, sw, w4.z);
+          w4.w = fmaf(bw.w, sw, w4.w);
         }
-        if (px.x >= 0) TapFma<T>::fma(v0, w4.x * sw, acc);
-        if (px.y >= 0) TapFma<T>::fma(v1, w4.y * sw, acc);
-        if (px.z >= 0) TapFma<T>::fma(v2, w4.z * sw, acc);
-        if (px.w >= 0) TapFma<T>::fma(v3, w4.w * sw, acc);
+        if (px.x >= 0) TapFma<T>::fma(v0, w4.x, acc);
+        if (px.y >= 0) TapFma<T>::fma(v1, w4.y, acc);
+        if (px.z >= 0) TapFma<T>::fma(v2, w4.z, acc);
+        if (px.w >= 0) TapFma<T>::fma(v3, w4.w, acc);
       }
     }
     __syncwarp();  // s_surv is rewritten by the next pair round
@@ -832,6 +857,9 @@ __global__ void __launch_bounds__(kGatherThreads, 4) dfa_gather_warp_kernel(Gath
 
 // The Sparse4D v3 shape the fast kernels are compiled for.
 constexpr int kFastNC = 6, kFastNL = 4, kFastNP = 13, kFastG = 8;
+// anchors (warps) per block of dfa_gather_warp_kernel: small blocks retire as soon as their own
+// anchors are done, so uneven anchors do not leave finished warps waiting for block-mates
+constexpr int kWarpBlock = 1;
 
 size_t gather_workspace_bytes(int64_t bs, int ncam, int nl, int np, int G) {
   return (size_t)bs * (ncam + 1) * nl * np * G * sizeof(float);
@@ -857,11 +885,13 @@ int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream) {
     cam_softmax_prep_kernel<kFastNC, LPG, kFastG><<<(unsigned)p.bs, kGatherThreads, 0, stream>>>(p.weights_cam, p.cam_ws);
     int st = cuda_check(cudaGetLastError(), "cam_softmax_prep_kernel launch");
     if (st) return st;
-    const unsigned wgrid = (unsigned)(((int64_t)p.bs * p.num_anchor + kGatherWarps - 1) / kGatherWarps);
+    const unsigned wgrid = (unsigned)(((int64_t)p.bs * p.num_anchor + kWarpBlock - 1) / kWarpBlock);
     if (feat_dtype == S4D_DTYPE_BF16)
-      dfa_gather_warp_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG, 1><<<wgrid, kGatherThreads, 0, stream>>>(p);
+      dfa_gather_warp_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock>
+          <<<wgrid, kWarpBlock * 32, 0, stream>>>(p);
     else
-      dfa_gather_warp_kernel<float, kFastNC, kFastNL, kFastNP, kFastG, 1><<<wgrid, kGatherThreads, 0, stream>>>(p);
+      dfa_gather_warp_kernel<float, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock>
+          <<<wgrid, kWarpBlock * 32, 0, stream>>>(p);
     return cuda_check(cudaGetLastError(), "dfa_gather_warp_kernel launch");
   }
   if (fast_path_ok(p)) {
