@@ -674,7 +674,7 @@ struct SampleRec {
 };
 
 template <typename T, int NC, int NL, int NP, int G, int MODE, int WARPS>
-__global__ void __launch_bounds__(WARPS * 32, 32 / WARPS) dfa_gather_warp_kernel(GatherParams p) {
+__global__ void __launch_bounds__(WARPS * 32) dfa_gather_warp_kernel(GatherParams p) {
   constexpr int NLP = NL * NP;
   constexpr int LPG = NLP * G;
   constexpr int NW = NC * LPG;
