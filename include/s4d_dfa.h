@@ -1,7 +1,7 @@
 /*
  * s4d_dfa.h -- C ABI of the B200 (sm_100a) DeformableFeatureAggregation hot path.
  *
- * Two operators, each a set of hand-written CUDA kernels:
+ * Three operators, each a set of hand-written CUDA kernels:
  *
  *   s4d_kps_project            anchor decode -> 7 fixed + N learnable keypoints -> yaw rotation
  *                              -> per-camera lidar2img projection -> depth clamp and
@@ -11,6 +11,8 @@
  *                              group, fused with the multi-camera, multi-scale bilinear gather
  *                              (zeros padding, align_corners=False) and the weighted sum over
  *                              cameras, levels and points.
+ *   s4d_dfa_weights_fc /       the dense linears before and after the gather on the tensor
+ *   s4d_dfa_output_proj        cores (tcgen05), with the embed add and the residual fused.
  *
  * Conventions
  *   - Every pointer is a DEVICE pointer of the current CUDA device unless stated otherwise.
@@ -62,8 +64,15 @@ enum { S4D_DTYPE_F32 = 0, S4D_DTYPE_BF16 = 1 };
 enum { S4D_LAYOUT_CAM_MAJOR = 0, S4D_LAYOUT_PT_MAJOR = 1, S4D_LAYOUT_GRID = 2 };
 
 /* Bits of the optional device error_flag (OR-ed by kernels, never cleared by them). */
-enum { S4D_FLAG_BAD_LEVEL = 1 /* a (camera, level) spatial_shape / scale_start_index entry
-                                 lies outside mc_ms_feat; its samples were skipped */ };
+enum {
+  S4D_FLAG_BAD_LEVEL = 1,   /* a (camera, level) spatial_shape / scale_start_index entry lies
+                               outside mc_ms_feat; its samples were skipped */
+  S4D_FLAG_WAIT_TIMEOUT = 2 /* a tensor-core kernel gave up (after 2 s) waiting on one of its own
+                               pipeline barriers; its outputs were not written.  Never expected. */
+};
+
+/* Residual modes of s4d_dfa_output_proj (the reference module's residual_mode). */
+enum { S4D_RESIDUAL_NONE = 0, S4D_RESIDUAL_ADD = 1, S4D_RESIDUAL_CAT = 2 };
 
 /* Human-readable name of a status code. */
 S4D_API const char* s4d_status_string(int status);
@@ -190,6 +199,54 @@ S4D_API int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, i
  * Host-only, launches nothing. */
 S4D_API size_t s4d_dfa_workspace_bytes(int64_t bs, int64_t num_cams, int64_t num_levels, int64_t num_pts,
                                        int64_t num_groups, int split_logits);
+
+/* ---- the DFA linears on the tensor cores (tcgen05, TF32 operands, fp32 accumulation) ------
+ *
+ * TF32 keeps 10 mantissa bits of every operand (the reference's TT path runs these linears in
+ * bf16, 7 bits); products are accumulated in fp32.  Matrices are fp32, row-major, with row
+ * strides ("ld") in floats; every matrix pointer and bias must be 16-byte aligned and every
+ * ld a multiple of 4.  Implemented: embed_dims == 256. */
+
+/* The two linears that read the instance feature, in one tensor-core pass over 128-row tiles:
+ *   logits    [rows, num_logits]    = (instance_feature + anchor_embed) . weights_fc^T
+ *   learnable [rows, num_learnable] = instance_feature . learnable_fc^T + learnable_bias
+ * The sum instance_feature + anchor_embed is formed tile by tile in shared memory and never
+ * written to HBM.  logits is the per-anchor term of the split logits of
+ * s4d_deformable_aggregation (the weights_fc bias belongs to the per-camera term).
+ * Replaces weights_fc(instance_feature + anchor_embed + camera_embed) of
+ * model/deformable_feature_aggregation.py:719-798 (test/dfa_pcc.py:306-320) for its
+ * per-anchor part, and the keypoint generator's learnable_fc
+ * (model/deformable_feature_aggregation.py:651-677, test/dfa_pcc.py:231-233).
+ *   instance_feature, anchor_embed  [rows, embed_dims] with row strides instance_ld, embed_ld
+ *   weights_fc_weight   [num_logits, embed_dims] contiguous (out, in)
+ *   learnable_fc_weight [num_learnable, embed_dims] contiguous, or NULL when num_learnable == 0
+ *   learnable_bias      [num_learnable] or NULL (zero)
+ *   logits              [rows, num_logits] contiguous
+ *   learnable           [rows, num_learnable] contiguous (4-byte aligned is enough), or NULL
+ *                       when num_learnable == 0
+ *   error_flag          optional [1] i32, OR-ed with S4D_FLAG_WAIT_TIMEOUT
+ * Implemented: num_logits == 416 (4 levels x 13 points x 8 groups), num_learnable <= 32. */
+S4D_API int s4d_dfa_weights_fc(const float* instance_feature, int64_t instance_ld, const float* anchor_embed,
+                               int64_t embed_ld, int64_t rows, const float* weights_fc_weight,
+                               const float* learnable_fc_weight, const float* learnable_bias, int64_t num_logits,
+                               int64_t num_learnable, int64_t embed_dims, float* logits, float* learnable,
+                               int32_t* error_flag, void* stream);
+
+/* output_proj with the residual fused into its epilogue:
+ *   out[:, :C] = features . weight^T + bias                        (residual_mode NONE)
+ *   out[:, :C] = features . weight^T + bias + instance_feature     (ADD)
+ *   out[:, :C] = features . weight^T + bias, out[:, C:2C] = instance_feature   (CAT)
+ * Replaces output_proj + the residual cat/add of model/deformable_feature_aggregation.py:934-950
+ * (test/dfa_pcc.py:299-304).
+ *   features          [rows, C] contiguous (the s4d_deformable_aggregation output)
+ *   weight            [C, C] (out, in) contiguous; bias [C] or NULL
+ *   instance_feature  [rows, C] with row stride instance_ld (ADD and CAT only; must not
+ *                     overlap out)
+ *   out               [rows, out_ld], out_ld >= 2C for CAT, >= C otherwise
+ *   error_flag        optional [1] i32, OR-ed with S4D_FLAG_WAIT_TIMEOUT */
+S4D_API int s4d_dfa_output_proj(const float* features, int64_t rows, const float* weight, const float* bias,
+                                const float* instance_feature, int64_t instance_ld, int residual_mode, float* out,
+                                int64_t out_ld, int64_t embed_dims, int32_t* error_flag, void* stream);
 
 #ifdef __cplusplus
 }

@@ -26,6 +26,11 @@ S4D_LAYOUT_PT_MAJOR = 1
 S4D_LAYOUT_GRID = 2
 
 S4D_FLAG_BAD_LEVEL = 1
+S4D_FLAG_WAIT_TIMEOUT = 2
+
+S4D_RESIDUAL_NONE = 0
+S4D_RESIDUAL_ADD = 1
+S4D_RESIDUAL_CAT = 2
 
 _i64, _int, _p, _sz = C.c_int64, C.c_int, C.c_void_p, C.c_size_t
 
@@ -44,6 +49,8 @@ SIGNATURES = {
                                           _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                           _p, _p, _p, _sz, _p]),
     "s4d_dfa_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _int]),
+    "s4d_dfa_weights_fc": (_int, [_p, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "s4d_dfa_output_proj": (_int, [_p, _i64, _p, _p, _p, _i64, _int, _p, _i64, _i64, _p, _p]),
 }
 
 _lib = None

@@ -1,5 +1,5 @@
 // extern "C" entry points of include/s4d_dfa.h: argument validation on the host, then the
-// launches of kps_project.cu and dfa_gather.cu.  Nothing here allocates, frees or
+// launches of kps_project.cu, dfa_gather.cu and linear_tc.cu.  Nothing here allocates, frees or
 // synchronises.
 #include <stdarg.h>
 #include <stdio.h>
@@ -44,7 +44,7 @@ const char* s4d_status_string(int status) {
 
 const char* s4d_last_error(void) { return g_last_error; }
 
-int s4d_abi_version(void) { return 101; }
+int s4d_abi_version(void) { return 102; }
 
 size_t s4d_kps_workspace_bytes(int64_t bs, int64_t num_anchor, int64_t num_cams, int64_t num_pts) {
   if (bs <= 0 || num_anchor <= 0 || num_cams <= 0 || num_pts <= 0) return 0;
@@ -217,6 +217,81 @@ int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, int64_t n
   if (gather_smem_bytes(p.num_cams, p.num_levels, p.num_pts, p.num_groups, p.cam_begin, p.cam_end) > 200 * 1024)
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: per-anchor staging exceeds shared memory");
   return launch_gather(p, feat_dtype, static_cast<cudaStream_t>(stream));
+}
+
+int s4d_dfa_weights_fc(const float* instance_feature, int64_t instance_ld, const float* anchor_embed,
+                       int64_t embed_ld, int64_t rows, const float* weights_fc_weight,
+                       const float* learnable_fc_weight, const float* learnable_bias, int64_t num_logits,
+                       int64_t num_learnable, int64_t embed_dims, float* logits, float* learnable,
+                       int32_t* error_flag, void* stream) {
+  set_error("%s", "");
+  if (rows < 0 || num_logits <= 0 || num_learnable < 0)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_weights_fc: bad sizes");
+  if (embed_dims != 256) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_weights_fc: embed_dims must be 256");
+  if (num_logits != 416 || num_learnable > 32)
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_weights_fc: implemented for num_logits 416, num_learnable <= 32");
+  if (rows >= kMaxElems) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_weights_fc: rows must be < 2^31");
+  if (rows == 0) return S4D_OK;
+  if (instance_feature == nullptr || anchor_embed == nullptr || weights_fc_weight == nullptr || logits == nullptr ||
+      (num_learnable > 0 && (learnable == nullptr || learnable_fc_weight == nullptr)))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_weights_fc: null pointer");
+  if (instance_ld < embed_dims || embed_ld < embed_dims || instance_ld % 4 != 0 || embed_ld % 4 != 0)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_weights_fc: row strides must be >= embed_dims and multiples of 4");
+  if (!aligned(instance_feature, 16) || !aligned(anchor_embed, 16) || !aligned(weights_fc_weight, 16) ||
+      !aligned(logits, 16) || (learnable_fc_weight != nullptr && !aligned(learnable_fc_weight, 16)) ||
+      (learnable_bias != nullptr && !aligned(learnable_bias, 4)) || (learnable != nullptr && !aligned(learnable, 4)))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_weights_fc: misaligned pointer");
+  WfcParams p{};
+  p.inst = instance_feature;
+  p.inst_ld = instance_ld;
+  p.embed = anchor_embed;
+  p.embed_ld = embed_ld;
+  p.w_fc = weights_fc_weight;
+  p.w_kps = num_learnable > 0 ? learnable_fc_weight : weights_fc_weight;
+  p.learn_bias = num_learnable > 0 ? learnable_bias : nullptr;
+  p.logits = logits;
+  p.learnable = learnable;
+  p.rows = rows;
+  p.n_logits = (int)num_logits;
+  p.n_learn = (int)num_learnable;
+  p.k = (int)embed_dims;
+  p.error_flag = error_flag;
+  return launch_weights_fc(p, static_cast<cudaStream_t>(stream));
+}
+
+int s4d_dfa_output_proj(const float* features, int64_t rows, const float* weight, const float* bias,
+                        const float* instance_feature, int64_t instance_ld, int residual_mode, float* out,
+                        int64_t out_ld, int64_t embed_dims, int32_t* error_flag, void* stream) {
+  set_error("%s", "");
+  if (rows < 0) return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj: negative rows");
+  if (residual_mode != S4D_RESIDUAL_NONE && residual_mode != S4D_RESIDUAL_ADD && residual_mode != S4D_RESIDUAL_CAT)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj: unknown residual_mode");
+  if (embed_dims != 256) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_output_proj: embed_dims must be 256");
+  if (rows >= kMaxElems) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_output_proj: rows must be < 2^31");
+  const bool res = residual_mode != S4D_RESIDUAL_NONE;
+  if (out_ld < (residual_mode == S4D_RESIDUAL_CAT ? 2 : 1) * embed_dims || out_ld % 4 != 0)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj: out_ld too small or not a multiple of 4");
+  if (res && (instance_ld < embed_dims || instance_ld % 4 != 0))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj: instance_ld must be >= embed_dims and a multiple of 4");
+  if (rows == 0) return S4D_OK;
+  if (features == nullptr || weight == nullptr || out == nullptr || (res && instance_feature == nullptr))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj: null pointer");
+  if (!aligned(features, 16) || !aligned(weight, 16) || !aligned(out, 16) || (bias != nullptr && !aligned(bias, 16)) ||
+      (res && !aligned(instance_feature, 16)))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj: misaligned pointer");
+  OprojParams p{};
+  p.feat = features;
+  p.w = weight;
+  p.bias = bias;
+  p.res = res ? instance_feature : nullptr;
+  p.res_ld = instance_ld;
+  p.res_mode = residual_mode;
+  p.out = out;
+  p.out_ld = out_ld;
+  p.rows = rows;
+  p.k = (int)embed_dims;
+  p.error_flag = error_flag;
+  return launch_output_proj(p, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -1,0 +1,574 @@
+// Dense linears of the DFA layer on the 5th-generation tensor cores (tcgen05, TF32 operands,
+// fp32 accumulation in tensor memory), with the layer's elementwise work fused around them.
+//
+//   weights_fc   logits = (inst + embed) . W_fc^T and learnable = inst . W_kps^T + b_kps in one
+//                pass over 128-row tiles (model/deformable_feature_aggregation.py:651-677,719-798;
+//                test/dfa_pcc.py:231-233,306-320).  The sum inst + embed is formed in shared
+//                memory, never in HBM.
+//   output_proj  feats . W_o^T + b_o written straight into the residual output, the instance
+//                feature copied beside it (cat) or added to it (add)
+//                (model/deformable_feature_aggregation.py:934-950; test/dfa_pcc.py:299-304).
+//
+// Both kernels: one CTA per 128-row tile, 6 warps.
+//   warp 0     TMA producer: A and B tiles of 32 fp32 (128-byte rows, 128-byte swizzle, zero
+//              fill past the last row) into a 2-stage shared-memory ring;
+//   warp 1     allocates the tensor-memory accumulator (128 lanes x N fp32 columns); one thread
+//              issues tcgen05.mma (M 128, K 8, N <= 256 per instruction) and commits each stage
+//              back to the producer;
+//   warps 2-5  during the main loop: weights_fc adds the embed tile into the instance tile's
+//              twin in shared memory (the MMA waits for it); output_proj copies the instance
+//              rows for the residual cat.  After it: tcgen05.ld of their 32 TMEM lanes (warp
+//              index mod 4), bias / residual in registers, the tile staged in shared memory
+//              with the 128-byte swizzle and written by TMA bulk-tensor stores.
+// Every barrier wait is bounded: after 2 s the CTA raises S4D_FLAG_WAIT_TIMEOUT, lets its copies
+// and MMAs finish, frees tensor memory and returns without writing its outputs.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "params.cuh"
+
+namespace s4d {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 32;  // fp32 per stage row: 128 bytes, one swizzle span
+constexpr int kThreads = 192;
+constexpr int kStages = 2;
+constexpr int kATile = kBM * kBK * 4;  // 16 KiB
+constexpr int kStageChunk = 32 * 32 * 4;  // one 32x32 fp32 output box (4 KiB)
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+// ---- PTX wrappers ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits until the phase with `parity` has completed.  Returns false without waiting further
+// once another role of the CTA has given up (abort_flag set), or after kWaitLimitNs, in which
+// case it sets abort_flag itself.  With abort_flag == nullptr only the time limit applies.
+__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_test(bar, parity)) return true;
+  const unsigned long long t0 = now_ns();
+  for (;;) {
+    if (mbar_test(bar, parity)) return true;
+    if (abort_flag != nullptr && *abort_flag) return false;
+    if (now_ns() - t0 > kWaitLimitNs) {
+      if (abort_flag != nullptr) *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+// 2-D tiled TMA load of one box of `map` at (x, y), completion counted on `bar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// 2-D tiled TMA store of one box from shared memory to `map` at (x, y); rows and columns
+// outside the map are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_le1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Generic-proxy shared-memory writes become visible to the async proxy (TMA, tensor cores).
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(cols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] . B[smem]^T, both K-major TF32, fp32 accumulate.
+__device__ __forceinline__ void mma_tf32(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on `bar` when every tcgen05.mma issued so far by this thread has completed.
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile of 128-byte rows stored with the 128-byte
+// swizzle (what a TMA box of 32 fp32 x rows with CU_TENSOR_MAP_SWIZZLE_128B writes, from a
+// 1024-byte aligned base): start address >> 4 in bits 0-13; leading-dimension offset 16 B
+// (not used by swizzled K-major layouts) in bits 16-29; 1024 B between 8-row groups in bits
+// 32-45; descriptor version 1 in bits 46-47; swizzle mode 2 (128 B) in bits 61-63.  Adding 2
+// to the descriptor advances the start by 32 bytes, i.e. by the 8 fp32 of one MMA's K step.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
+         (uint64_t(2) << 61);
+}
+
+// Instruction descriptor of kind::tf32: D f32 (bits 4-5 = 1), A and B TF32 (bits 7-9 and
+// 10-12 = 2), both K-major (bits 15, 16 = 0), N >> 3 in bits 17-22, M >> 4 in bits 24-28.
+__host__ __device__ constexpr uint32_t tf32_idesc(int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+}
+
+// 32 consecutive accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---- shared pieces of the two kernels ------------------------------------------------------
+
+struct Ctl {
+  uint64_t* bars;
+  uint32_t* tmem_slot;
+  volatile int* abort_flag;
+};
+
+// Barrier block after the stages: full[2], aux[2], empty[2], acc, then the TMEM slot and the
+// abort flag.
+template <int STAGE_BYTES>
+__device__ __forceinline__ Ctl carve(unsigned char* smem) {
+  Ctl c;
+  c.bars = reinterpret_cast<uint64_t*>(smem + kStages * STAGE_BYTES);
+  c.tmem_slot = reinterpret_cast<uint32_t*>(c.bars + 3 * kStages + 1);
+  c.abort_flag = reinterpret_cast<volatile int*>(c.tmem_slot + 1);
+  return c;
+}
+
+__device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
+  return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+}
+
+// Bytes of dynamic shared memory for a given stage size (1 KiB alignment slack + control).
+constexpr size_t smem_bytes(int stage_bytes) { return size_t(kStages) * stage_bytes + 1024 + 8 * (3 * kStages + 1) + 16; }
+
+// Writes 32 fp32 of this thread's row into a 32x32 staging box laid out as the 128-byte
+// swizzled TMA box: 16-byte chunk j of row r lands at chunk j ^ (r & 7), so the 8 rows a
+// quarter-warp writes hit 8 different bank groups.
+__device__ __forceinline__ void stage_row(unsigned char* box, int r, const float (&f)[32]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<float4*>(box + r * 128 + ((j ^ (r & 7)) << 4)) =
+        make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3]);
+}
+
+// The epilogue warp `q` streams accumulator columns [0, ncols) of its 32 rows to `map` (a
+// 32x32-box, 128-byte swizzle store map) through two 4 KiB staging boxes at `stage`,
+// adding bias[col] and, when res != null, res[row * res_ld + col].
+__device__ __forceinline__ void store_columns(uint32_t tmem, int q, int lane, int64_t tile_row0, int ncols,
+                                              const CUtensorMap* map, unsigned char* stage, const float* bias,
+                                              const float* res, int64_t res_ld, int64_t rows) {
+  const int64_t row = tile_row0 + q * 32 + lane;
+  for (int c = 0; c < ncols / 32; ++c) {
+    uint32_t v[32];
+    tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c * 32), v);
+    float f[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
+    if (bias != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 b = __ldg(reinterpret_cast<const float4*>(bias + c * 32) + i);
+        f[4 * i] += b.x, f[4 * i + 1] += b.y, f[4 * i + 2] += b.z, f[4 * i + 3] += b.w;
+      }
+    }
+    if (res != nullptr && row < rows) {
+      const float4* r4 = reinterpret_cast<const float4*>(res + row * res_ld + c * 32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 r = ldg_nc_f4(r4 + i);
+        f[4 * i] += r.x, f[4 * i + 1] += r.y, f[4 * i + 2] += r.z, f[4 * i + 3] += r.w;
+      }
+    }
+    unsigned char* box = stage + (c & 1) * kStageChunk;
+    if (lane == 0 && c >= 2) bulk_wait_read_le1();  // the store that last used this box has read it
+    __syncwarp();
+    stage_row(box, lane, f);
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map, smem_u32(box), c * 32, int(tile_row0 + q * 32));
+      bulk_commit();
+    }
+  }
+  if (lane == 0) bulk_wait_all();
+  __syncwarp();
+}
+
+// Common prologue: barrier init, TMEM allocation, hand-off of the TMEM address.
+__device__ __forceinline__ uint32_t prologue(const Ctl& c, uint32_t cols, int aux_count) {
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    const uint32_t b0 = smem_u32(c.bars);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(b0 + 8 * s, 1);                                    // full: TMA bytes landed
+      mbar_init(b0 + 8 * (kStages + s), aux_count > 0 ? aux_count : 1);  // aux: shared-memory sum ready
+      mbar_init(b0 + 8 * (2 * kStages + s), 1);                    // empty: MMAs of the stage done
+    }
+    mbar_init(b0 + 8 * (3 * kStages), 1);  // acc: accumulator complete
+    *c.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(smem_u32(c.tmem_slot), cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  return *c.tmem_slot;
+}
+
+__device__ __forceinline__ void epilogue_teardown(const Ctl& c, uint32_t tmem, uint32_t cols, int32_t* error_flag) {
+  tc_fence_before();
+  __syncthreads();
+  if ((threadIdx.x >> 5) == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, cols);
+  }
+  if (threadIdx.x == 0 && *c.abort_flag && error_flag != nullptr) atomicOr(error_flag, S4D_FLAG_WAIT_TIMEOUT);
+}
+
+// Producer drain: no copy may still be landing in shared memory when the CTA exits.
+__device__ __forceinline__ void drain_loads(uint32_t full0, int issued) {
+  for (int kb = issued > kStages ? issued - kStages : 0; kb < issued; ++kb)
+    mbar_wait(full0 + 8 * (kb % kStages), (kb / kStages) & 1, nullptr);
+}
+
+// Warp-uniform wait for the accumulator (tcgen05.ld is warp-collective).
+__device__ __forceinline__ bool wait_accumulator(const Ctl& c, uint32_t acc_bar) {
+  const bool done = __all_sync(0xffffffffu, mbar_wait(acc_bar, 0, c.abort_flag));
+  const int aborted = __shfl_sync(0xffffffffu, *c.abort_flag, 0);
+  tc_fence_after();
+  return done && !aborted;
+}
+
+// ---- weights_fc -----------------------------------------------------------------------------
+
+template <int NW>
+struct Wfc {
+  static constexpr int kSplit = NW > 256 ? 2 : 1;  // MMAs per K step for the logits
+  static constexpr int kNmma = NW / kSplit;
+  static constexpr int kNL = 32;                     // learnable columns (one N-32 MMA)
+  static constexpr int kBW = NW * kBK * 4;
+  static constexpr int kBL = kNL * kBK * 4;
+  static constexpr int kStage = 2 * kATile + kBW + kBL;  // inst, embed (+= inst), W_fc, W_kps
+  static constexpr uint32_t kCols = 512;
+  static constexpr size_t kSmem = smem_bytes(kStage);
+  static_assert(NW % 32 == 0 && kNmma % 16 == 0 && kNmma <= 256 && NW + kNL <= 512, "logit columns");
+  static_assert(kBW % 1024 == 0 && kStage % 1024 == 0 && (kNmma * kBK * 4) % 1024 == 0, "swizzle alignment");
+  static_assert(4 * 2 * kStageChunk <= kStages * kStage, "epilogue staging fits in the stages");
+};
+
+template <int NW>
+__global__ void __launch_bounds__(kThreads, 1)
+    weights_fc_kernel(const __grid_constant__ CUtensorMap map_inst, const __grid_constant__ CUtensorMap map_embed,
+                      const __grid_constant__ CUtensorMap map_wfc, const __grid_constant__ CUtensorMap map_wkps,
+                      const __grid_constant__ CUtensorMap map_logits, const WfcParams p) {
+  using S = Wfc<NW>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = aligned_smem(smem_raw);
+  const Ctl c = carve<S::kStage>(smem);
+  const uint32_t full0 = smem_u32(c.bars), sum0 = full0 + 8 * kStages, empty0 = full0 + 16 * kStages,
+                 acc_bar = full0 + 24 * kStages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kbs = p.k / kBK;
+  const int64_t row0 = int64_t(blockIdx.x) * kBM;
+  const uint32_t tmem = prologue(c, S::kCols, 128);
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      int issued = 0;
+      for (int kb = 0; kb < kbs; ++kb) {
+        const int s = kb % kStages;
+        if (kb >= kStages && !mbar_wait(empty0 + 8 * s, ((kb / kStages) - 1) & 1, c.abort_flag)) break;
+        const uint32_t st = smem_u32(smem + s * S::kStage), fb = full0 + 8 * s;
+        mbar_expect_tx(fb, S::kStage);
+        tma_load_2d(st, &map_inst, fb, kb * kBK, int(row0));
+        tma_load_2d(st + kATile, &map_embed, fb, kb * kBK, int(row0));
+#pragma unroll
+        for (int j = 0; j < S::kSplit; ++j)
+          tma_load_2d(st + 2 * kATile + j * S::kNmma * kBK * 4, &map_wfc, fb, kb * kBK, j * S::kNmma);
+        tma_load_2d(st + 2 * kATile + S::kBW, &map_wkps, fb, kb * kBK, 0);
+        issued = kb + 1;
+      }
+      drain_loads(full0, issued);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      for (int kb = 0; kb < kbs; ++kb) {
+        const int s = kb % kStages;
+        if (!mbar_wait(full0 + 8 * s, (kb / kStages) & 1, c.abort_flag)) break;
+        if (!mbar_wait(sum0 + 8 * s, (kb / kStages) & 1, c.abort_flag)) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + s * S::kStage);
+        const uint64_t a_inst = sw128_desc(st), a_sum = sw128_desc(st + kATile);
+        const uint64_t b_kps = sw128_desc(st + 2 * kATile + S::kBW);
+#pragma unroll
+        for (int k = 0; k < kBK / 8; ++k) {
+          const uint32_t acc = (kb | k) != 0;
+#pragma unroll
+          for (int j = 0; j < S::kSplit; ++j)
+            mma_tf32(tmem + j * S::kNmma, a_sum + 2 * k, sw128_desc(st + 2 * kATile + j * S::kNmma * kBK * 4) + 2 * k,
+                     tf32_idesc(S::kNmma), acc);
+          mma_tf32(tmem + NW, a_inst + 2 * k, b_kps + 2 * k, tf32_idesc(S::kNL), acc);
+        }
+        mma_commit(empty0 + 8 * s);
+      }
+      mma_commit(acc_bar);  // also on the abort path: nothing may run once tensor memory is freed
+      mbar_wait(acc_bar, 0, nullptr);
+    }
+  } else {
+    // Main loop: embed tile += inst tile (same box, same swizzle: the same byte offsets hold the
+    // same (row, k) element), 8 float4 per thread per stage.
+    const int t = threadIdx.x - 64;
+    for (int kb = 0; kb < kbs; ++kb) {
+      const int s = kb % kStages;
+      if (!mbar_wait(full0 + 8 * s, (kb / kStages) & 1, c.abort_flag)) break;
+      const float4* src = reinterpret_cast<const float4*>(smem + s * S::kStage);
+      float4* dst = reinterpret_cast<float4*>(smem + s * S::kStage + kATile);
+#pragma unroll
+      for (int i = 0; i < kATile / 16 / 128; ++i) {
+        const float4 a = src[t + 128 * i];
+        float4 b = dst[t + 128 * i];
+        b.x += a.x, b.y += a.y, b.z += a.z, b.w += a.w;
+        dst[t + 128 * i] = b;
+      }
+      fence_proxy_async();
+      mbar_arrive(sum0 + 8 * s);
+    }
+    // Epilogue: logits through TMA stores, learnable columns (not 16-byte rows) by plain stores.
+    const int q = warp & 3;
+    if (wait_accumulator(c, acc_bar)) {
+      store_columns(tmem, q, lane, row0, NW, &map_logits, smem + q * 2 * kStageChunk, nullptr, nullptr, 0, p.rows);
+      uint32_t v[32];
+      tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(NW), v);
+      const int64_t row = row0 + q * 32 + lane;
+      if (row < p.rows && p.n_learn > 0) {
+        float* dst = p.learnable + row * p.n_learn;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < p.n_learn) dst[i] = __uint_as_float(v[i]) + (p.learn_bias != nullptr ? __ldg(p.learn_bias + i) : 0.f);
+      }
+    }
+  }
+  epilogue_teardown(c, tmem, S::kCols, p.error_flag);
+}
+
+// ---- output_proj ----------------------------------------------------------------------------
+
+struct Oproj {
+  static constexpr int kN = 256;
+  static constexpr int kStage = kATile + kN * kBK * 4;  // feats tile, W_o tile
+  static constexpr uint32_t kCols = 256;
+  static constexpr size_t kSmem = smem_bytes(kStage);
+  static_assert(kStage % 1024 == 0, "swizzle alignment");
+  static_assert(4 * 2 * kStageChunk <= kStages * kStage, "epilogue staging fits in the stages");
+};
+
+__global__ void __launch_bounds__(kThreads, 2)
+    output_proj_kernel(const __grid_constant__ CUtensorMap map_feat, const __grid_constant__ CUtensorMap map_w,
+                       const __grid_constant__ CUtensorMap map_out, const OprojParams p) {
+  using S = Oproj;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = aligned_smem(smem_raw);
+  const Ctl c = carve<S::kStage>(smem);
+  const uint32_t full0 = smem_u32(c.bars), empty0 = full0 + 16 * kStages, acc_bar = full0 + 24 * kStages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kbs = S::kN / kBK;
+  const int64_t row0 = int64_t(blockIdx.x) * kBM;
+  const uint32_t tmem = prologue(c, S::kCols, 0);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < kbs; ++kb) {
+        const int s = kb % kStages;
+        if (kb >= kStages && !mbar_wait(empty0 + 8 * s, ((kb / kStages) - 1) & 1, c.abort_flag)) break;
+        const uint32_t st = smem_u32(smem + s * S::kStage), fb = full0 + 8 * s;
+        mbar_expect_tx(fb, S::kStage);
+        tma_load_2d(st, &map_feat, fb, kb * kBK, int(row0));
+        tma_load_2d(st + kATile, &map_w, fb, kb * kBK, 0);
+        issued = kb + 1;
+      }
+      drain_loads(full0, issued);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      for (int kb = 0; kb < kbs; ++kb) {
+        const int s = kb % kStages;
+        if (!mbar_wait(full0 + 8 * s, (kb / kStages) & 1, c.abort_flag)) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + s * S::kStage);
+        const uint64_t a = sw128_desc(st), b = sw128_desc(st + kATile);
+#pragma unroll
+        for (int k = 0; k < kBK / 8; ++k) mma_tf32(tmem, a + 2 * k, b + 2 * k, tf32_idesc(S::kN), (kb | k) != 0);
+        mma_commit(empty0 + 8 * s);
+      }
+      mma_commit(acc_bar);
+      mbar_wait(acc_bar, 0, nullptr);
+    }
+  } else {
+    const int q = warp & 3;
+    if (p.res_mode == S4D_RESIDUAL_CAT) {
+      // The residual half of the output is a plain copy: done while the tensor cores run, 8
+      // rows (16 float4 per lane) in flight per step.
+      const int64_t r_begin = row0 + q * 32;
+      const int64_t r_end = min(r_begin + 32, p.rows);
+      for (int64_t r = r_begin; r < r_end; r += 8) {
+        float4 buf[8][2];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (r + i < r_end) {
+            const float4* src = reinterpret_cast<const float4*>(p.res + (r + i) * p.res_ld);
+            buf[i][0] = ldg_nc_f4(src + lane);
+            buf[i][1] = ldg_nc_f4(src + 32 + lane);
+          }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (r + i < r_end) {
+            float4* dst = reinterpret_cast<float4*>(p.out + (r + i) * p.out_ld + S::kN);
+            dst[lane] = buf[i][0];
+            dst[32 + lane] = buf[i][1];
+          }
+      }
+    }
+    if (wait_accumulator(c, acc_bar))
+      store_columns(tmem, q, lane, row0, S::kN, &map_out, smem + q * 2 * kStageChunk, p.bias,
+                    p.res_mode == S4D_RESIDUAL_ADD ? p.res : nullptr, p.res_ld, p.rows);
+  }
+  epilogue_teardown(c, tmem, S::kCols, p.error_flag);
+}
+
+// ---- host side ----------------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+// Tensor map of an fp32 row-major matrix [rows, cols] with row stride ld (floats): boxes of
+// 32 columns x box_rows rows, 128-byte swizzle, zero fill outside the matrix.
+int make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (fn == nullptr) return fail(S4D_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the CUDA driver");
+  const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(ld) * 4};
+  const cuuint32_t box[2] = {uint32_t(kBK), uint32_t(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (CUresult %d) for a [%lld, %lld] matrix, ld %lld", int(r),
+              (long long)rows, (long long)cols, (long long)ld);
+    return S4D_ERR_CUDA;
+  }
+  return S4D_OK;
+}
+
+template <typename K>
+int set_smem(K kernel, size_t bytes, const char* what) {
+  return cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)), what);
+}
+
+}  // namespace
+
+int launch_weights_fc(const WfcParams& p, cudaStream_t stream) {
+  if (p.rows <= 0) return S4D_OK;
+  if (p.n_logits != 416 || p.k != 256 || p.n_learn > 32)
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "weights_fc: implemented for 416 logit columns, embed_dims 256, "
+                                           "<= 32 learnable columns");
+  using S = Wfc<416>;
+  CUtensorMap mi, me, mw, mk, mo;
+  int st = make_map(&mi, p.inst, p.rows, p.k, p.inst_ld, kBM);
+  if (st == S4D_OK) st = make_map(&me, p.embed, p.rows, p.k, p.embed_ld, kBM);
+  if (st == S4D_OK) st = make_map(&mw, p.w_fc, p.n_logits, p.k, p.k, S::kNmma);
+  if (st == S4D_OK) st = make_map(&mk, p.w_kps, p.n_learn > 0 ? p.n_learn : 1, p.k, p.k, S::kNL);
+  if (st == S4D_OK) st = make_map(&mo, p.logits, p.rows, p.n_logits, p.n_logits, 32);
+  if (st == S4D_OK) st = set_smem(weights_fc_kernel<416>, S::kSmem, "cudaFuncSetAttribute(weights_fc_kernel)");
+  if (st != S4D_OK) return st;
+  weights_fc_kernel<416><<<unsigned((p.rows + kBM - 1) / kBM), kThreads, S::kSmem, stream>>>(mi, me, mw, mk, mo, p);
+  return cuda_check(cudaGetLastError(), "weights_fc_kernel launch");
+}
+
+int launch_output_proj(const OprojParams& p, cudaStream_t stream) {
+  if (p.rows <= 0) return S4D_OK;
+  if (p.k != 256) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "output_proj: implemented for embed_dims 256");
+  using S = Oproj;
+  CUtensorMap mf, mw, mo;
+  int st = make_map(&mf, p.feat, p.rows, p.k, p.k, kBM);
+  if (st == S4D_OK) st = make_map(&mw, p.w, S::kN, p.k, p.k, S::kN);
+  if (st == S4D_OK) st = make_map(&mo, p.out, p.rows, S::kN, p.out_ld, 32);
+  if (st == S4D_OK) st = set_smem(output_proj_kernel, S::kSmem, "cudaFuncSetAttribute(output_proj_kernel)");
+  if (st != S4D_OK) return st;
+  output_proj_kernel<<<unsigned((p.rows + kBM - 1) / kBM), kThreads, S::kSmem, stream>>>(mf, mw, mo, p);
+  return cuda_check(cudaGetLastError(), "output_proj_kernel launch");
+}
+
+}  // namespace s4d

@@ -46,6 +46,39 @@ struct GatherParams {
   int layout;
 };
 
+// Tensor-core linears (linear_tc.cu).  Row strides are in floats.
+struct WfcParams {
+  const float* inst;  // [rows, k], row stride inst_ld
+  int64_t inst_ld;
+  const float* embed;  // [rows, k], row stride embed_ld
+  int64_t embed_ld;
+  const float* w_fc;        // [n_logits, k]
+  const float* w_kps;       // [n_learn, k] or null
+  const float* learn_bias;  // [n_learn] or null
+  float* logits;            // [rows, n_logits]
+  float* learnable;         // [rows, n_learn]
+  int64_t rows;
+  int n_logits, n_learn, k;
+  int32_t* error_flag;
+};
+
+struct OprojParams {
+  const float* feat;  // [rows, k]
+  const float* w;     // [k, k]
+  const float* bias;  // [k] or null
+  const float* res;   // residual rows, row stride res_ld (add / cat)
+  int64_t res_ld;
+  int res_mode;
+  float* out;  // [rows, out_ld]
+  int64_t out_ld;
+  int64_t rows;
+  int k;
+  int32_t* error_flag;
+};
+
+int launch_weights_fc(const WfcParams& p, cudaStream_t stream);
+int launch_output_proj(const OprojParams& p, cudaStream_t stream);
+
 int launch_kps_project(KpsParams k, int32_t* visible_idx, int32_t* visible_count, void* workspace,
                        cudaStream_t stream);
 size_t kps_workspace_bytes(int64_t total);

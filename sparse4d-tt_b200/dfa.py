@@ -88,8 +88,10 @@ class DeformableFeatureAggregation:
 
     ``model_config`` may carry ``"FEATURE_DTYPE"`` (``torch.bfloat16`` default, or
     ``torch.float32``): the dtype feature maps are packed to when ``run`` receives a list; and
-    ``"MATMUL_PRECISION"``: ``"fp32"`` (default) or ``"tf32"`` for the layer's linears
-    (TF32 tensor cores, fp32 accumulation; the reference's TT path runs them in bf16).
+    ``"MATMUL_PRECISION"``: ``"fp32"`` (default, cuBLAS fp32 GEMMs) or ``"tf32"`` for the
+    layer's linears: TF32 operands, fp32 accumulation (the reference's TT path runs them in
+    bf16).  With ``"tf32"`` and split logits they run on this library's tcgen05 kernels
+    (``ops.weights_fc_into`` / ``ops.output_proj_into``), the embed add and the residual fused.
     ``split_logits=True`` (default) evaluates ``weights_fc(f + cam) = weights_fc(f) + W cam``
     as two smaller GEMMs (Ncam times fewer FLOPs) and combines the two terms inside the gather
     kernel instead of materialising the ``[bs, A, Ncam, L*P*G]`` logits (same result up to
@@ -143,9 +145,16 @@ class DeformableFeatureAggregation:
         self.weights_fc_bias = t("weights_fc_bias")
         self.output_proj_weight = t("output_proj_weight")
         self.output_proj_bias = t("output_proj_bias")
+        # TF32 linears run on this library's tensor-core kernels: weights_fc + learnable_fc
+        # in one pass (embed add folded in) and output_proj with the residual fused.
+        lpg = num_levels * num_pts * num_groups
+        self._tc = (self.matmul_precision == "high" and self.split_logits
+                    and ops.weights_fc_supported(lpg, 3 * num_learnable_pts, embed_dims)
+                    and residual_mode in ops.RESIDUAL_MODES)
         # Per-frame caches, cleared by the head at the start of a frame
         # (model/sparse4d_head.py:290-296 resets the same attribute names).
         self._cached_camera_embed = None
+        self._cached_camera_logits = None
         self._cached_proj_rm = None
         self._cached_wh_rm = None
         self._cam_key = None
@@ -164,11 +173,31 @@ class DeformableFeatureAggregation:
         return F.layer_norm(x, (C,), self.cam_ln2_weight, self.cam_ln2_bias, 1e-5)
 
     def _camera_embed(self, projection_mat: Tensor, bs: int) -> Tensor:
+        """Camera embedding, cached per frame like the reference's ``_cached_camera_embed``
+        (``model/deformable_feature_aggregation.py:741-747``, cleared per frame by the head,
+        ``model/sparse4d_head.py:290-296``), and re-computed when the projection tensor changes."""
         key = (projection_mat.data_ptr(), projection_mat._version, tuple(projection_mat.shape))
         if self._cached_camera_embed is None or self._cam_key != key:
             self._cached_camera_embed = self._camera_encoder(projection_mat, bs)
+            self._cached_camera_logits = None
             self._cam_key = key
         return self._cached_camera_embed
+
+    def _camera_logits(self, projection_mat: Tensor, bs: int) -> Tensor:
+        """Per-camera term of the split logits, ``weights_fc(camera_embed)`` with the bias:
+        ``[bs, Ncam, L, P, G]``, cached with the camera embedding."""
+        cam = self._camera_embed(projection_mat, bs)
+        if self._cached_camera_logits is None:
+            lpg = (self.num_levels, self.num_pts, self.num_groups)
+            wc = F.linear(cam, self.weights_fc_weight, self.weights_fc_bias)
+            self._cached_camera_logits = wc.reshape(bs, self.num_cams, *lpg).contiguous()
+        return self._cached_camera_logits
+
+    def reset_frame_cache(self) -> None:
+        """Drops the per-frame camera caches (what the head does at the start of every frame)."""
+        self._cached_camera_embed = None
+        self._cached_camera_logits = None
+        self._cam_key = None
 
     def _get_weights(self, instance_feature: Tensor, anchor_embed: Tensor, projection_mat: Tensor, bs: int,
                      num_anchor: int):
@@ -180,11 +209,10 @@ class DeformableFeatureAggregation:
         if not self.use_camera_embed:
             w = F.linear(feature, self.weights_fc_weight, self.weights_fc_bias)
             return w.reshape(bs, num_anchor, self.num_cams, *lpg), None
-        cam = self._camera_embed(projection_mat, bs)
         if self.split_logits:
             wa = F.linear(feature, self.weights_fc_weight).reshape(bs, num_anchor, *lpg)
-            wc = F.linear(cam, self.weights_fc_weight, self.weights_fc_bias).reshape(bs, self.num_cams, *lpg)
-            return wa, wc
+            return wa, self._camera_logits(projection_mat, bs)
+        cam = self._camera_embed(projection_mat, bs)
         w = F.linear(feature[:, :, None] + cam[:, None], self.weights_fc_weight, self.weights_fc_bias)
         return w.reshape(bs, num_anchor, self.num_cams, *lpg), None
 
@@ -213,9 +241,20 @@ class DeformableFeatureAggregation:
         image_wh = image_wh.reshape(bs, self.num_cams, 2).float().contiguous()
         mc_ms_feat, spatial_shape, scale_start = self._features(feature_maps, spatial_shapes, bs)
 
-        with _matmul_precision(self.matmul_precision):
-            logits, logits_cam = self._get_weights(instance_feature, anchor_embed, projection_mat, bs, num_anchor)
-            learn = F.linear(instance_feature, self.learnable_fc_weight, self.learnable_fc_bias).contiguous()
+        C = self.embed_dims
+        rows = bs * num_anchor
+        if self._tc:
+            inst2d, embed2d = ops.row_view(instance_feature, C), ops.row_view(anchor_embed, C)
+            logits = torch.empty(bs, num_anchor, self.num_levels, self.num_pts, self.num_groups, device=dev)
+            learn = torch.empty(bs, num_anchor, 3 * self.num_learnable_pts, device=dev)
+            ops.weights_fc_into(logits.view(rows, -1), learn.view(rows, -1), inst2d, embed2d, self.weights_fc_weight,
+                                self.learnable_fc_weight, self.learnable_fc_bias)
+            with _matmul_precision(self.matmul_precision):
+                logits_cam = self._camera_logits(projection_mat, bs)
+        else:
+            with _matmul_precision(self.matmul_precision):
+                logits, logits_cam = self._get_weights(instance_feature, anchor_embed, projection_mat, bs, num_anchor)
+                learn = F.linear(instance_feature, self.learnable_fc_weight, self.learnable_fc_bias).contiguous()
         loc = torch.empty(bs, num_anchor, self.num_cams, self.num_pts, 2, dtype=torch.float32, device=dev)
         ops.kps_project_into(anchor, learn, self.fix_scale, projection_mat, image_wh, sample_location=loc)
 
@@ -244,6 +283,12 @@ class DeformableFeatureAggregation:
 
             dist.all_reduce(feats, group=self.process_group)
 
+        if self._tc:
+            width = 2 * C if self.residual_mode == "cat" else C
+            out = torch.empty(bs, num_anchor, width, device=dev)
+            ops.output_proj_into(out.view(rows, width), feats.view(rows, C), self.output_proj_weight,
+                                 self.output_proj_bias, inst2d, self.residual_mode)
+            return out
         with _matmul_precision(self.matmul_precision):
             out = F.linear(feats, self.output_proj_weight, self.output_proj_bias)
         inst = instance_feature.to(out.dtype)

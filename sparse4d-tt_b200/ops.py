@@ -11,6 +11,10 @@
 * ``kps_project_fused(key_points, anchor, projection_mat, image_wh, num_cams, num_pts)`` --
   same arguments and output layout as ``ttnn.kps_project_fused``
   (``tt-metal/ops/kps_project_fused/kps_project_fused_nanobind.cpp:69-91``).
+* ``weights_fc_into`` / ``output_proj_into`` -- the layer's linears on the tensor cores
+  (tcgen05, TF32 operands, fp32 accumulation): ``weights_fc`` (per-anchor logits) + the
+  keypoint ``learnable_fc`` in one pass with the embed add folded in, and ``output_proj`` with
+  the residual cat/add fused (``model/deformable_feature_aggregation.py:651-677,719-798,934-950``).
 * ``pack_feature_maps(feature_maps)`` -- per-level maps to the packed channels-last
   ``mc_ms_feat`` layout.
 
@@ -68,6 +72,90 @@ def _check_contig(name: str, **ts: Optional[Tensor]) -> None:
 def _check_dtype(name: str, t: Optional[Tensor], dtypes: Sequence[torch.dtype], what: str) -> None:
     if t is not None and t.dtype not in dtypes:
         raise TypeError(f"{name}: {what} must be one of {list(dtypes)}, got {t.dtype}")
+
+
+# ---------------------------------------------------------------------------------------------
+# dense linears on the tensor cores
+# ---------------------------------------------------------------------------------------------
+
+RESIDUAL_MODES = {"none": L.S4D_RESIDUAL_NONE, "add": L.S4D_RESIDUAL_ADD, "cat": L.S4D_RESIDUAL_CAT}
+
+
+def row_view(t: Tensor, cols: int) -> Tensor:
+    """``t [..., cols]`` as a 2-D ``[rows, cols]`` fp32 view the tensor-core kernels can read
+    in place (unit column stride, row stride a multiple of 4 floats, 16-byte aligned base);
+    a contiguous copy when the strides do not allow that."""
+    _require(t.shape[-1] == cols, f"expected a last dimension of {cols}, got {tuple(t.shape)}")
+    v = t.reshape(-1, cols)
+    if v.stride(1) != 1 or v.stride(0) % 4 != 0 or v.stride(0) < cols or v.data_ptr() % 16 != 0:
+        v = v.contiguous()
+    return v
+
+
+def weights_fc_supported(num_logits: int, num_learnable: int, embed_dims: int) -> bool:
+    """Shapes ``weights_fc_into`` implements (the Sparse4D v3 layer: 4 x 13 x 8 logits)."""
+    return num_logits == 416 and 0 <= num_learnable <= 32 and embed_dims == 256
+
+
+def weights_fc_into(logits: Tensor, learnable: Optional[Tensor], instance_feature: Tensor, anchor_embed: Tensor,
+                    weights_fc_weight: Tensor, learnable_fc_weight: Optional[Tensor],
+                    learnable_bias: Optional[Tensor] = None, error_flag: Optional[Tensor] = None) -> None:
+    """``logits [rows, n] = (instance_feature + anchor_embed) W_fc^T`` and ``learnable [rows, m]
+    = instance_feature W_kps^T + learnable_bias`` in one tensor-core pass.  ``instance_feature``
+    and ``anchor_embed`` are ``[rows, C]`` row views (``row_view``)."""
+    name = "weights_fc"
+    dev = _require_cuda(name, logits, learnable, instance_feature, anchor_embed, weights_fc_weight,
+                        learnable_fc_weight, learnable_bias, error_flag)
+    _check_contig(name, logits=logits, learnable=learnable, weights_fc_weight=weights_fc_weight,
+                  learnable_fc_weight=learnable_fc_weight, learnable_bias=learnable_bias)
+    for k, t in (("logits", logits), ("learnable", learnable), ("instance_feature", instance_feature),
+                 ("anchor_embed", anchor_embed), ("weights_fc_weight", weights_fc_weight),
+                 ("learnable_fc_weight", learnable_fc_weight), ("learnable_bias", learnable_bias)):
+        _check_dtype(name, t, (torch.float32,), k)
+    _check_dtype(name, error_flag, (torch.int32,), "error_flag")
+    rows, c = instance_feature.shape
+    _require(tuple(anchor_embed.shape) == (rows, c), "anchor_embed must match instance_feature")
+    _require(instance_feature.stride(1) == 1 and anchor_embed.stride(1) == 1, "inputs need a unit column stride")
+    n = int(weights_fc_weight.shape[0])
+    _require(tuple(weights_fc_weight.shape) == (n, c), f"weights_fc_weight must be [n, {c}]")
+    _require(tuple(logits.shape) == (rows, n), f"logits must be [{rows}, {n}]")
+    m = 0 if learnable is None else int(learnable.shape[1])
+    _require(learnable is None or tuple(learnable.shape) == (rows, m), f"learnable must be [{rows}, m]")
+    _require(m == 0 or (learnable_fc_weight is not None and tuple(learnable_fc_weight.shape) == (m, c)),
+             f"learnable_fc_weight must be [{m}, {c}]")
+    _require(learnable_bias is None or tuple(learnable_bias.shape) == (m,), f"learnable_bias must be [{m}]")
+    st = L.lib().s4d_dfa_weights_fc(instance_feature.data_ptr(), instance_feature.stride(0), anchor_embed.data_ptr(),
+                                    anchor_embed.stride(0), rows, weights_fc_weight.data_ptr(),
+                                    _ptr(learnable_fc_weight), _ptr(learnable_bias), n, m, c, logits.data_ptr(),
+                                    _ptr(learnable), _ptr(error_flag), _stream_ptr(dev))
+    L.check(name, st)
+
+
+def output_proj_into(out: Tensor, features: Tensor, weight: Tensor, bias: Optional[Tensor],
+                     instance_feature: Optional[Tensor] = None, residual_mode: str = "cat",
+                     error_flag: Optional[Tensor] = None) -> Tensor:
+    """``out[:, :C] = features W^T + bias`` with the residual fused: ``"cat"`` also writes
+    ``out[:, C:2C] = instance_feature``, ``"add"`` adds it, ``"none"`` ignores it.  ``out`` is
+    ``[rows, >= 2C or C]`` (row stride a multiple of 4), ``instance_feature`` a row view."""
+    name = "output_proj"
+    mode = RESIDUAL_MODES[residual_mode]
+    dev = _require_cuda(name, out, features, weight, bias, instance_feature, error_flag)
+    _check_contig(name, features=features, weight=weight, bias=bias)
+    for k, t in (("out", out), ("features", features), ("weight", weight), ("bias", bias),
+                 ("instance_feature", instance_feature)):
+        _check_dtype(name, t, (torch.float32,), k)
+    _check_dtype(name, error_flag, (torch.int32,), "error_flag")
+    rows, c = features.shape
+    _require(tuple(weight.shape) == (c, c), f"weight must be [{c}, {c}]")
+    _require(out.dim() == 2 and out.shape[0] == rows and out.stride(1) == 1, f"out must be a [{rows}, n] row view")
+    if mode != L.S4D_RESIDUAL_NONE:
+        _require(instance_feature is not None and tuple(instance_feature.shape) == (rows, c)
+                 and instance_feature.stride(1) == 1, f"instance_feature must be a [{rows}, {c}] row view")
+    st = L.lib().s4d_dfa_output_proj(features.data_ptr(), rows, weight.data_ptr(), _ptr(bias), _ptr(instance_feature),
+                                     0 if instance_feature is None else instance_feature.stride(0), mode,
+                                     out.data_ptr(), out.stride(0), c, _ptr(error_flag), _stream_ptr(dev))
+    L.check(name, st)
+    return out
 
 
 # ---------------------------------------------------------------------------------------------

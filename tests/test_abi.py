@@ -33,7 +33,7 @@ def lib():
 
 def test_every_declared_symbol_is_exported(lib):
     names = declared_functions()
-    assert len(names) == 9, names
+    assert len(names) == 11, names
     for n in names:
         assert hasattr(lib, n), n
         assert n in L.SIGNATURES, f"{n} has no ctypes signature"
@@ -52,7 +52,7 @@ def test_status_strings_and_version(lib):
     assert L.status_string(0) == "S4D_OK"
     assert L.status_string(2) == "S4D_ERR_UNSUPPORTED_SHAPE"
     assert L.status_string(99) == "S4D_ERR_UNKNOWN"
-    assert lib.s4d_abi_version() == 101
+    assert lib.s4d_abi_version() == 102
 
 
 def test_dfa_workspace_bytes(lib):
@@ -177,3 +177,62 @@ def test_ops_reject_cpu_tensors():
     with pytest.raises(ValueError, match="CUDA"):
         ops.kps_project_into(torch.zeros(1, 2, 11), torch.zeros(1, 2, 18), torch.zeros(7, 3),
                              torch.zeros(1, 6, 4, 4), torch.zeros(1, 6, 2))
+
+
+def _wfc(lib, **kw):
+    a = dict(inst=16, ild=256, emb=16, eld=256, rows=900, wfc=16, wkps=16, n=416, m=18, C=256, bias=16, logits=16,
+             learn=16)
+    a.update(kw)
+    st = lib.s4d_dfa_weights_fc(a["inst"], a["ild"], a["emb"], a["eld"], a["rows"], a["wfc"], a["wkps"], a["bias"],
+                                a["n"], a["m"], a["C"], a["logits"], a["learn"], None, None)
+    return st, lib.s4d_last_error().decode()
+
+
+def _oproj(lib, **kw):
+    a = dict(feat=16, rows=900, w=16, b=16, inst=16, ild=512, mode=2, out=16, old=512, C=256)
+    a.update(kw)
+    st = lib.s4d_dfa_output_proj(a["feat"], a["rows"], a["w"], a["b"], a["inst"], a["ild"], a["mode"], a["out"],
+                                 a["old"], a["C"], None, None)
+    return st, lib.s4d_last_error().decode()
+
+
+@pytest.mark.parametrize("kw,status,text", [
+    (dict(C=128), L.S4D_ERR_UNSUPPORTED_SHAPE, "embed_dims"),
+    (dict(m=40), L.S4D_ERR_UNSUPPORTED_SHAPE, "num_learnable <= 32"),
+    (dict(n=408), L.S4D_ERR_UNSUPPORTED_SHAPE, "num_logits 416"),
+    (dict(rows=-1), L.S4D_ERR_INVALID_ARG, "sizes"),
+    (dict(inst=None), L.S4D_ERR_INVALID_ARG, "null"),
+    (dict(learn=None), L.S4D_ERR_INVALID_ARG, "null"),
+    (dict(wkps=None), L.S4D_ERR_INVALID_ARG, "null"),
+    (dict(wkps=8), L.S4D_ERR_INVALID_ARG, "misaligned"),
+    (dict(ild=254), L.S4D_ERR_INVALID_ARG, "strides"),
+    (dict(eld=258), L.S4D_ERR_INVALID_ARG, "strides"),
+    (dict(inst=8), L.S4D_ERR_INVALID_ARG, "misaligned"),
+    (dict(logits=20), L.S4D_ERR_INVALID_ARG, "misaligned"),
+])
+def test_weights_fc_rejects(lib, kw, status, text):
+    st, msg = _wfc(lib, **kw)
+    assert st == status and text in msg, msg
+
+
+def test_weights_fc_zero_rows_is_ok(lib):
+    assert _wfc(lib, rows=0)[0] == L.S4D_OK
+
+
+@pytest.mark.parametrize("kw,status,text", [
+    (dict(C=512), L.S4D_ERR_UNSUPPORTED_SHAPE, "embed_dims"),
+    (dict(mode=3), L.S4D_ERR_INVALID_ARG, "residual_mode"),
+    (dict(old=256), L.S4D_ERR_INVALID_ARG, "out_ld"),
+    (dict(old=514), L.S4D_ERR_INVALID_ARG, "out_ld"),
+    (dict(ild=100), L.S4D_ERR_INVALID_ARG, "instance_ld"),
+    (dict(inst=None), L.S4D_ERR_INVALID_ARG, "null"),
+    (dict(b=8), L.S4D_ERR_INVALID_ARG, "misaligned"),
+    (dict(out=8), L.S4D_ERR_INVALID_ARG, "misaligned"),
+])
+def test_output_proj_rejects(lib, kw, status, text):
+    st, msg = _oproj(lib, **kw)
+    assert st == status and text in msg, msg
+
+
+def test_output_proj_modes_without_residual(lib):
+    assert _oproj(lib, rows=0, inst=None, mode=0, old=256)[0] == L.S4D_OK

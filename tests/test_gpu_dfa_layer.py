@@ -74,7 +74,9 @@ def test_layer_bf16_tf32_linears(cuda_device):
     """The benchmark's configuration: bf16 maps, split logits, TF32 linears; against the
     reference's rows and the fp32 oracle at the bf16 tolerance."""
     g, cfg, ins, params = regen("standard_s1_bf16")
-    out = _run(_module(params, cfg, torch.bfloat16, True, "tf32"), ins, cfg)
+    mod = _module(params, cfg, torch.bfloat16, True, "tf32")
+    assert mod._tc  # the linears run on the library's tensor-core kernels
+    out = _run(mod, ins, cfg)
     assert torch.get_float32_matmul_precision() == "highest"  # restored after the layer
     sel = out[..., :256].reshape(900, 256).numpy()[g["rows"]]
     p, mre, xre = pcc(sel, g["out_rows"]), mean_rel_err(sel, g["out_rows"]), max_rel_err(sel, g["out_rows"])
@@ -138,5 +140,37 @@ def test_stacked_layers_small_batch(cuda_device):
         ref = oto.dfa_layer(params, inst, anchor, ins.anchor_embed, ins.feature_maps, ins.projection_mat,
                             ins.image_wh)
         assert (out - ref).abs().max().item() <= FP32_ATOL, layer
+        inst = ref[..., :256].contiguous()
+        anchor = syn.refine_anchors(anchor, gen)
+
+
+@pytest.mark.parametrize("mode", ["cat", "add"])
+def test_stacked_layers_tf32_strided_instance(cuda_device, mode):
+    """Six stacked layers with the tensor-core linears, each fed the previous layer's output as
+    a strided [.., :256] view of a [.., 512] buffer (read in place by TMA), against the oracle
+    fed the same values.  Residual "add" writes [.., 256]."""
+    cfg = syn.DFAConfig(bs=2, num_anchor=900)
+    ins = syn.make_inputs(cfg, 23, feature_dtype=torch.bfloat16)
+    gen = torch.Generator().manual_seed(77)
+    d = torch.device("cuda:0")
+    packed = ops.pack_feature_maps([m.to(d) for m in ins.feature_maps], dtype=torch.bfloat16)
+    anchor, inst = ins.anchor, ins.instance_feature
+    for layer in range(6):
+        params = syn.make_params(cfg, torch.Generator().manual_seed(700 + layer))
+        mod = DeformableFeatureAggregation("cuda:0", params, {"FEATURE_DTYPE": torch.bfloat16,
+                                                              "MATMUL_PRECISION": "tf32"}, residual_mode=mode)
+        assert mod._tc
+        buf = torch.full((cfg.bs, cfg.num_anchor, 512), float("nan"), device=d)
+        buf[..., :256] = inst.to(d)
+        out = mod.run(buf[..., :256], anchor.to(d), ins.anchor_embed.to(d), packed, ins.projection_mat.to(d),
+                      ins.image_wh.to(d), cfg.spatial_shapes, cfg.bs, cfg.num_anchor)
+        torch.cuda.synchronize()
+        out = out.cpu()
+        ref = oto.dfa_layer(params, inst, anchor, ins.anchor_embed, ins.feature_maps, ins.projection_mat,
+                            ins.image_wh, residual_mode=mode)
+        assert out.shape == ref.shape
+        p_, xre = pcc(out, ref), max_rel_err(out, ref)
+        print(f"layer {layer} {mode}: pcc={p_:.7f} max_rel={xre:.2e}")
+        assert p_ >= BF16_PCC and xre <= BF16_REL, layer
         inst = ref[..., :256].contiguous()
         anchor = syn.refine_anchors(anchor, gen)
