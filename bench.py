@@ -87,7 +87,7 @@ def workload_config(frames, layers, world):
         "accumulate": "f32", "logits": "split (per-anchor + per-camera terms, summed in the gather kernel)",
         "linears": "TF32 operands, fp32 accumulation: weights_fc + learnable_fc (embed add folded in) and "
                    "output_proj (residual cat fused) on this library's tcgen05 kernels; the per-frame "
-                   "camera encoder on cuBLAS, recomputed every step",
+                   "camera encoder + per-camera logits on this library's fp32 kernels, recomputed every step",
         "parallelism": f"dp{world} (frames)",
         "l2": "inputs larger than L2 (1.47 GB of maps per GPU, re-read by every layer)",
     }
@@ -277,10 +277,11 @@ class Workload:
 
 
 def launches_per_layer(w):
-    """This library's kernels per DFA layer: keypoints, camera softmax prep and gather, plus
-    the two tensor-core linears (weights_fc + learnable_fc, output_proj + residual) when the
-    layer runs them."""
-    return 3 + (2 if w.mods[0]._tc else 0)
+    """This library's kernels per DFA layer: keypoints, camera softmax prep and gather; the two
+    camera-encoder launches (split logits); the two tensor-core linears (weights_fc +
+    learnable_fc, output_proj + residual) when the layer runs them."""
+    m = w.mods[0]
+    return 3 + (2 if m.split_logits else 0) + (2 if m._tc else 0)
 
 
 def unique_tap_pixels(loc, spatial_shapes, start, num_feat):

@@ -232,6 +232,36 @@ S4D_API int s4d_dfa_weights_fc(const float* instance_feature, int64_t instance_l
                                int64_t num_learnable, int64_t embed_dims, float* logits, float* learnable,
                                int32_t* error_flag, void* stream);
 
+/* The per-frame camera terms, one CTA per frame (fp32):
+ *   camera_embed [bs, Ncam, C]          = LN2(ReLU(W2 LN1(ReLU(W1 x + b1)) + b2)),
+ *                                         x = projection_mat[b, c, :3, :4] (12 values)
+ *   camera_logits [bs, Ncam, num_logits] = weights_fc(camera_embed) with its bias, the
+ *                                         per-camera term of the split logits of
+ *                                         s4d_deformable_aggregation
+ * LayerNorms use eps 1e-5 and the biased variance.  Replaces the camera encoder
+ * (Linear-ReLU-LN-Linear-ReLU-LN) of model/deformable_feature_aggregation.py:679-717
+ * (test/dfa_pcc.py:272-279,309-312) and weights_fc on its output (:719-798).
+ *   projection_mat       [bs, Ncam, 4, 4]
+ *   cam_linear1_weight   [C, 12], cam_linear1_bias [C]; cam_ln1_weight/bias [C]
+ *   cam_linear2_weight   [C, C] (16-byte aligned), cam_linear2_bias [C]; cam_ln2_weight/bias [C]
+ *   weights_fc_weight    [num_logits, C] (16-byte aligned), weights_fc_bias [num_logits]
+ *   camera_embed         [bs, Ncam, C] or NULL (not needed by the split-logit gather)
+ *   camera_logits        [bs, Ncam, num_logits]
+ *   workspace            >= s4d_dfa_camera_workspace_bytes(bs, Ncam, C) bytes, 4-byte aligned
+ *                        (the hidden layer between the two launches)
+ * Implemented: 1 <= Ncam <= 8, C == 256. */
+S4D_API int s4d_dfa_camera_logits(const float* projection_mat, int64_t bs, int64_t num_cams,
+                                  const float* cam_linear1_weight, const float* cam_linear1_bias,
+                                  const float* cam_ln1_weight, const float* cam_ln1_bias,
+                                  const float* cam_linear2_weight, const float* cam_linear2_bias,
+                                  const float* cam_ln2_weight, const float* cam_ln2_bias,
+                                  const float* weights_fc_weight, const float* weights_fc_bias, int64_t num_logits,
+                                  int64_t embed_dims, float* camera_embed, float* camera_logits, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+/* Bytes of the workspace of s4d_dfa_camera_logits (bs * Ncam * C floats).  Host-only. */
+S4D_API size_t s4d_dfa_camera_workspace_bytes(int64_t bs, int64_t num_cams, int64_t embed_dims);
+
 /* output_proj with the residual fused into its epilogue:
  *   out[:, :C] = features . weight^T + bias                        (residual_mode NONE)
  *   out[:, :C] = features . weight^T + bias + instance_feature     (ADD)

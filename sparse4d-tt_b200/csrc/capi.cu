@@ -259,6 +259,57 @@ int s4d_dfa_weights_fc(const float* instance_feature, int64_t instance_ld, const
   return launch_weights_fc(p, static_cast<cudaStream_t>(stream));
 }
 
+size_t s4d_dfa_camera_workspace_bytes(int64_t bs, int64_t num_cams, int64_t embed_dims) {
+  if (bs <= 0 || num_cams <= 0 || embed_dims <= 0) return 0;
+  return size_t(bs) * size_t(num_cams) * size_t(embed_dims) * sizeof(float);
+}
+
+int s4d_dfa_camera_logits(const float* projection_mat, int64_t bs, int64_t num_cams, const float* cam_linear1_weight,
+                          const float* cam_linear1_bias, const float* cam_ln1_weight, const float* cam_ln1_bias,
+                          const float* cam_linear2_weight, const float* cam_linear2_bias, const float* cam_ln2_weight,
+                          const float* cam_ln2_bias, const float* weights_fc_weight, const float* weights_fc_bias,
+                          int64_t num_logits, int64_t embed_dims, float* camera_embed, float* camera_logits,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  set_error("%s", "");
+  if (bs < 0 || num_cams <= 0 || num_logits <= 0) return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_camera_logits: bad sizes");
+  if (num_cams > 8 || embed_dims != 256)
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_camera_logits: implemented for 1..8 cameras and embed_dims 256");
+  if (bs >= (1 << 30) || num_logits >= (1 << 24))
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_camera_logits: too many frames or logits");
+  if (bs == 0) return S4D_OK;
+  if (projection_mat == nullptr || cam_linear1_weight == nullptr || cam_linear1_bias == nullptr ||
+      cam_ln1_weight == nullptr || cam_ln1_bias == nullptr || cam_linear2_weight == nullptr ||
+      cam_linear2_bias == nullptr || cam_ln2_weight == nullptr || cam_ln2_bias == nullptr ||
+      weights_fc_weight == nullptr || weights_fc_bias == nullptr || camera_logits == nullptr)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_camera_logits: null pointer");
+  if (!aligned(cam_linear2_weight, 16) || !aligned(weights_fc_weight, 16))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_camera_logits: the C x C and weights_fc matrices must be 16-byte aligned");
+  if (workspace == nullptr || !aligned(workspace, 4) ||
+      workspace_bytes < s4d_dfa_camera_workspace_bytes(bs, num_cams, embed_dims))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_camera_logits: workspace missing or smaller than "
+                                     "s4d_dfa_camera_workspace_bytes()");
+  CamEncParams p{};
+  p.proj = projection_mat;
+  p.w1 = cam_linear1_weight;
+  p.b1 = cam_linear1_bias;
+  p.ln1_w = cam_ln1_weight;
+  p.ln1_b = cam_ln1_bias;
+  p.w2 = cam_linear2_weight;
+  p.b2 = cam_linear2_bias;
+  p.ln2_w = cam_ln2_weight;
+  p.ln2_b = cam_ln2_bias;
+  p.w_fc = weights_fc_weight;
+  p.b_fc = weights_fc_bias;
+  p.camera_embed = camera_embed;
+  p.logits = camera_logits;
+  p.hidden = static_cast<float*>(workspace);
+  p.bs = (int)bs;
+  p.num_cams = (int)num_cams;
+  p.num_logits = (int)num_logits;
+  p.embed_dims = (int)embed_dims;
+  return launch_camera_logits(p, static_cast<cudaStream_t>(stream));
+}
+
 int s4d_dfa_output_proj(const float* features, int64_t rows, const float* weight, const float* bias,
                         const float* instance_feature, int64_t instance_ld, int residual_mode, float* out,
                         int64_t out_ld, int64_t embed_dims, int32_t* error_flag, void* stream) {

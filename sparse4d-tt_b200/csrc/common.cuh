@@ -23,6 +23,22 @@ inline int cuda_check(cudaError_t e, const char* what) {
   return S4D_ERR_CUDA;
 }
 
+// Quotient of a non-negative integer n < 2^31 by a runtime divisor d >= 1 with one multiply-high
+// and a shift, by the round-up method of Granlund & Montgomery ("Division by invariant integers
+// using multiplication", PLDI 1994): with l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1,
+// floor(n / d) == (umulhi(n, m) + n) >> l for every n < 2^32 whose sum does not overflow, which
+// n < 2^31 guarantees.
+struct FastDiv {
+  uint32_t d = 1, m = 1, l = 0;
+  FastDiv() = default;
+  __host__ explicit FastDiv(uint32_t div) : d(div) {
+    l = 0;
+    while ((uint64_t(1) << l) < div) ++l;
+    m = uint32_t(((uint64_t(1) << 32) * ((uint64_t(1) << l) - div)) / div + 1);
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const { return (__umulhi(n, m) + n) >> l; }
+};
+
 // 8 consecutive bf16 channels (one 16-byte vector) widened to fp32.
 __device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};

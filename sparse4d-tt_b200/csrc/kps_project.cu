@@ -36,11 +36,11 @@ __device__ __forceinline__ float sigmoid_rn(float x) {
 }
 
 // Rotated + translated keypoint p of anchor n (fp32, fixed order).
-__device__ __forceinline__ void keypoint(const KpsParams& k, int64_t n, int p, float& px, float& py, float& pz) {
-  const float* a = k.anchor + n * k.anchor_dim;
+__device__ __forceinline__ void keypoint(const KpsParams& k, uint32_t n, int p, float& px, float& py, float& pz) {
+  const float* a = k.anchor + (int64_t)n * k.anchor_dim;
   float kx, ky, kz;
   if (k.kp_pre != nullptr) {
-    const float* q = k.kp_pre + (n * k.num_pts + p) * 3;
+    const float* q = k.kp_pre + ((int64_t)n * k.num_pts + p) * 3;
     kx = q[0];
     ky = q[1];
     kz = q[2];
@@ -52,7 +52,7 @@ __device__ __forceinline__ void keypoint(const KpsParams& k, int64_t n, int p, f
       ky = __fmul_rn(fs[1], sy);
       kz = __fmul_rn(fs[2], sz);
     } else {
-      const float* lg = k.learnable + n * (int64_t)(k.num_learnable * 3) + (p - k.num_fix) * 3;
+      const float* lg = k.learnable + (int64_t)n * (k.num_learnable * 3) + (p - k.num_fix) * 3;
       kx = __fmul_rn(__fsub_rn(sigmoid_rn(lg[0]), 0.5f), sx);
       ky = __fmul_rn(__fsub_rn(sigmoid_rn(lg[1]), 0.5f), sy);
       kz = __fmul_rn(__fsub_rn(sigmoid_rn(lg[2]), 0.5f), sz);
@@ -74,22 +74,25 @@ __global__ void __launch_bounds__(kKpsThreads) kps_project_kernel(KpsParams k) {
   // Keypoints of the anchors this block's elements belong to, computed once each (not once per
   // camera) and shared through shared memory.
   __shared__ float s_kp[kMaxBlockKeypoints * 3];
+  // Index arithmetic in 32 bits (the host guarantees total < 2^31) with multiply-high divisions.
   const int lane = threadIdx.x & 31;
-  const int64_t block_base = (int64_t)blockIdx.x * kElemsPerBlock;
-  const int per_anchor = k.num_cams * k.num_pts;
-  const int64_t n0 = block_base / per_anchor;
-  const int64_t last = block_base + kElemsPerBlock - 1 < k.total ? block_base + kElemsPerBlock - 1 : k.total - 1;
-  const int nkp = (int)(last / per_anchor - n0 + 1) * k.num_pts;
+  const uint32_t total = (uint32_t)k.total;
+  const uint32_t block_base = blockIdx.x * kElemsPerBlock;
+  const uint32_t per_anchor = k.num_cams * k.num_pts;
+  const uint32_t n0 = k.div_anchor_elems.div(block_base);
+  const uint32_t last = block_base + kElemsPerBlock - 1 < total ? block_base + kElemsPerBlock - 1 : total - 1;
+  const int nkp = (int)(k.div_anchor_elems.div(last) - n0 + 1) * k.num_pts;
   for (int i = threadIdx.x; i < nkp; i += kKpsThreads) {
-    const int64_t n = n0 + i / k.num_pts;
-    const int p = i % k.num_pts;
+    const uint32_t j = k.div_pts.div(i);
+    const uint32_t n = n0 + j;
+    const int p = i - (int)j * k.num_pts;
     float px, py, pz;
     keypoint(k, n, p, px, py, pz);
     s_kp[3 * i] = px;
     s_kp[3 * i + 1] = py;
     s_kp[3 * i + 2] = pz;
     if (k.key_points != nullptr) {  // anchors shared by two blocks are written twice, identically
-      float* kp = k.key_points + (n * k.num_pts + p) * 3;
+      float* kp = k.key_points + ((int64_t)n * k.num_pts + p) * 3;
       kp[0] = px;
       kp[1] = py;
       kp[2] = pz;
@@ -99,23 +102,23 @@ __global__ void __launch_bounds__(kKpsThreads) kps_project_kernel(KpsParams k) {
   int count = 0;
 #pragma unroll
   for (int r = 0; r < kKpsRounds; ++r) {
-    const int64_t e = block_base + r * kKpsThreads + threadIdx.x;
+    const uint32_t e = block_base + r * kKpsThreads + threadIdx.x;
     bool vis = false;
-    if (e < k.total) {
-      const int64_t n = e / per_anchor;  // linear anchor index b * A + a
-      const int rem = (int)(e - n * per_anchor);
-      const int c = rem / k.num_pts;
-      const int p = rem - c * k.num_pts;
-      const int b = (int)(n / k.num_anchor);
+    if (e < total) {
+      const uint32_t n = k.div_anchor_elems.div(e);  // linear anchor index b * A + a
+      const uint32_t rem = e - n * per_anchor;
+      const uint32_t c = k.div_pts.div(rem);
+      const int p = (int)(rem - c * k.num_pts);
+      const uint32_t b = k.div_anchors.div(n);
       const int ik = (int)(n - n0) * k.num_pts + p;
       const float px = s_kp[3 * ik], py = s_kp[3 * ik + 1], pz = s_kp[3 * ik + 2];
-      const float* P = k.proj + ((int64_t)b * k.num_cams + c) * 16;
+      const float* P = k.proj + (b * k.num_cams + c) * 16;
       const float X0 = proj_row(P, px, py, pz);
       const float X1 = proj_row(P + 4, px, py, pz);
       const float X2 = proj_row(P + 8, px, py, pz);
       const bool in_front = X2 > 1e-5f;
       const float z = X2 < 1e-5f ? 1e-5f : X2;  // torch.clamp(min=1e-5): NaN stays NaN
-      const float* wh = k.wh + ((int64_t)b * k.num_cams + c) * 2;
+      const float* wh = k.wh + (b * k.num_cams + c) * 2;
       const float u = __fdiv_rn(__fdiv_rn(X0, z), wh[0]);
       const float v = __fdiv_rn(__fdiv_rn(X1, z), wh[1]);
       vis = in_front && u >= 0.0f && u <= 1.0f && v >= 0.0f && v <= 1.0f;
@@ -124,7 +127,7 @@ __global__ void __launch_bounds__(kKpsThreads) kps_project_kernel(KpsParams k) {
         if (k.layout == S4D_LAYOUT_CAM_MAJOR) {
           reinterpret_cast<float2*>(k.loc)[e] = make_float2(u, v);
         } else if (k.layout == S4D_LAYOUT_PT_MAJOR) {
-          reinterpret_cast<float2*>(k.loc)[(n * k.num_pts + p) * k.num_cams + c] = make_float2(u, v);
+          reinterpret_cast<float2*>(k.loc)[((int64_t)n * k.num_pts + p) * k.num_cams + c] = make_float2(u, v);
         } else {  // GRID: [ncam, n_total, P, 2], 2*uv - 1 clamped to [-2, 2]
           const int64_t n_total = (int64_t)k.bs * k.num_anchor;
           const float gx = fminf(fmaxf(__fsub_rn(__fmul_rn(u, 2.0f), 1.0f), -2.0f), 2.0f);
@@ -159,8 +162,9 @@ __global__ void __launch_bounds__(kKpsThreads) kps_project_kernel(KpsParams k) {
 // read directly (no inter-block waiting; the project kernel has finished in stream order).
 __global__ void __launch_bounds__(kKpsThreads) kps_compact_kernel(const int32_t* __restrict__ block_counts,
                                                                   const uint32_t* __restrict__ vis_words,
-                                                                  int num_blocks, int64_t total, int num_anchor,
-                                                                  int num_cams, int num_pts, int4* __restrict__ idx,
+                                                                  int num_blocks, FastDiv div_anchor_elems,
+                                                                  FastDiv div_pts, FastDiv div_anchors,
+                                                                  int4* __restrict__ idx,
                                                                   int32_t* __restrict__ count_out) {
   __shared__ int s_part[kKpsThreads / 32];
   __shared__ int s_word_off[kWordsPerBlock];
@@ -192,21 +196,20 @@ __global__ void __launch_bounds__(kKpsThreads) kps_compact_kernel(const int32_t*
     *count_out = block_off + s_word_off[kWordsPerBlock - 1] + __popc(s_words[kWordsPerBlock - 1]);
   }
   if (idx == nullptr) return;
-  const int per_anchor = num_cams * num_pts;
 #pragma unroll
   for (int r = 0; r < kKpsRounds; ++r) {
     const int word_id = r * (kKpsThreads / 32) + warp;
     const uint32_t w = s_words[word_id];
     if ((w >> lane) & 1u) {
-      const int64_t e = (int64_t)blockIdx.x * kElemsPerBlock + r * kKpsThreads + threadIdx.x;
+      const uint32_t e = blockIdx.x * kElemsPerBlock + r * kKpsThreads + threadIdx.x;
       const int pos = block_off + s_word_off[word_id] + __popc(w & ((1u << lane) - 1u));
-      const int64_t n = e / per_anchor;
-      const int rem = (int)(e - n * per_anchor);
-      const int c = rem / num_pts;
-      idx[pos] = make_int4((int)(n / num_anchor), (int)(n % num_anchor), c, rem - c * num_pts);
+      const uint32_t n = div_anchor_elems.div(e);
+      const uint32_t rem = e - n * div_anchor_elems.d;
+      const uint32_t c = div_pts.div(rem);
+      const uint32_t b = div_anchors.div(n);
+      idx[pos] = make_int4((int)b, (int)(n - b * div_anchors.d), (int)c, (int)(rem - c * div_pts.d));
     }
   }
-  (void)total;
 }
 
 int64_t kps_num_blocks(int64_t total) { return (total + kElemsPerBlock - 1) / kElemsPerBlock; }
@@ -229,11 +232,14 @@ int launch_kps_project(KpsParams k, int32_t* visible_idx, int32_t* visible_count
     k.block_counts = nullptr;
     k.vis_words = nullptr;
   }
+  k.div_anchor_elems = FastDiv((uint32_t)(k.num_cams * k.num_pts));
+  k.div_pts = FastDiv((uint32_t)k.num_pts);
+  k.div_anchors = FastDiv((uint32_t)k.num_anchor);
   kps_project_kernel<<<(unsigned)nb, kKpsThreads, 0, stream>>>(k);
   int st = cuda_check(cudaGetLastError(), "kps_project_kernel launch");
   if (st != S4D_OK || !compact) return st;
   kps_compact_kernel<<<(unsigned)nb, kKpsThreads, 0, stream>>>(
-      k.block_counts, k.vis_words, (int)nb, k.total, k.num_anchor, k.num_cams, k.num_pts,
+      k.block_counts, k.vis_words, (int)nb, k.div_anchor_elems, k.div_pts, k.div_anchors,
       reinterpret_cast<int4*>(visible_idx), visible_count);
   return cuda_check(cudaGetLastError(), "kps_compact_kernel launch");
 }

@@ -24,6 +24,9 @@ struct KpsParams {
   uint8_t* mask;
   int32_t* block_counts;  // [num_blocks] (compaction only)
   uint32_t* vis_words;    // [num_blocks * 32] (compaction only)
+  FastDiv div_anchor_elems;  // by num_cams * num_pts (element -> linear anchor)
+  FastDiv div_pts;           // by num_pts
+  FastDiv div_anchors;       // by num_anchor (linear anchor -> batch)
 };
 
 // Largest Ncam*L*P*G the gather stages per anchor in shared memory (48 KiB of fp32).
@@ -76,6 +79,19 @@ struct OprojParams {
   int32_t* error_flag;
 };
 
+// Camera encoder + per-camera logit term (camera_encoder.cu).
+struct CamEncParams {
+  const float* proj;  // [bs, num_cams, 4, 4]
+  const float *w1, *b1, *ln1_w, *ln1_b;  // Linear 12 -> C, LayerNorm
+  const float *w2, *b2, *ln2_w, *ln2_b;  // Linear C -> C, LayerNorm
+  const float *w_fc, *b_fc;              // weights_fc [num_logits, C], [num_logits]
+  float* camera_embed;                   // [bs, num_cams, C] or null
+  float* logits;                         // [bs, num_cams, num_logits]
+  float* hidden;                         // [bs, num_cams, C] scratch (workspace)
+  int bs, num_cams, num_logits, embed_dims;
+};
+
+int launch_camera_logits(const CamEncParams& p, cudaStream_t stream);
 int launch_weights_fc(const WfcParams& p, cudaStream_t stream);
 int launch_output_proj(const OprojParams& p, cudaStream_t stream);
 

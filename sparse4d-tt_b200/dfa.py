@@ -119,7 +119,7 @@ class DeformableFeatureAggregation:
         if prec not in MATMUL_PRECISIONS:
             raise ValueError(f"MATMUL_PRECISION must be one of {sorted(MATMUL_PRECISIONS)}")
         self.matmul_precision = MATMUL_PRECISIONS[prec]
-        self.split_logits = bool(split_logits and use_camera_embed)
+        self.split_logits = bool(split_logits and use_camera_embed and num_cams <= 8 and embed_dims == 256)
         self.process_group = mesh_device if _is_process_group(mesh_device) else None
         if mesh_device is not None and self.process_group is None:
             raise ValueError("mesh_device must be a torch.distributed ProcessGroup (camera sharding)")
@@ -185,12 +185,18 @@ class DeformableFeatureAggregation:
 
     def _camera_logits(self, projection_mat: Tensor, bs: int) -> Tensor:
         """Per-camera term of the split logits, ``weights_fc(camera_embed)`` with the bias:
-        ``[bs, Ncam, L, P, G]``, cached with the camera embedding."""
-        cam = self._camera_embed(projection_mat, bs)
-        if self._cached_camera_logits is None:
+        ``[bs, Ncam, L, P, G]``, cached per frame.  One kernel computes the camera encoder and
+        this term together (``ops.camera_logits_into``)."""
+        key = (projection_mat.data_ptr(), projection_mat._version, tuple(projection_mat.shape))
+        if self._cached_camera_logits is None or self._cam_key != key:
             lpg = (self.num_levels, self.num_pts, self.num_groups)
-            wc = F.linear(cam, self.weights_fc_weight, self.weights_fc_bias)
-            self._cached_camera_logits = wc.reshape(bs, self.num_cams, *lpg).contiguous()
+            wc = torch.empty(bs, self.num_cams, *lpg, device=self.device)
+            emb = torch.empty(bs, self.num_cams, self.embed_dims, device=self.device)
+            ops.camera_logits_into(wc, projection_mat, self.cam_linear1_weight, self.cam_linear1_bias,
+                                   self.cam_ln1_weight, self.cam_ln1_bias, self.cam_linear2_weight,
+                                   self.cam_linear2_bias, self.cam_ln2_weight, self.cam_ln2_bias,
+                                   self.weights_fc_weight, self.weights_fc_bias, camera_embed=emb)
+            self._cached_camera_embed, self._cached_camera_logits, self._cam_key = emb, wc, key
         return self._cached_camera_logits
 
     def reset_frame_cache(self) -> None:

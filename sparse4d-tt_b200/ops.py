@@ -131,6 +131,49 @@ def weights_fc_into(logits: Tensor, learnable: Optional[Tensor], instance_featur
     L.check(name, st)
 
 
+def camera_logits_into(camera_logits: Tensor, projection_mat: Tensor, cam_linear1_weight: Tensor,
+                       cam_linear1_bias: Tensor, cam_ln1_weight: Tensor, cam_ln1_bias: Tensor,
+                       cam_linear2_weight: Tensor, cam_linear2_bias: Tensor, cam_ln2_weight: Tensor,
+                       cam_ln2_bias: Tensor, weights_fc_weight: Tensor, weights_fc_bias: Tensor,
+                       camera_embed: Optional[Tensor] = None, workspace: Optional[Tensor] = None) -> Tensor:
+    """Camera encoder + ``weights_fc`` on its output, one CTA per frame:
+    ``camera_logits [bs, Ncam, n]`` (and optionally ``camera_embed [bs, Ncam, C]``) from
+    ``projection_mat [bs, Ncam, 4, 4]`` (``model/deformable_feature_aggregation.py:679-717``)."""
+    name = "camera_logits"
+    ts = dict(camera_logits=camera_logits, projection_mat=projection_mat, cam_linear1_weight=cam_linear1_weight,
+              cam_linear1_bias=cam_linear1_bias, cam_ln1_weight=cam_ln1_weight, cam_ln1_bias=cam_ln1_bias,
+              cam_linear2_weight=cam_linear2_weight, cam_linear2_bias=cam_linear2_bias,
+              cam_ln2_weight=cam_ln2_weight, cam_ln2_bias=cam_ln2_bias, weights_fc_weight=weights_fc_weight,
+              weights_fc_bias=weights_fc_bias, camera_embed=camera_embed)
+    dev = _require_cuda(name, *ts.values())
+    _check_contig(name, **ts)
+    for k, t in ts.items():
+        _check_dtype(name, t, (torch.float32,), k)
+    _require(projection_mat.dim() == 4 and tuple(projection_mat.shape[2:]) == (4, 4),
+             "projection_mat must be [bs, Ncam, 4, 4]")
+    bs, nc = int(projection_mat.shape[0]), int(projection_mat.shape[1])
+    n, c = weights_fc_weight.shape
+    _require(tuple(cam_linear1_weight.shape) == (c, 12) and tuple(cam_linear2_weight.shape) == (c, c),
+             f"camera encoder weights must be [{c}, 12] and [{c}, {c}]")
+    for k in ("cam_linear1_bias", "cam_ln1_weight", "cam_ln1_bias", "cam_linear2_bias", "cam_ln2_weight",
+              "cam_ln2_bias"):
+        _require(tuple(ts[k].shape) == (c,), f"{k} must be [{c}]")
+    _require(tuple(weights_fc_bias.shape) == (n,), f"weights_fc_bias must be [{n}]")
+    _require(camera_logits.numel() == bs * nc * n, f"camera_logits must hold [{bs}, {nc}, {n}]")
+    _require(camera_embed is None or camera_embed.numel() == bs * nc * c, f"camera_embed must hold [{bs}, {nc}, {c}]")
+    if workspace is None:
+        workspace = torch.empty(bs * nc * c, dtype=torch.float32, device=dev)
+    _require_cuda(name, workspace)
+    ws_bytes = workspace.numel() * workspace.element_size()
+    st = L.lib().s4d_dfa_camera_logits(
+        projection_mat.data_ptr(), bs, nc, cam_linear1_weight.data_ptr(), cam_linear1_bias.data_ptr(),
+        cam_ln1_weight.data_ptr(), cam_ln1_bias.data_ptr(), cam_linear2_weight.data_ptr(), cam_linear2_bias.data_ptr(),
+        cam_ln2_weight.data_ptr(), cam_ln2_bias.data_ptr(), weights_fc_weight.data_ptr(), weights_fc_bias.data_ptr(),
+        n, c, _ptr(camera_embed), camera_logits.data_ptr(), workspace.data_ptr(), ws_bytes, _stream_ptr(dev))
+    L.check(name, st)
+    return camera_logits
+
+
 def output_proj_into(out: Tensor, features: Tensor, weight: Tensor, bias: Optional[Tensor],
                      instance_feature: Optional[Tensor] = None, residual_mode: str = "cat",
                      error_flag: Optional[Tensor] = None) -> Tensor:

@@ -110,17 +110,41 @@ def camera_ring(num_cams: int, image_wh: Tuple[int, int], dtype=torch.float32) -
     return torch.stack(mats).to(dtype)
 
 
+# Every draw below is identical on every host CPU.  torch's CPU uniform sampler is scalar per
+# element and float32 add / multiply are exact IEEE operations, but its normal sampler and its
+# float32 log / sin / cos pick a SIMD code path per host, whose last bits differ between
+# machines; so normals come from Box-Muller over float64 uniforms and every transcendental
+# function is evaluated in float64 and rounded once to float32.  (A float64 result that differs
+# by one ulp between hosts rounds to the same float32 unless it sits within 2^-29 of a rounding
+# tie.)
+_NORMAL_CHUNK = 1 << 22
+
+
+def normal(shape, gen: torch.Generator) -> torch.Tensor:
+    """N(0, 1) float32 draws of ``shape`` from ``gen``, reproducible across host CPUs."""
+    n = math.prod(shape)
+    out = torch.empty(n, dtype=torch.float32)
+    for start in range(0, n, 2 * _NORMAL_CHUNK):
+        m = min(2 * _NORMAL_CHUNK, n - start)
+        half = (m + 1) // 2
+        u = torch.rand(2, half, dtype=torch.float64, generator=gen)
+        r = torch.sqrt(-2.0 * torch.log1p(-u[0]))  # 1 - u in (0, 1]
+        t = (2.0 * math.pi) * u[1]
+        out[start:start + m] = torch.cat([r * torch.cos(t), r * torch.sin(t)])[:m].float()
+    return out.reshape(shape)
+
+
 def make_anchors(bs: int, num_anchor: int, gen: torch.Generator) -> torch.Tensor:
     a = torch.zeros(bs, num_anchor, 11)
     a[..., X] = torch.rand(bs, num_anchor, generator=gen) * 100.0 - 50.0
     a[..., Y] = torch.rand(bs, num_anchor, generator=gen) * 100.0 - 50.0
     a[..., Z] = torch.rand(bs, num_anchor, generator=gen) * 6.0 - 4.0
     size = torch.rand(bs, num_anchor, 3, generator=gen) * 4.5 + 0.5
-    a[..., W:H + 1] = size.log()
+    a[..., W:H + 1] = size.double().log().float()
     yaw = torch.rand(bs, num_anchor, generator=gen) * (2 * math.pi) - math.pi
-    a[..., SIN_YAW] = yaw.sin()
-    a[..., COS_YAW] = yaw.cos()
-    a[..., VX:VY + 1] = torch.randn(bs, num_anchor, 2, generator=gen) * 2.0
+    a[..., SIN_YAW] = yaw.double().sin().float()
+    a[..., COS_YAW] = yaw.double().cos().float()
+    a[..., VX:VY + 1] = normal((bs, num_anchor, 2), gen) * 2.0
     return a
 
 
@@ -128,11 +152,11 @@ def refine_anchors(anchor: torch.Tensor, gen: torch.Generator, sigma: float = 0.
     """Stand-in for the decoder's box refinement between stacked DFA layers: N(0, sigma)
     offsets on centre, log-size, yaw (sin/cos, renormalised) and velocity."""
     a = anchor.clone()
-    noise = torch.randn(a.shape, generator=gen) * sigma
+    noise = normal(tuple(a.shape), gen) * sigma
     a[..., X:H + 1] += noise[..., X:H + 1]
     a[..., VX:VZ] += noise[..., VX:VZ]
-    sc = a[..., SIN_YAW:COS_YAW + 1] + noise[..., SIN_YAW:COS_YAW + 1]
-    a[..., SIN_YAW:COS_YAW + 1] = sc / sc.norm(dim=-1, keepdim=True).clamp(min=1e-6)
+    sc = (a[..., SIN_YAW:COS_YAW + 1] + noise[..., SIN_YAW:COS_YAW + 1]).double()
+    a[..., SIN_YAW:COS_YAW + 1] = (sc / sc.norm(dim=-1, keepdim=True).clamp(min=1e-6)).float()
     return a
 
 
@@ -188,15 +212,15 @@ def make_inputs(
     (used for large benchmark batches, never for parity)."""
     gen = torch.Generator().manual_seed(seed)
     bs, A, C = cfg.bs, cfg.num_anchor, cfg.embed_dims
-    inst = torch.randn(bs, A, C, generator=gen)
+    inst = normal((bs, A, C), gen)
     anchor = make_anchors(bs, A, gen)
-    embed = torch.randn(bs, A, C, generator=gen)
+    embed = normal((bs, A, C), gen)
     proj = camera_ring(cfg.num_cams, cfg.image_wh).unsqueeze(0).expand(bs, -1, -1, -1).contiguous()
     wh = torch.tensor(cfg.image_wh, dtype=torch.float32).expand(bs, cfg.num_cams, 2).contiguous()
     maps = []
     if device == "cpu":
         for h, w in cfg.spatial_shapes:
-            fm = torch.randn(bs, cfg.num_cams, C, h, w, generator=gen)
+            fm = normal((bs, cfg.num_cams, C, h, w), gen)
             if feature_dtype is not None and feature_dtype != torch.float32:
                 fm = fm.to(feature_dtype).float()
             maps.append(fm)

@@ -33,7 +33,7 @@ def lib():
 
 def test_every_declared_symbol_is_exported(lib):
     names = declared_functions()
-    assert len(names) == 11, names
+    assert len(names) == 13, names
     for n in names:
         assert hasattr(lib, n), n
         assert n in L.SIGNATURES, f"{n} has no ctypes signature"
@@ -236,3 +236,36 @@ def test_output_proj_rejects(lib, kw, status, text):
 
 def test_output_proj_modes_without_residual(lib):
     assert _oproj(lib, rows=0, inst=None, mode=0, old=256)[0] == L.S4D_OK
+
+
+def _cam(lib, **kw):
+    a = dict(proj=16, bs=32, nc=6, w=16, n=416, C=256, emb=None, out=16, ws=16, wsb=32 * 6 * 256 * 4)
+    a.update(kw)
+    w = a["w"]
+    st = lib.s4d_dfa_camera_logits(a["proj"], a["bs"], a["nc"], w, w, w, w, w, w, w, w, w, w, a["n"], a["C"], a["emb"],
+                                   a["out"], a["ws"], a["wsb"], None)
+    return st, lib.s4d_last_error().decode()
+
+
+@pytest.mark.parametrize("kw,status,text", [
+    (dict(nc=9), L.S4D_ERR_UNSUPPORTED_SHAPE, "1..8 cameras"),
+    (dict(C=128), L.S4D_ERR_UNSUPPORTED_SHAPE, "embed_dims 256"),
+    (dict(nc=0), L.S4D_ERR_INVALID_ARG, "bad sizes"),
+    (dict(bs=-1), L.S4D_ERR_INVALID_ARG, "bad sizes"),
+    (dict(out=None), L.S4D_ERR_INVALID_ARG, "null"),
+    (dict(w=8), L.S4D_ERR_INVALID_ARG, "16-byte aligned"),
+    (dict(ws=None), L.S4D_ERR_INVALID_ARG, "workspace"),
+    (dict(wsb=1000), L.S4D_ERR_INVALID_ARG, "workspace"),
+])
+def test_camera_logits_rejects(lib, kw, status, text):
+    st, msg = _cam(lib, **kw)
+    assert st == status and text in msg, msg
+
+
+def test_camera_logits_zero_frames_is_ok(lib):
+    assert _cam(lib, bs=0)[0] == L.S4D_OK
+
+
+def test_camera_workspace_bytes(lib):
+    assert lib.s4d_dfa_camera_workspace_bytes(32, 6, 256) == 32 * 6 * 256 * 4
+    assert lib.s4d_dfa_camera_workspace_bytes(0, 6, 256) == 0

@@ -86,7 +86,14 @@ def test_kps_reference_dummy_inputs(cuda_device, bs):
     (inst, anchor, embed, maps, proj, wh), params = fx.reference_dummy_case(bs)
     learn = oto.learnable_logits(inst, params)
     loc, mask, idx, cnt, kp = _run(anchor, learn, params["kps_fix_scale"], proj, wh)
-    ref_vis = fx.unpack_bits(g["vis_bits"], (bs, 900, 6, 13))
+    if fx.same_inputs(g, anchor=anchor, instance_feature=inst, projection_mat=proj):
+        ref_vis = fx.unpack_bits(g["vis_bits"], (bs, 900, 6, 13))
+    else:  # this host's CPU drew other last bits: the oracle on these inputs is the reference
+        print("refdummy inputs differ from the fixture's in the last bits on this host; "
+              "indices checked against the numpy oracle on the same inputs")
+        kp_np = onp.key_points(anchor.numpy(), learn.numpy(), params["kps_fix_scale"].numpy())
+        _, _, ref_vis = onp.project(kp_np, proj.numpy(), wh.numpy())
+        assert abs(int(ref_vis.sum()) - int(g["n_visible"])) <= 8
     assert cnt == int(ref_vis.sum())
     assert np.array_equal(idx.numpy(), np.argwhere(ref_vis).astype(np.int32))
     rows = g["rows"]

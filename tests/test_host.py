@@ -114,3 +114,26 @@ def test_refine_anchors_keeps_unit_yaw():
     n = r[..., 6:8].norm(dim=-1)
     np.testing.assert_allclose(n.numpy(), 1.0, atol=1e-5)
     assert (r[..., 0:3] - a[..., 0:3]).abs().max() < 1.0
+
+
+def _fastdiv(d):
+    """Python replica of FastDiv (csrc/common.cuh): l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1."""
+    l = 0
+    while (1 << l) < d:
+        l += 1
+    m = ((1 << 32) * ((1 << l) - d)) // d + 1
+    m &= 0xFFFFFFFF
+    return lambda n: ((((n * m) >> 32) + n) & 0xFFFFFFFF) >> l
+
+
+@pytest.mark.parametrize("d", [1, 2, 3, 6, 7, 13, 78, 900, 1800, 3600, 65537, 1 << 20, (1 << 31) - 1])
+def test_fastdiv_is_exact_below_2_31(d):
+    import random
+
+    q = _fastdiv(d)
+    rng = random.Random(d)
+    ns = [0, 1, d - 1, d, d + 1, (1 << 31) - 1, (1 << 31) - 2, (1 << 30)]
+    ns += [rng.randrange(1 << 31) for _ in range(20000)]
+    ns += [k * d + r for k in (1, 2, 1000, ((1 << 31) - 1) // d) for r in (-1, 0, 1) if 0 <= k * d + r < (1 << 31)]
+    for n in ns:
+        assert q(n) == n // d, (n, d)
