@@ -71,6 +71,9 @@ enum {
                                pipeline barriers; its outputs were not written.  Never expected. */
 };
 
+/* Layouts of the per-level maps s4d_pack_feature_maps reads. */
+enum { S4D_MAPS_NCHW = 0 /* [bs, Ncam, C, H, W] */, S4D_MAPS_NHWC = 1 /* [bs, Ncam, H, W, C] */ };
+
 /* Residual modes of s4d_dfa_output_proj (the reference module's residual_mode). */
 enum { S4D_RESIDUAL_NONE = 0, S4D_RESIDUAL_ADD = 1, S4D_RESIDUAL_CAT = 2 };
 
@@ -193,6 +196,23 @@ S4D_API int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, i
                                int64_t num_cams, int64_t num_levels, int64_t num_pts, int64_t num_groups,
                                int64_t embed_dims, int64_t cam_begin, int64_t cam_end, float* out,
                                int32_t* error_flag, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Per-level feature maps -> the packed mc_ms_feat layout of s4d_deformable_aggregation, with
+ * the element type cast fused in: mc_ms_feat[b, c * sum(HW) + start(l) + y * W(l) + x, ch],
+ * start(l) = sum of H*W of the levels before l (the scale_start_index of s4d / ops.level_tables).
+ * Replaces the per-level reshape + typecast the reference applies to its FPN outputs before the
+ * DFA (model/sparse4d.py:549-558; FPN output format model/fpn.py:90-98).
+ *   levels       HOST array of num_levels DEVICE pointers, level l [bs, Ncam, C, H, W] (NCHW) or
+ *                [bs, Ncam, H, W, C] (NHWC; the reference's [1, 1, N*H*W, C] levels are NHWC with
+ *                bs * Ncam = N), element type src_dtype, contiguous, 16-byte aligned
+ *   level_hw     HOST array [num_levels][2] of (H, W)
+ *   mc_ms_feat   [bs, Ncam * sum(HW), C] of dst_dtype, 16-byte aligned
+ * Implemented: 1 <= num_levels <= 8, C a multiple of 64.
+ */
+S4D_API int s4d_pack_feature_maps(const void* const* levels, int layout, int src_dtype, int64_t bs, int64_t num_cams,
+                                  int64_t num_levels, const int32_t* level_hw, int64_t embed_dims, int dst_dtype,
+                                  void* mc_ms_feat, void* stream);
 
 /* Bytes of the optional workspace of s4d_deformable_aggregation (split logits only: the
  * per-frame camera softmax factors, bs * (Ncam + 1) * L * P * G floats; 0 otherwise).

@@ -3,19 +3,25 @@
 Public API:
   DeformableFeatureAggregation, preprocess_dfa_parameters   -- drop-in module (dfa.py)
   deformable_aggregation, kps_project, kps_project_fused,
-  pack_feature_maps, level_tables                           -- operators (ops.py)
+  pack_feature_maps, level_tables, weights_fc_into,
+  output_proj_into, camera_logits_into                      -- operators (ops.py)
+  DFAStack, capture                                         -- CUDA-graph execution (graph.py)
 The operators run hand-written sm_100a CUDA kernels from lib/libs4d_dfa.so through the C ABI
 of include/s4d_dfa.h; the library is loaded on first use and its absence raises.
 """
 from . import synthetic  # noqa: F401
 from .dfa import DeformableFeatureAggregation, preprocess_dfa_parameters  # noqa: F401
+from .graph import DFAStack, capture  # noqa: F401
 from .ops import (  # noqa: F401
     deformable_aggregation,
     deformable_aggregation_into,
     kps_project,
     kps_project_fused,
     kps_project_into,
+    camera_logits_into,
     level_tables,
+    output_proj_into,
     pack_feature_maps,
     visible_indices,
+    weights_fc_into,
 )

@@ -28,6 +28,9 @@ S4D_LAYOUT_GRID = 2
 S4D_FLAG_BAD_LEVEL = 1
 S4D_FLAG_WAIT_TIMEOUT = 2
 
+S4D_MAPS_NCHW = 0
+S4D_MAPS_NHWC = 1
+
 S4D_RESIDUAL_NONE = 0
 S4D_RESIDUAL_ADD = 1
 S4D_RESIDUAL_CAT = 2
@@ -53,6 +56,7 @@ SIGNATURES = {
     "s4d_dfa_camera_logits": (_int, [_p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p, _p,
                                      _p, _sz, _p]),
     "s4d_dfa_camera_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "s4d_pack_feature_maps": (_int, [_p, _int, _int, _i64, _i64, _i64, _p, _i64, _int, _p, _p]),
     "s4d_dfa_output_proj": (_int, [_p, _i64, _p, _p, _p, _i64, _int, _p, _i64, _i64, _p, _p]),
 }
 

@@ -259,6 +259,49 @@ int s4d_dfa_weights_fc(const float* instance_feature, int64_t instance_ld, const
   return launch_weights_fc(p, static_cast<cudaStream_t>(stream));
 }
 
+int s4d_pack_feature_maps(const void* const* levels, int layout, int src_dtype, int64_t bs, int64_t num_cams,
+                          int64_t num_levels, const int32_t* level_hw, int64_t embed_dims, int dst_dtype,
+                          void* mc_ms_feat, void* stream) {
+  set_error("%s", "");
+  if (layout != S4D_MAPS_NCHW && layout != S4D_MAPS_NHWC)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_pack_feature_maps: unknown layout");
+  if ((src_dtype != S4D_DTYPE_F32 && src_dtype != S4D_DTYPE_BF16) ||
+      (dst_dtype != S4D_DTYPE_F32 && dst_dtype != S4D_DTYPE_BF16))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_pack_feature_maps: unknown dtype");
+  if (bs < 0 || num_cams <= 0 || num_levels <= 0 || embed_dims <= 0)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_pack_feature_maps: bad sizes");
+  if (num_levels > kMaxPackLevels || embed_dims % 64 != 0)
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_pack_feature_maps: implemented for <= 8 levels, C a multiple of 64");
+  if (bs * num_cams > 65535) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_pack_feature_maps: bs * Ncam must be <= 65535");
+  if (bs == 0) return S4D_OK;
+  if (levels == nullptr || level_hw == nullptr || mc_ms_feat == nullptr)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_pack_feature_maps: null pointer");
+  if (!aligned(mc_ms_feat, 16)) return fail(S4D_ERR_INVALID_ARG, "s4d_pack_feature_maps: mc_ms_feat must be 16-byte aligned");
+  PackParams p{};
+  int64_t per_cam = 0;
+  for (int64_t l = 0; l < num_levels; ++l) {
+    const int64_t h = level_hw[2 * l], w = level_hw[2 * l + 1];
+    if (h <= 0 || w <= 0) return fail(S4D_ERR_INVALID_ARG, "s4d_pack_feature_maps: level sizes must be positive");
+    if (levels[l] == nullptr || !aligned(levels[l], 16))
+      return fail(S4D_ERR_INVALID_ARG, "s4d_pack_feature_maps: null or misaligned level pointer");
+    p.src[l] = levels[l];
+    p.h[l] = (int)h;
+    p.w[l] = (int)w;
+    per_cam += h * w;
+  }
+  if (per_cam * num_cams * bs * embed_dims >= ((int64_t)1 << 40) || per_cam * embed_dims >= kMaxElems)
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_pack_feature_maps: maps too large");
+  p.num_levels = (int)num_levels;
+  p.bs = (int)bs;
+  p.num_cams = (int)num_cams;
+  p.channels = (int)embed_dims;
+  p.layout = layout;
+  p.src_dtype = src_dtype;
+  p.dst_dtype = dst_dtype;
+  p.dst = mc_ms_feat;
+  return launch_pack_maps(p, static_cast<cudaStream_t>(stream));
+}
+
 size_t s4d_dfa_camera_workspace_bytes(int64_t bs, int64_t num_cams, int64_t embed_dims) {
   if (bs <= 0 || num_cams <= 0 || embed_dims <= 0) return 0;
   return size_t(bs) * size_t(num_cams) * size_t(embed_dims) * sizeof(float);

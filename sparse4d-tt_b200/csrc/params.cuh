@@ -92,6 +92,18 @@ struct CamEncParams {
 };
 
 int launch_camera_logits(const CamEncParams& p, cudaStream_t stream);
+
+// Packing of per-level feature maps (pack_maps.cu).
+constexpr int kMaxPackLevels = 8;
+struct PackParams {
+  const void* src[kMaxPackLevels];
+  int h[kMaxPackLevels], w[kMaxPackLevels];
+  int num_levels, bs, num_cams, channels;
+  int layout, src_dtype, dst_dtype;
+  void* dst;
+};
+
+int launch_pack_maps(const PackParams& p, cudaStream_t stream);
 int launch_weights_fc(const WfcParams& p, cudaStream_t stream);
 int launch_output_proj(const OprojParams& p, cudaStream_t stream);
 

@@ -155,6 +155,9 @@ class DeformableFeatureAggregation:
         # (model/sparse4d_head.py:290-296 resets the same attribute names).
         self._cached_camera_embed = None
         self._cached_camera_logits = None
+        self._cached_camera_ws = None
+        self._side: Optional[torch.cuda.Stream] = None
+        self._side_pending = False
         self._cached_proj_rm = None
         self._cached_wh_rm = None
         self._cam_key = None
@@ -183,21 +186,41 @@ class DeformableFeatureAggregation:
             self._cam_key = key
         return self._cached_camera_embed
 
-    def _camera_logits(self, projection_mat: Tensor, bs: int) -> Tensor:
+    def _camera_logits(self, projection_mat: Tensor, bs: int, side: bool = False) -> Tensor:
         """Per-camera term of the split logits, ``weights_fc(camera_embed)`` with the bias:
-        ``[bs, Ncam, L, P, G]``, cached per frame.  One kernel computes the camera encoder and
-        this term together (``ops.camera_logits_into``)."""
+        ``[bs, Ncam, L, P, G]``, cached per frame.  Two kernels compute the camera encoder and
+        this term together (``ops.camera_logits_into``).  With ``side=True`` they run on this
+        module's side stream, forked from the current stream, so that they overlap the
+        per-anchor work; ``_join_side()`` makes the current stream wait for them.  Their
+        outputs and workspace stay in the per-frame cache, so no buffer the side stream writes
+        is handed back to the allocator before the join."""
         key = (projection_mat.data_ptr(), projection_mat._version, tuple(projection_mat.shape))
         if self._cached_camera_logits is None or self._cam_key != key:
             lpg = (self.num_levels, self.num_pts, self.num_groups)
             wc = torch.empty(bs, self.num_cams, *lpg, device=self.device)
             emb = torch.empty(bs, self.num_cams, self.embed_dims, device=self.device)
-            ops.camera_logits_into(wc, projection_mat, self.cam_linear1_weight, self.cam_linear1_bias,
-                                   self.cam_ln1_weight, self.cam_ln1_bias, self.cam_linear2_weight,
-                                   self.cam_linear2_bias, self.cam_ln2_weight, self.cam_ln2_bias,
-                                   self.weights_fc_weight, self.weights_fc_bias, camera_embed=emb)
+            ws = torch.empty(bs * self.num_cams * self.embed_dims, device=self.device)
+            ctx = contextlib.nullcontext()
+            if side:
+                if self._side is None:
+                    self._side = torch.cuda.Stream(self.device)
+                self._side.wait_stream(torch.cuda.current_stream(self.device))
+                ctx = torch.cuda.stream(self._side)
+                self._side_pending = True
+            with ctx:
+                ops.camera_logits_into(wc, projection_mat, self.cam_linear1_weight, self.cam_linear1_bias,
+                                       self.cam_ln1_weight, self.cam_ln1_bias, self.cam_linear2_weight,
+                                       self.cam_linear2_bias, self.cam_ln2_weight, self.cam_ln2_bias,
+                                       self.weights_fc_weight, self.weights_fc_bias, camera_embed=emb,
+                                       workspace=ws)
             self._cached_camera_embed, self._cached_camera_logits, self._cam_key = emb, wc, key
+            self._cached_camera_ws = ws
         return self._cached_camera_logits
+
+    def _join_side(self) -> None:
+        if self._side_pending:
+            torch.cuda.current_stream(self.device).wait_stream(self._side)
+            self._side_pending = False
 
     def reset_frame_cache(self) -> None:
         """Drops the per-frame camera caches (what the head does at the start of every frame)."""
@@ -250,19 +273,23 @@ class DeformableFeatureAggregation:
         C = self.embed_dims
         rows = bs * num_anchor
         if self._tc:
+            # On a side stream the camera terms overlap the next two kernels; that pays while the
+            # GPU is the bottleneck (graph capture, large batches), not for small eager calls, whose
+            # time is host work that the extra stream bookkeeping would lengthen.
+            side = rows >= 8192 or torch.cuda.is_current_stream_capturing()
+            logits_cam = self._camera_logits(projection_mat, bs, side=side)
             inst2d, embed2d = ops.row_view(instance_feature, C), ops.row_view(anchor_embed, C)
             logits = torch.empty(bs, num_anchor, self.num_levels, self.num_pts, self.num_groups, device=dev)
             learn = torch.empty(bs, num_anchor, 3 * self.num_learnable_pts, device=dev)
             ops.weights_fc_into(logits.view(rows, -1), learn.view(rows, -1), inst2d, embed2d, self.weights_fc_weight,
                                 self.learnable_fc_weight, self.learnable_fc_bias)
-            with _matmul_precision(self.matmul_precision):
-                logits_cam = self._camera_logits(projection_mat, bs)
         else:
             with _matmul_precision(self.matmul_precision):
                 logits, logits_cam = self._get_weights(instance_feature, anchor_embed, projection_mat, bs, num_anchor)
                 learn = F.linear(instance_feature, self.learnable_fc_weight, self.learnable_fc_bias).contiguous()
         loc = torch.empty(bs, num_anchor, self.num_cams, self.num_pts, 2, dtype=torch.float32, device=dev)
         ops.kps_project_into(anchor, learn, self.fix_scale, projection_mat, image_wh, sample_location=loc)
+        self._join_side()  # the camera terms are needed from here on
 
         cam_begin, cam_end = 0, self.num_cams
         if self.process_group is not None:

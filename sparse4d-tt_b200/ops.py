@@ -25,6 +25,7 @@ There is no CPU path: CPU tensors are rejected.
 """
 from __future__ import annotations
 
+import ctypes as C
 from typing import List, Optional, Sequence, Tuple, Union
 
 import torch
@@ -460,20 +461,43 @@ def level_tables(spatial_shapes: Sequence[Tuple[int, int]], num_cams: int, devic
     return shape, start, per_cam * num_cams
 
 
-def pack_feature_maps(feature_maps: List[Tensor], dtype: Optional[torch.dtype] = None, channels_last: bool = False):
+def pack_feature_maps(feature_maps: List[Tensor], dtype: Optional[torch.dtype] = None, channels_last: bool = False,
+                      out: Optional[Tensor] = None):
     """Pack per-level maps into ``(mc_ms_feat [bs, Ncam*sum(HW), C], spatial_shape,
-    scale_start_index)``.  Maps are NCHW ``[bs, Ncam, C, H, W]`` (the oracle's format), or with
-    ``channels_last=True`` ``[bs, Ncam, H, W, C]``.  This is one copy of the maps; producers
-    that can write the packed layout directly skip it."""
+    scale_start_index)`` with one kernel launch per level (``s4d_pack_feature_maps``: a tiled
+    transpose for NCHW maps, a vector copy for channels-last ones, the cast to ``dtype`` fused
+    in).  Maps are NCHW ``[bs, Ncam, C, H, W]`` (the oracle's format), or with
+    ``channels_last=True`` ``[bs, Ncam, H, W, C]``; fp32 or bf16.  ``out`` may be a
+    preallocated ``mc_ms_feat``."""
+    name = "pack_feature_maps"
+    maps = [f if f.is_contiguous() else f.contiguous() for f in feature_maps]
+    dev = _require_cuda(name, *maps, out)
+    _require(len(maps) > 0, f"{name}: no maps")
+    for f in maps:
+        _check_dtype(name, f, (torch.float32, torch.bfloat16), "feature map")
+        _require(f.dtype == maps[0].dtype and f.dim() == 5, f"{name}: maps must be 5-D and share one dtype")
+    bs, nc = int(maps[0].shape[0]), int(maps[0].shape[1])
     if channels_last:
-        bs, nc = feature_maps[0].shape[:2]
-        shapes = [(int(f.shape[2]), int(f.shape[3])) for f in feature_maps]
-        cols = [f.reshape(bs, nc, -1, f.shape[-1]) for f in feature_maps]
+        shapes = [(int(f.shape[2]), int(f.shape[3])) for f in maps]
+        c = int(maps[0].shape[4])
+        _require(all(tuple(f.shape[:2]) == (bs, nc) and f.shape[4] == c for f in maps), f"{name}: inconsistent maps")
     else:
-        bs, nc = feature_maps[0].shape[:2]
-        shapes = [(int(f.shape[3]), int(f.shape[4])) for f in feature_maps]
-        cols = [f.flatten(3).transpose(2, 3) for f in feature_maps]
-    packed = torch.cat(cols, dim=2).reshape(bs, -1, cols[0].shape[-1])
-    packed = packed.to(dtype).contiguous() if dtype is not None else packed.contiguous()
-    shape, start, _ = level_tables(shapes, nc, device=packed.device)
-    return packed, shape, start
+        shapes = [(int(f.shape[3]), int(f.shape[4])) for f in maps]
+        c = int(maps[0].shape[2])
+        _require(all(tuple(f.shape[:3]) == (bs, nc, c) for f in maps), f"{name}: inconsistent maps")
+    dtype = dtype or maps[0].dtype
+    _check_dtype(name, torch.empty(0, dtype=dtype), (torch.float32, torch.bfloat16), "dtype")
+    rows = nc * sum(h * w for h, w in shapes)
+    if out is None:
+        out = torch.empty(bs, rows, c, dtype=dtype, device=dev)
+    _require(tuple(out.shape) == (bs, rows, c) and out.dtype == dtype and out.is_contiguous(),
+             f"{name}: out must be a contiguous [{bs}, {rows}, {c}] {dtype} tensor")
+    ptrs = (C.c_void_p * len(maps))(*[f.data_ptr() for f in maps])
+    hw = (C.c_int32 * (2 * len(maps)))(*[v for s_ in shapes for v in s_])
+    code = lambda t: L.S4D_DTYPE_BF16 if t == torch.bfloat16 else L.S4D_DTYPE_F32  # noqa: E731
+    st = L.lib().s4d_pack_feature_maps(ptrs, L.S4D_MAPS_NHWC if channels_last else L.S4D_MAPS_NCHW,
+                                       code(maps[0].dtype), bs, nc, len(maps), hw, c, code(dtype), out.data_ptr(),
+                                       _stream_ptr(dev))
+    L.check(name, st)
+    shape, start, _ = level_tables(shapes, nc, device=dev)
+    return out, shape, start

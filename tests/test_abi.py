@@ -33,7 +33,7 @@ def lib():
 
 def test_every_declared_symbol_is_exported(lib):
     names = declared_functions()
-    assert len(names) == 13, names
+    assert len(names) == 14, names
     for n in names:
         assert hasattr(lib, n), n
         assert n in L.SIGNATURES, f"{n} has no ctypes signature"
@@ -269,3 +269,32 @@ def test_camera_logits_zero_frames_is_ok(lib):
 def test_camera_workspace_bytes(lib):
     assert lib.s4d_dfa_camera_workspace_bytes(32, 6, 256) == 32 * 6 * 256 * 4
     assert lib.s4d_dfa_camera_workspace_bytes(0, 6, 256) == 0
+
+
+def _pack(lib, **kw):
+    a = dict(levels=[16, 16], layout=0, sd=0, bs=2, nc=6, nl=2, hw=[4, 4, 2, 2], C=256, dd=1, out=16)
+    a.update(kw)
+    lv = None if a["levels"] is None else (C.c_void_p * len(a["levels"]))(*a["levels"])
+    hw = (C.c_int32 * len(a["hw"]))(*a["hw"])
+    st = lib.s4d_pack_feature_maps(lv, a["layout"], a["sd"], a["bs"], a["nc"], a["nl"], hw, a["C"], a["dd"], a["out"],
+                                   None)
+    return st, lib.s4d_last_error().decode()
+
+
+@pytest.mark.parametrize("kw,status,text", [
+    (dict(layout=2), L.S4D_ERR_INVALID_ARG, "layout"),
+    (dict(sd=5), L.S4D_ERR_INVALID_ARG, "dtype"),
+    (dict(C=96), L.S4D_ERR_UNSUPPORTED_SHAPE, "multiple of 64"),
+    (dict(nl=9, levels=[16] * 9, hw=[2] * 18), L.S4D_ERR_UNSUPPORTED_SHAPE, "8 levels"),
+    (dict(levels=[16, 8]), L.S4D_ERR_INVALID_ARG, "misaligned"),
+    (dict(hw=[4, 0, 2, 2]), L.S4D_ERR_INVALID_ARG, "positive"),
+    (dict(out=None), L.S4D_ERR_INVALID_ARG, "null"),
+    (dict(out=8), L.S4D_ERR_INVALID_ARG, "16-byte aligned"),
+])
+def test_pack_rejects(lib, kw, status, text):
+    st, msg = _pack(lib, **kw)
+    assert st == status and text in msg, msg
+
+
+def test_pack_zero_batch_is_ok(lib):
+    assert _pack(lib, bs=0)[0] == L.S4D_OK

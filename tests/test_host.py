@@ -40,18 +40,11 @@ def test_synthetic_visibility_fraction():
     assert 0.10 < vis.float().mean().item() < 0.22
 
 
-@pytest.mark.parametrize("channels_last", [False, True])
-def test_pack_feature_maps_matches_numpy(channels_last):
-    rng = np.random.default_rng(1)
-    maps = [rng.standard_normal((2, 3, 256, h, w)).astype(np.float32) for h, w in ((4, 6), (2, 3))]
-    feat_np, shape_np, start_np = onp.pack_feature_maps(maps)
-    tm = [torch.from_numpy(m) for m in maps]
-    if channels_last:
-        tm = [m.permute(0, 1, 3, 4, 2).contiguous() for m in tm]
-    feat, shape, start = ops.pack_feature_maps(tm, channels_last=channels_last)
-    assert np.array_equal(feat.numpy(), feat_np)
-    assert np.array_equal(shape.numpy(), shape_np) and np.array_equal(start.numpy(), start_np)
-    assert feat.shape == (2, 3 * (24 + 6), 256)
+def test_pack_feature_maps_has_no_cpu_path():
+    """Packing runs on the GPU only (s4d_pack_feature_maps); CPU tensors are rejected loudly."""
+    maps = [torch.zeros(1, 2, 64, 4, 6), torch.zeros(1, 2, 64, 2, 3)]
+    with pytest.raises(ValueError, match="no CPU path"):
+        ops.pack_feature_maps(maps)
 
 
 def test_level_tables():
