@@ -214,6 +214,46 @@ S4D_API int s4d_pack_feature_maps(const void* const* levels, int layout, int src
                                   int64_t num_levels, const int32_t* level_hw, int64_t embed_dims, int dst_dtype,
                                   void* mc_ms_feat, void* stream);
 
+/* ---- InstanceBank (inference): temporal projection and confidence top-k -------------------
+ * Anchors are 11 fp32: x y z, log w l h, sin cos, vx vy vz.  Every array is contiguous. */
+
+/* anchor_out = the cached anchors moved by -velocity * time_interval[b] and transformed by
+ * T_temp2cur[b] (centre and velocity rotated by T[:3, :3], centre translated by T[:3, 3]; the
+ * [cos, sin] pair rotated by T[:2, :2] and stored in the (sin, cos) slots, as the reference does).
+ * Replaces InstanceBank._anchor_projection and its device form in InstanceBank.get()
+ * (model/instance_bank.py:322-369, :116-161).  The reference's get() passes -(t_now - t_cached).
+ *   anchor [bs, num, 11], T_temp2cur [bs, 4, 4], time_interval [bs] or NULL (no motion term),
+ *   anchor_out [bs, num, 11] (may equal anchor). */
+S4D_API int s4d_instance_bank_project(const float* anchor, const float* T_temp2cur, const float* time_interval,
+                                      int64_t bs, int64_t num, float* anchor_out, void* stream);
+
+/* InstanceBank.cache() (model/instance_bank.py:248-306): score = sigmoid(max over classes of
+ * confidence) (evaluated in double, rounded once), for the first num_temp anchors
+ * max(prev_conf * decay, score); the num_temp best anchors (scores descending, ties by ascending
+ * index, NaN last) are gathered.
+ *   feature [bs, A, C], anchor [bs, A, 11], confidence [bs, A, num_cls], prev_conf [bs, num_temp]
+ *   or NULL (first frame); outputs cached_feature [bs, num_temp, C], cached_anchor
+ *   [bs, num_temp, 11], cached_conf [bs, num_temp] (may be NULL), top_idx [bs, num_temp] i32
+ *   (may be NULL).  Outputs must not overlap inputs.  Implemented: A <= 4096. */
+S4D_API int s4d_instance_bank_cache(const float* feature, const float* anchor, const float* confidence,
+                                    const float* prev_conf, float decay, int64_t bs, int64_t num_anchor,
+                                    int64_t num_cls, int64_t embed_dims, int64_t num_temp, float* cached_feature,
+                                    float* cached_anchor, float* cached_conf, int32_t* top_idx, void* stream);
+
+/* InstanceBank.update() (model/instance_bank.py:188-246): for every frame whose mask byte is
+ * non-zero (|time gap| within the limit), out = [cached rows | the A - num_temp best new rows by
+ * max-over-classes confidence (same order rule as cache)]; for the others out = the frame's own
+ * rows.
+ *   feature [bs, A, C], anchor [bs, A, 11], confidence [bs, A, num_cls], cached_feature
+ *   [bs, num_temp, C], cached_anchor [bs, num_temp, 11], mask [bs] u8 or NULL (all merge);
+ *   out_feature [bs, A, C], out_anchor [bs, A, 11], new_idx [bs, A - num_temp] i32 or NULL.
+ *   Outputs must not overlap inputs.  Implemented: A <= 4096. */
+S4D_API int s4d_instance_bank_update(const float* feature, const float* anchor, const float* confidence,
+                                     const float* cached_feature, const float* cached_anchor, const uint8_t* mask,
+                                     int64_t bs, int64_t num_anchor, int64_t num_cls, int64_t embed_dims,
+                                     int64_t num_temp, float* out_feature, float* out_anchor, int32_t* new_idx,
+                                     void* stream);
+
 /* Bytes of the optional workspace of s4d_deformable_aggregation (split logits only: the
  * per-frame camera softmax factors, bs * (Ncam + 1) * L * P * G floats; 0 otherwise).
  * Host-only, launches nothing. */

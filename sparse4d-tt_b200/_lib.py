@@ -57,6 +57,9 @@ SIGNATURES = {
                                      _p, _sz, _p]),
     "s4d_dfa_camera_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "s4d_pack_feature_maps": (_int, [_p, _int, _int, _i64, _i64, _i64, _p, _i64, _int, _p, _p]),
+    "s4d_instance_bank_project": (_int, [_p, _p, _p, _i64, _i64, _p, _p]),
+    "s4d_instance_bank_cache": (_int, [_p, _p, _p, _p, C.c_float, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p]),
+    "s4d_instance_bank_update": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
     "s4d_dfa_output_proj": (_int, [_p, _i64, _p, _p, _p, _i64, _int, _p, _i64, _i64, _p, _p]),
 }
 

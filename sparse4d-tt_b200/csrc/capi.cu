@@ -302,6 +302,89 @@ int s4d_pack_feature_maps(const void* const* levels, int layout, int src_dtype, 
   return launch_pack_maps(p, static_cast<cudaStream_t>(stream));
 }
 
+int s4d_instance_bank_project(const float* anchor, const float* T_temp2cur, const float* time_interval, int64_t bs,
+                              int64_t num, float* anchor_out, void* stream) {
+  set_error("%s", "");
+  if (bs < 0 || num < 0) return fail(S4D_ERR_INVALID_ARG, "s4d_instance_bank_project: negative size");
+  if (bs * num >= kMaxElems) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_instance_bank_project: too many anchors");
+  if (bs * num == 0) return S4D_OK;
+  if (anchor == nullptr || T_temp2cur == nullptr || anchor_out == nullptr)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_instance_bank_project: null pointer");
+  IbProjectParams p{anchor, T_temp2cur, time_interval, anchor_out, (int)bs, (int)num, 11};
+  return launch_ib_project(p, static_cast<cudaStream_t>(stream));
+}
+
+static int ib_check(const char* fn, int64_t bs, int64_t num_anchor, int64_t num_cls, int64_t embed_dims,
+                    int64_t num_temp) {
+  if (bs < 0 || num_anchor <= 0 || num_cls <= 0 || embed_dims <= 0 || num_temp <= 0 || num_temp > num_anchor) {
+    set_error("%s: need bs >= 0, num_anchor, num_cls, embed_dims > 0 and 0 < num_temp <= num_anchor", fn);
+    return S4D_ERR_INVALID_ARG;
+  }
+  if (num_anchor > 4096 || bs >= 65536 || bs * num_anchor * embed_dims >= ((int64_t)1 << 40)) {
+    set_error("%s: implemented for num_anchor <= 4096 and bs < 65536", fn);
+    return S4D_ERR_UNSUPPORTED_SHAPE;
+  }
+  return S4D_OK;
+}
+
+int s4d_instance_bank_cache(const float* feature, const float* anchor, const float* confidence, const float* prev_conf,
+                            float decay, int64_t bs, int64_t num_anchor, int64_t num_cls, int64_t embed_dims,
+                            int64_t num_temp, float* cached_feature, float* cached_anchor, float* cached_conf,
+                            int32_t* top_idx, void* stream) {
+  set_error("%s", "");
+  int st = ib_check("s4d_instance_bank_cache", bs, num_anchor, num_cls, embed_dims, num_temp);
+  if (st != S4D_OK || bs == 0) return st;
+  if (feature == nullptr || anchor == nullptr || confidence == nullptr || cached_feature == nullptr ||
+      cached_anchor == nullptr)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_instance_bank_cache: null pointer");
+  IbSelectParams p{};
+  p.feature = feature;
+  p.anchor = anchor;
+  p.confidence = confidence;
+  p.prev_conf = prev_conf;
+  p.decay = decay;
+  p.out_feature = cached_feature;
+  p.out_anchor = cached_anchor;
+  p.out_conf = cached_conf;
+  p.out_idx = top_idx;
+  p.bs = (int)bs;
+  p.num_anchor = (int)num_anchor;
+  p.num_cls = (int)num_cls;
+  p.embed_dims = (int)embed_dims;
+  p.anchor_dim = 11;
+  p.num_temp = (int)num_temp;
+  return launch_ib_select(p, true, static_cast<cudaStream_t>(stream));
+}
+
+int s4d_instance_bank_update(const float* feature, const float* anchor, const float* confidence,
+                             const float* cached_feature, const float* cached_anchor, const uint8_t* mask, int64_t bs,
+                             int64_t num_anchor, int64_t num_cls, int64_t embed_dims, int64_t num_temp,
+                             float* out_feature, float* out_anchor, int32_t* new_idx, void* stream) {
+  set_error("%s", "");
+  int st = ib_check("s4d_instance_bank_update", bs, num_anchor, num_cls, embed_dims, num_temp);
+  if (st != S4D_OK || bs == 0) return st;
+  if (feature == nullptr || anchor == nullptr || confidence == nullptr || cached_feature == nullptr ||
+      cached_anchor == nullptr || out_feature == nullptr || out_anchor == nullptr)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_instance_bank_update: null pointer");
+  IbSelectParams p{};
+  p.feature = feature;
+  p.anchor = anchor;
+  p.confidence = confidence;
+  p.cached_feature = cached_feature;
+  p.cached_anchor = cached_anchor;
+  p.mask = mask;
+  p.out_feature = out_feature;
+  p.out_anchor = out_anchor;
+  p.out_idx = new_idx;
+  p.bs = (int)bs;
+  p.num_anchor = (int)num_anchor;
+  p.num_cls = (int)num_cls;
+  p.embed_dims = (int)embed_dims;
+  p.anchor_dim = 11;
+  p.num_temp = (int)num_temp;
+  return launch_ib_select(p, false, static_cast<cudaStream_t>(stream));
+}
+
 size_t s4d_dfa_camera_workspace_bytes(int64_t bs, int64_t num_cams, int64_t embed_dims) {
   if (bs <= 0 || num_cams <= 0 || embed_dims <= 0) return 0;
   return size_t(bs) * size_t(num_cams) * size_t(embed_dims) * sizeof(float);

@@ -104,6 +104,34 @@ struct PackParams {
 };
 
 int launch_pack_maps(const PackParams& p, cudaStream_t stream);
+
+// InstanceBank (instance_bank.cu).
+struct IbProjectParams {
+  const float* anchor;         // [bs, num, 11]
+  const float* T;              // [bs, 4, 4]
+  const float* time_interval;  // [bs] or null (no motion term)
+  float* out;                  // [bs, num, 11]
+  int bs, num, anchor_dim;
+};
+
+struct IbSelectParams {
+  const float* feature;     // [bs, A, C]
+  const float* anchor;      // [bs, A, D]
+  const float* confidence;  // [bs, A, num_cls]
+  const float* prev_conf;   // CACHE: [bs, num_temp] or null
+  float decay;
+  const float* cached_feature;  // UPDATE: [bs, num_temp, C]
+  const float* cached_anchor;   // UPDATE: [bs, num_temp, D]
+  const uint8_t* mask;          // UPDATE: [bs] or null (all frames merge)
+  float* out_feature;           // CACHE: [bs, num_temp, C]; UPDATE: [bs, A, C]
+  float* out_anchor;            // CACHE: [bs, num_temp, D]; UPDATE: [bs, A, D]
+  float* out_conf;              // CACHE: [bs, num_temp] or null
+  int32_t* out_idx;             // CACHE: [bs, num_temp]; UPDATE: [bs, A - num_temp]; or null
+  int bs, num_anchor, num_cls, embed_dims, anchor_dim, num_temp, sort_size;
+};
+
+int launch_ib_project(const IbProjectParams& p, cudaStream_t stream);
+int launch_ib_select(IbSelectParams p, bool cache, cudaStream_t stream);
 int launch_weights_fc(const WfcParams& p, cudaStream_t stream);
 int launch_output_proj(const OprojParams& p, cudaStream_t stream);
 

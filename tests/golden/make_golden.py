@@ -194,6 +194,30 @@ def reference_dummy(ref, name, bs):
     print(f"{name}: visible={int(masks(res)[1].sum())} -> {os.path.getsize(path)} bytes")
 
 
+def instance_bank_projection(name, seed=7, bs=2, num=600):
+    """The reference's own InstanceBank._anchor_projection (model/instance_bank.py:322-369, plain
+    torch) on seeded cached anchors, ego transforms and time gaps; inputs and outputs stored
+    whole (small)."""
+    import importlib
+
+    sys.path.insert(0, REF_ROOT)
+    ib = importlib.import_module("model.instance_bank")
+    gen = torch.Generator().manual_seed(seed)
+    anchor = syn.make_anchors(bs, num, gen)
+    T = torch.zeros(bs, 4, 4)
+    for b in range(bs):
+        yaw = float(torch.rand(1, generator=gen)) * 0.4 - 0.2
+        c, s_ = np.cos(yaw), np.sin(yaw)
+        T[b, :3, :3] = torch.tensor([[c, -s_, 0.0], [s_, c, 0.0], [0.0, 0.0, 1.0]], dtype=torch.float32)
+        T[b, :3, 3] = torch.rand(3, generator=gen) * 4.0 - 2.0
+        T[b, 3, 3] = 1.0
+    ti = -(torch.rand(bs, generator=gen) * 0.6)  # get() passes -(t_now - t_cached)
+    out = ib.InstanceBank._anchor_projection(anchor, T, ti)
+    path = os.path.join(HERE, name + ".npz")
+    np.savez_compressed(path, anchor=anchor.numpy(), T=T.numpy(), time_interval=ti.numpy(), out=out.numpy())
+    print(f"{name}: {bs}x{num} anchors -> {os.path.getsize(path)} bytes")
+
+
 def main():
     torch.set_num_threads(os.cpu_count() or 1)
     ref = import_reference()
@@ -208,6 +232,7 @@ def main():
                    feature_dtype=torch.bfloat16, large=True)
     reference_dummy(ref, "refdummy_bs1", 1)
     reference_dummy(ref, "refdummy_bs2", 2)
+    instance_bank_projection("instance_bank_projection")
 
 
 if __name__ == "__main__":

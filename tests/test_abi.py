@@ -33,7 +33,7 @@ def lib():
 
 def test_every_declared_symbol_is_exported(lib):
     names = declared_functions()
-    assert len(names) == 14, names
+    assert len(names) == 17, names
     for n in names:
         assert hasattr(lib, n), n
         assert n in L.SIGNATURES, f"{n} has no ctypes signature"
@@ -298,3 +298,16 @@ def test_pack_rejects(lib, kw, status, text):
 
 def test_pack_zero_batch_is_ok(lib):
     assert _pack(lib, bs=0)[0] == L.S4D_OK
+
+
+def test_instance_bank_rejects(lib):
+    assert lib.s4d_instance_bank_project(16, 16, None, -1, 10, 16, None) == L.S4D_ERR_INVALID_ARG
+    assert lib.s4d_instance_bank_project(None, 16, None, 1, 10, 16, None) == L.S4D_ERR_INVALID_ARG
+    assert lib.s4d_instance_bank_project(16, 16, None, 0, 10, 16, None) == L.S4D_OK
+    args = [16, 16, 16, None, 0.6, 2, 900, 10, 256, 600, 16, 16, None, None, None]
+    assert lib.s4d_instance_bank_cache(*args[:9], 901, *args[10:]) == L.S4D_ERR_INVALID_ARG  # num_temp > A
+    assert lib.s4d_instance_bank_cache(*args[:6], 5000, *args[7:]) == L.S4D_ERR_UNSUPPORTED_SHAPE
+    assert lib.s4d_instance_bank_cache(None, *args[1:]) == L.S4D_ERR_INVALID_ARG
+    uargs = [16, 16, 16, 16, 16, None, 2, 900, 10, 256, 600, 16, 16, None, None]
+    assert lib.s4d_instance_bank_update(*uargs[:11], None, *uargs[12:]) == L.S4D_ERR_INVALID_ARG
+    assert lib.s4d_instance_bank_update(*uargs[:6], 0, *uargs[7:]) == L.S4D_OK
