@@ -10,7 +10,8 @@ import os
 import threading
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_PKG, "lib", "libs4d_dfa.so")
+# The in-tree build; S4D_LIB may point at another build of the same ABI.
+LIB_PATH = os.environ.get("S4D_LIB") or os.path.join(_PKG, "lib", "libs4d_dfa.so")
 
 S4D_OK = 0
 S4D_ERR_INVALID_ARG = 1

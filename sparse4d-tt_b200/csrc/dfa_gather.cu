@@ -666,15 +666,22 @@ __global__ void __launch_bounds__(kGatherThreads) cam_softmax_prep_kernel(const 
 //   output    normalised in registers (1 / sum of the lane's group) and stored by each lane.
 // -----------------------------------------------------------------------------------------------
 // One in-bounds sample of a warp's anchor, as the merging step shares it between lanes.
+template <int G>
 struct SampleRec {
-  int4 pix;    // the 4 taps' feature rows (-1: outside the map)
-  float4 bw;   // their bilinear weights
-  int e1, e2;  // logit offsets: anchor term lp*G, camera term c*LPG + lp*G
-  int pad0, pad1;
+  int4 pix;     // the 4 taps' feature rows (-1: outside the map)
+  float4 bw;    // their bilinear weights
+  float sw[G];  // per group: unnormalised softmax weight (factorised mode), or the logit (exact mode)
 };
 
+// Resident one-warp blocks per SM the register allocator must allow: the kernel is bound by how
+// many anchors are in flight, and 28 (72 registers) measured faster than 25 (80 registers,
+// 311 vs 231 us per 32-frame launch) for bf16 maps.
+#ifndef S4D_GATHER_MIN_BLOCKS_BF16
+#define S4D_GATHER_MIN_BLOCKS_BF16 28
+#endif
 template <typename T, int NC, int NL, int NP, int G, int MODE, int WARPS>
-__global__ void __launch_bounds__(WARPS * 32) dfa_gather_warp_kernel(GatherParams p) {
+__global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BLOCKS_BF16 : 24)
+    dfa_gather_warp_kernel(GatherParams p) {
   constexpr int NLP = NL * NP;
   constexpr int LPG = NLP * G;
   constexpr int NW = NC * LPG;
@@ -683,9 +690,10 @@ __global__ void __launch_bounds__(WARPS * 32) dfa_gather_warp_kernel(GatherParam
   constexpr float kLog2e = 1.4426950408889634f;
   static_assert(LPG % 32 == 0 && 32 % G == 0 && G >= 4 && (G & (G - 1)) == 0, "warp gather shape");
   __shared__ __align__(16) int4 s_lvl[NC * NL];  // (H, W, start, ok)
+  __shared__ __align__(16) float4 s_win[NC];     // per camera: (u_lo, u_hi, v_lo, v_hi)
   __shared__ __align__(16) float s_ea[MODE == 1 ? WARPS * LPG : 1];
   __shared__ unsigned char s_surv[WARPS][32];
-  __shared__ SampleRec s_rec[WARPS][32];
+  __shared__ __align__(16) SampleRec<G> s_rec[WARPS][32];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < NC * NL; i += WARPS * 32) {
@@ -695,6 +703,23 @@ __global__ void __launch_bounds__(WARPS * 32) dfa_gather_warp_kernel(GatherParam
     if (!ok && c >= p.cam_begin && c < p.cam_end && p.error_flag != nullptr && blockIdx.x == 0)
       atomicOr(p.error_flag, S4D_FLAG_BAD_LEVEL);
     s_lvl[i] = make_int4(H, W, st, ok ? 1 : 0);
+    // A sample of level l has an in-bounds tap iff u in (-0.5 / W, 1 + 0.5 / W) (v likewise), so
+    // the union over the camera's valid levels is the window of its narrowest level.  The
+    // survivor test below uses it (1e-3 wider, a superset of the exact per-level test).
+    if (i % NL == NL - 1) {
+      int wmin = 0, hmin = 0;
+      for (int l = 0; l < NL; ++l) {
+        const int j = c * NL + l;
+        const int Hl = p.spatial_shape[2 * j], Wl = p.spatial_shape[2 * j + 1], sl = p.scale_start[j];
+        if (Hl > 0 && Wl > 0 && sl >= 0 && (int64_t)sl + (int64_t)Hl * Wl <= p.num_feat) {
+          wmin = wmin == 0 || Wl < wmin ? Wl : wmin;
+          hmin = hmin == 0 || Hl < hmin ? Hl : hmin;
+        }
+      }
+      s_win[c] = wmin == 0 ? make_float4(1.0f, 0.0f, 1.0f, 0.0f)  // no valid level: empty window
+                           : make_float4(-0.5f / wmin - 1e-3f, 1.0f + 0.5f / wmin + 1e-3f, -0.5f / hmin - 1e-3f,
+                                         1.0f + 0.5f / hmin + 1e-3f);
+    }
   }
   __syncthreads();  // the only block barrier: every thread reaches it before any warp leaves
   const int64_t anchor_lin = (int64_t)blockIdx.x * WARPS + warp;
@@ -760,9 +785,12 @@ __global__ void __launch_bounds__(WARPS * 32) dfa_gather_warp_kernel(GatherParam
     const int q = base + lane;
     const int cq = q / NP;
     float2 uv = make_float2(-4.0f, -4.0f);
-    if (q < NPAIR) uv = __ldg(locp + q);
-    const bool maybe = q < NPAIR && cq >= p.cam_begin && cq < p.cam_end && uv.x > -0.5f && uv.x < 1.5f &&
-                       uv.y > -0.5f && uv.y < 1.5f;
+    bool maybe = false;
+    if (q < NPAIR) {
+      uv = __ldg(locp + q);
+      const float4 wn = s_win[cq];
+      maybe = cq >= p.cam_begin && cq < p.cam_end && uv.x > wn.x && uv.x < wn.y && uv.y > wn.z && uv.y < wn.w;
+    }
     const uint32_t keep = __ballot_sync(0xffffffffu, maybe);
     if (keep == 0u) continue;
     if (maybe) s_surv[warp][__popc(keep & lt)] = (unsigned char)lane;
@@ -781,7 +809,7 @@ __global__ void __launch_bounds__(WARPS * 32) dfa_gather_warp_kernel(GatherParam
       const int cs = qs / NP, ps = qs - (qs / NP) * NP;
       uint64_t key = 0xffffffff00000000ull | (uint32_t)lane;  // invalid lanes only match themselves
       bool valid = false;
-      SampleRec rec;
+      SampleRec<G> rec;
       if (idx < n) {
         const int4 lv = s_lvl[cs * NL + l];
         const float Wf = (float)lv.y, Hf = (float)lv.x;
@@ -798,8 +826,18 @@ __global__ void __launch_bounds__(WARPS * 32) dfa_gather_warp_kernel(GatherParam
           rec.bw = make_float4((x1f - ix) * (y1f - iy), (ix - x0f) * (y1f - iy), (x1f - ix) * (iy - y0f),
                                (ix - x0f) * (iy - y0f));
           const int lp = l * NP + ps;
-          rec.e1 = lp * G;
-          rec.e2 = cs * LPG + lp * G;
+          const int e1 = lp * G, e2 = cs * LPG + lp * G;  // anchor-term and camera-term offsets
+          // This sample's weight for every group, computed once here rather than by every lane of
+          // every block it joins: exp(wa - M1) * exp(wc - M2) from the per-anchor table and the
+          // per-frame camera factors, or (exact mode) the logit itself.
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            if (!exact) {
+              rec.sw[g] = ea[e1 + g] * __ldg(ec_tab + e2 + g);
+            } else {
+              rec.sw[g] = MODE == 0 ? __ldg(wrow + e2 + g) : __ldg(wrow + e1 + g) + __ldg(wcam + e2 + g);
+            }
+          }
           // (camera, level) and the top-left tap (x0, y0 >= -1) identify the 2x2 block
           key = ((uint64_t)(cs * NL + l) << 32) | (uint32_t)((y0 + 1) * (lv.y + 1) + (x0 + 1));
           valid = true;
@@ -827,14 +865,8 @@ __global__ void __launch_bounds__(WARPS * 32) dfa_gather_warp_kernel(GatherParam
           const int j = __ffs(mem) - 1;
           mem &= mem - 1u;
           const float4 bw = s_rec[warp][j].bw;
-          const int i1 = s_rec[warp][j].e1 + gch, i2 = s_rec[warp][j].e2 + gch;
-          float sw;
-          if (!exact) {
-            sw = ea[i1] * __ldg(ec_tab + i2);
-          } else {
-            const float lg = MODE == 0 ? __ldg(wrow + i2) : __ldg(wrow + i1) + __ldg(wcam + i2);
-            sw = ex2_approx(fmaf(lg, kLog2e, -mlg));
-          }
+          float sw = s_rec[warp][j].sw[gch];
+          if (exact) sw = ex2_approx(fmaf(sw, kLog2e, -mlg));
           w4.x = fmaf(bw.x, sw, w4.x);
           w4.y = fmaf(bw.y, sw, w4.y);
           w4.z = fmaf(bw.z, sw, w4.z);
