@@ -178,7 +178,9 @@ S4D_API int s4d_kps_project_fused(const float* key_points, const float* anchor, 
  *                     split: weights [bs, A, L, P, G] is the per-anchor term and weights_cam
  *                     [bs, Ncam, L, P, G] the per-camera term; logit = weights + weights_cam.
  *   weights_are_logits 1: softmax over (cam, level, pt) per group first (over ALL Ncam cameras
- *                     even when [cam_begin, cam_end) is a sub-range); 0: use as given
+ *                     even when [cam_begin, cam_end) is a sub-range); 0: use as given;
+ *                     2: as 1, split logits whose per-frame camera factors are already in the
+ *                     workspace (from s4d_dfa_camera_factors; the Sparse4D v3 shape only)
  *   cam_begin/cam_end only cameras in [cam_begin, cam_end) are sampled (camera sharding)
  *   out               [bs, A, C] f32, summed over points
  *   error_flag        optional [1] i32, OR-ed with S4D_FLAG_* bits
@@ -253,6 +255,17 @@ S4D_API int s4d_instance_bank_update(const float* feature, const float* anchor, 
                                      int64_t bs, int64_t num_anchor, int64_t num_cls, int64_t embed_dims,
                                      int64_t num_temp, float* out_feature, float* out_anchor, int32_t* new_idx,
                                      void* stream);
+
+/* The per-frame camera factors of the split-logit softmax, written into the workspace that
+ * s4d_deformable_aggregation then reads with weights_are_logits = 2: per frame and (level, point,
+ * group) column, exp(weights_cam - M2[group]) for every camera and their sum over cameras
+ * (M2 = the frame's per-group maximum).  They depend only on the per-camera term, so they can be
+ * computed once per frame, e.g. next to s4d_dfa_camera_logits on another stream.
+ *   weights_cam [bs, Ncam, L, P, G]; workspace >= s4d_dfa_workspace_bytes(..., split_logits=1)
+ *   bytes, 16-byte aligned.  Implemented: Ncam 6, L 4, P 13, G 8. */
+S4D_API int s4d_dfa_camera_factors(const float* weights_cam, int64_t bs, int64_t num_cams, int64_t num_levels,
+                                   int64_t num_pts, int64_t num_groups, void* workspace, size_t workspace_bytes,
+                                   void* stream);
 
 /* Bytes of the optional workspace of s4d_deformable_aggregation (split logits only: the
  * per-frame camera softmax factors, bs * (Ncam + 1) * L * P * G floats; 0 otherwise).

@@ -53,6 +53,7 @@ SIGNATURES = {
                                           _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                           _p, _p, _p, _sz, _p]),
     "s4d_dfa_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _int]),
+    "s4d_dfa_camera_factors": (_int, [_p, _i64, _i64, _i64, _i64, _i64, _p, _sz, _p]),
     "s4d_dfa_weights_fc": (_int, [_p, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _p]),
     "s4d_dfa_camera_logits": (_int, [_p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p, _p,
                                      _p, _sz, _p]),

@@ -51,6 +51,21 @@ size_t s4d_kps_workspace_bytes(int64_t bs, int64_t num_anchor, int64_t num_cams,
   return kps_workspace_bytes(bs * num_anchor * num_cams * num_pts);
 }
 
+int s4d_dfa_camera_factors(const float* weights_cam, int64_t bs, int64_t num_cams, int64_t num_levels,
+                           int64_t num_pts, int64_t num_groups, void* workspace, size_t workspace_bytes, void* stream) {
+  set_error("%s", "");
+  if (bs < 0 || num_cams <= 0 || num_levels <= 0 || num_pts <= 0 || num_groups <= 0)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_camera_factors: bad sizes");
+  if (bs >= (1 << 24)) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_camera_factors: too many frames");
+  if (bs == 0) return S4D_OK;
+  if (weights_cam == nullptr || workspace == nullptr || !aligned(workspace, 16))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_camera_factors: null weights_cam or missing / misaligned workspace");
+  if (workspace_bytes < gather_workspace_bytes(bs, (int)num_cams, (int)num_levels, (int)num_pts, (int)num_groups))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_camera_factors: workspace smaller than s4d_dfa_workspace_bytes()");
+  return launch_cam_factors(weights_cam, static_cast<float*>(workspace), (int)bs, (int)num_cams, (int)num_levels,
+                            (int)num_pts, (int)num_groups, static_cast<cudaStream_t>(stream));
+}
+
 size_t s4d_dfa_workspace_bytes(int64_t bs, int64_t num_cams, int64_t num_levels, int64_t num_pts,
                                int64_t num_groups, int split_logits) {
   if (!split_logits || bs <= 0 || num_cams <= 0 || num_levels <= 0 || num_pts <= 0 || num_groups <= 0) return 0;
@@ -166,8 +181,17 @@ int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, int64_t n
     return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: need 0 <= cam_begin <= cam_end <= num_cams");
   if (weights_cam != nullptr && layout != S4D_LAYOUT_CAM_MAJOR)
     return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: split logits (weights_cam) need CAM_MAJOR");
+  if (weights_are_logits < 0 || weights_are_logits > 2)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: weights_are_logits must be 0, 1 or 2");
   if (weights_cam != nullptr && !weights_are_logits)
     return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: split weights are only defined for logits");
+  if (weights_are_logits == 2 && (weights_cam == nullptr || workspace == nullptr))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: prepared camera factors (weights_are_logits 2) "
+                                     "need weights_cam and the workspace they were written to");
+  if (weights_are_logits == 2 && !(num_cams == 6 && num_levels == 4 && num_pts == 13 && num_groups == 8 &&
+                                   layout == S4D_LAYOUT_CAM_MAJOR))
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: prepared camera factors are implemented "
+                                           "for 6 cameras, 4 levels, 13 points, 8 groups");
   if (embed_dims != 256)
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: embed_dims must be 256");
   if (num_groups > 32 || (num_groups & (num_groups - 1)) != 0)
@@ -205,6 +229,7 @@ int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, int64_t n
   p.cam_begin = (int)cam_begin;
   p.cam_end = (int)cam_end;
   p.logits = weights_are_logits ? 1 : 0;
+  p.factors_ready = weights_are_logits == 2 ? 1 : 0;
   p.layout = layout;
   p.cam_ws = nullptr;
   if (weights_cam != nullptr && workspace != nullptr) {

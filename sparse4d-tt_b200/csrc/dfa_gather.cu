@@ -908,15 +908,27 @@ size_t gather_smem_bytes(int ncam, int nl, int np, int G, int cam_begin, int cam
   return gather_smem_layout(ncam, nl, np, G, cam_begin, cam_end).bytes;
 }
 
+int launch_cam_factors(const float* weights_cam, float* cam_ws, int bs, int ncam, int nl, int np, int G,
+                       cudaStream_t stream) {
+  if (ncam != kFastNC || nl != kFastNL || np != kFastNP || G != kFastG)
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "camera factors: implemented for 6 cameras, 4 levels, 13 points, 8 groups");
+  if (bs <= 0) return S4D_OK;
+  constexpr int LPG = kFastNL * kFastNP * kFastG;
+  cam_softmax_prep_kernel<kFastNC, LPG, kFastG><<<(unsigned)bs, kGatherThreads, 0, stream>>>(weights_cam, cam_ws);
+  return cuda_check(cudaGetLastError(), "cam_softmax_prep_kernel launch");
+}
+
 int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream) {
   const size_t smem = gather_smem_bytes(p.num_cams, p.num_levels, p.num_pts, p.num_groups, p.cam_begin, p.cam_end);
   const unsigned grid = (unsigned)((int64_t)p.bs * p.num_anchor);
   if (fast_path_ok(p) && p.weights_cam != nullptr && p.cam_ws != nullptr) {
-    // split logits with a workspace: per-frame camera factors, then one warp per anchor
-    constexpr int LPG = kFastNL * kFastNP * kFastG;
-    cam_softmax_prep_kernel<kFastNC, LPG, kFastG><<<(unsigned)p.bs, kGatherThreads, 0, stream>>>(p.weights_cam, p.cam_ws);
-    int st = cuda_check(cudaGetLastError(), "cam_softmax_prep_kernel launch");
-    if (st) return st;
+    // split logits with a workspace: per-frame camera factors (unless already there), then one
+    // warp per anchor
+    if (!p.factors_ready) {
+      int st = launch_cam_factors(p.weights_cam, p.cam_ws, p.bs, p.num_cams, p.num_levels, p.num_pts, p.num_groups,
+                                  stream);
+      if (st) return st;
+    }
     const unsigned wgrid = (unsigned)(((int64_t)p.bs * p.num_anchor + kWarpBlock - 1) / kWarpBlock);
     if (feat_dtype == S4D_DTYPE_BF16)
       dfa_gather_warp_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock>

@@ -47,6 +47,7 @@ struct GatherParams {
   int cam_begin, cam_end;
   int logits;
   int layout;
+  int factors_ready;  // split logits: cam_ws already holds the camera factors (no prep launch)
 };
 
 // Tensor-core linears (linear_tc.cu).  Row strides are in floats.
@@ -140,6 +141,8 @@ int launch_kps_project(KpsParams k, int32_t* visible_idx, int32_t* visible_count
 size_t kps_workspace_bytes(int64_t total);
 
 int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream);
+int launch_cam_factors(const float* weights_cam, float* cam_ws, int bs, int ncam, int nl, int np, int G,
+                       cudaStream_t stream);
 size_t gather_workspace_bytes(int64_t bs, int ncam, int nl, int np, int G);
 size_t gather_smem_bytes(int ncam, int nl, int np, int G, int cam_begin, int cam_end);
 

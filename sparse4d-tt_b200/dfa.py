@@ -156,6 +156,9 @@ class DeformableFeatureAggregation:
         self._cached_camera_embed = None
         self._cached_camera_logits = None
         self._cached_camera_ws = None
+        self._cached_camera_factors = None
+        # the Sparse4D v3 shape has a kernel for the per-frame camera softmax factors
+        self._factors_ok = (num_cams, num_levels, num_pts, num_groups) == (6, 4, 13, 8)
         self._side: Optional[torch.cuda.Stream] = None
         self._side_pending = False
         self._cached_proj_rm = None
@@ -207,14 +210,20 @@ class DeformableFeatureAggregation:
                 self._side.wait_stream(torch.cuda.current_stream(self.device))
                 ctx = torch.cuda.stream(self._side)
                 self._side_pending = True
+            factors = None
+            if self._factors_ok:
+                factors = ops.dfa_workspace(bs, self.num_cams, self.num_levels, self.num_pts, self.num_groups,
+                                            self.device)
             with ctx:
                 ops.camera_logits_into(wc, projection_mat, self.cam_linear1_weight, self.cam_linear1_bias,
                                        self.cam_ln1_weight, self.cam_ln1_bias, self.cam_linear2_weight,
                                        self.cam_linear2_bias, self.cam_ln2_weight, self.cam_ln2_bias,
                                        self.weights_fc_weight, self.weights_fc_bias, camera_embed=emb,
                                        workspace=ws)
+                if factors is not None:  # the softmax's per-frame camera factors, off the gather's path
+                    ops.camera_factors_into(factors, wc)
             self._cached_camera_embed, self._cached_camera_logits, self._cam_key = emb, wc, key
-            self._cached_camera_ws = ws
+            self._cached_camera_ws, self._cached_camera_factors = ws, factors
         return self._cached_camera_logits
 
     def _join_side(self) -> None:
@@ -226,6 +235,7 @@ class DeformableFeatureAggregation:
         """Drops the per-frame camera caches (what the head does at the start of every frame)."""
         self._cached_camera_embed = None
         self._cached_camera_logits = None
+        self._cached_camera_factors = None
         self._cam_key = None
 
     def _get_weights(self, instance_feature: Tensor, anchor_embed: Tensor, projection_mat: Tensor, bs: int,
@@ -303,11 +313,13 @@ class DeformableFeatureAggregation:
         if log is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
-        ws = None
+        ws, ready = None, False
         if logits_cam is not None:
-            ws = ops.dfa_workspace(bs, self.num_cams, self.num_levels, self.num_pts, self.num_groups, dev)
+            ws, ready = self._cached_camera_factors, self._cached_camera_factors is not None
+            if ws is None:
+                ws = ops.dfa_workspace(bs, self.num_cams, self.num_levels, self.num_pts, self.num_groups, dev)
         ops.deformable_aggregation_into(feats, mc_ms_feat, spatial_shape, scale_start, loc, logits, True,
-                                        logits_cam, cam_begin, cam_end, workspace=ws)
+                                        logits_cam, cam_begin, cam_end, workspace=ws, factors_ready=ready)
         if log is not None:
             ev[1].record()
             log.append(ev)

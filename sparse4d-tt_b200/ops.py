@@ -234,10 +234,11 @@ def deformable_aggregation_into(out: Tensor, mc_ms_feat: Tensor, spatial_shape: 
                                 sample_location: Tensor, weights: Tensor, weights_are_logits: bool = True,
                                 weights_cam: Optional[Tensor] = None, cam_begin: int = 0, cam_end: int = -1,
                                 layout: Union[int, str] = "cam_major", error_flag: Optional[Tensor] = None,
-                                workspace: Optional[Tensor] = None) -> Tensor:
+                                workspace: Optional[Tensor] = None, factors_ready: bool = False) -> Tensor:
     """Writes the fused gather into ``out [bs, A, C]`` (fp32) and returns it.  With split
     logits (``weights_cam``) an optional ``workspace`` of ``dfa_workspace_bytes(...)`` bytes
-    lets the kernel factorise the softmax."""
+    lets the kernel factorise the softmax; ``factors_ready=True`` says ``camera_factors_into``
+    already wrote the factors there (the gather call then launches no factor kernel)."""
     name = "deformable_aggregation"
     lay = LAYOUTS[layout] if isinstance(layout, str) else int(layout)
     dev = _require_cuda(name, out, mc_ms_feat, spatial_shape, scale_start_index, sample_location, weights,
@@ -265,7 +266,8 @@ def deformable_aggregation_into(out: Tensor, mc_ms_feat: Tensor, spatial_shape: 
     st = L.lib().s4d_deformable_aggregation(
         mc_ms_feat.data_ptr(), L.S4D_DTYPE_BF16 if mc_ms_feat.dtype == torch.bfloat16 else L.S4D_DTYPE_F32,
         int(mc_ms_feat.shape[1]), spatial_shape.data_ptr(), scale_start_index.data_ptr(),
-        sample_location.data_ptr(), weights.data_ptr(), _ptr(weights_cam), 1 if weights_are_logits else 0, lay,
+        sample_location.data_ptr(), weights.data_ptr(), _ptr(weights_cam),
+        (2 if factors_ready else 1) if weights_are_logits else 0, lay,
         bs, A, nc, nl, P, G, C, int(cam_begin), ce, out.data_ptr(), _ptr(error_flag), _ptr(workspace), ws_bytes,
         _stream_ptr(dev))
     L.check(name, st)
@@ -276,6 +278,22 @@ def dfa_workspace_bytes(bs: int, num_cams: int, num_levels: int, num_pts: int, n
                         split_logits: bool) -> int:
     return int(L.lib().s4d_dfa_workspace_bytes(bs, num_cams, num_levels, num_pts, num_groups,
                                                1 if split_logits else 0))
+
+
+def camera_factors_into(workspace: Tensor, weights_cam: Tensor) -> Tensor:
+    """The per-frame camera softmax factors of split logits ``weights_cam [bs, Ncam, L, P, G]``
+    into ``workspace`` (from ``dfa_workspace``), for ``deformable_aggregation_into(...,
+    workspace=workspace, factors_ready=True)``."""
+    name = "camera_factors"
+    dev = _require_cuda(name, workspace, weights_cam)
+    _check_contig(name, workspace=workspace, weights_cam=weights_cam)
+    _check_dtype(name, weights_cam, (torch.float32,), "weights_cam")
+    _require(weights_cam.dim() == 5, "weights_cam must be [bs, Ncam, L, P, G]")
+    bs, nc, nl, npt, g = (int(v) for v in weights_cam.shape)
+    st = L.lib().s4d_dfa_camera_factors(weights_cam.data_ptr(), bs, nc, nl, npt, g, workspace.data_ptr(),
+                                        workspace.numel() * workspace.element_size(), _stream_ptr(dev))
+    L.check(name, st)
+    return workspace
 
 
 def dfa_workspace(bs: int, num_cams: int, num_levels: int, num_pts: int, num_groups: int,

@@ -33,7 +33,7 @@ def lib():
 
 def test_every_declared_symbol_is_exported(lib):
     names = declared_functions()
-    assert len(names) == 17, names
+    assert len(names) == 18, names
     for n in names:
         assert hasattr(lib, n), n
         assert n in L.SIGNATURES, f"{n} has no ctypes signature"
@@ -311,3 +311,14 @@ def test_instance_bank_rejects(lib):
     uargs = [16, 16, 16, 16, 16, None, 2, 900, 10, 256, 600, 16, 16, None, None]
     assert lib.s4d_instance_bank_update(*uargs[:11], None, *uargs[12:]) == L.S4D_ERR_INVALID_ARG
     assert lib.s4d_instance_bank_update(*uargs[:6], 0, *uargs[7:]) == L.S4D_OK
+
+
+def test_prepared_factors_rejects(lib):
+    st, msg = _gather(lib, logits=2, wc=8)  # no workspace
+    assert st == L.S4D_ERR_INVALID_ARG and "prepared" in msg
+    st, msg = _gather(lib, logits=2, wc=None, ws=16, wsb=1 << 20)
+    assert st == L.S4D_ERR_INVALID_ARG and "prepared" in msg
+    st, msg = _gather(lib, logits=3)
+    assert st == L.S4D_ERR_INVALID_ARG and "0, 1 or 2" in msg
+    assert lib.s4d_dfa_camera_factors(16, 2, 6, 4, 13, 8, 16, 16, None) == L.S4D_ERR_INVALID_ARG  # too small
+    assert lib.s4d_dfa_camera_factors(16, 0, 6, 4, 13, 8, None, 0, None) == L.S4D_OK

@@ -276,3 +276,24 @@ def test_gather_linearity_full_size(cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(o2, o1 * 2)
     assert pcc(ob.cpu(), o1.cpu()) >= BF16_PCC
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gather_prepared_camera_factors(cuda_device, dtype):
+    """Factors written by camera_factors_into (as the module does on its camera stream) and read
+    with factors_ready=True give exactly the result of the gather call computing them itself."""
+    maps, uv, _ = _small_case(21, bs=2, A=90)
+    gen = torch.Generator().manual_seed(23)
+    wa = (torch.randn(2, 90, 4, 13, 8, generator=gen) * 2).cuda()
+    wc = (torch.randn(2, 6, 4, 13, 8, generator=gen) * 2).cuda()
+    d = torch.device("cuda:0")
+    feat, shape, start = ops.pack_feature_maps([m.to(d) for m in maps], dtype=dtype)
+    loc = uv.contiguous().to(d)
+    ws_a = ops.dfa_workspace(2, 6, 4, 13, 8, d)
+    a = torch.empty(2, 90, 256, device=d)
+    ops.deformable_aggregation_into(a, feat, shape, start, loc, wa, True, wc, workspace=ws_a)
+    ws_b = ops.camera_factors_into(ops.dfa_workspace(2, 6, 4, 13, 8, d), wc)
+    b = torch.empty(2, 90, 256, device=d)
+    ops.deformable_aggregation_into(b, feat, shape, start, loc, wa, True, wc, workspace=ws_b, factors_ready=True)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b) and torch.equal(ws_a, ws_b)
