@@ -18,6 +18,9 @@
 // same expression order bit for bit:
 //   X_r = ((P[r][0]*px + P[r][1]*py) + P[r][2]*pz) + P[r][3];   z = X_2 < 1e-5 ? 1e-5 : X_2
 //   u = (X_0 / z) / w;   v = (X_1 / z) / h
+// u and v are first formed with one fast division each; where either lies within 1e-5 of 0 or 1
+// (or is not finite) the correctly rounded divisions above are used instead, so the visibility
+// decisions are those of the exact expression and the sample locations are within a few ulp.
 #include "params.cuh"
 
 namespace s4d {
@@ -119,8 +122,16 @@ __global__ void __launch_bounds__(kKpsThreads) kps_project_kernel(KpsParams k) {
       const bool in_front = X2 > 1e-5f;
       const float z = X2 < 1e-5f ? 1e-5f : X2;  // torch.clamp(min=1e-5): NaN stays NaN
       const float* wh = k.wh + (b * k.num_cams + c) * 2;
-      const float u = __fdiv_rn(__fdiv_rn(X0, z), wh[0]);
-      const float v = __fdiv_rn(__fdiv_rn(X1, z), wh[1]);
+      // Fast quotients first (a few ulp from the correctly rounded (X / z) / w); the exact IEEE
+      // divisions are redone where a fast u or v lies within 1e-5 of the frustum bounds 0 and 1,
+      // the only place the two could disagree on visibility, so masks and indices stay exact.
+      float u = __fdividef(X0, z * wh[0]);
+      float v = __fdividef(X1, z * wh[1]);
+      if (fabsf(u) < 1e-5f || fabsf(u - 1.0f) < 1e-5f || fabsf(v) < 1e-5f || fabsf(v - 1.0f) < 1e-5f ||
+          !(fabsf(u) < 1e30f && fabsf(v) < 1e30f)) {
+        u = __fdiv_rn(__fdiv_rn(X0, z), wh[0]);
+        v = __fdiv_rn(__fdiv_rn(X1, z), wh[1]);
+      }
       vis = in_front && u >= 0.0f && u <= 1.0f && v >= 0.0f && v <= 1.0f;
       if (k.mask != nullptr) k.mask[e] = in_front ? 1 : 0;
       if (k.loc != nullptr) {
