@@ -124,6 +124,24 @@ S4D_API int s4d_kps_project(const float* anchor, int64_t anchor_dim, const float
                     float* key_points, float* sample_location, uint8_t* depth_mask, int32_t* visible_idx,
                     int32_t* visible_count, void* workspace, size_t workspace_bytes, void* stream);
 
+/* s4d_kps_project with the learnable keypoint logits computed in the kernel from the instance
+ * feature: logit[n, o] = learnable_fc_bias[o] + instance_feature[n, :] . learnable_fc_weight[o, :]
+ * (fp32), the keypoint generator's learnable_fc (model/deformable_feature_aggregation.py:651-677,
+ * test/dfa_pcc.py:231-233) fused with the projection.  The call then depends only on the layer's
+ * inputs, not on another linear's output.
+ *   instance_feature    [bs * A, embed_dims] rows of stride instance_ld (floats), 16-byte aligned
+ *   learnable_fc_weight [num_learnable * 3, embed_dims], 16-byte aligned; learnable_fc_bias or NULL
+ * instance_ld is a multiple of 4.  Implemented: embed_dims 256, num_learnable <= 10,
+ * Ncam * P >= 57 (Sparse4D: 6 * 13).  Other arguments as s4d_kps_project. */
+S4D_API int s4d_kps_project_linear(const float* anchor, int64_t anchor_dim, const float* fix_scale, int64_t num_fix,
+                                   const float* instance_feature, int64_t instance_ld,
+                                   const float* learnable_fc_weight, const float* learnable_fc_bias,
+                                   int64_t num_learnable, int64_t embed_dims, const float* projection_mat,
+                                   const float* image_wh, int64_t bs, int64_t num_anchor, int64_t num_cams,
+                                   int layout, float* key_points, float* sample_location, uint8_t* depth_mask,
+                                   int32_t* visible_idx, int32_t* visible_count, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
 /*
  * s4d_kps_project without a workspace, for callers that cannot allocate device memory (an FFI
  * host without a CUDA allocator, a fixed device-memory budget, a loop that must not allocate

@@ -46,6 +46,8 @@ SIGNATURES = {
     "s4d_kps_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
     "s4d_kps_project": (_int, [_p, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _int,
                                _p, _p, _p, _p, _p, _p, _sz, _p]),
+    "s4d_kps_project_linear": (_int, [_p, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _i64, _p, _p, _i64, _i64, _i64,
+                                      _int, _p, _p, _p, _p, _p, _p, _sz, _p]),
     "s4d_kps_project_noalloc": (_int, [_p, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _int,
                                        _p, _p, _p, _p, _p, _p]),
     "s4d_kps_project_fused": (_int, [_p, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _p]),

@@ -72,11 +72,20 @@ size_t s4d_dfa_workspace_bytes(int64_t bs, int64_t num_cams, int64_t num_levels,
   return gather_workspace_bytes(bs, (int)num_cams, (int)num_levels, (int)num_pts, (int)num_groups);
 }
 
-int s4d_kps_project(const float* anchor, int64_t anchor_dim, const float* fix_scale, int64_t num_fix,
-                    const float* learnable, int64_t num_learnable, const float* projection_mat,
-                    const float* image_wh, int64_t bs, int64_t num_anchor, int64_t num_cams, int layout,
-                    float* key_points, float* sample_location, uint8_t* depth_mask, int32_t* visible_idx,
-                    int32_t* visible_count, void* workspace, size_t workspace_bytes, void* stream) {
+// The learnable_fc inputs of s4d_kps_project_linear (null for s4d_kps_project).
+struct KpsLinear {
+  const float* inst;
+  int64_t inst_ld;
+  const float* w;
+  const float* b;
+  int64_t embed_dims;
+};
+
+static int kps_entry(const KpsLinear* lin, const float* anchor, int64_t anchor_dim, const float* fix_scale,
+                     int64_t num_fix, const float* learnable, int64_t num_learnable, const float* projection_mat,
+                     const float* image_wh, int64_t bs, int64_t num_anchor, int64_t num_cams, int layout,
+                     float* key_points, float* sample_location, uint8_t* depth_mask, int32_t* visible_idx,
+                     int32_t* visible_count, void* workspace, size_t workspace_bytes, void* stream) {
   set_error("%s", "");
   if (bs < 0 || num_anchor < 0 || num_cams < 0 || num_fix < 0 || num_learnable < 0)
     return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: negative size");
@@ -98,8 +107,25 @@ int s4d_kps_project(const float* anchor, int64_t anchor_dim, const float* fix_sc
   }
   if (anchor == nullptr || projection_mat == nullptr || image_wh == nullptr)
     return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: null input pointer");
-  if ((num_fix > 0 && fix_scale == nullptr) || (num_learnable > 0 && learnable == nullptr))
+  if ((num_fix > 0 && fix_scale == nullptr) || (num_learnable > 0 && learnable == nullptr && lin == nullptr))
     return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: null fix_scale / learnable with a non-zero count");
+  if (lin != nullptr && num_learnable > 0) {
+    if (lin->inst == nullptr || lin->w == nullptr)
+      return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project_linear: null instance_feature / learnable_fc_weight");
+    if (lin->embed_dims != 256)
+      return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project_linear: embed_dims must be 256");
+    if (num_learnable * 3 > kKpsMaxFusedLogits)
+      return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project_linear: at most 10 learnable keypoints");
+    if (lin->inst_ld < lin->embed_dims || lin->inst_ld % 4 != 0)
+      return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project_linear: instance_ld must be >= embed_dims and a multiple of 4");
+    if (!aligned(lin->inst, 16) || !aligned(lin->w, 16) || (lin->b != nullptr && !aligned(lin->b, 4)))
+      return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project_linear: instance_feature and learnable_fc_weight must be "
+                                       "16-byte aligned");
+    // the anchors one block of 1024 elements can touch must fit the kernel's staging
+    if (1024 / (num_cams * num_pts) + 2 > kKpsMaxFusedAnchors)
+      return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project_linear: needs Ncam * P >= 57 (at most 20 anchors per "
+                                             "1024 elements)");
+  }
   if (sample_location != nullptr && !aligned(sample_location, 8))
     return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: sample_location must be 8-byte aligned");
   if (visible_idx != nullptr && !aligned(visible_idx, 16))
@@ -129,7 +155,38 @@ int s4d_kps_project(const float* anchor, int64_t anchor_dim, const float* fix_sc
   k.key_points = key_points;
   k.loc = sample_location;
   k.mask = depth_mask;
+  if (lin != nullptr && num_learnable > 0) {
+    k.learnable = nullptr;
+    k.inst = lin->inst;
+    k.inst_ld = lin->inst_ld;
+    k.w_kps = lin->w;
+    k.b_kps = lin->b;
+    k.embed_dims = (int)lin->embed_dims;
+  }
   return launch_kps_project(k, visible_idx, visible_count, workspace, st);
+}
+
+int s4d_kps_project(const float* anchor, int64_t anchor_dim, const float* fix_scale, int64_t num_fix,
+                    const float* learnable, int64_t num_learnable, const float* projection_mat,
+                    const float* image_wh, int64_t bs, int64_t num_anchor, int64_t num_cams, int layout,
+                    float* key_points, float* sample_location, uint8_t* depth_mask, int32_t* visible_idx,
+                    int32_t* visible_count, void* workspace, size_t workspace_bytes, void* stream) {
+  return kps_entry(nullptr, anchor, anchor_dim, fix_scale, num_fix, learnable, num_learnable, projection_mat,
+                   image_wh, bs, num_anchor, num_cams, layout, key_points, sample_location, depth_mask, visible_idx,
+                   visible_count, workspace, workspace_bytes, stream);
+}
+
+int s4d_kps_project_linear(const float* anchor, int64_t anchor_dim, const float* fix_scale, int64_t num_fix,
+                           const float* instance_feature, int64_t instance_ld, const float* learnable_fc_weight,
+                           const float* learnable_fc_bias, int64_t num_learnable, int64_t embed_dims,
+                           const float* projection_mat, const float* image_wh, int64_t bs, int64_t num_anchor,
+                           int64_t num_cams, int layout, float* key_points, float* sample_location,
+                           uint8_t* depth_mask, int32_t* visible_idx, int32_t* visible_count, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  const KpsLinear lin{instance_feature, instance_ld, learnable_fc_weight, learnable_fc_bias, embed_dims};
+  return kps_entry(&lin, anchor, anchor_dim, fix_scale, num_fix, nullptr, num_learnable, projection_mat, image_wh,
+                   bs, num_anchor, num_cams, layout, key_points, sample_location, depth_mask, visible_idx,
+                   visible_count, workspace, workspace_bytes, stream);
 }
 
 int s4d_kps_project_fused(const float* key_points, const float* anchor, int64_t anchor_dim,

@@ -38,8 +38,10 @@ __device__ __forceinline__ float sigmoid_rn(float x) {
   return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
 }
 
-// Rotated + translated keypoint p of anchor n (fp32, fixed order).
-__device__ __forceinline__ void keypoint(const KpsParams& k, uint32_t n, int p, float& px, float& py, float& pz) {
+// Rotated + translated keypoint p of anchor n (fp32, fixed order); `lg` holds the anchor's
+// learnable logits (global memory, or the block's shared-memory copy).
+__device__ __forceinline__ void keypoint(const KpsParams& k, uint32_t n, int p, const float* lg_anchor, float& px,
+                                         float& py, float& pz) {
   const float* a = k.anchor + (int64_t)n * k.anchor_dim;
   float kx, ky, kz;
   if (k.kp_pre != nullptr) {
@@ -55,7 +57,7 @@ __device__ __forceinline__ void keypoint(const KpsParams& k, uint32_t n, int p, 
       ky = __fmul_rn(fs[1], sy);
       kz = __fmul_rn(fs[2], sz);
     } else {
-      const float* lg = k.learnable + (int64_t)n * (k.num_learnable * 3) + (p - k.num_fix) * 3;
+      const float* lg = lg_anchor + (p - k.num_fix) * 3;
       kx = __fmul_rn(__fsub_rn(sigmoid_rn(lg[0]), 0.5f), sx);
       ky = __fmul_rn(__fsub_rn(sigmoid_rn(lg[1]), 0.5f), sy);
       kz = __fmul_rn(__fsub_rn(sigmoid_rn(lg[2]), 0.5f), sz);
@@ -73,6 +75,7 @@ __device__ __forceinline__ float proj_row(const float* r, float px, float py, fl
   return __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(r[0], px), __fmul_rn(r[1], py)), __fmul_rn(r[2], pz)), r[3]);
 }
 
+template <bool FUSED>
 __global__ void __launch_bounds__(kKpsThreads) kps_project_kernel(KpsParams k) {
   // Keypoints of the anchors this block's elements belong to, computed once each (not once per
   // camera) and shared through shared memory.
@@ -85,12 +88,58 @@ __global__ void __launch_bounds__(kKpsThreads) kps_project_kernel(KpsParams k) {
   const uint32_t n0 = k.div_anchor_elems.div(block_base);
   const uint32_t last = block_base + kElemsPerBlock - 1 < total ? block_base + kElemsPerBlock - 1 : total - 1;
   const int nkp = (int)(k.div_anchor_elems.div(last) - n0 + 1) * k.num_pts;
+  const int nl3 = k.num_learnable * 3;
+  // In-kernel learnable logits (the keypoint generator's learnable_fc, fp32) of the block's
+  // anchors: their instance rows are staged in shared memory in 8 chunks of 32 floats (chunk
+  // stride 36 floats, so the 8 chunks a warp reads at once sit in different banks); thread
+  // t = 8 o + kc keeps learnable_fc row o, chunk kc in registers and sums that chunk for every
+  // anchor; the 8 chunk sums of (anchor, o) meet by shuffles.  The weights are read once per block.
+  __shared__ __align__(16) float s_x[1][FUSED ? kKpsMaxFusedAnchors * 8 * 36 : 4];
+  __shared__ float s_lg[FUSED ? kKpsMaxFusedAnchors * kKpsMaxFusedLogits : 1];
+  if (FUSED) {
+    const int n_anc = nkp / k.num_pts;
+    for (int idx = threadIdx.x; idx < n_anc * 64; idx += kKpsThreads) {
+      const int j = idx >> 6, q = idx & 63;
+      const float4 v = __ldg(reinterpret_cast<const float4*>(k.inst + (int64_t)(n0 + j) * k.inst_ld) + q);
+      *reinterpret_cast<float4*>(&s_x[0][j * 288 + (q >> 3) * 36 + (q & 7) * 4]) = v;
+    }
+    const int o = threadIdx.x >> 3, kc = threadIdx.x & 7;
+    const bool active = o < nl3;
+    float w[32];
+    const float4* wr = reinterpret_cast<const float4*>(k.w_kps + (int64_t)(active ? o : 0) * 256 + kc * 32);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = __ldg(wr + i);
+      w[4 * i] = v.x, w[4 * i + 1] = v.y, w[4 * i + 2] = v.z, w[4 * i + 3] = v.w;
+    }
+    const float bias = active && k.b_kps != nullptr ? __ldg(k.b_kps + o) : 0.f;
+    __syncthreads();
+    for (int j = 0; j < n_anc; ++j) {
+      const float4* x = reinterpret_cast<const float4*>(&s_x[0][j * 288 + kc * 36]);
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 v = x[i];
+        a0 = fmaf(v.x, w[4 * i], a0);
+        a1 = fmaf(v.y, w[4 * i + 1], a1);
+        a0 = fmaf(v.z, w[4 * i + 2], a0);
+        a1 = fmaf(v.w, w[4 * i + 3], a1);
+      }
+      float acc = a0 + a1;
+      acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      if (active && kc == 0) s_lg[j * nl3 + o] = acc + bias;
+    }
+    __syncthreads();
+  }
   for (int i = threadIdx.x; i < nkp; i += kKpsThreads) {
     const uint32_t j = k.div_pts.div(i);
     const uint32_t n = n0 + j;
     const int p = i - (int)j * k.num_pts;
+    const float* lg = FUSED ? s_lg + j * nl3 : (k.learnable != nullptr ? k.learnable + (int64_t)n * nl3 : nullptr);
     float px, py, pz;
-    keypoint(k, n, p, px, py, pz);
+    keypoint(k, n, p, lg, px, py, pz);
     s_kp[3 * i] = px;
     s_kp[3 * i + 1] = py;
     s_kp[3 * i + 2] = pz;
@@ -246,7 +295,10 @@ int launch_kps_project(KpsParams k, int32_t* visible_idx, int32_t* visible_count
   k.div_anchor_elems = FastDiv((uint32_t)(k.num_cams * k.num_pts));
   k.div_pts = FastDiv((uint32_t)k.num_pts);
   k.div_anchors = FastDiv((uint32_t)k.num_anchor);
-  kps_project_kernel<<<(unsigned)nb, kKpsThreads, 0, stream>>>(k);
+  if (k.inst != nullptr)
+    kps_project_kernel<true><<<(unsigned)nb, kKpsThreads, 0, stream>>>(k);
+  else
+    kps_project_kernel<false><<<(unsigned)nb, kKpsThreads, 0, stream>>>(k);
   int st = cuda_check(cudaGetLastError(), "kps_project_kernel launch");
   if (st != S4D_OK || !compact) return st;
   kps_compact_kernel<<<(unsigned)nb, kKpsThreads, 0, stream>>>(

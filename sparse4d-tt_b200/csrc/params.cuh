@@ -27,7 +27,19 @@ struct KpsParams {
   FastDiv div_anchor_elems;  // by num_cams * num_pts (element -> linear anchor)
   FastDiv div_pts;           // by num_pts
   FastDiv div_anchors;       // by num_anchor (linear anchor -> batch)
+  // Learnable keypoint logits computed in the kernel from the instance feature (instead of
+  // `learnable`): logit[o] = b_kps[o] + inst[n, :] . w_kps[o, :].
+  const float* inst;  // [n, embed_dims] rows of stride inst_ld, or null
+  int64_t inst_ld;
+  const float* w_kps;  // [num_learnable * 3, embed_dims]
+  const float* b_kps;  // [num_learnable * 3] or null
+  int embed_dims;
 };
+
+// In-kernel learnable logits of kps_project_kernel: at most this many anchors per block (their
+// instance rows are staged in shared memory), embed_dims 256, at most 32 logits per anchor.
+constexpr int kKpsMaxFusedAnchors = 20;
+constexpr int kKpsMaxFusedLogits = 32;
 
 // Largest Ncam*L*P*G the gather stages per anchor in shared memory (48 KiB of fp32).
 constexpr int kGatherMaxWeights = 12288;

@@ -150,7 +150,8 @@ class DeformableFeatureAggregation:
         lpg = num_levels * num_pts * num_groups
         self._tc = (self.matmul_precision == "high" and self.split_logits
                     and ops.weights_fc_supported(lpg, 3 * num_learnable_pts, embed_dims)
-                    and residual_mode in ops.RESIDUAL_MODES)
+                    and residual_mode in ops.RESIDUAL_MODES
+                    and 1024 // (num_cams * num_pts) + 2 <= 20 and num_learnable_pts <= 10)
         # Per-frame caches, cleared by the head at the start of a frame
         # (model/sparse4d_head.py:290-296 resets the same attribute names).
         self._cached_camera_embed = None
@@ -160,6 +161,7 @@ class DeformableFeatureAggregation:
         # the Sparse4D v3 shape has a kernel for the per-frame camera softmax factors
         self._factors_ok = (num_cams, num_levels, num_pts, num_groups) == (6, 4, 13, 8)
         self._side: Optional[torch.cuda.Stream] = None
+        self._side_kps: Optional[torch.cuda.Stream] = None
         self._side_pending = False
         self._cached_proj_rm = None
         self._cached_wh_rm = None
@@ -286,19 +288,42 @@ class DeformableFeatureAggregation:
             # On a side stream the camera terms overlap the next two kernels; that pays while the
             # GPU is the bottleneck (graph capture, large batches), not for small eager calls, whose
             # time is host work that the extra stream bookkeeping would lengthen.
-            side = rows >= 8192 or torch.cuda.is_current_stream_capturing()
+            capturing = torch.cuda.is_current_stream_capturing()
+            side = rows >= 8192 or capturing
             logits_cam = self._camera_logits(projection_mat, bs, side=side)
             inst2d, embed2d = ops.row_view(instance_feature, C), ops.row_view(anchor_embed, C)
+            loc = torch.empty(bs, num_anchor, self.num_cams, self.num_pts, 2, dtype=torch.float32, device=dev)
             logits = torch.empty(bs, num_anchor, self.num_levels, self.num_pts, self.num_groups, device=dev)
-            learn = torch.empty(bs, num_anchor, 3 * self.num_learnable_pts, device=dev)
-            ops.weights_fc_into(logits.view(rows, -1), learn.view(rows, -1), inst2d, embed2d, self.weights_fc_weight,
-                                self.learnable_fc_weight, self.learnable_fc_bias)
+            if rows <= 4096:
+                # Small batches are latency-bound: the keypoints compute their own learnable logits
+                # and, under capture, run on a second side stream beside weights_fc (and the camera
+                # terms) instead of after it.
+                ctx = contextlib.nullcontext()
+                if capturing:
+                    if self._side_kps is None:
+                        self._side_kps = torch.cuda.Stream(dev)
+                    self._side_kps.wait_stream(torch.cuda.current_stream(dev))
+                    ctx = torch.cuda.stream(self._side_kps)
+                with ctx:
+                    ops.kps_project_linear_into(anchor, inst2d, self.learnable_fc_weight, self.learnable_fc_bias,
+                                                self.fix_scale, projection_mat, image_wh, sample_location=loc)
+                ops.weights_fc_into(logits.view(rows, -1), None, inst2d, embed2d, self.weights_fc_weight, None,
+                                    None)
+                if capturing:
+                    torch.cuda.current_stream(dev).wait_stream(self._side_kps)
+            else:
+                # Large batches: the tensor-core pass produces the learnable logits almost for free
+                # (one N-32 MMA per K step), then the plain keypoint kernel runs.
+                learn = torch.empty(bs, num_anchor, 3 * self.num_learnable_pts, device=dev)
+                ops.weights_fc_into(logits.view(rows, -1), learn.view(rows, -1), inst2d, embed2d,
+                                    self.weights_fc_weight, self.learnable_fc_weight, self.learnable_fc_bias)
+                ops.kps_project_into(anchor, learn, self.fix_scale, projection_mat, image_wh, sample_location=loc)
         else:
             with _matmul_precision(self.matmul_precision):
                 logits, logits_cam = self._get_weights(instance_feature, anchor_embed, projection_mat, bs, num_anchor)
                 learn = F.linear(instance_feature, self.learnable_fc_weight, self.learnable_fc_bias).contiguous()
-        loc = torch.empty(bs, num_anchor, self.num_cams, self.num_pts, 2, dtype=torch.float32, device=dev)
-        ops.kps_project_into(anchor, learn, self.fix_scale, projection_mat, image_wh, sample_location=loc)
+            loc = torch.empty(bs, num_anchor, self.num_cams, self.num_pts, 2, dtype=torch.float32, device=dev)
+            ops.kps_project_into(anchor, learn, self.fix_scale, projection_mat, image_wh, sample_location=loc)
         self._join_side()  # the camera terms are needed from here on
 
         cam_begin, cam_end = 0, self.num_cams

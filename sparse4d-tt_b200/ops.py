@@ -392,6 +392,49 @@ def kps_project_into(anchor: Tensor, learnable_logits: Optional[Tensor], fix_sca
     L.check(name, st)
 
 
+def kps_project_linear_into(anchor: Tensor, instance_feature: Tensor, learnable_fc_weight: Tensor,
+                            learnable_fc_bias: Optional[Tensor], fix_scale: Optional[Tensor], projection_mat: Tensor,
+                            image_wh: Tensor, sample_location: Optional[Tensor] = None,
+                            depth_mask: Optional[Tensor] = None, key_points: Optional[Tensor] = None,
+                            layout: Union[int, str] = "cam_major") -> None:
+    """``kps_project_into`` with the learnable keypoint logits computed inside the kernel from
+    ``instance_feature`` (a ``[bs*A, C]`` row view, see ``row_view``) and the keypoint
+    generator's ``learnable_fc`` weight/bias (fp32), so the call needs no other linear first."""
+    name = "kps_project_linear"
+    lay = LAYOUTS[layout] if isinstance(layout, str) else int(layout)
+    dev = _require_cuda(name, anchor, instance_feature, learnable_fc_weight, learnable_fc_bias, fix_scale,
+                        projection_mat, image_wh, sample_location, depth_mask, key_points)
+    _check_contig(name, anchor=anchor, learnable_fc_weight=learnable_fc_weight, learnable_fc_bias=learnable_fc_bias,
+                  fix_scale=fix_scale, projection_mat=projection_mat, image_wh=image_wh,
+                  sample_location=sample_location, depth_mask=depth_mask, key_points=key_points)
+    for k, t in (("anchor", anchor), ("instance_feature", instance_feature), ("learnable_fc_weight", learnable_fc_weight),
+                 ("learnable_fc_bias", learnable_fc_bias), ("fix_scale", fix_scale), ("projection_mat", projection_mat),
+                 ("image_wh", image_wh), ("sample_location", sample_location), ("key_points", key_points)):
+        _check_dtype(name, t, (torch.float32,), k)
+    _check_dtype(name, depth_mask, (torch.uint8, torch.bool), "depth_mask")
+    _require(anchor.dim() == 3 and anchor.shape[-1] >= 8, "anchor must be [bs, A, >=8]")
+    bs, A = int(anchor.shape[0]), int(anchor.shape[1])
+    _require(projection_mat.dim() == 4 and projection_mat.shape[0] == bs and tuple(projection_mat.shape[2:]) == (4, 4),
+             "projection_mat must be [bs, Ncam, 4, 4]")
+    nc = int(projection_mat.shape[1])
+    _require(tuple(image_wh.shape) == (bs, nc, 2), "image_wh must be [bs, Ncam, 2]")
+    n_fix = 0 if fix_scale is None else int(fix_scale.shape[0])
+    m3, c = (int(v) for v in learnable_fc_weight.shape)
+    _require(m3 % 3 == 0, "learnable_fc_weight must be [3 * num_learnable, C]")
+    _require(instance_feature.dim() == 2 and tuple(instance_feature.shape) == (bs * A, c)
+             and instance_feature.stride(1) == 1, f"instance_feature must be a [{bs * A}, {c}] row view")
+    P = n_fix + m3 // 3
+    if sample_location is not None:
+        exp = (bs, A, nc, P, 2) if lay == L.S4D_LAYOUT_CAM_MAJOR else (bs, A, P, nc, 2)
+        _require(tuple(sample_location.shape) == exp, f"sample_location must be {list(exp)}")
+    st = L.lib().s4d_kps_project_linear(
+        anchor.data_ptr(), int(anchor.shape[2]), _ptr(fix_scale), n_fix, instance_feature.data_ptr(),
+        instance_feature.stride(0), learnable_fc_weight.data_ptr(), _ptr(learnable_fc_bias), m3 // 3, c,
+        projection_mat.data_ptr(), image_wh.data_ptr(), bs, A, nc, lay, _ptr(key_points), _ptr(sample_location),
+        _ptr(depth_mask), None, None, None, 0, _stream_ptr(dev))
+    L.check(name, st)
+
+
 @torch.library.custom_op("s4d::kps_project", mutates_args=())
 def kps_project(anchor: Tensor, learnable_logits: Optional[Tensor], fix_scale: Tensor, projection_mat: Tensor,
                 image_wh: Tensor, layout: int = 0) -> Tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:

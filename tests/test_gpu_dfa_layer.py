@@ -174,3 +174,20 @@ def test_stacked_layers_tf32_strided_instance(cuda_device, mode):
         assert p_ >= BF16_PCC and xre <= BF16_REL, layer
         inst = ref[..., :256].contiguous()
         anchor = syn.refine_anchors(anchor, gen)
+
+
+def test_layer_tf32_large_batch_path(cuda_device):
+    """Above 4096 anchor rows the tensor-core pass also produces the learnable logits and the plain
+    keypoint kernel follows (below it, the keypoint kernel computes them itself): 5 frames x 900
+    anchors through the module against the oracle, at the bf16 tolerance."""
+    cfg = syn.DFAConfig(bs=5, num_anchor=900)
+    ins = syn.make_inputs(cfg, 41, feature_dtype=torch.bfloat16)
+    params = syn.make_params(cfg, torch.Generator().manual_seed(141))
+    mod = _module(params, cfg, torch.bfloat16, True, "tf32")
+    assert mod._tc
+    out = _run(mod, ins, cfg)
+    ref = oto.dfa_layer(params, ins.instance_feature, ins.anchor, ins.anchor_embed, ins.feature_maps,
+                        ins.projection_mat, ins.image_wh)
+    p_, xre = pcc(out, ref), max_rel_err(out, ref)
+    print(f"5 x 900 tf32 layer: pcc={p_:.7f} max_rel={xre:.2e}")
+    assert p_ >= BF16_PCC and xre <= BF16_REL

@@ -172,3 +172,39 @@ def test_kps_deterministic(cuda_device):
     for x, y in zip(a, b):
         if isinstance(x, torch.Tensor):
             assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("strided", [False, True])
+def test_kps_linear_matches_given_logits(cuda_device, strided):
+    """s4d_kps_project_linear (learnable logits computed in the kernel, fp32) against
+    s4d_kps_project fed float64-accurate logits of the same linear: keypoints within fp32
+    rounding, sample locations within the projection tolerance where the depth is not tiny."""
+    cfg = syn.config_standard(2)
+    ins = syn.make_inputs(cfg, 31)
+    params = syn.make_params(cfg, torch.Generator().manual_seed(131))
+    params["kps_learnable_fc_bias"] = torch.randn(18, generator=torch.Generator().manual_seed(2)) * 0.1
+    d = torch.device("cuda:0")
+    inst = ins.instance_feature.reshape(-1, 256)
+    if strided:
+        wide = torch.zeros(inst.shape[0], 512)
+        wide[:, :256] = inst
+        inst_d = wide.to(d)[:, :256]
+    else:
+        inst_d = inst.to(d)
+    w, b = params["kps_learnable_fc_weight"].to(d), params["kps_learnable_fc_bias"].to(d)
+    bs, A = cfg.bs, cfg.num_anchor
+    loc = torch.empty(bs, A, 6, 13, 2, device=d)
+    kp = torch.empty(bs, A, 13, 3, device=d)
+    ops.kps_project_linear_into(ins.anchor.to(d), inst_d, w, b, params["kps_fix_scale"].to(d), ins.projection_mat.to(d),
+                                ins.image_wh.to(d), sample_location=loc, key_points=kp)
+    learn = (inst.double() @ params["kps_learnable_fc_weight"].double().T
+             + params["kps_learnable_fc_bias"].double()).float().reshape(bs, A, 18)
+    ref_loc, _, _, _, ref_kp = ops.kps_project(ins.anchor.to(d), learn.to(d), params["kps_fix_scale"].to(d),
+                                               ins.projection_mat.to(d), ins.image_wh.to(d))
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(kp.cpu().numpy(), ref_kp.cpu().numpy(), rtol=1e-5, atol=1e-4)
+    Pm = ins.projection_mat
+    depth = torch.einsum("bck,bapk->bacp", Pm[:, :, 2, :3], ref_kp.cpu()) + Pm[:, None, :, 2, 3, None]
+    well = (depth.abs() > 0.5).numpy()[..., None].repeat(2, -1)
+    err = (loc.cpu() - ref_loc.cpu()).abs().numpy()
+    assert np.all(err[well] <= 1e-3 * np.abs(ref_loc.cpu().numpy()[well]) + 1e-4)
