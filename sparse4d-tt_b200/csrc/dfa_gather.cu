@@ -821,21 +821,34 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BL
           const float x1f = x0f + 1.0f, y1f = y0f + 1.0f;
           const bool vx0 = x0 >= 0, vx1 = x0 + 1 < lv.y, vy0 = y0 >= 0, vy1 = y0 + 1 < lv.x;
           const int p00 = lv.z + y0 * lv.y + x0;
-          rec.pix = make_int4(vx0 && vy0 ? p00 : -1, vx1 && vy0 ? p00 + 1 : -1, vx0 && vy1 ? p00 + lv.y : -1,
-                              vx1 && vy1 ? p00 + lv.y + 1 : -1);
-          rec.bw = make_float4((x1f - ix) * (y1f - iy), (ix - x0f) * (y1f - iy), (x1f - ix) * (iy - y0f),
-                               (ix - x0f) * (iy - y0f));
+          // A tap outside the map is given the row of an in-bounds tap of the same block (a valid
+          // sample has one) and weight 0, so the gather loop loads and accumulates all 4 taps
+          // without tests; the extra load hits L1.
+          const bool t00 = vx0 && vy0, t01 = vx1 && vy0, t10 = vx0 && vy1, t11 = vx1 && vy1;
+          const int any = t00 ? p00 : t01 ? p00 + 1 : t10 ? p00 + lv.y : p00 + lv.y + 1;
+          rec.pix = make_int4(t00 ? p00 : any, t01 ? p00 + 1 : any, t10 ? p00 + lv.y : any, t11 ? p00 + lv.y + 1 : any);
+          rec.bw = make_float4(t00 ? (x1f - ix) * (y1f - iy) : 0.0f, t01 ? (ix - x0f) * (y1f - iy) : 0.0f,
+                               t10 ? (x1f - ix) * (iy - y0f) : 0.0f, t11 ? (ix - x0f) * (iy - y0f) : 0.0f);
           const int lp = l * NP + ps;
           const int e1 = lp * G, e2 = cs * LPG + lp * G;  // anchor-term and camera-term offsets
           // This sample's weight for every group, computed once here rather than by every lane of
           // every block it joins: exp(wa - M1) * exp(wc - M2) from the per-anchor table and the
           // per-frame camera factors, or (exact mode) the logit itself.
+          if (!exact && G % 4 == 0) {  // e1, e2 are multiples of G: 16-byte vectors
 #pragma unroll
-          for (int g = 0; g < G; ++g) {
-            if (!exact) {
-              rec.sw[g] = ea[e1 + g] * __ldg(ec_tab + e2 + g);
-            } else {
-              rec.sw[g] = MODE == 0 ? __ldg(wrow + e2 + g) : __ldg(wrow + e1 + g) + __ldg(wcam + e2 + g);
+            for (int g = 0; g < G; g += 4) {
+              const float4 a = *reinterpret_cast<const float4*>(ea + e1 + g);
+              const float4 c = __ldg(reinterpret_cast<const float4*>(ec_tab + e2 + g));
+              rec.sw[g] = a.x * c.x, rec.sw[g + 1] = a.y * c.y, rec.sw[g + 2] = a.z * c.z, rec.sw[g + 3] = a.w * c.w;
+            }
+          } else {
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+              if (!exact) {
+                rec.sw[g] = ea[e1 + g] * __ldg(ec_tab + e2 + g);
+              } else {
+                rec.sw[g] = MODE == 0 ? __ldg(wrow + e2 + g) : __ldg(wrow + e1 + g) + __ldg(wcam + e2 + g);
+              }
             }
           }
           // (camera, level) and the top-left tap (x0, y0 >= -1) identify the 2x2 block
@@ -853,11 +866,11 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BL
         leaders &= leaders - 1u;
         uint32_t mem = __shfl_sync(0xffffffffu, grp, ld);
         const int4 px = s_rec[warp][ld].pix;
-        V v0, v1, v2, v3;
-        if (px.x >= 0) TapFma<T>::load(fb, px.x, lane, v0);
-        if (px.y >= 0) TapFma<T>::load(fb, px.y, lane, v1);
-        if (px.z >= 0) TapFma<T>::load(fb, px.z, lane, v2);
-        if (px.w >= 0) TapFma<T>::load(fb, px.w, lane, v3);
+        V v0, v1, v2, v3;  // every tap row is in bounds (see the record): no tests
+        TapFma<T>::load(fb, px.x, lane, v0);
+        TapFma<T>::load(fb, px.y, lane, v1);
+        TapFma<T>::load(fb, px.z, lane, v2);
+        TapFma<T>::load(fb, px.w, lane, v3);
         // the block's weight for this lane's group: sum over its member samples of bilinear
         // weight x unnormalised softmax weight
         float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -872,10 +885,10 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BL
           w4.z = fmaf(bw.z, sw, w4.z);
           w4.w = fmaf(bw.w, sw, w4.w);
         }
-        if (px.x >= 0) TapFma<T>::fma(v0, w4.x, acc);
-        if (px.y >= 0) TapFma<T>::fma(v1, w4.y, acc);
-        if (px.z >= 0) TapFma<T>::fma(v2, w4.z, acc);
-        if (px.w >= 0) TapFma<T>::fma(v3, w4.w, acc);
+        TapFma<T>::fma(v0, w4.x, acc);
+        TapFma<T>::fma(v1, w4.y, acc);
+        TapFma<T>::fma(v2, w4.z, acc);
+        TapFma<T>::fma(v3, w4.w, acc);
       }
     }
     __syncwarp();  // s_surv is rewritten by the next pair round
