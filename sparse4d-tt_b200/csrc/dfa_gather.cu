@@ -722,8 +722,14 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BL
     }
   }
   __syncthreads();  // the only block barrier: every thread reaches it before any warp leaves
-  const int64_t anchor_lin = (int64_t)blockIdx.x * WARPS + warp;
-  if (anchor_lin >= (int64_t)p.bs * p.num_anchor) return;
+  // Persistent warps: each takes anchors from the launch's counter until none is left, so the
+  // level tables above are staged once per block and uneven anchors balance out.
+  const int64_t total_anchors = (int64_t)p.bs * p.num_anchor;
+  for (;;) {
+  unsigned ticket = 0;
+  if (lane == 0) ticket = atomicAdd(p.anchor_counter, 1u);
+  const int64_t anchor_lin = __shfl_sync(0xffffffffu, ticket, 0);
+  if (anchor_lin >= total_anchors) break;
   const int b = (int)(anchor_lin / p.num_anchor);
   const int gch = lane / (D / 8);  // group of this lane's output channels
 
@@ -898,6 +904,8 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BL
   float4* o = reinterpret_cast<float4*>(p.out + anchor_lin * kChannels + lane * 8);
   o[0] = make_float4(acc[0].x * inv, acc[0].y * inv, acc[1].x * inv, acc[1].y * inv);
   o[1] = make_float4(acc[2].x * inv, acc[2].y * inv, acc[3].x * inv, acc[3].y * inv);
+  __syncwarp();  // this anchor's shared-memory state is read before the next one writes it
+  }
 }
 
 // The Sparse4D v3 shape the fast kernels are compiled for.
@@ -906,8 +914,32 @@ constexpr int kFastNC = 6, kFastNL = 4, kFastNP = 13, kFastG = 8;
 // anchors are done, so uneven anchors do not leave finished warps waiting for block-mates
 constexpr int kWarpBlock = 1;
 
+// Workspace: the per-frame camera factors, then (16-byte aligned) the anchor counter of the
+// persistent warp kernel.
+static size_t factor_bytes(int64_t bs, int ncam, int nl, int np, int G) {
+  return ((size_t)bs * (ncam + 1) * nl * np * G * sizeof(float) + 15) & ~(size_t)15;
+}
+
 size_t gather_workspace_bytes(int64_t bs, int ncam, int nl, int np, int G) {
-  return (size_t)bs * (ncam + 1) * nl * np * G * sizeof(float);
+  return factor_bytes(bs, ncam, nl, np, G) + 16;
+}
+
+// One-warp blocks of the warp kernel that fit on the current device at once, cached per device
+// and feature type (index `which`).
+template <typename K>
+static int resident_warp_blocks(K kernel, int which) {
+  static int cache[2][64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148 * 28;
+  if (cache[which][dev] > 0) return cache[which][dev];
+  int per_sm = 0, sms = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kWarpBlock * 32, 0) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || per_sm <= 0 || sms <= 0) {
+    cudaGetLastError();
+    return 148 * 28;
+  }
+  cache[which][dev] = per_sm * sms;
+  return cache[which][dev];
 }
 
 static bool fast_path_ok(const GatherParams& p) {
@@ -942,13 +974,20 @@ int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream) {
                                   stream);
       if (st) return st;
     }
-    const unsigned wgrid = (unsigned)(((int64_t)p.bs * p.num_anchor + kWarpBlock - 1) / kWarpBlock);
+    GatherParams q = p;
+    q.anchor_counter = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(p.cam_ws) +
+                                                   factor_bytes(p.bs, p.num_cams, p.num_levels, p.num_pts, p.num_groups));
+    int st = cuda_check(cudaMemsetAsync(q.anchor_counter, 0, sizeof(unsigned), stream), "cudaMemsetAsync(counter)");
+    if (st) return st;
+    const int64_t anchors = (int64_t)p.bs * p.num_anchor;
+    auto kb = dfa_gather_warp_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock>;
+    auto kf = dfa_gather_warp_kernel<float, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock>;
+    const int64_t fit = feat_dtype == S4D_DTYPE_BF16 ? resident_warp_blocks(kb, 0) : resident_warp_blocks(kf, 1);
+    const unsigned wgrid = (unsigned)(anchors < fit ? anchors : fit);
     if (feat_dtype == S4D_DTYPE_BF16)
-      dfa_gather_warp_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock>
-          <<<wgrid, kWarpBlock * 32, 0, stream>>>(p);
+      kb<<<wgrid, kWarpBlock * 32, 0, stream>>>(q);
     else
-      dfa_gather_warp_kernel<float, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock>
-          <<<wgrid, kWarpBlock * 32, 0, stream>>>(p);
+      kf<<<wgrid, kWarpBlock * 32, 0, stream>>>(q);
     return cuda_check(cudaGetLastError(), "dfa_gather_warp_kernel launch");
   }
   if (fast_path_ok(p)) {

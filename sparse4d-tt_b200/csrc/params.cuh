@@ -60,6 +60,7 @@ struct GatherParams {
   int logits;
   int layout;
   int factors_ready;  // split logits: cam_ws already holds the camera factors (no prep launch)
+  unsigned* anchor_counter;  // warp kernel: next anchor to take (in the workspace, zeroed per launch)
 };
 
 // Tensor-core linears (linear_tc.cu).  Row strides are in floats.

@@ -56,7 +56,7 @@ def test_status_strings_and_version(lib):
 
 
 def test_dfa_workspace_bytes(lib):
-    assert lib.s4d_dfa_workspace_bytes(2, 6, 4, 13, 8, 1) == 2 * 7 * 416 * 4
+    assert lib.s4d_dfa_workspace_bytes(2, 6, 4, 13, 8, 1) == 2 * 7 * 416 * 4 + 16
     assert lib.s4d_dfa_workspace_bytes(2, 6, 4, 13, 8, 0) == 0
 
 

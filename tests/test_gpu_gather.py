@@ -296,4 +296,5 @@ def test_gather_prepared_camera_factors(cuda_device, dtype):
     b = torch.empty(2, 90, 256, device=d)
     ops.deformable_aggregation_into(b, feat, shape, start, loc, wa, True, wc, workspace=ws_b, factors_ready=True)
     torch.cuda.synchronize()
-    assert torch.equal(a, b) and torch.equal(ws_a, ws_b)
+    n = 2 * 7 * 416  # the factors (the workspace ends with the gather's anchor counter)
+    assert torch.equal(a, b) and torch.equal(ws_a[:n], ws_b[:n])
