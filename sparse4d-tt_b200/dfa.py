@@ -27,6 +27,7 @@ import torch
 import torch.nn.functional as F
 
 from . import ops
+from .timing import TimingEvent
 
 Tensor = torch.Tensor
 
@@ -166,9 +167,12 @@ class DeformableFeatureAggregation:
         self._cached_proj_rm = None
         self._cached_wh_rm = None
         self._cam_key = None
-        # When a list, every run() appends a (start, end) pair of CUDA events recorded on the
-        # launching stream around the gather kernel (used to time that kernel in place).
-        self.event_log: Optional[List[Tuple[torch.cuda.Event, torch.cuda.Event]]] = None
+        # When a list, every run() appends a (start, end) pair of timing events recorded on the
+        # launching stream around the gather kernel (used to time that kernel in place); under
+        # stream capture the two records are event-record nodes of the graph.
+        self.event_log: Optional[List[Tuple[TimingEvent, TimingEvent]]] = None
+        self._timing: Optional[torch.cuda.Stream] = None
+        self._timing_pending = False
 
     # ---- dense parts (cuBLAS through torch) -----------------------------------------------
     def _camera_encoder(self, projection_mat: Tensor, bs: int) -> Tensor:
@@ -232,6 +236,13 @@ class DeformableFeatureAggregation:
         if self._side_pending:
             torch.cuda.current_stream(self.device).wait_stream(self._side)
             self._side_pending = False
+
+    def join_timing_stream(self) -> None:
+        """Makes the current stream wait for the gather-timing branch of the last call (needed
+        before the end of a stream capture that logged events)."""
+        if self._timing_pending:
+            torch.cuda.current_stream(self.device).wait_stream(self._timing)
+            self._timing_pending = False
 
     def reset_frame_cache(self) -> None:
         """Drops the per-frame camera caches (what the head does at the start of every frame)."""
@@ -336,8 +347,15 @@ class DeformableFeatureAggregation:
         logits_cam = None if logits_cam is None else logits_cam.contiguous()
         log = self.event_log
         if log is not None:
-            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            ev[0].record()
+            # The two records run on a timing branch (forked from the launching stream, joined
+            # back at the next call or by join_timing_stream()), so no kernel waits on them.
+            self.join_timing_stream()
+            if self._timing is None:
+                self._timing = torch.cuda.Stream(dev)
+            cur = torch.cuda.current_stream(dev)
+            ev = (TimingEvent(), TimingEvent())
+            self._timing.wait_stream(cur)
+            ev[0].record(self._timing)
         ws, ready = None, False
         if logits_cam is not None:
             ws, ready = self._cached_camera_factors, self._cached_camera_factors is not None
@@ -346,7 +364,9 @@ class DeformableFeatureAggregation:
         ops.deformable_aggregation_into(feats, mc_ms_feat, spatial_shape, scale_start, loc, logits, True,
                                         logits_cam, cam_begin, cam_end, workspace=ws, factors_ready=ready)
         if log is not None:
-            ev[1].record()
+            self._timing.wait_stream(cur)
+            ev[1].record(self._timing)
+            self._timing_pending = True
             log.append(ev)
         if self.process_group is not None:
             import torch.distributed as dist

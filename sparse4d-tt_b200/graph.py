@@ -37,16 +37,19 @@ class CapturedCall:
         return self.output
 
 
-def capture(fn: Callable[[], object], warmup: int = 2, pool=None) -> CapturedCall:
+def capture(fn: Callable[[], object], warmup: int = 2, pool=None,
+            before_capture: Optional[Callable[[], None]] = None) -> CapturedCall:
     """Runs ``fn`` ``warmup`` times on a side stream (so allocations and lazy set-up happen
-    outside the graph), then records one call.  ``fn`` must launch its work on the current
-    stream and must not synchronise with the host."""
+    outside the graph), calls ``before_capture`` (if given), then records one call.  ``fn`` must
+    launch its work on the current stream and must not synchronise with the host."""
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
         for _ in range(warmup):
             fn()
     torch.cuda.current_stream().wait_stream(side)
+    if before_capture is not None:
+        before_capture()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, pool=pool):
         out = fn()
@@ -63,7 +66,7 @@ class DFAStack:
     layer's ``[bs, A, 2C]`` (residual ``cat``) or ``[bs, A, C]``."""
 
     def __init__(self, layers: Sequence, bs: int, num_anchor: int, spatial_shapes: Sequence[Tuple[int, int]],
-                 feature_dtype: torch.dtype = torch.bfloat16, warmup: int = 2):
+                 feature_dtype: torch.dtype = torch.bfloat16, warmup: int = 2, time_gathers: bool = False):
         if not layers:
             raise ValueError("DFAStack needs at least one layer")
         m0 = layers[0]
@@ -80,7 +83,20 @@ class DFAStack:
         self.projection_mat[..., 2, 2] = 1.0  # finite camera terms during warm-up
         self.projection_mat[..., 3, 3] = 1.0
         self.image_wh = torch.ones(bs, nc, 2, device=dev)
-        self._call = capture(self._forward, warmup=warmup)
+        self._gather_events = None
+        if not time_gathers:
+            self._call = capture(self._forward, warmup=warmup)
+            return
+        # Each layer's gather is bracketed by two event-record nodes of the graph: after a replay
+        # has completed they hold that replay's device timestamps.
+        def log_on():
+            for mod in self.layers:
+                mod.event_log = []
+
+        self._call = capture(self._forward, warmup=warmup, before_capture=log_on)
+        self._gather_events = [pair for mod in self.layers for pair in mod.event_log]
+        for mod in self.layers:
+            mod.event_log = None
 
     def _forward(self) -> Tensor:
         packed = (self.mc_ms_feat, self.spatial_shape, self.scale_start_index)
@@ -92,6 +108,8 @@ class DFAStack:
             out = mod.run(inst, self.anchors[i], self.anchor_embeds[i], packed, self.projection_mat, self.image_wh,
                           self.spatial_shapes, self.bs, self.num_anchor)
             inst = out[..., :C]
+        for mod in self.layers:
+            mod.join_timing_stream()
         return out
 
     @property
@@ -100,6 +118,13 @@ class DFAStack:
 
     def replay(self) -> Tensor:
         return self._call.replay()
+
+    def gather_times_ms(self) -> List[float]:
+        """Device time of every layer's gather launch in the latest completed replay, in
+        milliseconds (built with ``time_gathers=True``; call after the replay has finished)."""
+        if self._gather_events is None:
+            raise RuntimeError("DFAStack was built without time_gathers")
+        return [s.elapsed_time(e) for s, e in self._gather_events]
 
     def run(self, instance_feature: Optional[Tensor] = None, anchors: Optional[List[Tensor]] = None,
             anchor_embeds: Optional[List[Tensor]] = None, mc_ms_feat: Optional[Tensor] = None,

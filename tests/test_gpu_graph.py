@@ -85,3 +85,24 @@ def test_stack_recomputes_camera_terms(cuda_device):
     c = stack.run(projection_mat=ins.projection_mat).clone()
     torch.cuda.synchronize()
     assert not torch.equal(a, b) and torch.equal(a, c)
+
+
+def test_stack_timed_replays(cuda_device):
+    """time_gathers: each layer's gather launch is bracketed by event-record nodes of the graph,
+    which hold the device times of the latest replay; timing changes nothing in the output."""
+    cfg = syn.DFAConfig(bs=2, num_anchor=900)
+    layers = _layers(cfg, 2, seed=41)
+    plain = DFAStack(layers, 2, 900, cfg.spatial_shapes)
+    timed = DFAStack(layers, 2, 900, cfg.spatial_shapes, time_gathers=True)
+    ins, anchors, embeds = _inputs(cfg, 2, 13)
+    packed = ops.pack_feature_maps([m.to("cuda:0") for m in ins.feature_maps], dtype=torch.bfloat16)
+    a = plain.run(ins.instance_feature, anchors, embeds, packed[0], ins.projection_mat, ins.image_wh).clone()
+    for _ in range(3):
+        b = timed.run(ins.instance_feature, anchors, embeds, packed[0], ins.projection_mat, ins.image_wh)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    t = timed.gather_times_ms()
+    assert len(t) == 2 and all(0.0 < x < 50.0 for x in t), t
+    assert all(m.event_log is None for m in layers)
+    with pytest.raises(RuntimeError):
+        plain.gather_times_ms()
