@@ -668,7 +668,7 @@ __global__ void __launch_bounds__(kGatherThreads) cam_softmax_prep_kernel(const 
 // One in-bounds sample of a warp's anchor, as the merging step shares it between lanes.
 template <int G>
 struct SampleRec {
-  int4 pix;     // the 4 taps' feature rows (-1: outside the map)
+  int4 pix;     // the 4 taps' feature rows (all in bounds; a tap outside the map has weight 0)
   float4 bw;    // their bilinear weights
   float sw[G];  // per group: unnormalised softmax weight (factorised mode), or the logit (exact mode)
 };
@@ -693,7 +693,10 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BL
   __shared__ __align__(16) float4 s_win[NC];     // per camera: (u_lo, u_hi, v_lo, v_hi)
   __shared__ __align__(16) float s_ea[MODE == 1 ? WARPS * LPG : 1];
   __shared__ unsigned char s_surv[WARPS][32];
+  // per sub-round: the block leaders' records at 0..nlead-1 (lane order), the other members'
+  // after them; s_xm[k] = lane bits of leader k's other members
   __shared__ __align__(16) SampleRec<G> s_rec[WARPS][32];
+  __shared__ uint32_t s_xm[WARPS][32];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < NC * NL; i += WARPS * 32) {
@@ -863,33 +866,43 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BL
         }
       }
       const uint32_t grp = __match_any_sync(0xffffffffu, key);
-      uint32_t leaders = __ballot_sync(0xffffffffu, valid && lane == __ffs(grp) - 1);
+      const bool lead = valid && lane == __ffs(grp) - 1;
+      const uint32_t leaders = __ballot_sync(0xffffffffu, lead);
+      const uint32_t extras = __ballot_sync(0xffffffffu, valid && !lead);
+      const int nlead = __popc(leaders);
       __syncwarp();  // the previous sub-round's records have been read
-      if (valid) s_rec[warp][lane] = rec;
+      if (valid) {
+        const int slot = lead ? __popc(leaders & lt) : nlead + __popc(extras & lt);
+        s_rec[warp][slot] = rec;
+        if (lead) s_xm[warp][slot] = grp & ~(1u << lane);
+      }
       __syncwarp();
-      while (leaders != 0u) {
-        const int ld = __ffs(leaders) - 1;
-        leaders &= leaders - 1u;
-        uint32_t mem = __shfl_sync(0xffffffffu, grp, ld);
-        const int4 px = s_rec[warp][ld].pix;
+#pragma unroll 1
+      for (int k = 0; k < nlead; ++k) {
+        const int4 px = s_rec[warp][k].pix;
         V v0, v1, v2, v3;  // every tap row is in bounds (see the record): no tests
         TapFma<T>::load(fb, px.x, lane, v0);
         TapFma<T>::load(fb, px.y, lane, v1);
         TapFma<T>::load(fb, px.z, lane, v2);
         TapFma<T>::load(fb, px.w, lane, v3);
-        // the block's weight for this lane's group: sum over its member samples of bilinear
-        // weight x unnormalised softmax weight
-        float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        while (mem != 0u) {
-          const int j = __ffs(mem) - 1;
-          mem &= mem - 1u;
-          const float4 bw = s_rec[warp][j].bw;
-          float sw = s_rec[warp][j].sw[gch];
-          if (exact) sw = ex2_approx(fmaf(sw, kLog2e, -mlg));
-          w4.x = fmaf(bw.x, sw, w4.x);
-          w4.y = fmaf(bw.y, sw, w4.y);
-          w4.z = fmaf(bw.z, sw, w4.z);
-          w4.w = fmaf(bw.w, sw, w4.w);
+        // the block's weight for this lane's group: sum over its member samples (the leader's
+        // first, then the others in lane order) of bilinear weight x unnormalised softmax weight
+        const float4 bw = s_rec[warp][k].bw;
+        float sw = s_rec[warp][k].sw[gch];
+        if (exact) sw = ex2_approx(fmaf(sw, kLog2e, -mlg));
+        float4 w4 = make_float4(bw.x * sw, bw.y * sw, bw.z * sw, bw.w * sw);
+        uint32_t xm = s_xm[warp][k];
+        while (xm != 0u) {  // warp-uniform: most blocks have a single sample
+          const int j = __ffs(xm) - 1;
+          xm &= xm - 1u;
+          const int e = nlead + __popc(extras & ((1u << j) - 1u));
+          const float4 bwe = s_rec[warp][e].bw;
+          float swe = s_rec[warp][e].sw[gch];
+          if (exact) swe = ex2_approx(fmaf(swe, kLog2e, -mlg));
+          w4.x = fmaf(bwe.x, swe, w4.x);
+          w4.y = fmaf(bwe.y, swe, w4.y);
+          w4.z = fmaf(bwe.z, swe, w4.z);
+          w4.w = fmaf(bwe.w, swe, w4.w);
         }
         TapFma<T>::fma(v0, w4.x, acc);
         TapFma<T>::fma(v1, w4.y, acc);
