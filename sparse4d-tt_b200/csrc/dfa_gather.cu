@@ -381,6 +381,9 @@ struct TapFma<float> {
   }
 };
 
+// A hint to bring the line holding p into L1; no register is written.
+__device__ __forceinline__ void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
+
 template <typename T>
 struct TapVec {
   using type = uint4;
@@ -885,6 +888,14 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BL
         TapFma<T>::load(fb, px.y, lane, v1);
         TapFma<T>::load(fb, px.z, lane, v2);
         TapFma<T>::load(fb, px.w, lane, v3);
+        if (k + 1 < nlead) {  // the next block's rows towards L1 (no registers held)
+          const int4 pn = s_rec[warp][k + 1].pix;
+          const T* r = fb + lane * (kChannels / 32);
+          prefetch_l1(r + (int64_t)pn.x * kChannels);
+          prefetch_l1(r + (int64_t)pn.y * kChannels);
+          prefetch_l1(r + (int64_t)pn.z * kChannels);
+          prefetch_l1(r + (int64_t)pn.w * kChannels);
+        }
         // the block's weight for this lane's group: sum over its member samples (the leader's
         // first, then the others in lane order) of bilinear weight x unnormalised softmax weight
         const float4 bw = s_rec[warp][k].bw;
