@@ -265,9 +265,13 @@ class Workload:
             ops.kps_project_into(self.anchors[layer], learn, mod.fix_scale, self.proj, self.wh, sample_location=loc)
             touched = unique_tap_pixels(loc, cfg.spatial_shapes, self.start, self.num_feat)
             lpg = cfg.num_levels * cfg.num_pts * cfg.num_groups
+            if mod.fused_keypoints:  # the gather reads the anchors + keypoint logits, not locations
+                kps_in = (self.anchors[layer].numel() + learn.numel() + self.proj.numel() + self.wh.numel()) * 4
+            else:
+                kps_in = loc.numel() * 4
             b = (touched * cfg.embed_dims * 2
                  + self.frames * cfg.num_anchor * lpg * 4 + self.frames * cfg.num_cams * lpg * 4
-                 + loc.numel() * 4 + self.frames * cfg.num_anchor * cfg.embed_dims * 4)
+                 + kps_in + self.frames * cfg.num_anchor * cfg.embed_dims * 4)
             out_bytes.append((b, touched))
             out = mod.run(inst, self.anchors[layer], self.embeds[layer], self.packed, self.proj, self.wh,
                           cfg.spatial_shapes, self.frames, cfg.num_anchor)
@@ -276,11 +280,12 @@ class Workload:
 
 
 def launches_per_layer(w):
-    """This library's kernels per DFA layer: keypoints, camera softmax prep and gather; the two
-    camera-encoder launches (split logits); the two tensor-core linears (weights_fc +
-    learnable_fc, output_proj + residual) when the layer runs them."""
+    """This library's kernels per DFA layer: camera softmax factors and gather, plus the
+    keypoints unless the gather computes them; the two camera-encoder launches (split logits);
+    the two tensor-core linears (weights_fc + learnable_fc, output_proj + residual) when the
+    layer runs them."""
     m = w.mods[0]
-    return 3 + (2 if m.split_logits else 0) + (2 if m._tc else 0)
+    return 2 + (0 if m.fused_keypoints else 1) + (2 if m.split_logits else 0) + (2 if m._tc else 0)
 
 
 def unique_tap_pixels(loc, spatial_shapes, start, num_feat):
@@ -652,7 +657,7 @@ def run_ours(args):
             "config": workload_config(args.frames, args.layers, world),
             "keypoint_samples_per_s": value * SAMPLES_PER_CALL,
             "roofline": {
-                "kernel": "dfa_gather_warp_kernel<bf16> (+ cam_softmax_prep_kernel)", "bound": "hbm", "achieved": achieved, "peak": peak,
+                "kernel": "dfa_gather_warp_kernel<bf16> (keypoints + projection + gather)", "bound": "hbm", "achieved": achieved, "peak": peak,
                 "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)",
                 "traffic": traffic,
                 "traffic_source": "ncu dram__bytes_read+write of the layer-0 launch (profiles/dfa_gather_stacked_bs32.md),"

@@ -285,9 +285,36 @@ S4D_API int s4d_dfa_camera_factors(const float* weights_cam, int64_t bs, int64_t
                                    int64_t num_pts, int64_t num_groups, void* workspace, size_t workspace_bytes,
                                    void* stream);
 
+/* s4d_deformable_aggregation with the sample locations computed inside the gather from the
+ * anchors instead of read from a sample_location buffer: the keypoints and their projection of
+ * s4d_kps_project (same arithmetic, so the same (u, v) bits) followed by the gather, in one
+ * launch.  Replaces ttnn.kps_project_fused
+ * (tt-metal/ops/kps_project_fused/kps_project_fused.hpp:12-22) fed by
+ * _kps_generator_pre_rotation (model/deformable_feature_aggregation.py:651-677) together with
+ * the ops s4d_deformable_aggregation replaces; the sample locations are never written.
+ *   anchor            [bs * A, anchor_dim] f32 (anchor_dim >= 8: x, y, z, log w, log l, log h,
+ *                     sin, cos, ...)
+ *   fix_scale         [num_fix, 3] f32
+ *   learnable         [bs * A, (P - num_fix) * 3] f32 keypoint logits (learnable_fc output, e.g.
+ *                     the learnable columns of s4d_dfa_weights_fc), contiguous
+ *   projection_mat    [bs, Ncam, 4, 4] f32, 16-byte aligned; image_wh [bs, Ncam, 2] f32, 8-byte
+ *                     aligned
+ * The other arguments as s4d_deformable_aggregation with CAM_MAJOR split logits and prepared
+ * camera factors (weights_are_logits = 2: the workspace written by s4d_dfa_camera_factors).
+ * Implemented: Ncam 6, L 4, P 13, G 8, C 256. */
+S4D_API int s4d_deformable_aggregation_anchors(const void* mc_ms_feat, int feat_dtype, int64_t num_feat,
+                                               const int32_t* spatial_shape, const int32_t* scale_start_index,
+                                               const float* anchor, int64_t anchor_dim, const float* fix_scale,
+                                               int64_t num_fix, const float* learnable, const float* projection_mat,
+                                               const float* image_wh, const float* weights, const float* weights_cam,
+                                               int64_t bs, int64_t num_anchor, int64_t num_cams, int64_t num_levels,
+                                               int64_t num_pts, int64_t num_groups, int64_t embed_dims,
+                                               int64_t cam_begin, int64_t cam_end, float* out, int32_t* error_flag,
+                                               void* workspace, size_t workspace_bytes, void* stream);
+
 /* Bytes of the optional workspace of s4d_deformable_aggregation (split logits only: the
- * per-frame camera softmax factors, bs * (Ncam + 1) * L * P * G floats; 0 otherwise).
- * Host-only, launches nothing. */
+ * per-frame camera softmax factors, bs * (Ncam + 1) * L * P * G floats rounded up to 16 bytes,
+ * then 16 bytes for the gather's anchor counter; 0 otherwise).  Host-only, launches nothing. */
 S4D_API size_t s4d_dfa_workspace_bytes(int64_t bs, int64_t num_cams, int64_t num_levels, int64_t num_pts,
                                        int64_t num_groups, int split_logits);
 

@@ -54,6 +54,9 @@ SIGNATURES = {
     "s4d_deformable_aggregation": (_int, [_p, _int, _i64, _p, _p, _p, _p, _p, _int, _int,
                                           _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                           _p, _p, _p, _sz, _p]),
+    "s4d_deformable_aggregation_anchors": (_int, [_p, _int, _i64, _p, _p, _p, _i64, _p, _i64, _p, _p, _p, _p, _p,
+                                                  _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                                  _p, _p, _p, _sz, _p]),
     "s4d_dfa_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _int]),
     "s4d_dfa_camera_factors": (_int, [_p, _i64, _i64, _i64, _i64, _i64, _p, _sz, _p]),
     "s4d_dfa_weights_fc": (_int, [_p, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _p]),

@@ -44,7 +44,7 @@ const char* s4d_status_string(int status) {
 
 const char* s4d_last_error(void) { return g_last_error; }
 
-int s4d_abi_version(void) { return 102; }
+int s4d_abi_version(void) { return 103; }
 
 size_t s4d_kps_workspace_bytes(int64_t bs, int64_t num_anchor, int64_t num_cams, int64_t num_pts) {
   if (bs <= 0 || num_anchor <= 0 || num_cams <= 0 || num_pts <= 0) return 0;
@@ -219,14 +219,25 @@ int s4d_kps_project_fused(const float* key_points, const float* anchor, int64_t 
   return launch_kps_project(k, nullptr, nullptr, nullptr, static_cast<cudaStream_t>(stream));
 }
 
-int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, int64_t num_feat,
-                               const int32_t* spatial_shape, const int32_t* scale_start_index,
-                               const float* sample_location, const float* weights, const float* weights_cam,
-                               int weights_are_logits, int layout, int64_t bs, int64_t num_anchor,
-                               int64_t num_cams, int64_t num_levels, int64_t num_pts, int64_t num_groups,
-                               int64_t embed_dims, int64_t cam_begin, int64_t cam_end, float* out,
-                               int32_t* error_flag, void* workspace, size_t workspace_bytes, void* stream) {
-  set_error("%s", "");
+// Keypoint inputs of s4d_deformable_aggregation_anchors.
+struct GatherAnchors {
+  const float* anchor;
+  int64_t anchor_dim;
+  const float* fix_scale;
+  int64_t num_fix;
+  const float* learnable;
+  const float* proj;
+  const float* wh;
+};
+
+// Shared by s4d_deformable_aggregation (kps == null: sample_location given) and
+// s4d_deformable_aggregation_anchors (sample locations computed in the gather).
+static int gather_entry(const void* mc_ms_feat, int feat_dtype, int64_t num_feat, const int32_t* spatial_shape,
+                        const int32_t* scale_start_index, const float* sample_location, const GatherAnchors* kps,
+                        const float* weights, const float* weights_cam, int weights_are_logits, int layout, int64_t bs,
+                        int64_t num_anchor, int64_t num_cams, int64_t num_levels, int64_t num_pts,
+                        int64_t num_groups, int64_t embed_dims, int64_t cam_begin, int64_t cam_end, float* out,
+                        int32_t* error_flag, void* workspace, size_t workspace_bytes, void* stream) {
   if (bs < 0 || num_anchor < 0 || num_cams <= 0 || num_levels <= 0 || num_pts <= 0 || num_groups <= 0 ||
       embed_dims <= 0 || num_feat < 0)
     return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: sizes must be positive");
@@ -261,11 +272,11 @@ int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, int64_t n
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: num_feat must be < 2^31");
   if (bs * num_anchor == 0) return S4D_OK;
   if (mc_ms_feat == nullptr || spatial_shape == nullptr || scale_start_index == nullptr ||
-      sample_location == nullptr || weights == nullptr || out == nullptr)
+      (kps == nullptr && sample_location == nullptr) || weights == nullptr || out == nullptr)
     return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: null pointer");
   if (!aligned(mc_ms_feat, 16))
     return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: mc_ms_feat must be 16-byte aligned");
-  if (!aligned(sample_location, 8) || !aligned(weights, 4) || !aligned(out, 4))
+  if ((kps == nullptr && !aligned(sample_location, 8)) || !aligned(weights, 4) || !aligned(out, 4))
     return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: misaligned sample_location/weights/out");
   GatherParams p{};
   p.feat = mc_ms_feat;
@@ -298,7 +309,60 @@ int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, int64_t n
   }
   if (gather_smem_bytes(p.num_cams, p.num_levels, p.num_pts, p.num_groups, p.cam_begin, p.cam_end) > 200 * 1024)
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: per-anchor staging exceeds shared memory");
+  if (kps != nullptr) {
+    p.kps_anchor = kps->anchor;
+    p.kps_anchor_dim = (int)kps->anchor_dim;
+    p.kps_fix_scale = kps->fix_scale;
+    p.kps_num_fix = (int)kps->num_fix;
+    p.kps_learnable = kps->learnable;
+    p.kps_proj = kps->proj;
+    p.kps_wh = kps->wh;
+  }
   return launch_gather(p, feat_dtype, static_cast<cudaStream_t>(stream));
+}
+
+int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, int64_t num_feat,
+                               const int32_t* spatial_shape, const int32_t* scale_start_index,
+                               const float* sample_location, const float* weights, const float* weights_cam,
+                               int weights_are_logits, int layout, int64_t bs, int64_t num_anchor,
+                               int64_t num_cams, int64_t num_levels, int64_t num_pts, int64_t num_groups,
+                               int64_t embed_dims, int64_t cam_begin, int64_t cam_end, float* out,
+                               int32_t* error_flag, void* workspace, size_t workspace_bytes, void* stream) {
+  set_error("%s", "");
+  return gather_entry(mc_ms_feat, feat_dtype, num_feat, spatial_shape, scale_start_index, sample_location, nullptr,
+                      weights, weights_cam, weights_are_logits, layout, bs, num_anchor, num_cams, num_levels, num_pts,
+                      num_groups, embed_dims, cam_begin, cam_end, out, error_flag, workspace, workspace_bytes, stream);
+}
+
+int s4d_deformable_aggregation_anchors(const void* mc_ms_feat, int feat_dtype, int64_t num_feat,
+                                       const int32_t* spatial_shape, const int32_t* scale_start_index,
+                                       const float* anchor, int64_t anchor_dim, const float* fix_scale,
+                                       int64_t num_fix, const float* learnable, const float* projection_mat,
+                                       const float* image_wh, const float* weights, const float* weights_cam,
+                                       int64_t bs, int64_t num_anchor, int64_t num_cams, int64_t num_levels,
+                                       int64_t num_pts, int64_t num_groups, int64_t embed_dims, int64_t cam_begin,
+                                       int64_t cam_end, float* out, int32_t* error_flag, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  set_error("%s", "");
+  if (!(num_cams == 6 && num_levels == 4 && num_pts == 13 && num_groups == 8))
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE,
+                "s4d_deformable_aggregation_anchors: implemented for 6 cameras, 4 levels, 13 points, 8 groups");
+  if (anchor_dim < 8 || num_fix < 0 || num_fix > num_pts)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation_anchors: need anchor_dim >= 8, 0 <= num_fix <= P");
+  if (bs * num_anchor > 0) {
+    if (anchor == nullptr || projection_mat == nullptr || image_wh == nullptr ||
+        (num_fix > 0 && fix_scale == nullptr) || (num_fix < num_pts && learnable == nullptr))
+      return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation_anchors: null pointer");
+    if (!aligned(anchor, 4) || !aligned(projection_mat, 16) || !aligned(image_wh, 8) ||
+        (fix_scale != nullptr && !aligned(fix_scale, 4)) || (learnable != nullptr && !aligned(learnable, 4)) ||
+        !aligned(weights, 16) || !aligned(weights_cam, 16))
+      return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation_anchors: misaligned pointer (weights, weights_cam "
+                                       "and projection_mat need 16 bytes, image_wh 8)");
+  }
+  const GatherAnchors kps{anchor, anchor_dim, fix_scale, num_fix, learnable, projection_mat, image_wh};
+  return gather_entry(mc_ms_feat, feat_dtype, num_feat, spatial_shape, scale_start_index, nullptr, &kps, weights,
+                      weights_cam, 2, S4D_LAYOUT_CAM_MAJOR, bs, num_anchor, num_cams, num_levels, num_pts,
+                      num_groups, embed_dims, cam_begin, cam_end, out, error_flag, workspace, workspace_bytes, stream);
 }
 
 int s4d_dfa_weights_fc(const float* instance_feature, int64_t instance_ld, const float* anchor_embed,

@@ -31,6 +31,7 @@
 //      accumulate in fp32 registers; 32 resident warps per SM keep enough loads in flight;
 //   5. the 8 warps' partial sums are added through shared memory and scaled by 1/sum_exp.
 // No tensor cores: this is a gather with ~0.1 flop per byte.
+#include "kps_math.cuh"
 #include "params.cuh"
 
 namespace s4d {
@@ -682,7 +683,7 @@ struct SampleRec {
 #ifndef S4D_GATHER_MIN_BLOCKS_BF16
 #define S4D_GATHER_MIN_BLOCKS_BF16 28
 #endif
-template <typename T, int NC, int NL, int NP, int G, int MODE, int WARPS>
+template <typename T, int NC, int NL, int NP, int G, int MODE, int WARPS, bool KPS>
 __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BLOCKS_BF16 : 24)
     dfa_gather_warp_kernel(GatherParams p) {
   constexpr int NLP = NL * NP;
@@ -700,6 +701,8 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BL
   // after them; s_xm[k] = lane bits of leader k's other members
   __shared__ __align__(16) SampleRec<G> s_rec[WARPS][32];
   __shared__ uint32_t s_xm[WARPS][32];
+  __shared__ __align__(16) float4 s_kpt[KPS ? WARPS : 1][KPS ? NP : 1];  // KPS: the anchor's keypoints
+  __shared__ float s_kc[KPS ? WARPS : 1][KPS ? NP * 3 : 1];               // KPS: their scaled coordinates
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < NC * NL; i += WARPS * 32) {
@@ -739,6 +742,28 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BL
   const int b = (int)(anchor_lin / p.num_anchor);
   const int gch = lane / (D / 8);  // group of this lane's output channels
 
+  if (KPS) {  // the anchor's keypoints (kps_project's arithmetic)
+    const float* a = p.kps_anchor + anchor_lin * p.kps_anchor_dim;
+    const int nf = p.kps_num_fix, nlc = (NP - nf) * 3;
+    const float* lg = p.kps_learnable + anchor_lin * nlc;
+    // one scaled coordinate per lane, the learnable ones (a sigmoid each) first, so only the
+    // first of the two passes has sigmoids
+    for (int t = lane; t < NP * 3; t += 32) {
+      const bool learn = t < nlc;
+      const int u = learn ? t : t - nlc;
+      const int pt = (learn ? nf : 0) + u / 3, ax = u - (u / 3) * 3;
+      const float sc = expf(a[3 + ax]);
+      s_kc[warp][3 * pt + ax] = learn ? __fmul_rn(__fsub_rn(kps_sigmoid_rn(lg[u]), 0.5f), sc)
+                                      : __fmul_rn(p.kps_fix_scale[u], sc);
+    }
+    __syncwarp();
+    if (lane < NP) {
+      float px, py, pz;
+      kps_place(a, s_kc[warp][3 * lane], s_kc[warp][3 * lane + 1], s_kc[warp][3 * lane + 2], px, py, pz);
+      s_kpt[warp][lane] = make_float4(px, py, pz, 0.0f);
+    }
+    __syncwarp();
+  }
   const float* wrow = p.weights + anchor_lin * (MODE == 0 ? NW : LPG);
   const float* wcam = MODE == 0 ? nullptr : p.weights_cam + (int64_t)b * NW;
   const float* ec_tab = MODE == 1 ? p.cam_ws + (int64_t)b * (NC + 1) * LPG : nullptr;
@@ -799,7 +824,15 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BL
     float2 uv = make_float2(-4.0f, -4.0f);
     bool maybe = false;
     if (q < NPAIR) {
-      uv = __ldg(locp + q);
+      if (KPS) {  // project keypoint q % NP into camera cq
+        const float4 kp = s_kpt[warp][q - cq * NP];
+        const float4* P = reinterpret_cast<const float4*>(p.kps_proj) + ((int64_t)b * NC + cq) * 4;
+        const float2 wh = __ldg(reinterpret_cast<const float2*>(p.kps_wh) + (int64_t)b * NC + cq);
+        bool front;
+        kps_uv(__ldg(P), __ldg(P + 1), __ldg(P + 2), wh.x, wh.y, kp.x, kp.y, kp.z, uv.x, uv.y, front);
+      } else {
+        uv = __ldg(locp + q);
+      }
       const float4 wn = s_win[cq];
       maybe = cq >= p.cam_begin && cq < p.cam_end && uv.x > wn.x && uv.x < wn.y && uv.y > wn.z && uv.y < wn.w;
     }
@@ -952,7 +985,7 @@ size_t gather_workspace_bytes(int64_t bs, int ncam, int nl, int np, int G) {
 // and feature type (index `which`).
 template <typename K>
 static int resident_warp_blocks(K kernel, int which) {
-  static int cache[2][64] = {};
+  static int cache[4][64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148 * 28;
   if (cache[which][dev] > 0) return cache[which][dev];
@@ -1004,16 +1037,25 @@ int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream) {
     int st = cuda_check(cudaMemsetAsync(q.anchor_counter, 0, sizeof(unsigned), stream), "cudaMemsetAsync(counter)");
     if (st) return st;
     const int64_t anchors = (int64_t)p.bs * p.num_anchor;
-    auto kb = dfa_gather_warp_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock>;
-    auto kf = dfa_gather_warp_kernel<float, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock>;
-    const int64_t fit = feat_dtype == S4D_DTYPE_BF16 ? resident_warp_blocks(kb, 0) : resident_warp_blocks(kf, 1);
-    const unsigned wgrid = (unsigned)(anchors < fit ? anchors : fit);
-    if (feat_dtype == S4D_DTYPE_BF16)
-      kb<<<wgrid, kWarpBlock * 32, 0, stream>>>(q);
-    else
-      kf<<<wgrid, kWarpBlock * 32, 0, stream>>>(q);
+    auto launch = [&](auto kernel, int which) {
+      const int64_t fit = resident_warp_blocks(kernel, which);
+      kernel<<<(unsigned)(anchors < fit ? anchors : fit), kWarpBlock * 32, 0, stream>>>(q);
+    };
+    const bool bf = feat_dtype == S4D_DTYPE_BF16;
+    if (p.kps_anchor != nullptr) {
+      if (bf)
+        launch(dfa_gather_warp_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock, true>, 2);
+      else
+        launch(dfa_gather_warp_kernel<float, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock, true>, 3);
+    } else if (bf) {
+      launch(dfa_gather_warp_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock, false>, 0);
+    } else {
+      launch(dfa_gather_warp_kernel<float, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock, false>, 1);
+    }
     return cuda_check(cudaGetLastError(), "dfa_gather_warp_kernel launch");
   }
+  if (p.kps_anchor != nullptr)  // only the warp kernel computes sample locations; the others read p.loc
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "gather from anchors: needs the split-logit warp path");
   if (fast_path_ok(p)) {
     if (feat_dtype == S4D_DTYPE_BF16)
       dfa_gather_fast_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG><<<grid, kGatherThreads, 0, stream>>>(p);

@@ -13,14 +13,11 @@
 // one ballot word per 32 elements and one visible count per block; the scatter kernel sums the
 // counts of the blocks before it, scans its own 32 words and writes the rows.
 //
-// Arithmetic order is fixed and fused multiply-add is disabled on every line that decides a
-// mask bit (the __f*_rn intrinsics), so the integer outputs reproduce a CPU evaluation of the
-// same expression order bit for bit:
-//   X_r = ((P[r][0]*px + P[r][1]*py) + P[r][2]*pz) + P[r][3];   z = X_2 < 1e-5 ? 1e-5 : X_2
-//   u = (X_0 / z) / w;   v = (X_1 / z) / h
-// u and v are first formed with one fast division each; where either lies within 1e-5 of 0 or 1
-// (or is not finite) the correctly rounded divisions above are used instead, so the visibility
-// decisions are those of the exact expression and the sample locations are within a few ulp.
+// The keypoint and projection arithmetic (fixed order, no fused multiply-add on any line that
+// decides a mask bit, so the integer outputs reproduce a CPU evaluation of the same expression
+// order bit for bit) is in kps_math.cuh, shared with the gather that computes its own sample
+// locations.
+#include "kps_math.cuh"
 #include "params.cuh"
 
 namespace s4d {
@@ -34,10 +31,6 @@ constexpr int kMaxPts = 64;                                // keypoints per anch
 constexpr int kMaxBlockKeypoints = kElemsPerBlock + 2 * kMaxPts;
 
 
-__device__ __forceinline__ float sigmoid_rn(float x) {
-  return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
-}
-
 // Rotated + translated keypoint p of anchor n (fp32, fixed order); `lg` holds the anchor's
 // learnable logits (global memory, or the block's shared-memory copy).
 __device__ __forceinline__ void keypoint(const KpsParams& k, uint32_t n, int p, const float* lg_anchor, float& px,
@@ -50,29 +43,9 @@ __device__ __forceinline__ void keypoint(const KpsParams& k, uint32_t n, int p, 
     ky = q[1];
     kz = q[2];
   } else {
-    const float sx = expf(a[3]), sy = expf(a[4]), sz = expf(a[5]);
-    if (p < k.num_fix) {
-      const float* fs = k.fix_scale + p * 3;
-      kx = __fmul_rn(fs[0], sx);
-      ky = __fmul_rn(fs[1], sy);
-      kz = __fmul_rn(fs[2], sz);
-    } else {
-      const float* lg = lg_anchor + (p - k.num_fix) * 3;
-      kx = __fmul_rn(__fsub_rn(sigmoid_rn(lg[0]), 0.5f), sx);
-      ky = __fmul_rn(__fsub_rn(sigmoid_rn(lg[1]), 0.5f), sy);
-      kz = __fmul_rn(__fsub_rn(sigmoid_rn(lg[2]), 0.5f), sz);
-    }
+    kps_scaled(a, k.fix_scale, k.num_fix, lg_anchor, p, kx, ky, kz);
   }
-  const float s = a[6], c = a[7];
-  const float rx = __fsub_rn(__fmul_rn(c, kx), __fmul_rn(s, ky));
-  const float ry = __fadd_rn(__fmul_rn(s, kx), __fmul_rn(c, ky));
-  px = __fadd_rn(rx, a[0]);
-  py = __fadd_rn(ry, a[1]);
-  pz = __fadd_rn(kz, a[2]);
-}
-
-__device__ __forceinline__ float proj_row(const float* r, float px, float py, float pz) {
-  return __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(r[0], px), __fmul_rn(r[1], py)), __fmul_rn(r[2], pz)), r[3]);
+  kps_place(a, kx, ky, kz, px, py, pz);
 }
 
 template <bool FUSED>
@@ -164,23 +137,12 @@ __global__ void __launch_bounds__(kKpsThreads) kps_project_kernel(KpsParams k) {
       const uint32_t b = k.div_anchors.div(n);
       const int ik = (int)(n - n0) * k.num_pts + p;
       const float px = s_kp[3 * ik], py = s_kp[3 * ik + 1], pz = s_kp[3 * ik + 2];
+      float u, v;
+      bool in_front;
       const float* P = k.proj + (b * k.num_cams + c) * 16;
-      const float X0 = proj_row(P, px, py, pz);
-      const float X1 = proj_row(P + 4, px, py, pz);
-      const float X2 = proj_row(P + 8, px, py, pz);
-      const bool in_front = X2 > 1e-5f;
-      const float z = X2 < 1e-5f ? 1e-5f : X2;  // torch.clamp(min=1e-5): NaN stays NaN
       const float* wh = k.wh + (b * k.num_cams + c) * 2;
-      // Fast quotients first (a few ulp from the correctly rounded (X / z) / w); the exact IEEE
-      // divisions are redone where a fast u or v lies within 1e-5 of the frustum bounds 0 and 1,
-      // the only place the two could disagree on visibility, so masks and indices stay exact.
-      float u = __fdividef(X0, z * wh[0]);
-      float v = __fdividef(X1, z * wh[1]);
-      if (fabsf(u) < 1e-5f || fabsf(u - 1.0f) < 1e-5f || fabsf(v) < 1e-5f || fabsf(v - 1.0f) < 1e-5f ||
-          !(fabsf(u) < 1e30f && fabsf(v) < 1e30f)) {
-        u = __fdiv_rn(__fdiv_rn(X0, z), wh[0]);
-        v = __fdiv_rn(__fdiv_rn(X1, z), wh[1]);
-      }
+      kps_uv(make_float4(P[0], P[1], P[2], P[3]), make_float4(P[4], P[5], P[6], P[7]),
+             make_float4(P[8], P[9], P[10], P[11]), wh[0], wh[1], px, py, pz, u, v, in_front);
       vis = in_front && u >= 0.0f && u <= 1.0f && v >= 0.0f && v <= 1.0f;
       if (k.mask != nullptr) k.mask[e] = in_front ? 1 : 0;
       if (k.loc != nullptr) {

@@ -61,6 +61,15 @@ struct GatherParams {
   int layout;
   int factors_ready;  // split logits: cam_ws already holds the camera factors (no prep launch)
   unsigned* anchor_counter;  // warp kernel: next anchor to take (in the workspace, zeroed per launch)
+  // Sample locations computed in the gather from the anchors (kps_anchor != null; loc unused):
+  // keypoints as kps_project's, projected with kps_proj [bs, Ncam, 4, 4] and kps_wh [bs, Ncam, 2].
+  const float* kps_anchor;     // [bs * A, kps_anchor_dim]
+  int kps_anchor_dim;
+  const float* kps_fix_scale;  // [kps_num_fix, 3]
+  int kps_num_fix;
+  const float* kps_learnable;  // [bs * A, (P - kps_num_fix) * 3] logits
+  const float* kps_proj;
+  const float* kps_wh;
 };
 
 // Tensor-core linears (linear_tc.cu).  Row strides are in floats.

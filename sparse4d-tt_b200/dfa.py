@@ -161,6 +161,9 @@ class DeformableFeatureAggregation:
         self._cached_camera_factors = None
         # the Sparse4D v3 shape has a kernel for the per-frame camera softmax factors
         self._factors_ok = (num_cams, num_levels, num_pts, num_groups) == (6, 4, 13, 8)
+        # ... and for the gather that computes its own sample locations from the anchors
+        # (s4d_deformable_aggregation_anchors): no keypoint launch, no location buffer.
+        self.fused_keypoints = self._tc and self._factors_ok
         self._side: Optional[torch.cuda.Stream] = None
         self._side_kps: Optional[torch.cuda.Stream] = None
         self._side_pending = False
@@ -303,9 +306,17 @@ class DeformableFeatureAggregation:
             side = rows >= 8192 or capturing
             logits_cam = self._camera_logits(projection_mat, bs, side=side)
             inst2d, embed2d = ops.row_view(instance_feature, C), ops.row_view(anchor_embed, C)
-            loc = torch.empty(bs, num_anchor, self.num_cams, self.num_pts, 2, dtype=torch.float32, device=dev)
             logits = torch.empty(bs, num_anchor, self.num_levels, self.num_pts, self.num_groups, device=dev)
-            if rows <= 4096:
+            if self.fused_keypoints:
+                # The gather computes the sample locations itself from the anchors (no keypoint
+                # launch, no location buffer); the tensor-core pass supplies the learnable
+                # keypoint logits (one N-32 MMA per K step).
+                learn = torch.empty(bs, num_anchor, 3 * self.num_learnable_pts, device=dev)
+                ops.weights_fc_into(logits.view(rows, -1), learn.view(rows, -1), inst2d, embed2d,
+                                    self.weights_fc_weight, self.learnable_fc_weight, self.learnable_fc_bias)
+                loc = None
+            elif rows <= 4096:
+                loc = torch.empty(bs, num_anchor, self.num_cams, self.num_pts, 2, dtype=torch.float32, device=dev)
                 # Small batches are latency-bound: the keypoints compute their own learnable logits
                 # and, under capture, run on a second side stream beside weights_fc (and the camera
                 # terms) instead of after it.
@@ -325,6 +336,7 @@ class DeformableFeatureAggregation:
             else:
                 # Large batches: the tensor-core pass produces the learnable logits almost for free
                 # (one N-32 MMA per K step), then the plain keypoint kernel runs.
+                loc = torch.empty(bs, num_anchor, self.num_cams, self.num_pts, 2, dtype=torch.float32, device=dev)
                 learn = torch.empty(bs, num_anchor, 3 * self.num_learnable_pts, device=dev)
                 ops.weights_fc_into(logits.view(rows, -1), learn.view(rows, -1), inst2d, embed2d,
                                     self.weights_fc_weight, self.learnable_fc_weight, self.learnable_fc_bias)
@@ -361,8 +373,15 @@ class DeformableFeatureAggregation:
             ws, ready = self._cached_camera_factors, self._cached_camera_factors is not None
             if ws is None:
                 ws = ops.dfa_workspace(bs, self.num_cams, self.num_levels, self.num_pts, self.num_groups, dev)
-        ops.deformable_aggregation_into(feats, mc_ms_feat, spatial_shape, scale_start, loc, logits, True,
-                                        logits_cam, cam_begin, cam_end, workspace=ws, factors_ready=ready)
+        if loc is None:  # the camera factors are prepared whenever the shape has the kernel for them
+            if not ready:
+                raise RuntimeError("DeformableFeatureAggregation: camera factors missing for the gather from anchors")
+            ops.deformable_aggregation_anchors_into(feats, mc_ms_feat, spatial_shape, scale_start, anchor,
+                                                    self.fix_scale, learn.view(rows, -1), projection_mat, image_wh,
+                                                    logits, logits_cam, ws, cam_begin, cam_end)
+        else:
+            ops.deformable_aggregation_into(feats, mc_ms_feat, spatial_shape, scale_start, loc, logits, True,
+                                            logits_cam, cam_begin, cam_end, workspace=ws, factors_ready=ready)
         if log is not None:
             self._timing.wait_stream(cur)
             ev[1].record(self._timing)

@@ -274,6 +274,56 @@ def deformable_aggregation_into(out: Tensor, mc_ms_feat: Tensor, spatial_shape: 
     return out
 
 
+def deformable_aggregation_anchors_into(out: Tensor, mc_ms_feat: Tensor, spatial_shape: Tensor,
+                                        scale_start_index: Tensor, anchor: Tensor, fix_scale: Tensor,
+                                        learnable: Optional[Tensor], projection_mat: Tensor, image_wh: Tensor,
+                                        weights: Tensor, weights_cam: Tensor, workspace: Tensor, cam_begin: int = 0,
+                                        cam_end: int = -1, error_flag: Optional[Tensor] = None) -> Tensor:
+    """``deformable_aggregation_into`` with the sample locations computed inside the gather from
+    ``anchor [bs, A, D]``, ``fix_scale [num_fix, 3]``, the keypoint logits ``learnable [bs*A,
+    (P - num_fix)*3]``, ``projection_mat [bs, Ncam, 4, 4]`` and ``image_wh [bs, Ncam, 2]``
+    (the same (u, v) as ``kps_project_into``), for split logits whose camera factors
+    ``camera_factors_into`` already wrote into ``workspace``."""
+    name = "deformable_aggregation_anchors"
+    dev = _require_cuda(name, out, mc_ms_feat, spatial_shape, scale_start_index, anchor, fix_scale, learnable,
+                        projection_mat, image_wh, weights, weights_cam, workspace, error_flag)
+    _check_contig(name, out=out, mc_ms_feat=mc_ms_feat, spatial_shape=spatial_shape,
+                  scale_start_index=scale_start_index, anchor=anchor, fix_scale=fix_scale, learnable=learnable,
+                  projection_mat=projection_mat, image_wh=image_wh, weights=weights, weights_cam=weights_cam,
+                  workspace=workspace)
+    _check_dtype(name, mc_ms_feat, (torch.float32, torch.bfloat16), "mc_ms_feat")
+    _check_dtype(name, spatial_shape, (torch.int32,), "spatial_shape")
+    _check_dtype(name, scale_start_index, (torch.int32,), "scale_start_index")
+    for k, t in (("anchor", anchor), ("fix_scale", fix_scale), ("learnable", learnable),
+                 ("projection_mat", projection_mat), ("image_wh", image_wh), ("weights", weights),
+                 ("weights_cam", weights_cam), ("out", out)):
+        _check_dtype(name, t, (torch.float32,), k)
+    _check_dtype(name, error_flag, (torch.int32,), "error_flag")
+    _require(mc_ms_feat.dim() == 3 and weights_cam.dim() == 5, "mc_ms_feat [bs, num_feat, C], weights_cam "
+             "[bs, Ncam, L, P, G]")
+    bs, nc, nl, P, G = (int(v) for v in weights_cam.shape)
+    A = int(out.shape[1])
+    C = int(mc_ms_feat.shape[2])
+    _require(tuple(out.shape) == (bs, A, C), f"out must be [{bs}, A, {C}]")
+    _require(anchor.numel() == bs * A * int(anchor.shape[-1]), "anchor must be [bs, A, D]")
+    _require(tuple(projection_mat.shape[-2:]) == (4, 4) and projection_mat.numel() == bs * nc * 16,
+             f"projection_mat must be [{bs}, {nc}, 4, 4]")
+    _require(image_wh.numel() == bs * nc * 2, f"image_wh must be [{bs}, {nc}, 2]")
+    num_fix = int(fix_scale.shape[0])
+    _require(learnable is None or learnable.numel() == bs * A * (P - num_fix) * 3,
+             f"learnable must hold {(P - num_fix) * 3} logits per anchor")
+    ce = nc if cam_end is None or cam_end < 0 else int(cam_end)
+    st = L.lib().s4d_deformable_aggregation_anchors(
+        mc_ms_feat.data_ptr(), L.S4D_DTYPE_BF16 if mc_ms_feat.dtype == torch.bfloat16 else L.S4D_DTYPE_F32,
+        int(mc_ms_feat.shape[1]), spatial_shape.data_ptr(), scale_start_index.data_ptr(), anchor.data_ptr(),
+        int(anchor.shape[-1]), fix_scale.data_ptr(), num_fix, _ptr(learnable), projection_mat.data_ptr(),
+        image_wh.data_ptr(), weights.data_ptr(), weights_cam.data_ptr(), bs, A, nc, nl, P, G, C, int(cam_begin), ce,
+        out.data_ptr(), _ptr(error_flag), workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+        _stream_ptr(dev))
+    L.check(name, st)
+    return out
+
+
 def dfa_workspace_bytes(bs: int, num_cams: int, num_levels: int, num_pts: int, num_groups: int,
                         split_logits: bool) -> int:
     return int(L.lib().s4d_dfa_workspace_bytes(bs, num_cams, num_levels, num_pts, num_groups,

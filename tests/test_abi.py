@@ -33,7 +33,7 @@ def lib():
 
 def test_every_declared_symbol_is_exported(lib):
     names = declared_functions()
-    assert len(names) == 19, names
+    assert len(names) == 20, names
     for n in names:
         assert hasattr(lib, n), n
         assert n in L.SIGNATURES, f"{n} has no ctypes signature"
@@ -52,7 +52,7 @@ def test_status_strings_and_version(lib):
     assert L.status_string(0) == "S4D_OK"
     assert L.status_string(2) == "S4D_ERR_UNSUPPORTED_SHAPE"
     assert L.status_string(99) == "S4D_ERR_UNKNOWN"
-    assert lib.s4d_abi_version() == 102
+    assert lib.s4d_abi_version() == 103
 
 
 def test_dfa_workspace_bytes(lib):
@@ -322,3 +322,41 @@ def test_prepared_factors_rejects(lib):
     assert st == L.S4D_ERR_INVALID_ARG and "0, 1 or 2" in msg
     assert lib.s4d_dfa_camera_factors(16, 2, 6, 4, 13, 8, 16, 16, None) == L.S4D_ERR_INVALID_ARG  # too small
     assert lib.s4d_dfa_camera_factors(16, 0, 6, 4, 13, 8, None, 0, None) == L.S4D_OK
+
+
+def _gather_anchors(lib, **kw):
+    a = dict(feat=16, dtype=1, num_feat=100, shape=16, start=16, anchor=16, adim=11, fix=16, nfix=7, learn=16,
+             proj=16, wh=16, w=16, wc=16, bs=1, A=4, nc=6, nl=4, np=13, G=8, C=256, cb=0, ce=6, out=16, flag=None,
+             ws=16, wsb=1 << 20)
+    a.update(kw)
+    st = lib.s4d_deformable_aggregation_anchors(
+        a["feat"], a["dtype"], a["num_feat"], a["shape"], a["start"], a["anchor"], a["adim"], a["fix"], a["nfix"],
+        a["learn"], a["proj"], a["wh"], a["w"], a["wc"], a["bs"], a["A"], a["nc"], a["nl"], a["np"], a["G"], a["C"],
+        a["cb"], a["ce"], a["out"], a["flag"], a["ws"], a["wsb"], None)
+    return st, lib.s4d_last_error().decode()
+
+
+@pytest.mark.parametrize("kw,status,text", [
+    (dict(nc=5, ce=5), L.S4D_ERR_UNSUPPORTED_SHAPE, "6 cameras"),
+    (dict(np=12), L.S4D_ERR_UNSUPPORTED_SHAPE, "13 points"),
+    (dict(adim=7), L.S4D_ERR_INVALID_ARG, "anchor_dim"),
+    (dict(nfix=14), L.S4D_ERR_INVALID_ARG, "num_fix"),
+    (dict(anchor=None), L.S4D_ERR_INVALID_ARG, "null"),
+    (dict(learn=None), L.S4D_ERR_INVALID_ARG, "null"),
+    (dict(proj=8), L.S4D_ERR_INVALID_ARG, "projection_mat"),
+    (dict(wh=4), L.S4D_ERR_INVALID_ARG, "image_wh"),
+    (dict(w=8), L.S4D_ERR_INVALID_ARG, "weights"),
+    (dict(ws=None, wsb=0), L.S4D_ERR_INVALID_ARG, "prepared"),
+    (dict(wc=None), L.S4D_ERR_INVALID_ARG, "prepared"),
+    (dict(C=128), L.S4D_ERR_UNSUPPORTED_SHAPE, "embed_dims"),
+    (dict(wsb=64), L.S4D_ERR_INVALID_ARG, "workspace"),
+])
+def test_gather_anchors_rejects_on_host(lib, kw, status, text):
+    st, msg = _gather_anchors(lib, **kw)
+    assert st == status, (st, msg)
+    assert text in msg
+
+
+def test_gather_anchors_empty_batch_is_a_noop(lib):
+    st, msg = _gather_anchors(lib, bs=0, anchor=None, learn=None, feat=None, out=None)
+    assert st == L.S4D_OK, msg
