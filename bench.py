@@ -602,6 +602,11 @@ def run_ours(args):
         w.step()
     torch.cuda.synchronize()
     bytes_per_layer = w.algorithmic_bytes_per_layer()
+    # the same step launched eagerly, layer by layer (host launch cost included), timed before
+    # any graph exists
+    for _ in range(args.warmup):
+        w.step()
+    eager_ms = time_steps(w.step, args.steps, barrier)
     stack = w.graph_stack()
     for _ in range(args.warmup):
         stack.replay()
@@ -612,10 +617,6 @@ def run_ours(args):
     ms = time_steps(stack.replay, args.steps, barrier)
     clock_info = clocks.stop()
     g_ms = stack.gather_times_ms()  # the gather launches of the last timed replay
-    # the same step launched eagerly, layer by layer (host launch cost included)
-    for _ in range(args.warmup):
-        w.step()
-    eager_ms = time_steps(w.step, args.steps, barrier)
 
     t = torch.tensor([ms, eager_ms], device=device)
     if pg is not None:

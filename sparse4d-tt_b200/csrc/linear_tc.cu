@@ -10,8 +10,8 @@
 //                (model/deformable_feature_aggregation.py:934-950; test/dfa_pcc.py:299-304).
 //
 // Both kernels: one CTA per 128-row tile, 6 warps.
-//   warp 0     TMA producer: A and B tiles of 32 fp32 (128-byte rows, 128-byte swizzle, zero
-//              fill past the last row) into a 2-stage shared-memory ring;
+//   warp 0     TMA producer: A and B tiles of 16 fp32 (64-byte rows, 64-byte swizzle, zero
+//              fill past the last row) into a 4-stage shared-memory ring;
 //   warp 1     allocates the tensor-memory accumulator (128 lanes x N fp32 columns); one thread
 //              issues tcgen05.mma (M 128, K 8, N <= 256 per instruction) and commits each stage
 //              back to the producer;
@@ -32,10 +32,10 @@ namespace s4d {
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kBK = 32;  // fp32 per stage row: 128 bytes, one swizzle span
+constexpr int kBK = 16;  // fp32 per stage row: 64 bytes, one 64-byte swizzle span
 constexpr int kThreads = 192;
-constexpr int kStages = 2;
-constexpr int kATile = kBM * kBK * 4;  // 16 KiB
+constexpr int kStages = 4;
+constexpr int kATile = kBM * kBK * 4;  // 8 KiB
 constexpr int kStageChunk = 32 * 32 * 4;  // one 32x32 fp32 output box (4 KiB)
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
@@ -141,15 +141,15 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-// Shared-memory matrix descriptor of a K-major tile of 128-byte rows stored with the 128-byte
-// swizzle (what a TMA box of 32 fp32 x rows with CU_TENSOR_MAP_SWIZZLE_128B writes, from a
-// 1024-byte aligned base): start address >> 4 in bits 0-13; leading-dimension offset 16 B
-// (not used by swizzled K-major layouts) in bits 16-29; 1024 B between 8-row groups in bits
-// 32-45; descriptor version 1 in bits 46-47; swizzle mode 2 (128 B) in bits 61-63.  Adding 2
+// Shared-memory matrix descriptor of a K-major tile of 64-byte rows stored with the 64-byte
+// swizzle (what a TMA box of 16 fp32 x rows with CU_TENSOR_MAP_SWIZZLE_64B writes, from a
+// 512-byte aligned base): start address >> 4 in bits 0-13; leading-dimension offset 16 B
+// (not used by swizzled K-major layouts) in bits 16-29; 512 B between 8-row groups in bits
+// 32-45; descriptor version 1 in bits 46-47; swizzle mode 4 (64 B) in bits 61-63.  Adding 2
 // to the descriptor advances the start by 32 bytes, i.e. by the 8 fp32 of one MMA's K step.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
-         (uint64_t(2) << 61);
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
+  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(512 >> 4) << 32) | (uint64_t(1) << 46) |
+         (uint64_t(4) << 61);
 }
 
 // Instruction descriptor of kind::tf32: D f32 (bits 4-5 = 1), A and B TF32 (bits 7-9 and
@@ -309,7 +309,7 @@ struct Wfc {
   static constexpr uint32_t kCols = 512;
   static constexpr size_t kSmem = smem_bytes(kStage);
   static_assert(NW % 32 == 0 && kNmma % 16 == 0 && kNmma <= 256 && NW + kNL <= 512, "logit columns");
-  static_assert(kBW % 1024 == 0 && kStage % 1024 == 0 && (kNmma * kBK * 4) % 1024 == 0, "swizzle alignment");
+  static_assert(kBW % 512 == 0 && kStage % 1024 == 0 && (kNmma * kBK * 4) % 512 == 0, "swizzle alignment");
   static_assert(4 * 2 * kStageChunk <= kStages * kStage, "epilogue staging fits in the stages");
 };
 
@@ -355,14 +355,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(sum0 + 8 * s, (kb / kStages) & 1, c.abort_flag)) break;
         tc_fence_after();
         const uint32_t st = smem_u32(smem + s * S::kStage);
-        const uint64_t a_inst = sw128_desc(st), a_sum = sw128_desc(st + kATile);
-        const uint64_t b_kps = sw128_desc(st + 2 * kATile + S::kBW);
+        const uint64_t a_inst = sw64_desc(st), a_sum = sw64_desc(st + kATile);
+        const uint64_t b_kps = sw64_desc(st + 2 * kATile + S::kBW);
 #pragma unroll
         for (int k = 0; k < kBK / 8; ++k) {
           const uint32_t acc = (kb | k) != 0;
 #pragma unroll
           for (int j = 0; j < S::kSplit; ++j)
-            mma_tf32(tmem + j * S::kNmma, a_sum + 2 * k, sw128_desc(st + 2 * kATile + j * S::kNmma * kBK * 4) + 2 * k,
+            mma_tf32(tmem + j * S::kNmma, a_sum + 2 * k, sw64_desc(st + 2 * kATile + j * S::kNmma * kBK * 4) + 2 * k,
                      tf32_idesc(S::kNmma), acc);
           mma_tf32(tmem + NW, a_inst + 2 * k, b_kps + 2 * k, tf32_idesc(S::kNL), acc);
         }
@@ -453,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (!mbar_wait(full0 + 8 * s, (kb / kStages) & 1, c.abort_flag)) break;
         tc_fence_after();
         const uint32_t st = smem_u32(smem + s * S::kStage);
-        const uint64_t a = sw128_desc(st), b = sw128_desc(st + kATile);
+        const uint64_t a = sw64_desc(st), b = sw64_desc(st + kATile);
 #pragma unroll
         for (int k = 0; k < kBK / 8; ++k) mma_tf32(tmem, a + 2 * k, b + 2 * k, tf32_idesc(S::kN), (kb | k) != 0);
         mma_commit(empty0 + 8 * s);
@@ -512,17 +512,20 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// Tensor map of an fp32 row-major matrix [rows, cols] with row stride ld (floats): boxes of
-// 32 columns x box_rows rows, 128-byte swizzle, zero fill outside the matrix.
-int make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// Tensor map of an fp32 row-major matrix [rows, cols] with row stride ld (floats), zero fill
+// outside the matrix: operand loads use boxes of kBK (16) columns x box_rows rows with the
+// 64-byte swizzle; `store` maps (the epilogue's) boxes of 32 columns with the 128-byte swizzle.
+int make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+             bool store = false) {
   EncodeTiledFn fn = encode_tiled();
   if (fn == nullptr) return fail(S4D_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the CUDA driver");
   const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
   const cuuint64_t strides[1] = {cuuint64_t(ld) * 4};
-  const cuuint32_t box[2] = {uint32_t(kBK), uint32_t(box_rows)};
+  const cuuint32_t box[2] = {uint32_t(store ? 32 : kBK), uint32_t(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, store ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (CUresult %d) for a [%lld, %lld] matrix, ld %lld", int(r),
@@ -550,7 +553,7 @@ int launch_weights_fc(const WfcParams& p, cudaStream_t stream) {
   if (st == S4D_OK) st = make_map(&me, p.embed, p.rows, p.k, p.embed_ld, kBM);
   if (st == S4D_OK) st = make_map(&mw, p.w_fc, p.n_logits, p.k, p.k, S::kNmma);
   if (st == S4D_OK) st = make_map(&mk, p.w_kps, p.n_learn > 0 ? p.n_learn : 1, p.k, p.k, S::kNL);
-  if (st == S4D_OK) st = make_map(&mo, p.logits, p.rows, p.n_logits, p.n_logits, 32);
+  if (st == S4D_OK) st = make_map(&mo, p.logits, p.rows, p.n_logits, p.n_logits, 32, true);
   if (st == S4D_OK) st = set_smem(weights_fc_kernel<416>, S::kSmem, "cudaFuncSetAttribute(weights_fc_kernel)");
   if (st != S4D_OK) return st;
   weights_fc_kernel<416><<<unsigned((p.rows + kBM - 1) / kBM), kThreads, S::kSmem, stream>>>(mi, me, mw, mk, mo, p);
@@ -564,7 +567,7 @@ int launch_output_proj(const OprojParams& p, cudaStream_t stream) {
   CUtensorMap mf, mw, mo;
   int st = make_map(&mf, p.feat, p.rows, p.k, p.k, kBM);
   if (st == S4D_OK) st = make_map(&mw, p.w, S::kN, p.k, p.k, S::kN);
-  if (st == S4D_OK) st = make_map(&mo, p.out, p.rows, S::kN, p.out_ld, 32);
+  if (st == S4D_OK) st = make_map(&mo, p.out, p.rows, S::kN, p.out_ld, 32, true);
   if (st == S4D_OK) st = set_smem(output_proj_kernel, S::kSmem, "cudaFuncSetAttribute(output_proj_kernel)");
   if (st != S4D_OK) return st;
   output_proj_kernel<<<unsigned((p.rows + kBM - 1) / kBM), kThreads, S::kSmem, stream>>>(mf, mw, mo, p);
