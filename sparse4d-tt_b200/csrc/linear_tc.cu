@@ -3,8 +3,8 @@
 //
 //   weights_fc   logits = (inst + embed) . W_fc^T and learnable = inst . W_kps^T + b_kps in one
 //                pass over 128-row tiles (model/deformable_feature_aggregation.py:651-677,719-798;
-//                test/dfa_pcc.py:231-233,306-320).  The sum inst + embed is formed in shared
-//                memory, never in HBM.
+//                test/dfa_pcc.py:231-233,306-320).  The sum is never formed: inst . W_fc^T and
+//                embed . W_fc^T accumulate into the same tensor-memory columns from one W tile.
 //   output_proj  feats . W_o^T + b_o written straight into the residual output, the instance
 //                feature copied beside it (cat) or added to it (add)
 //                (model/deformable_feature_aggregation.py:934-950; test/dfa_pcc.py:299-304).
@@ -15,9 +15,8 @@
 //   warp 1     allocates the tensor-memory accumulator (128 lanes x N fp32 columns); one thread
 //              issues tcgen05.mma (M 128, K 8, N <= 256 per instruction) and commits each stage
 //              back to the producer;
-//   warps 2-5  during the main loop: weights_fc adds the embed tile into the instance tile's
-//              twin in shared memory (the MMA waits for it); output_proj copies the instance
-//              rows for the residual cat.  After it: tcgen05.ld of their 32 TMEM lanes (warp
+//   warps 2-5  during the main loop: output_proj copies the instance rows for the residual cat
+//              (weights_fc has nothing for them to do).  After it: tcgen05.ld of their 32 TMEM lanes (warp
 //              index mod 4), bias / residual in registers, the tile staged in shared memory
 //              with the 128-byte swizzle and written by TMA bulk-tensor stores.
 // Every barrier wait is bounded: after 2 s the CTA raises S4D_FLAG_WAIT_TIMEOUT, lets its copies
@@ -180,7 +179,7 @@ struct Ctl {
   volatile int* abort_flag;
 };
 
-// Barrier block after the stages: full[2], aux[2], empty[2], acc, then the TMEM slot and the
+// Barrier block after the stages: full[S], aux[S] (unused slots), empty[S], acc, then the TMEM slot and the
 // abort flag.
 template <int STAGE_BYTES>
 __device__ __forceinline__ Ctl carve(unsigned char* smem) {
@@ -258,7 +257,7 @@ __device__ __forceinline__ uint32_t prologue(const Ctl& c, uint32_t cols, int au
     const uint32_t b0 = smem_u32(c.bars);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(b0 + 8 * s, 1);                                    // full: TMA bytes landed
-      mbar_init(b0 + 8 * (kStages + s), aux_count > 0 ? aux_count : 1);  // aux: shared-memory sum ready
+      mbar_init(b0 + 8 * (kStages + s), aux_count > 0 ? aux_count : 1);  // aux: not waited on by these kernels
       mbar_init(b0 + 8 * (2 * kStages + s), 1);                    // empty: MMAs of the stage done
     }
     mbar_init(b0 + 8 * (3 * kStages), 1);  // acc: accumulator complete
@@ -305,7 +304,7 @@ struct Wfc {
   static constexpr int kNL = 32;                     // learnable columns (one N-32 MMA)
   static constexpr int kBW = NW * kBK * 4;
   static constexpr int kBL = kNL * kBK * 4;
-  static constexpr int kStage = 2 * kATile + kBW + kBL;  // inst, embed (+= inst), W_fc, W_kps
+  static constexpr int kStage = 2 * kATile + kBW + kBL;  // inst, embed, W_fc, W_kps
   static constexpr uint32_t kCols = 512;
   static constexpr size_t kSmem = smem_bytes(kStage);
   static_assert(NW % 32 == 0 && kNmma % 16 == 0 && kNmma <= 256 && NW + kNL <= 512, "logit columns");
@@ -322,12 +321,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
   const Ctl c = carve<S::kStage>(smem);
-  const uint32_t full0 = smem_u32(c.bars), sum0 = full0 + 8 * kStages, empty0 = full0 + 16 * kStages,
-                 acc_bar = full0 + 24 * kStages;
+  const uint32_t full0 = smem_u32(c.bars), empty0 = full0 + 16 * kStages, acc_bar = full0 + 24 * kStages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kbs = p.k / kBK;
   const int64_t row0 = int64_t(blockIdx.x) * kBM;
-  const uint32_t tmem = prologue(c, S::kCols, 128);
+  const uint32_t tmem = prologue(c, S::kCols, 0);
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer
@@ -352,18 +350,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < kbs; ++kb) {
         const int s = kb % kStages;
         if (!mbar_wait(full0 + 8 * s, (kb / kStages) & 1, c.abort_flag)) break;
-        if (!mbar_wait(sum0 + 8 * s, (kb / kStages) & 1, c.abort_flag)) break;
         tc_fence_after();
         const uint32_t st = smem_u32(smem + s * S::kStage);
-        const uint64_t a_inst = sw64_desc(st), a_sum = sw64_desc(st + kATile);
+        const uint64_t a_inst = sw64_desc(st), a_emb = sw64_desc(st + kATile);
         const uint64_t b_kps = sw64_desc(st + 2 * kATile + S::kBW);
 #pragma unroll
         for (int k = 0; k < kBK / 8; ++k) {
           const uint32_t acc = (kb | k) != 0;
 #pragma unroll
-          for (int j = 0; j < S::kSplit; ++j)
-            mma_tf32(tmem + j * S::kNmma, a_sum + 2 * k, sw64_desc(st + 2 * kATile + j * S::kNmma * kBK * 4) + 2 * k,
-                     tf32_idesc(S::kNmma), acc);
+          for (int j = 0; j < S::kSplit; ++j) {
+            const uint64_t b = sw64_desc(st + 2 * kATile + j * S::kNmma * kBK * 4) + 2 * k;
+            mma_tf32(tmem + j * S::kNmma, a_inst + 2 * k, b, tf32_idesc(S::kNmma), acc);
+            mma_tf32(tmem + j * S::kNmma, a_emb + 2 * k, b, tf32_idesc(S::kNmma), 1);
+          }
           mma_tf32(tmem + NW, a_inst + 2 * k, b_kps + 2 * k, tf32_idesc(S::kNL), acc);
         }
         mma_commit(empty0 + 8 * s);
@@ -372,24 +371,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(acc_bar, 0, nullptr);
     }
   } else {
-    // Main loop: embed tile += inst tile (same box, same swizzle: the same byte offsets hold the
-    // same (row, k) element), 8 float4 per thread per stage.
-    const int t = threadIdx.x - 64;
-    for (int kb = 0; kb < kbs; ++kb) {
-      const int s = kb % kStages;
-      if (!mbar_wait(full0 + 8 * s, (kb / kStages) & 1, c.abort_flag)) break;
-      const float4* src = reinterpret_cast<const float4*>(smem + s * S::kStage);
-      float4* dst = reinterpret_cast<float4*>(smem + s * S::kStage + kATile);
-#pragma unroll
-      for (int i = 0; i < kATile / 16 / 128; ++i) {
-        const float4 a = src[t + 128 * i];
-        float4 b = dst[t + 128 * i];
-        b.x += a.x, b.y += a.y, b.z += a.z, b.w += a.w;
-        dst[t + 128 * i] = b;
-      }
-      fence_proxy_async();
-      mbar_arrive(sum0 + 8 * s);
-    }
     // Epilogue: logits through TMA stores, learnable columns (not 16-byte rows) by plain stores.
     const int q = warp & 3;
     if (wait_accumulator(c, acc_bar)) {
