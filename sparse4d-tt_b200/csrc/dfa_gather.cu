@@ -677,14 +677,21 @@ struct SampleRec {
   float sw[G];  // per group: unnormalised softmax weight (factorised mode), or the logit (exact mode)
 };
 
-// Resident one-warp blocks per SM the register allocator must allow: the kernel is bound by how
-// many anchors are in flight, and 28 (72 registers) measured faster than 25 (80 registers,
-// 311 vs 231 us per 32-frame launch) for bf16 maps.
+// Resident one-warp blocks per SM the register allocator must allow (for bf16 maps): the kernel
+// is bound by how many anchors are in flight.  Reading sample locations, 28 (72 registers)
+// measured fastest (25 / 80 registers: 311 vs 231 us per 32-frame launch; 32 / 64 registers:
+// 181 vs 178 us); computing them from the anchors, 32 (64 registers, the most one-warp blocks
+// an SM holds) measured fastest (187 vs 191 us).
 #ifndef S4D_GATHER_MIN_BLOCKS_BF16
 #define S4D_GATHER_MIN_BLOCKS_BF16 28
 #endif
+#ifndef S4D_GATHER_KPS_MIN_BLOCKS_BF16
+#define S4D_GATHER_KPS_MIN_BLOCKS_BF16 32
+#endif
 template <typename T, int NC, int NL, int NP, int G, int MODE, int WARPS, bool KPS>
-__global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? S4D_GATHER_MIN_BLOCKS_BF16 : 24)
+__global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? (KPS ? S4D_GATHER_KPS_MIN_BLOCKS_BF16
+                                                                     : S4D_GATHER_MIN_BLOCKS_BF16)
+                                                              : 24)
     dfa_gather_warp_kernel(GatherParams p) {
   constexpr int NLP = NL * NP;
   constexpr int LPG = NLP * G;
