@@ -746,7 +746,7 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? (KPS ? S4D_GATHER
   if (lane == 0) ticket = atomicAdd(p.anchor_counter, 1u);
   const int64_t anchor_lin = __shfl_sync(0xffffffffu, ticket, 0);
   if (anchor_lin >= total_anchors) break;
-  const int b = (int)(anchor_lin / p.num_anchor);
+  const int b = (int)p.div_anchor.div((uint32_t)anchor_lin);  // anchors < 2^31
   const int gch = lane / (D / 8);  // group of this lane's output channels
 
   if (KPS) {  // the anchor's keypoints (kps_project's arithmetic)
@@ -851,10 +851,12 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? (KPS ? S4D_GATHER
     // the same 32-lane sub-round: samples whose 2x2 tap block coincides are merged there.
     const int nsurv = __popc(keep);
     const int n = nsurv * NL;
+    // idx / nsurv for idx < 4 * 32 as (idx * ceil(2^16 / nsurv)) >> 16 (exact for nsurv <= 32)
+    const uint32_t inv_surv = (65536u + nsurv - 1) / (uint32_t)nsurv;
 #pragma unroll 1
     for (int sub = 0; sub < n; sub += 32) {
       const int idx = sub + lane;
-      const int l = idx / nsurv, k = idx - (idx / nsurv) * nsurv;
+      const int l = (int)(((uint32_t)idx * inv_surv) >> 16), k = idx - l * nsurv;
       const int src = idx < n ? s_surv[warp][k] : 0;
       const float2 uvs = make_float2(__shfl_sync(0xffffffffu, uv.x, src), __shfl_sync(0xffffffffu, uv.y, src));
       const int qs = base + src;
@@ -1039,6 +1041,7 @@ int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream) {
       if (st) return st;
     }
     GatherParams q = p;
+    q.div_anchor = FastDiv((uint32_t)p.num_anchor);
     q.anchor_counter = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(p.cam_ws) +
                                                    factor_bytes(p.bs, p.num_cams, p.num_levels, p.num_pts, p.num_groups));
     int st = cuda_check(cudaMemsetAsync(q.anchor_counter, 0, sizeof(unsigned), stream), "cudaMemsetAsync(counter)");

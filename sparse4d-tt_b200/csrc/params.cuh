@@ -61,6 +61,7 @@ struct GatherParams {
   int layout;
   int factors_ready;  // split logits: cam_ws already holds the camera factors (no prep launch)
   unsigned* anchor_counter;  // warp kernel: next anchor to take (in the workspace, zeroed per launch)
+  FastDiv div_anchor;        // warp kernel: by num_anchor (linear anchor -> frame)
   // Sample locations computed in the gather from the anchors (kps_anchor != null; loc unused):
   // keypoints as kps_project's, projected with kps_proj [bs, Ncam, 4, 4] and kps_wh [bs, Ncam, 2].
   const float* kps_anchor;     // [bs * A, kps_anchor_dim]
