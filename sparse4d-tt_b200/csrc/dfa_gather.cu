@@ -31,6 +31,8 @@
 //      accumulate in fp32 registers; 32 resident warps per SM keep enough loads in flight;
 //   5. the 8 warps' partial sums are added through shared memory and scaled by 1/sum_exp.
 // No tensor cores: this is a gather with ~0.1 flop per byte.
+#include <type_traits>
+
 #include "kps_math.cuh"
 #include "params.cuh"
 
@@ -922,46 +924,54 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? (KPS ? S4D_GATHER
         if (lead) s_xm[warp][slot] = grp & ~(1u << lane);
       }
       __syncwarp();
+      // the tap loop, instantiated for the two softmax modes (exact is fixed per anchor)
+      auto tap_loop = [&](auto ex) {
+        constexpr bool EX = decltype(ex)::value;
 #pragma unroll 1
-      for (int k = 0; k < nlead; ++k) {
-        const int4 px = s_rec[warp][k].pix;
-        V v0, v1, v2, v3;  // every tap row is in bounds (see the record): no tests
-        TapFma<T>::load(fb, px.x, lane, v0);
-        TapFma<T>::load(fb, px.y, lane, v1);
-        TapFma<T>::load(fb, px.z, lane, v2);
-        TapFma<T>::load(fb, px.w, lane, v3);
-        if (k + 1 < nlead) {  // the next block's rows towards L1 (no registers held)
-          const int4 pn = s_rec[warp][k + 1].pix;
-          const T* r = fb + lane * (kChannels / 32);
-          prefetch_l1(r + (int64_t)pn.x * kChannels);
-          prefetch_l1(r + (int64_t)pn.y * kChannels);
-          prefetch_l1(r + (int64_t)pn.z * kChannels);
-          prefetch_l1(r + (int64_t)pn.w * kChannels);
+        for (int k = 0; k < nlead; ++k) {
+          const int4 px = s_rec[warp][k].pix;
+          V v0, v1, v2, v3;  // every tap row is in bounds (see the record): no tests
+          TapFma<T>::load(fb, px.x, lane, v0);
+          TapFma<T>::load(fb, px.y, lane, v1);
+          TapFma<T>::load(fb, px.z, lane, v2);
+          TapFma<T>::load(fb, px.w, lane, v3);
+          if (k + 1 < nlead) {  // the next block's rows towards L1 (no registers held)
+            const int4 pn = s_rec[warp][k + 1].pix;
+            const T* r = fb + lane * (kChannels / 32);
+            prefetch_l1(r + (int64_t)pn.x * kChannels);
+            prefetch_l1(r + (int64_t)pn.y * kChannels);
+            prefetch_l1(r + (int64_t)pn.z * kChannels);
+            prefetch_l1(r + (int64_t)pn.w * kChannels);
+          }
+          // the block's weight for this lane's group: sum over its member samples (the leader's
+          // first, then the others in lane order) of bilinear weight x unnormalised softmax weight
+          const float4 bw = s_rec[warp][k].bw;
+          float sw = s_rec[warp][k].sw[gch];
+          if (EX) sw = ex2_approx(fmaf(sw, kLog2e, -mlg));
+          float4 w4 = make_float4(bw.x * sw, bw.y * sw, bw.z * sw, bw.w * sw);
+          uint32_t xm = s_xm[warp][k];
+          while (xm != 0u) {  // warp-uniform: most blocks have a single sample
+            const int j = __ffs(xm) - 1;
+            xm &= xm - 1u;
+            const int e = nlead + __popc(extras & ((1u << j) - 1u));
+            const float4 bwe = s_rec[warp][e].bw;
+            float swe = s_rec[warp][e].sw[gch];
+            if (EX) swe = ex2_approx(fmaf(swe, kLog2e, -mlg));
+            w4.x = fmaf(bwe.x, swe, w4.x);
+            w4.y = fmaf(bwe.y, swe, w4.y);
+            w4.z = fmaf(bwe.z, swe, w4.z);
+            w4.w = fmaf(bwe.w, swe, w4.w);
+          }
+          TapFma<T>::fma(v0, w4.x, acc);
+          TapFma<T>::fma(v1, w4.y, acc);
+          TapFma<T>::fma(v2, w4.z, acc);
+          TapFma<T>::fma(v3, w4.w, acc);
         }
-        // the block's weight for this lane's group: sum over its member samples (the leader's
-        // first, then the others in lane order) of bilinear weight x unnormalised softmax weight
-        const float4 bw = s_rec[warp][k].bw;
-        float sw = s_rec[warp][k].sw[gch];
-        if (exact) sw = ex2_approx(fmaf(sw, kLog2e, -mlg));
-        float4 w4 = make_float4(bw.x * sw, bw.y * sw, bw.z * sw, bw.w * sw);
-        uint32_t xm = s_xm[warp][k];
-        while (xm != 0u) {  // warp-uniform: most blocks have a single sample
-          const int j = __ffs(xm) - 1;
-          xm &= xm - 1u;
-          const int e = nlead + __popc(extras & ((1u << j) - 1u));
-          const float4 bwe = s_rec[warp][e].bw;
-          float swe = s_rec[warp][e].sw[gch];
-          if (exact) swe = ex2_approx(fmaf(swe, kLog2e, -mlg));
-          w4.x = fmaf(bwe.x, swe, w4.x);
-          w4.y = fmaf(bwe.y, swe, w4.y);
-          w4.z = fmaf(bwe.z, swe, w4.z);
-          w4.w = fmaf(bwe.w, swe, w4.w);
-        }
-        TapFma<T>::fma(v0, w4.x, acc);
-        TapFma<T>::fma(v1, w4.y, acc);
-        TapFma<T>::fma(v2, w4.z, acc);
-        TapFma<T>::fma(v3, w4.w, acc);
-      }
+      };
+      if (exact)
+        tap_loop(std::true_type{});
+      else
+        tap_loop(std::false_type{});
     }
     __syncwarp();  // s_surv is rewritten by the next pair round
   }
