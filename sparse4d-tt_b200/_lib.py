@@ -82,6 +82,10 @@ class S4DError(RuntimeError):
         super().__init__(f"{fn}: {status_string(status)}: {msg}")
 
 
+# Version of include/s4d_dfa.h these bindings are written for (s4d_abi_version()).
+ABI_VERSION = 103
+
+
 def lib():
     global _lib
     if _lib is None:
@@ -96,6 +100,10 @@ def lib():
                     fn = getattr(handle, name)
                     fn.restype = res
                     fn.argtypes = args
+                version = handle.s4d_abi_version()
+                if version != ABI_VERSION:
+                    raise RuntimeError(f"{LIB_PATH} has C ABI version {version}, these bindings expect "
+                                       f"{ABI_VERSION}; rebuild it (python sparse4d-tt_b200/build.py)")
                 _lib = handle
     return _lib
 

@@ -52,7 +52,7 @@ def test_status_strings_and_version(lib):
     assert L.status_string(0) == "S4D_OK"
     assert L.status_string(2) == "S4D_ERR_UNSUPPORTED_SHAPE"
     assert L.status_string(99) == "S4D_ERR_UNKNOWN"
-    assert lib.s4d_abi_version() == 103
+    assert lib.s4d_abi_version() == 103 == L.ABI_VERSION
 
 
 def test_dfa_workspace_bytes(lib):
