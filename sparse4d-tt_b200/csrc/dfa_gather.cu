@@ -927,7 +927,10 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? (KPS ? S4D_GATHER
       // the tap loop, instantiated for the two softmax modes (exact is fixed per anchor)
       auto tap_loop = [&](auto ex) {
         constexpr bool EX = decltype(ex)::value;
-#pragma unroll 1
+        // unrolled so that the next blocks' loads are scheduled among this block's FMAs (4 fits
+        // the 64 registers of the variant that computes its sample locations without spilling)
+        constexpr int kTapUnroll = KPS ? 4 : 2;
+#pragma unroll kTapUnroll
         for (int k = 0; k < nlead; ++k) {
           const int4 px = s_rec[warp][k].pix;
           V v0, v1, v2, v3;  // every tap row is in bounds (see the record): no tests
