@@ -163,7 +163,7 @@ class DeformableFeatureAggregation:
         self._factors_ok = (num_cams, num_levels, num_pts, num_groups) == (6, 4, 13, 8)
         # ... and for the gather that computes its own sample locations from the anchors
         # (s4d_deformable_aggregation_anchors): no keypoint launch, no location buffer.
-        self.fused_keypoints = self._tc and self._factors_ok
+        self.fused_keypoints = self._tc and self._factors_ok and num_learnable_pts > 0
         self._side: Optional[torch.cuda.Stream] = None
         self._side_kps: Optional[torch.cuda.Stream] = None
         self._side_pending = False
