@@ -251,7 +251,8 @@ class Workload:
     def algorithmic_bytes_per_layer(self):
         """Compulsory HBM bytes of each layer's gather launch: unique in-bounds tap pixels x
         256 ch x 2 B + split logits + sample locations + output.  Computed from the sample
-        locations of an untimed pass (replaying the module's own keypoint step)."""
+        locations of an untimed pass (replaying the module's own keypoint step).  Returns per
+        layer (bytes, unique tap pixels, in-bounds samples)."""
         import torch.nn.functional as F
 
         from sparse4d_tt_b200 import ops
@@ -264,6 +265,7 @@ class Workload:
             loc = torch.empty(self.frames, cfg.num_anchor, cfg.num_cams, cfg.num_pts, 2, device=dev)
             ops.kps_project_into(self.anchors[layer], learn, mod.fix_scale, self.proj, self.wh, sample_location=loc)
             touched = unique_tap_pixels(loc, cfg.spatial_shapes, self.start, self.num_feat)
+            inb = inbounds_samples(loc, cfg.spatial_shapes)
             lpg = cfg.num_levels * cfg.num_pts * cfg.num_groups
             if mod.fused_keypoints:  # the gather reads the anchors + keypoint logits, not locations
                 kps_in = (self.anchors[layer].numel() + learn.numel() + self.proj.numel() + self.wh.numel()) * 4
@@ -272,7 +274,7 @@ class Workload:
             b = (touched * cfg.embed_dims * 2
                  + self.frames * cfg.num_anchor * lpg * 4 + self.frames * cfg.num_cams * lpg * 4
                  + kps_in + self.frames * cfg.num_anchor * cfg.embed_dims * 4)
-            out_bytes.append((b, touched))
+            out_bytes.append((b, touched, inb))
             out = mod.run(inst, self.anchors[layer], self.embeds[layer], self.packed, self.proj, self.wh,
                           cfg.spatial_shapes, self.frames, cfg.num_anchor)
             inst = out[..., : cfg.embed_dims]
@@ -286,6 +288,18 @@ def launches_per_layer(w):
     layer runs them."""
     m = w.mods[0]
     return 2 + (0 if m.fused_keypoints else 1) + (2 if m.split_logits else 0) + (2 if m._tc else 0)
+
+
+def inbounds_samples(loc, spatial_shapes):
+    """Number of (batch, anchor, camera, point, level) samples of ``loc [bs, A, Ncam, P, 2]``
+    with at least one in-bounds bilinear tap (grid_sample, align_corners=False): the samples
+    whose taps the gather loads."""
+    n = 0
+    for h, w in spatial_shapes:
+        ix = ((loc[..., 0] * 2 - 1 + 1) * w - 1) * 0.5
+        iy = ((loc[..., 1] * 2 - 1 + 1) * h - 1) * 0.5
+        n += int(((ix > -1) & (ix < w) & (iy > -1) & (iy < h)).sum())
+    return n
 
 
 def unique_tap_pixels(loc, spatial_shapes, start, num_feat):
@@ -424,6 +438,54 @@ def bs1_leg(device, iters=200):
     }
 
 
+def kps_leg(device, iters=200):
+    """Keypoints only (one frame, 900 anchors, 13 points, 6 cameras): s4d_kps_project writing
+    the sample locations, the depth mask and the compacted visible (b, anchor, cam, pt) list,
+    timed alone with a >= 2x L2 write between iterations."""
+    import torch.nn.functional as F
+
+    from sparse4d_tt_b200 import DeformableFeatureAggregation, ops
+    from sparse4d_tt_b200 import synthetic as syn
+
+    cfg = syn.config_standard(1)
+    ins = syn.make_inputs(cfg, 0)
+    params = syn.make_params(cfg, torch.Generator().manual_seed(100))
+    mod = DeformableFeatureAggregation(device, params, {"FEATURE_DTYPE": torch.float32}, split_logits=True)
+    anchor, inst = ins.anchor.to(device), ins.instance_feature.to(device)
+    proj, wh = ins.projection_mat.to(device), ins.image_wh.to(device)
+    learn = F.linear(inst, mod.learnable_fc_weight, mod.learnable_fc_bias).contiguous()
+    A, nc, P = cfg.num_anchor, cfg.num_cams, cfg.num_pts
+    loc = torch.empty(1, A, nc, P, 2, device=device)
+    mask = torch.empty(1, A, nc, P, dtype=torch.uint8, device=device)
+    idx = torch.empty(A * nc * P, 4, dtype=torch.int32, device=device)
+    cnt = torch.zeros(1, dtype=torch.int32, device=device)
+    ws = torch.empty(max(ops.kps_workspace_bytes(1, A, nc, P), 16), dtype=torch.uint8, device=device)
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    flush = torch.empty(max(2 * l2, 256 << 20) // 4, dtype=torch.float32, device=device)
+
+    def call():
+        ops.kps_project_into(anchor, learn, mod.fix_scale, proj, wh, sample_location=loc, depth_mask=mask,
+                             visible_idx=idx, visible_count=cnt, workspace=ws)
+
+    for _ in range(10):
+        call()
+    times = []
+    for _ in range(iters):
+        flush.fill_(1.0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        call()
+        e1.record()
+        times.append((e0, e1))
+    torch.cuda.synchronize()
+    ms = sorted(s.elapsed_time(e) for s, e in times)
+    med_us = 1000 * ms[len(ms) // 2]
+    return {"workload": "1 frame, 900 anchors x 13 points x 6 cameras: keypoints, projection, depth mask and "
+                        "compacted visible indices; L2 written (>= 2x L2) before every iteration",
+            "median_us": med_us, "p10_us": 1000 * ms[len(ms) // 10], "p90_us": 1000 * ms[(9 * len(ms)) // 10],
+            "calls_per_s": 1e6 / med_us, "visible": int(cnt.item()), "launches_per_call": 2}
+
+
 def pack_leg(device, frames=32, iters=10):
     """FPN outputs -> packed mc_ms_feat: 32 frames of NCHW fp32 maps (6 cams, 4 levels, 256 ch)
     transposed and cast to the packed bf16 layout (s4d_pack_feature_maps), timed with CUDA
@@ -483,10 +545,29 @@ def cpu_baseline(seconds=12.0, max_calls=40):
         call()
         times.append(time.perf_counter() - t0)
     med = statistics.median(times)
+
+    # keypoints only (kps_generator + project_points + mask + nonzero), the same frame
+    def kps_call():
+        with torch.no_grad():
+            kp = oto.key_points(ins.anchor, ins.instance_feature, params)
+            uv, depth = oto.project_points_with_depth(kp, ins.projection_mat, ins.image_wh)
+            _, vis = oto.visibility(uv, depth)
+            return oto.visible_indices(vis)
+
+    for _ in range(3):
+        kps_call()
+    k_times = []
+    for _ in range(50):
+        t0 = time.perf_counter()
+        kps_call()
+        k_times.append(time.perf_counter() - t0)
+    k_med = statistics.median(k_times)
     return {"value": 1.0 / med, "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"{len(times)} single-frame DFA layer calls (900 anchors, 704x256 maps as fp32, all linears "
                       f"included) after 2 warm-ups; median {med * 1e3:.1f} ms/call; torch {torch.__version__} CPU",
-            "median_ms": med * 1e3, "cpu": _cpu_model()}
+            "median_ms": med * 1e3, "cpu": _cpu_model(),
+            "kps": {"median_ms": k_med * 1e3, "calls_per_s": 1.0 / k_med,
+                    "sample": "50 keypoint-only calls (1 frame, 900 anchors, learnable_fc included) after 3 warm-ups"}}
 
 
 def _cpu_model():
@@ -636,15 +717,17 @@ def run_ours(args):
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e_steps,
                "path": "DFAStack.run (the 6-layer CUDA graph), inputs from pinned host memory"}
 
-    bs1 = pack = None
+    bs1 = pack = kps = None
     if rank == 0 and not args.no_bs1:
         bs1 = bs1_leg(device)
         pack = pack_leg(device)
+        kps = kps_leg(device)
     barrier()
 
     if rank == 0:
         peak, src = measured_hbm()
-        alg = statistics.mean(b for b, _ in bytes_per_layer)
+        alg = statistics.mean(b for b, _, _ in bytes_per_layer)
+        inb_per_call = statistics.mean(n for _, _, n in bytes_per_layer) / args.frames
         g_avg_ms = statistics.mean(g_ms)
         achieved = alg / (g_avg_ms / 1e3) / 1e9
         prof = read_profile_traffic()
@@ -657,6 +740,8 @@ def run_ours(args):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded camera ring, Xavier init)",
             "config": workload_config(args.frames, args.layers, world),
             "keypoint_samples_per_s": value * SAMPLES_PER_CALL,
+            "inbounds_samples_per_s": value * inb_per_call,
+            "inbounds_samples_per_call": inb_per_call,
             "roofline": {
                 "kernel": "dfa_gather_warp_kernel<bf16> (keypoints + projection + gather)", "bound": "hbm", "achieved": achieved, "peak": peak,
                 "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)",
@@ -664,7 +749,7 @@ def run_ours(args):
                 "traffic_source": "ncu dram__bytes_read+write of the layer-0 launch (profiles/dfa_gather_stacked_bs32.md),"
                                   " scaled to the average launch by algorithmic bytes" if prof else None,
                 "algorithmic_bytes_per_launch": alg,
-                "unique_tap_pixels_per_launch": statistics.mean(t for _, t in bytes_per_layer),
+                "unique_tap_pixels_per_launch": statistics.mean(t for _, t, _ in bytes_per_layer),
                 "avg_launch_us": g_avg_ms * 1e3, "launches_timed": len(g_ms),
                 "launch_timing": "CUDA events of the graph's event-record nodes around each layer's gather, "
                                  "last replay of the timed region",
@@ -679,6 +764,7 @@ def run_ours(args):
             "e2e": e2e,
             "bs1": bs1,
             "pack": pack,
+            "kps": kps,
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
