@@ -410,7 +410,7 @@ def bs1_leg(device, iters=200):
 
     res = {}
     for name, fn in (("gather", gather), ("layer", layer), ("layer_graph", stack.replay)):
-        for _ in range(10):
+        for _ in range(20):  # warm-up
             fn()
         times = []
         for _ in range(iters):
@@ -467,7 +467,7 @@ def kps_leg(device, iters=200):
         ops.kps_project_into(anchor, learn, mod.fix_scale, proj, wh, sample_location=loc, depth_mask=mask,
                              visible_idx=idx, visible_count=cnt, workspace=ws)
 
-    for _ in range(10):
+    for _ in range(20):  # warm-up
         call()
     times = []
     for _ in range(iters):
