@@ -439,11 +439,11 @@ def bs1_leg(device, iters=200):
 
 
 def kps_leg(device, iters=200):
-    """Keypoints only (one frame, 900 anchors, 13 points, 6 cameras): s4d_kps_project writing
-    the sample locations, the depth mask and the compacted visible (b, anchor, cam, pt) list,
-    timed alone with a >= 2x L2 write between iterations."""
-    import torch.nn.functional as F
-
+    """Keypoints only (one frame, 900 anchors, 13 points, 6 cameras): s4d_kps_project_linear
+    computing the learnable keypoint logits (the keypoint generator's learnable_fc) from the
+    instance features, then the keypoints, projection, depth mask and the compacted visible (b,
+    anchor, cam, pt) list -- the same work the CPU baseline's keypoint leg times -- timed alone
+    with a >= 2x L2 write between iterations."""
     from sparse4d_tt_b200 import DeformableFeatureAggregation, ops
     from sparse4d_tt_b200 import synthetic as syn
 
@@ -453,7 +453,7 @@ def kps_leg(device, iters=200):
     mod = DeformableFeatureAggregation(device, params, {"FEATURE_DTYPE": torch.float32}, split_logits=True)
     anchor, inst = ins.anchor.to(device), ins.instance_feature.to(device)
     proj, wh = ins.projection_mat.to(device), ins.image_wh.to(device)
-    learn = F.linear(inst, mod.learnable_fc_weight, mod.learnable_fc_bias).contiguous()
+    inst2d = ops.row_view(inst, cfg.embed_dims)
     A, nc, P = cfg.num_anchor, cfg.num_cams, cfg.num_pts
     loc = torch.empty(1, A, nc, P, 2, device=device)
     mask = torch.empty(1, A, nc, P, dtype=torch.uint8, device=device)
@@ -464,8 +464,9 @@ def kps_leg(device, iters=200):
     flush = torch.empty(max(2 * l2, 256 << 20) // 4, dtype=torch.float32, device=device)
 
     def call():
-        ops.kps_project_into(anchor, learn, mod.fix_scale, proj, wh, sample_location=loc, depth_mask=mask,
-                             visible_idx=idx, visible_count=cnt, workspace=ws)
+        ops.kps_project_linear_into(anchor, inst2d, mod.learnable_fc_weight, mod.learnable_fc_bias, mod.fix_scale,
+                                    proj, wh, sample_location=loc, depth_mask=mask, visible_idx=idx,
+                                    visible_count=cnt, workspace=ws)
 
     for _ in range(20):  # warm-up
         call()
@@ -480,8 +481,10 @@ def kps_leg(device, iters=200):
     torch.cuda.synchronize()
     ms = sorted(s.elapsed_time(e) for s, e in times)
     med_us = 1000 * ms[len(ms) // 2]
-    return {"workload": "1 frame, 900 anchors x 13 points x 6 cameras: keypoints, projection, depth mask and "
-                        "compacted visible indices; L2 written (>= 2x L2) before every iteration",
+    return {"workload": "1 frame, 900 anchors x 13 points x 6 cameras: learnable keypoint logits (learnable_fc), "
+                        "keypoints, projection, depth mask and compacted visible indices; L2 written (>= 2x L2) "
+                        "before every iteration",
+            "entry": "s4d_kps_project_linear (learnable_fc + keypoints + projection + masks, then the compaction)",
             "median_us": med_us, "p10_us": 1000 * ms[len(ms) // 10], "p90_us": 1000 * ms[(9 * len(ms)) // 10],
             "calls_per_s": 1e6 / med_us, "visible": int(cnt.item()), "launches_per_call": 2}
 
@@ -581,22 +584,38 @@ def _cpu_model():
     return "unknown"
 
 
+GATHER_SOURCES = ("dfa_gather.cu", "kps_math.cuh", "common.cuh", "params.cuh")
+
+
+def gather_source_sha16():
+    """First 16 hex digits of the SHA-256 of the gather kernel's sources (the files the
+    dfa_gather_warp_kernel is compiled from), which ties an ncu capture to the code it measured."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for name in GATHER_SOURCES:
+        with open(os.path.join(REPO, "sparse4d-tt_b200", "csrc", name), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()[:16]
+
+
 def read_profile_traffic():
     """(DRAM bytes, algorithmic bytes) of one captured gather launch from the committed ncu
-    summary, or None."""
+    summary, or None when there is none or it was captured from other kernel sources than the
+    ones built now (its ``kernel_source_sha16`` line differs from ``gather_source_sha16()``)."""
     path = os.path.join(REPO, "profiles", "dfa_gather_stacked_bs32.md")
     vals = {}
     try:
         with open(path) as f:
             for ln in f:
-                for key in ("traffic_bytes_per_launch", "algorithmic_bytes_same_launch"):
+                for key in ("traffic_bytes_per_launch", "algorithmic_bytes_same_launch", "kernel_source_sha16"):
                     if ln.startswith(key + ":"):
-                        vals[key] = float(ln.split(":", 1)[1].strip())
+                        vals[key] = ln.split(":", 1)[1].strip()
     except Exception:
         return None
-    if len(vals) != 2:
+    if len(vals) != 3 or vals["kernel_source_sha16"] != gather_source_sha16():
         return None
-    return vals["traffic_bytes_per_launch"], vals["algorithmic_bytes_same_launch"]
+    return float(vals["traffic_bytes_per_launch"]), float(vals["algorithmic_bytes_same_launch"])
 
 
 # ---------------------------------------------------------------------------------------------
@@ -608,6 +627,11 @@ def run_reference(args):
         return
     res = cpu_baseline_steps(args.steps, args.warmup)
     cfg = workload_config(args.frames, args.layers, world)
+    # The same workload, sampled: a step here is ONE DFA call of it (1 frame through 1 layer),
+    # so DFA calls/s is per call on both arms.
+    cfg["reference_step"] = ("1 frame through 1 DFA layer of this workload per step (bounded CPU sample); the "
+                             "oracle's fp32 arithmetic on the same bf16-valued maps upcast to fp32, all linears "
+                             "in fp32")
     line = {
         "impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
@@ -746,8 +770,11 @@ def run_ours(args):
                 "kernel": "dfa_gather_warp_kernel<bf16> (keypoints + projection + gather)", "bound": "hbm", "achieved": achieved, "peak": peak,
                 "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)",
                 "traffic": traffic,
-                "traffic_source": "ncu dram__bytes_read+write of the layer-0 launch (profiles/dfa_gather_stacked_bs32.md),"
-                                  " scaled to the average launch by algorithmic bytes" if prof else None,
+                "traffic_source": ("ncu dram__bytes_read+write of the layer-0 launch (profiles/dfa_gather_stacked_bs32.md, "
+                                   "captured from these kernel sources), scaled to the average launch by algorithmic "
+                                   "bytes") if prof else
+                                  "none: no ncu capture of the current kernel sources is committed",
+                "kernel_source_sha16": gather_source_sha16(),
                 "algorithmic_bytes_per_launch": alg,
                 "unique_tap_pixels_per_launch": statistics.mean(t for _, t, _ in bytes_per_layer),
                 "avg_launch_us": g_avg_ms * 1e3, "launches_timed": len(g_ms),

@@ -150,9 +150,11 @@ S4D_API int s4d_kps_project_linear(const float* anchor, int64_t anchor_dim, cons
  * Same arguments and results as s4d_kps_project minus workspace/workspace_bytes.  The
  * compaction scratch is a 528 KiB array compiled into the library (held on every GPU that
  * loads the library until exit), so bs*A*Ncam*P is limited to 4,194,304 elements; larger calls
- * return S4D_ERR_UNSUPPORTED_SHAPE.  The first call on a device looks the array's device
- * address up (cudaGetSymbolAddress) with that device current; make it before any stream
- * capture.  All calls share the array: calls that overlap on the GPU race.  Allocates nothing.
+ * return S4D_ERR_UNSUPPORTED_SHAPE.  Every call looks the array's device address up
+ * (cudaGetSymbolAddress) on the current device, so nothing goes stale across a device reset;
+ * the first call in a context may load the library's device code there, so make it before
+ * any stream capture.  All calls share the array: calls that overlap on the GPU race.
+ * Allocates nothing.
  */
 S4D_API int s4d_kps_project_noalloc(const float* anchor, int64_t anchor_dim, const float* fix_scale,
                                     int64_t num_fix, const float* learnable, int64_t num_learnable,

@@ -47,8 +47,11 @@ const char* s4d_last_error(void) { return g_last_error; }
 int s4d_abi_version(void) { return 103; }
 
 size_t s4d_kps_workspace_bytes(int64_t bs, int64_t num_anchor, int64_t num_cams, int64_t num_pts) {
-  if (bs <= 0 || num_anchor <= 0 || num_cams <= 0 || num_pts <= 0) return 0;
-  return kps_workspace_bytes(bs * num_anchor * num_cams * num_pts);
+  int64_t total = 0;
+  if (bs <= 0 || num_anchor <= 0 || num_cams <= 0 || num_pts <= 0 ||
+      !size_product({bs, num_anchor, num_cams, num_pts}, kMaxElems, &total))
+    return 0;  // nothing to compact, or a size s4d_kps_project rejects
+  return kps_workspace_bytes(total);
 }
 
 int s4d_dfa_camera_factors(const float* weights_cam, int64_t bs, int64_t num_cams, int64_t num_levels,
@@ -56,7 +59,9 @@ int s4d_dfa_camera_factors(const float* weights_cam, int64_t bs, int64_t num_cam
   set_error("%s", "");
   if (bs < 0 || num_cams <= 0 || num_levels <= 0 || num_pts <= 0 || num_groups <= 0)
     return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_camera_factors: bad sizes");
-  if (bs >= (1 << 24)) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_camera_factors: too many frames");
+  int64_t n_w = 0;
+  if (bs >= (1 << 24) || !size_product({num_cams, num_levels, num_pts, num_groups}, kGatherMaxWeights + 1, &n_w))
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_camera_factors: too many frames or Ncam*L*P*G > 12288");
   if (bs == 0) return S4D_OK;
   if (weights_cam == nullptr || workspace == nullptr || !aligned(workspace, 16))
     return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_camera_factors: null weights_cam or missing / misaligned workspace");
@@ -68,7 +73,10 @@ int s4d_dfa_camera_factors(const float* weights_cam, int64_t bs, int64_t num_cam
 
 size_t s4d_dfa_workspace_bytes(int64_t bs, int64_t num_cams, int64_t num_levels, int64_t num_pts,
                                int64_t num_groups, int split_logits) {
-  if (!split_logits || bs <= 0 || num_cams <= 0 || num_levels <= 0 || num_pts <= 0 || num_groups <= 0) return 0;
+  int64_t n_w = 0;
+  if (!split_logits || bs <= 0 || num_cams <= 0 || num_levels <= 0 || num_pts <= 0 || num_groups <= 0 ||
+      bs >= (1 << 24) || !size_product({num_cams, num_levels, num_pts, num_groups}, kGatherMaxWeights + 1, &n_w))
+    return 0;  // no workspace needed, or a size the gather rejects
   return gather_workspace_bytes(bs, (int)num_cams, (int)num_levels, (int)num_pts, (int)num_groups);
 }
 
@@ -95,8 +103,9 @@ static int kps_entry(const KpsLinear* lin, const float* anchor, int64_t anchor_d
   const int64_t num_pts = num_fix + num_learnable;
   if (num_pts == 0) return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project: no keypoints");
   if (num_pts > 64) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project: at most 64 keypoints per anchor");
-  const int64_t total = bs * num_anchor * num_cams * num_pts;
-  if (total >= kMaxElems || num_cams * num_pts >= (1 << 24))
+  int64_t total = 0, cam_pts = 0;
+  if (!size_product({bs, num_anchor, num_cams, num_pts}, kMaxElems, &total) ||
+      !size_product({num_cams, num_pts}, 1 << 24, &cam_pts))
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project: bs*A*Ncam*P must be < 2^31");
   const bool compact = visible_idx != nullptr || visible_count != nullptr;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -196,8 +205,9 @@ int s4d_kps_project_fused(const float* key_points, const float* anchor, int64_t 
   if (n < 0 || num_cams < 0 || num_pts < 0) return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project_fused: negative size");
   if (num_pts > 64) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project_fused: at most 64 keypoints per anchor");
   if (anchor_dim < 8) return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project_fused: anchor_dim must be >= 8");
-  const int64_t total = n * num_cams * num_pts;
-  if (total >= kMaxElems) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project_fused: n*Ncam*P must be < 2^31");
+  int64_t total = 0;
+  if (!size_product({n, num_cams, num_pts}, kMaxElems, &total))
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project_fused: n*Ncam*P must be < 2^31");
   if (total == 0) return S4D_OK;
   if (key_points == nullptr || anchor == nullptr || projection_mat == nullptr || image_wh == nullptr ||
       grid == nullptr)
@@ -264,13 +274,14 @@ static int gather_entry(const void* mc_ms_feat, int feat_dtype, int64_t num_feat
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: embed_dims must be 256");
   if (num_groups > 32 || (num_groups & (num_groups - 1)) != 0)
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: num_groups must be 1, 2, 4, 8, 16 or 32");
-  if (num_cams * num_levels * num_pts * num_groups > kGatherMaxWeights)
+  int64_t n_w = 0, anchors = 0, rows = 0;
+  if (!size_product({num_cams, num_levels, num_pts, num_groups}, kGatherMaxWeights + 1, &n_w))
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: Ncam*L*P*G must be <= 12288");
-  if (bs * num_anchor >= kMaxElems || bs * num_feat >= ((int64_t)1 << 40))
+  if (!size_product({bs, num_anchor}, kMaxElems, &anchors) || !size_product({bs, num_feat}, (int64_t)1 << 40, &rows))
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: too many anchors or feature rows");
   if (num_feat >= kMaxElems)
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_deformable_aggregation: num_feat must be < 2^31");
-  if (bs * num_anchor == 0) return S4D_OK;
+  if (anchors == 0) return S4D_OK;
   if (mc_ms_feat == nullptr || spatial_shape == nullptr || scale_start_index == nullptr ||
       (kps == nullptr && sample_location == nullptr) || weights == nullptr || out == nullptr)
     return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: null pointer");
@@ -349,7 +360,7 @@ int s4d_deformable_aggregation_anchors(const void* mc_ms_feat, int feat_dtype, i
                 "s4d_deformable_aggregation_anchors: implemented for 6 cameras, 4 levels, 13 points, 8 groups");
   if (anchor_dim < 8 || num_fix < 0 || num_fix > num_pts)
     return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation_anchors: need anchor_dim >= 8, 0 <= num_fix <= P");
-  if (bs * num_anchor > 0) {
+  if (bs > 0 && num_anchor > 0) {
     if (anchor == nullptr || projection_mat == nullptr || image_wh == nullptr ||
         (num_fix > 0 && fix_scale == nullptr) || (num_fix < num_pts && learnable == nullptr))
       return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation_anchors: null pointer");
@@ -435,7 +446,9 @@ int s4d_pack_feature_maps(const void* const* levels, int layout, int src_dtype, 
     p.w[l] = (int)w;
     per_cam += h * w;
   }
-  if (per_cam * num_cams * bs * embed_dims >= ((int64_t)1 << 40) || per_cam * embed_dims >= kMaxElems)
+  int64_t elems = 0, cam_elems = 0;
+  if (!size_product({per_cam, num_cams, bs, embed_dims}, (int64_t)1 << 40, &elems) ||
+      !size_product({per_cam, embed_dims}, kMaxElems, &cam_elems))
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_pack_feature_maps: maps too large");
   p.num_levels = (int)num_levels;
   p.bs = (int)bs;
@@ -452,8 +465,10 @@ int s4d_instance_bank_project(const float* anchor, const float* T_temp2cur, cons
                               int64_t num, float* anchor_out, void* stream) {
   set_error("%s", "");
   if (bs < 0 || num < 0) return fail(S4D_ERR_INVALID_ARG, "s4d_instance_bank_project: negative size");
-  if (bs * num >= kMaxElems) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_instance_bank_project: too many anchors");
-  if (bs * num == 0) return S4D_OK;
+  int64_t total = 0;
+  if (!size_product({bs, num}, kMaxElems, &total))
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_instance_bank_project: too many anchors");
+  if (total == 0) return S4D_OK;
   if (anchor == nullptr || T_temp2cur == nullptr || anchor_out == nullptr)
     return fail(S4D_ERR_INVALID_ARG, "s4d_instance_bank_project: null pointer");
   IbProjectParams p{anchor, T_temp2cur, time_interval, anchor_out, (int)bs, (int)num, 11};
@@ -466,7 +481,8 @@ static int ib_check(const char* fn, int64_t bs, int64_t num_anchor, int64_t num_
     set_error("%s: need bs >= 0, num_anchor, num_cls, embed_dims > 0 and 0 < num_temp <= num_anchor", fn);
     return S4D_ERR_INVALID_ARG;
   }
-  if (num_anchor > 4096 || bs >= 65536 || bs * num_anchor * embed_dims >= ((int64_t)1 << 40)) {
+  int64_t elems = 0;
+  if (num_anchor > 4096 || bs >= 65536 || !size_product({bs, num_anchor, embed_dims}, (int64_t)1 << 40, &elems)) {
     set_error("%s: implemented for num_anchor <= 4096 and bs < 65536", fn);
     return S4D_ERR_UNSUPPORTED_SHAPE;
   }
@@ -532,8 +548,10 @@ int s4d_instance_bank_update(const float* feature, const float* anchor, const fl
 }
 
 size_t s4d_dfa_camera_workspace_bytes(int64_t bs, int64_t num_cams, int64_t embed_dims) {
-  if (bs <= 0 || num_cams <= 0 || embed_dims <= 0) return 0;
-  return size_t(bs) * size_t(num_cams) * size_t(embed_dims) * sizeof(float);
+  int64_t elems = 0;
+  if (bs <= 0 || num_cams <= 0 || embed_dims <= 0 || !size_product({bs, num_cams, embed_dims}, (int64_t)1 << 40, &elems))
+    return 0;  // nothing to compute, or a size s4d_dfa_camera_logits rejects
+  return size_t(elems) * sizeof(float);
 }
 
 int s4d_dfa_camera_logits(const float* projection_mat, int64_t bs, int64_t num_cams, const float* cam_linear1_weight,

@@ -5,6 +5,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <initializer_list>
+
 #include "s4d_dfa.h"
 
 namespace s4d {
@@ -21,6 +23,18 @@ inline int cuda_check(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return S4D_OK;
   set_error("%s: %s", what, cudaGetErrorString(e));
   return S4D_ERR_CUDA;
+}
+
+// Product of sizes passed through the C ABI, computed without signed overflow: true and *out set
+// when every factor is >= 0 and the product is < limit; false when a factor is negative, the
+// product overflows int64_t or it reaches limit.
+inline bool size_product(std::initializer_list<int64_t> factors, int64_t limit, int64_t* out) {
+  int64_t r = 1;
+  for (int64_t v : factors) {
+    if (v < 0 || __builtin_mul_overflow(r, v, &r)) return false;
+  }
+  *out = r;
+  return r < limit;
 }
 
 // Quotient of a non-negative integer n < 2^31 by a runtime divisor d >= 1 with one multiply-high

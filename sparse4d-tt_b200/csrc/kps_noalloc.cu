@@ -11,14 +11,15 @@
 //
 // The scratch array (kScratchBytes, 528 KiB) lives in this file as a static __device__ array:
 // every GPU that loads the library holds it until the process exits.  Host code cannot use the
-// array's name as a device address, so the first call on each device (with that device
-// current) looks the address up with cudaGetSymbolAddress and keeps it; make that first call
-// before any stream capture.  All calls share the one array and it keeps the previous call's
-// contents; nothing in it has to start at zero, because the projection kernel writes every
-// count and ballot word the compaction kernel then reads.  Two calls that overlap on the GPU
-// (different streams, or different host threads without ordering) race on the array.
-#include <mutex>
-
+// array's name as a device address, so every call looks the address up with
+// cudaGetSymbolAddress on the current device.  Nothing is cached between calls, so a device
+// reset or a new primary context between calls cannot leave a stale address behind.  The
+// first call in a context may load the library's device code there (lazy module loading);
+// make that first call before any stream capture.  All calls share the one array and it keeps
+// the previous call's contents; nothing in it has to start at zero, because the projection
+// kernel writes every count and ballot word the compaction kernel then reads.  Two calls that
+// overlap on the GPU (different streams, or different host threads without ordering) race on
+// the array.
 #include "params.cuh"
 
 namespace s4d {
@@ -33,23 +34,12 @@ constexpr size_t kScratchBytes = ((kBlocks * sizeof(int32_t) + 255) & ~(size_t)2
 
 static __device__ __align__(256) unsigned char g_kps_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_mu;
-void* g_scratch_addr[kMaxDevices] = {};
-
+// Device address of g_kps_scratch in the current device's context.
 int scratch_address(void** out) {
-  int dev = -1;
-  int st = cuda_check(cudaGetDevice(&dev), "s4d_kps_project_noalloc: cudaGetDevice");
+  void* p = nullptr;
+  const int st = cuda_check(cudaGetSymbolAddress(&p, g_kps_scratch), "s4d_kps_project_noalloc: cudaGetSymbolAddress");
   if (st) return st;
-  if (dev < 0 || dev >= kMaxDevices) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project_noalloc: device index >= 64");
-  std::lock_guard<std::mutex> lock(g_mu);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
-    st = cuda_check(cudaGetSymbolAddress(&p, g_kps_scratch), "s4d_kps_project_noalloc: cudaGetSymbolAddress");
-    if (st) return st;
-    g_scratch_addr[dev] = p;
-  }
-  *out = g_scratch_addr[dev];
+  *out = p;
   return S4D_OK;
 }
 
@@ -67,11 +57,13 @@ extern "C" int s4d_kps_project_noalloc(const float* anchor, int64_t anchor_dim, 
   set_error("%s", "");
   if (bs < 0 || num_anchor < 0 || num_cams < 0 || num_fix < 0 || num_learnable < 0)
     return fail(S4D_ERR_INVALID_ARG, "s4d_kps_project_noalloc: negative size");
-  const int64_t total = bs * num_anchor * num_cams * (num_fix + num_learnable);
-  if (total > kMaxElements) {
-    set_error("s4d_kps_project_noalloc: bs*A*Ncam*P = %lld exceeds the built-in scratch limit of %lld elements; "
+  if (num_fix > 64 || num_learnable > 64)  // s4d_kps_project takes at most 64 keypoints per anchor
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_kps_project_noalloc: at most 64 keypoints per anchor");
+  int64_t total = 0;
+  if (!size_product({bs, num_anchor, num_cams, num_fix + num_learnable}, kMaxElements + 1, &total)) {
+    set_error("s4d_kps_project_noalloc: bs*A*Ncam*P exceeds the built-in scratch limit of %lld elements; "
               "use s4d_kps_project with a workspace",
-              (long long)total, (long long)kMaxElements);
+              (long long)kMaxElements);
     return S4D_ERR_UNSUPPORTED_SHAPE;
   }
   void* scratch = nullptr;

@@ -446,22 +446,29 @@ def kps_project_linear_into(anchor: Tensor, instance_feature: Tensor, learnable_
                             learnable_fc_bias: Optional[Tensor], fix_scale: Optional[Tensor], projection_mat: Tensor,
                             image_wh: Tensor, sample_location: Optional[Tensor] = None,
                             depth_mask: Optional[Tensor] = None, key_points: Optional[Tensor] = None,
-                            layout: Union[int, str] = "cam_major") -> None:
+                            layout: Union[int, str] = "cam_major", visible_idx: Optional[Tensor] = None,
+                            visible_count: Optional[Tensor] = None, workspace: Optional[Tensor] = None) -> None:
     """``kps_project_into`` with the learnable keypoint logits computed inside the kernel from
     ``instance_feature`` (a ``[bs*A, C]`` row view, see ``row_view``) and the keypoint
-    generator's ``learnable_fc`` weight/bias (fp32), so the call needs no other linear first."""
+    generator's ``learnable_fc`` weight/bias (fp32), so the call needs no other linear first.
+    ``visible_idx`` / ``visible_count`` (with a ``workspace`` of ``kps_workspace_bytes``) ask
+    for the compacted visible indices as in ``kps_project_into``."""
     name = "kps_project_linear"
     lay = LAYOUTS[layout] if isinstance(layout, str) else int(layout)
     dev = _require_cuda(name, anchor, instance_feature, learnable_fc_weight, learnable_fc_bias, fix_scale,
-                        projection_mat, image_wh, sample_location, depth_mask, key_points)
+                        projection_mat, image_wh, sample_location, depth_mask, key_points, visible_idx, visible_count,
+                        workspace)
     _check_contig(name, anchor=anchor, learnable_fc_weight=learnable_fc_weight, learnable_fc_bias=learnable_fc_bias,
                   fix_scale=fix_scale, projection_mat=projection_mat, image_wh=image_wh,
-                  sample_location=sample_location, depth_mask=depth_mask, key_points=key_points)
+                  sample_location=sample_location, depth_mask=depth_mask, key_points=key_points,
+                  visible_idx=visible_idx)
     for k, t in (("anchor", anchor), ("instance_feature", instance_feature), ("learnable_fc_weight", learnable_fc_weight),
                  ("learnable_fc_bias", learnable_fc_bias), ("fix_scale", fix_scale), ("projection_mat", projection_mat),
                  ("image_wh", image_wh), ("sample_location", sample_location), ("key_points", key_points)):
         _check_dtype(name, t, (torch.float32,), k)
     _check_dtype(name, depth_mask, (torch.uint8, torch.bool), "depth_mask")
+    _check_dtype(name, visible_idx, (torch.int32,), "visible_idx")
+    _check_dtype(name, visible_count, (torch.int32,), "visible_count")
     _require(anchor.dim() == 3 and anchor.shape[-1] >= 8, "anchor must be [bs, A, >=8]")
     bs, A = int(anchor.shape[0]), int(anchor.shape[1])
     _require(projection_mat.dim() == 4 and projection_mat.shape[0] == bs and tuple(projection_mat.shape[2:]) == (4, 4),
@@ -477,11 +484,18 @@ def kps_project_linear_into(anchor: Tensor, instance_feature: Tensor, learnable_
     if sample_location is not None:
         exp = (bs, A, nc, P, 2) if lay == L.S4D_LAYOUT_CAM_MAJOR else (bs, A, P, nc, 2)
         _require(tuple(sample_location.shape) == exp, f"sample_location must be {list(exp)}")
+    if depth_mask is not None:
+        _require(tuple(depth_mask.shape) == (bs, A, nc, P), f"depth_mask must be [{bs}, {A}, {nc}, {P}]")
+    if key_points is not None:
+        _require(tuple(key_points.shape) == (bs, A, P, 3), f"key_points must be [{bs}, {A}, {P}, 3]")
+    if visible_idx is not None:
+        _require(tuple(visible_idx.shape) == (bs * A * nc * P, 4), "visible_idx must be [bs*A*Ncam*P, 4]")
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     st = L.lib().s4d_kps_project_linear(
         anchor.data_ptr(), int(anchor.shape[2]), _ptr(fix_scale), n_fix, instance_feature.data_ptr(),
         instance_feature.stride(0), learnable_fc_weight.data_ptr(), _ptr(learnable_fc_bias), m3 // 3, c,
         projection_mat.data_ptr(), image_wh.data_ptr(), bs, A, nc, lay, _ptr(key_points), _ptr(sample_location),
-        _ptr(depth_mask), None, None, None, 0, _stream_ptr(dev))
+        _ptr(depth_mask), _ptr(visible_idx), _ptr(visible_count), _ptr(workspace), ws_bytes, _stream_ptr(dev))
     L.check(name, st)
 
 

@@ -1,9 +1,11 @@
 """Helpers shared by the golden-fixture generator and the tests that read the fixtures.
 
-The fixtures hold the reference's outputs on seeded inputs.  Inputs are not stored; they are
-regenerated from their seed (torch's CPU generator is deterministic for a given torch build),
-and the fixture stores checksums of every input so a regeneration that drifts fails loudly
-instead of comparing against the wrong case.
+The fixtures hold the reference's outputs on seeded inputs.  Inputs are regenerated from their
+seed (torch's CPU generator is deterministic for a given torch build), and the fixture stores
+checksums of every input so a regeneration that drifts fails loudly instead of comparing
+against the wrong case.  One exception: the keypoint inputs of the reference's own seed-42 case
+(``refdummy_kps_inputs.npz``) are stored bit for bit, because they pass through CPU ``sin`` /
+``cos`` and a linear whose last bits can differ between host CPUs.
 """
 from __future__ import annotations
 
@@ -95,6 +97,14 @@ def reference_dummy_case(bs: int, num_anchor: int = 900, num_cams: int = 6, embe
         "output_proj_bias": out_proj.bias.data.clone(),
     }
     return (inst, anchor, embed, maps, proj, wh), params
+
+
+def reference_dummy_kps_inputs(bs: int):
+    """``(anchor, learnable logits, fix_scale, projection_mat, image_wh)`` of the reference's own
+    seed-42 case as the reference computed them (``refdummy_kps_inputs.npz``, written by
+    ``make_golden.py``), as float32 CPU tensors."""
+    g = load("refdummy_kps_inputs")
+    return tuple(torch.from_numpy(g[f"{k}_bs{bs}"].copy()) for k in ("anchor", "learn", "fix_scale", "proj", "wh"))
 
 
 def same_inputs(g, **tensors) -> bool:

@@ -1,9 +1,9 @@
 """Generate the golden fixtures by running the REFERENCE's own PyTorch DFA.
 
-Run where the reference checkout is present (it is read from ``REF_ROOT``, default
-``/root/reference``), from the repository root:
+Run where the reference checkout is present, with ``REF_ROOT`` set to its root, from the
+repository root:
 
-    python tests/golden/make_golden.py
+    REF_ROOT=<reference checkout> python tests/golden/make_golden.py [fixture name ...]
 
 It imports ``test/dfa_pcc.py`` of the reference with a stand-in ``ttnn`` module (the
 reference imports ttnn at module top, ``test/dfa_pcc.py:37``, but its PyTorch DFA never
@@ -25,7 +25,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("REF_ROOT", "")
 sys.path.insert(0, REPO)
 sys.path.insert(0, HERE)
 
@@ -34,6 +34,8 @@ from sparse4d_tt_b200 import synthetic as syn  # noqa: E402
 
 
 def import_reference():
+    if not REF_ROOT or not os.path.isdir(os.path.join(REF_ROOT, "test")):
+        raise SystemExit("make_golden.py: set REF_ROOT to the root of the reference checkout")
     stub = types.ModuleType("ttnn")
 
     class _Any:
@@ -194,12 +196,36 @@ def reference_dummy(ref, name, bs):
     print(f"{name}: visible={int(masks(res)[1].sum())} -> {os.path.getsize(path)} bytes")
 
 
+def reference_dummy_kps_inputs(ref, name, batches=(1, 2)):
+    """Exact input bits of the reference's own e2e case (``create_dummy_inputs`` + ``build_pt_dfa``,
+    seed 42) for the keypoint path: anchors, the learnable-keypoint logits of the reference
+    module's own ``learnable_fc``, projection matrices and image sizes.  These are the inputs the
+    ``refdummy_bs*`` masks and indices were computed from; a host whose CPU rounds ``sin``/``cos``
+    or the linear differently in the last bit still feeds the GPU exactly these."""
+    out = {}
+    for bs in batches:
+        inst, anchor, embed, maps, metas = ref.create_dummy_inputs(bs, 900, 6, 256)
+        m = ref.build_pt_dfa().eval()
+        with torch.no_grad():
+            learn = m.kps_generator.learnable_fc(inst)
+        out[f"anchor_bs{bs}"] = anchor.numpy()
+        out[f"learn_bs{bs}"] = learn.numpy()
+        out[f"proj_bs{bs}"] = metas["projection_mat"].numpy()
+        out[f"wh_bs{bs}"] = metas["image_wh"].numpy()
+        out[f"fix_scale_bs{bs}"] = m.kps_generator.fix_scale.detach().numpy()
+    path = os.path.join(HERE, name + ".npz")
+    np.savez_compressed(path, **out)
+    print(f"{name}: {sorted(out)} -> {os.path.getsize(path)} bytes")
+
+
 def instance_bank_projection(name, seed=7, bs=2, num=600):
     """The reference's own InstanceBank._anchor_projection (model/instance_bank.py:322-369, plain
     torch) on seeded cached anchors, ego transforms and time gaps; inputs and outputs stored
     whole (small)."""
     import importlib
 
+    if not REF_ROOT:
+        raise SystemExit("make_golden.py: set REF_ROOT to the root of the reference checkout")
     sys.path.insert(0, REF_ROOT)
     ib = importlib.import_module("model.instance_bank")
     gen = torch.Generator().manual_seed(seed)
@@ -222,17 +248,25 @@ def main():
     torch.set_num_threads(os.cpu_count() or 1)
     ref = import_reference()
     small = syn.DFAConfig(bs=2, num_anchor=40, image_wh=(128, 64))
-    synthetic_case(ref, "small_b2_s3", small, seed=3, pseed=103)
-    synthetic_case(ref, "small_b1_s4_cam3", syn.DFAConfig(bs=1, num_anchor=24, num_cams=3, image_wh=(96, 64)),
-                   seed=4, pseed=104)
-    synthetic_case(ref, "standard_s0_fp32", syn.config_standard(1), seed=0, pseed=100, large=True)
-    synthetic_case(ref, "standard_s1_bf16", syn.config_standard(1), seed=1, pseed=101,
-                   feature_dtype=torch.bfloat16, large=True)
-    synthetic_case(ref, "highres_s2_bf16", syn.config_highres(1, 1800), seed=2, pseed=102,
-                   feature_dtype=torch.bfloat16, large=True)
-    reference_dummy(ref, "refdummy_bs1", 1)
-    reference_dummy(ref, "refdummy_bs2", 2)
-    instance_bank_projection("instance_bank_projection")
+    jobs = {
+        "small_b2_s3": lambda: synthetic_case(ref, "small_b2_s3", small, seed=3, pseed=103),
+        "small_b1_s4_cam3": lambda: synthetic_case(
+            ref, "small_b1_s4_cam3", syn.DFAConfig(bs=1, num_anchor=24, num_cams=3, image_wh=(96, 64)), seed=4,
+            pseed=104),
+        "standard_s0_fp32": lambda: synthetic_case(ref, "standard_s0_fp32", syn.config_standard(1), seed=0,
+                                                   pseed=100, large=True),
+        "standard_s1_bf16": lambda: synthetic_case(ref, "standard_s1_bf16", syn.config_standard(1), seed=1,
+                                                   pseed=101, feature_dtype=torch.bfloat16, large=True),
+        "highres_s2_bf16": lambda: synthetic_case(ref, "highres_s2_bf16", syn.config_highres(1, 1800), seed=2,
+                                                  pseed=102, feature_dtype=torch.bfloat16, large=True),
+        "refdummy_bs1": lambda: reference_dummy(ref, "refdummy_bs1", 1),
+        "refdummy_bs2": lambda: reference_dummy(ref, "refdummy_bs2", 2),
+        "refdummy_kps_inputs": lambda: reference_dummy_kps_inputs(ref, "refdummy_kps_inputs"),
+        "instance_bank_projection": lambda: instance_bank_projection("instance_bank_projection"),
+    }
+    names = sys.argv[1:] or list(jobs)
+    for n in names:
+        jobs[n]()
 
 
 if __name__ == "__main__":

@@ -360,3 +360,38 @@ def test_gather_anchors_rejects_on_host(lib, kw, status, text):
 def test_gather_anchors_empty_batch_is_a_noop(lib):
     st, msg = _gather_anchors(lib, bs=0, anchor=None, learn=None, feat=None, out=None)
     assert st == L.S4D_OK, msg
+
+
+def test_size_products_that_overflow_int64_are_rejected(lib):
+    """Sizes whose product overflows int64 must be rejected, not wrapped to a small value that
+    passes the limits (every check below returns before any pointer is used)."""
+    big = 1 << 40
+    st, msg = _kps(lib, bs=big, A=big)
+    assert st == L.S4D_ERR_UNSUPPORTED_SHAPE and "2^31" in msg, msg
+    st, msg = _kps(lib, bs=1 << 33, A=1 << 31)  # product 2^64 wraps to 0 in int64
+    assert st == L.S4D_ERR_UNSUPPORTED_SHAPE, msg
+    assert lib.s4d_kps_workspace_bytes(big, big, 6, 13) == 0
+    st, msg = _gather(lib, bs=1 << 33, A=1 << 31)
+    assert st == L.S4D_ERR_UNSUPPORTED_SHAPE and "too many" in msg, msg
+    st, msg = _gather(lib, np=1 << 40, nl=1 << 40)
+    assert st == L.S4D_ERR_UNSUPPORTED_SHAPE and "12288" in msg, msg
+    assert lib.s4d_kps_project_fused(16, 16, 11, 16, 16, 1 << 40, 1 << 30, 13, 16, None) == L.S4D_ERR_UNSUPPORTED_SHAPE
+    assert lib.s4d_dfa_workspace_bytes(2, 1 << 40, 1 << 40, 13, 8, 1) == 0
+    assert lib.s4d_dfa_camera_workspace_bytes(1 << 40, 1 << 40, 256) == 0
+    assert lib.s4d_instance_bank_project(16, 16, None, 1 << 33, 1 << 31, 16, None) == L.S4D_ERR_UNSUPPORTED_SHAPE
+
+
+def test_noalloc_limit_is_checked_on_the_host(lib):
+    """s4d_kps_project_noalloc rejects bs*A*Ncam*P above its built-in scratch (4,194,304
+    elements), including products that overflow, before touching the GPU."""
+    def call(bs, A, nc, nfix, nlearn):
+        st = lib.s4d_kps_project_noalloc(16, 11, 16, nfix, 16, nlearn, 16, 16, bs, A, nc, 0, None, None, None,
+                                         None, None, None)
+        return st, lib.s4d_last_error().decode()
+
+    st, msg = call(1, 838861, 1, 5, 0)  # 4,194,305 elements
+    assert st == L.S4D_ERR_UNSUPPORTED_SHAPE and "scratch limit" in msg, msg
+    st, msg = call(1 << 33, 1 << 31, 1, 1, 0)  # wraps to 0 in int64
+    assert st == L.S4D_ERR_UNSUPPORTED_SHAPE and "scratch limit" in msg, msg
+    st, msg = call(1, 1, 1, 1 << 62, 1 << 62)
+    assert st == L.S4D_ERR_UNSUPPORTED_SHAPE, msg

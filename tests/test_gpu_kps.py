@@ -83,18 +83,13 @@ def test_kps_bit_exact_masks_and_indices(cuda_device, name):
 def test_kps_reference_dummy_inputs(cuda_device, bs):
     """The reference's own e2e inputs (random N(0,1) projection matrices)."""
     g = fx.load(f"refdummy_bs{bs}")
-    (inst, anchor, embed, maps, proj, wh), params = fx.reference_dummy_case(bs)
-    learn = oto.learnable_logits(inst, params)
-    loc, mask, idx, cnt, kp = _run(anchor, learn, params["kps_fix_scale"], proj, wh)
-    if fx.same_inputs(g, anchor=anchor, instance_feature=inst, projection_mat=proj):
-        ref_vis = fx.unpack_bits(g["vis_bits"], (bs, 900, 6, 13))
-    else:  # this host's CPU drew other last bits: the oracle on these inputs is the reference
-        print("refdummy inputs differ from the fixture's in the last bits on this host; "
-              "indices checked against the numpy oracle on the same inputs")
-        kp_np = onp.key_points(anchor.numpy(), learn.numpy(), params["kps_fix_scale"].numpy())
-        _, _, ref_vis = onp.project(kp_np, proj.numpy(), wh.numpy())
-        assert abs(int(ref_vis.sum()) - int(g["n_visible"])) <= 8
-    assert cnt == int(ref_vis.sum())
+    # the exact input bits the reference computed the fixture's masks from (stored, so that a
+    # host whose CPU rounds sin/cos or the linear differently tests the same case)
+    anchor, learn, fix, proj, wh = fx.reference_dummy_kps_inputs(bs)
+    assert fx.same_inputs(g, anchor=anchor, projection_mat=proj)
+    loc, mask, idx, cnt, kp = _run(anchor, learn, fix, proj, wh)
+    ref_vis = fx.unpack_bits(g["vis_bits"], (bs, 900, 6, 13))
+    assert cnt == int(ref_vis.sum()) == int(g["n_visible"])
     assert np.array_equal(idx.numpy(), np.argwhere(ref_vis).astype(np.int32))
     rows = g["rows"]
     np.testing.assert_allclose(kp.reshape(bs * 900, 13, 3).numpy()[rows], g["kp_rows"], rtol=1e-5, atol=1e-5)
@@ -208,3 +203,30 @@ def test_kps_linear_matches_given_logits(cuda_device, strided):
     well = (depth.abs() > 0.5).numpy()[..., None].repeat(2, -1)
     err = (loc.cpu() - ref_loc.cpu()).abs().numpy()
     assert np.all(err[well] <= 1e-3 * np.abs(ref_loc.cpu().numpy()[well]) + 1e-4)
+
+
+def test_kps_linear_compaction_is_consistent(cuda_device):
+    """s4d_kps_project_linear with the compaction (the keypoint leg of the benchmark): the
+    compacted indices are exactly the (b, anchor, cam, pt) whose written depth mask is set and
+    whose written (u, v) lie in [0, 1], in lexicographic order."""
+    cfg = syn.config_standard(2)
+    ins = syn.make_inputs(cfg, 32)
+    params = syn.make_params(cfg, torch.Generator().manual_seed(132))
+    d = torch.device("cuda:0")
+    bs, A, nc, P = cfg.bs, cfg.num_anchor, cfg.num_cams, cfg.num_pts
+    loc = torch.empty(bs, A, nc, P, 2, device=d)
+    mask = torch.empty(bs, A, nc, P, dtype=torch.uint8, device=d)
+    idx = torch.empty(bs * A * nc * P, 4, dtype=torch.int32, device=d)
+    cnt = torch.zeros(1, dtype=torch.int32, device=d)
+    ws = torch.empty(max(ops.kps_workspace_bytes(bs, A, nc, P), 16), dtype=torch.uint8, device=d)
+    ops.kps_project_linear_into(ins.anchor.to(d), ins.instance_feature.reshape(-1, 256).to(d),
+                                params["kps_learnable_fc_weight"].to(d), params["kps_learnable_fc_bias"].to(d),
+                                params["kps_fix_scale"].to(d), ins.projection_mat.to(d), ins.image_wh.to(d),
+                                sample_location=loc, depth_mask=mask, visible_idx=idx, visible_count=cnt,
+                                workspace=ws)
+    torch.cuda.synchronize()
+    u, v = loc[..., 0].cpu(), loc[..., 1].cpu()
+    vis = mask.cpu().bool() & (u >= 0) & (u <= 1) & (v >= 0) & (v <= 1)
+    n = int(cnt.item())
+    assert n == int(vis.sum()) > 0
+    assert torch.equal(idx[:n].cpu(), torch.nonzero(vis).to(torch.int32))

@@ -150,3 +150,19 @@ def test_numpy_gather_edge_cases():
                                      torch.from_numpy(uv).permute(0, 2, 1, 3, 4), torch.from_numpy(logits))
     np.testing.assert_allclose(got, ref.numpy(), rtol=0, atol=1e-5)
     assert np.all(got[0, 4] == 0)
+
+
+@pytest.mark.parametrize("bs", [1, 2])
+def test_reference_dummy_kps_inputs_pin_the_masks(bs):
+    """The stored input bits of the reference's seed-42 case reproduce the fixture's input
+    checksums, and the numpy oracle's fixed-order projection of them gives the reference's
+    depth and visibility masks bit for bit (the GPU keypoint test feeds these same bits)."""
+    g = fx.load(f"refdummy_bs{bs}")
+    anchor, learn, fix, proj, wh = fx.reference_dummy_kps_inputs(bs)
+    assert fx.same_inputs(g, anchor=anchor, projection_mat=proj, image_wh=wh)
+    assert np.allclose(fx.checksum(fix), g["ck_param_kps_fix_scale"], rtol=1e-12, atol=0)
+    kp = onp.key_points(anchor.numpy(), learn.numpy(), fix.numpy())
+    _, mask, vis = onp.project(kp, proj.numpy(), wh.numpy())
+    assert np.array_equal(fx.pack_bits(mask), g["mask_bits"])
+    assert np.array_equal(fx.pack_bits(vis), g["vis_bits"])
+    assert int(vis.sum()) == int(g["n_visible"])

@@ -61,3 +61,36 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(cuda_device):
         0, None, None, None, None, None, None)
     assert st == L.S4D_ERR_UNSUPPORTED_SHAPE
     assert "scratch limit" in L.lib().s4d_last_error().decode()
+
+
+def _boundary_inputs(A, nc, nfix, nlearn, seed=33):
+    """One frame of A anchors seen by nc ring cameras, with nfix fixed and nlearn learnable
+    keypoints (random fixed scales and logits)."""
+    gen = torch.Generator().manual_seed(seed)
+    d = torch.device("cuda:0")
+    anchor = syn.make_anchors(1, A, gen)
+    learn = torch.randn(1, A, 3 * nlearn, generator=gen)
+    fix = torch.rand(nfix, 3, generator=gen) - 0.5
+    proj = syn.camera_ring(nc, (704, 256))[None]
+    wh = torch.tensor([704.0, 256.0]).expand(1, nc, 2)
+    return [t.to(d).contiguous() for t in (anchor, learn, fix, proj, wh)]
+
+
+def test_noalloc_accepts_exactly_its_limit(cuda_device):
+    """bs*A*Ncam*P of exactly 4,194,304 elements (the documented maximum) is accepted and
+    matches the workspace entry point, whose workspace at that size is what the built-in
+    scratch holds; one element more is rejected."""
+    ins = _boundary_inputs(65536, 4, 8, 8)  # 1 x 65,536 x 4 x 16 = 2^22
+    got = _noalloc(*ins)
+    ref = ops.kps_project(*ins)
+    torch.cuda.synchronize()
+    n = int(ref[3].item())
+    assert int(got[3].item()) == n > 0
+    assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1]) and torch.equal(got[4], ref[4])
+    assert torch.equal(got[2][:n], ref[2][:n])
+    anchor, learn, fix, proj, wh = _boundary_inputs(8, 1, 5, 0)
+    st = L.lib().s4d_kps_project_noalloc(
+        anchor.data_ptr(), 11, fix.data_ptr(), 5, None, 0, proj.data_ptr(), wh.data_ptr(), 1, 838861, 1, 0, None,
+        None, None, None, None, None)  # 1 x 838,861 x 1 x 5 = 2^22 + 1
+    assert st == L.S4D_ERR_UNSUPPORTED_SHAPE
+    assert "scratch limit" in L.lib().s4d_last_error().decode()
