@@ -59,6 +59,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-bs1", action="store_true")
+    ap.add_argument("--no-highres", action="store_true")
     ap.add_argument("--profile-gather", action="store_true",
                     help="profiling case: one layer over --frames frames, one warm-up call then one call "
                          "inside the NVTX range 'profile' (few launches before the profiled gather)")
@@ -195,14 +196,16 @@ class ClockSampler:
 # workload
 # ---------------------------------------------------------------------------------------------
 class Workload:
-    """Device-resident inputs of one step on one GPU."""
+    """Device-resident inputs of one step on one GPU (the standard 704x256, 900-anchor shape
+    unless ``cfg`` says otherwise; ``mesh_device`` / ``model_config`` go to every layer)."""
 
-    def __init__(self, frames, layers, device, seed):
+    def __init__(self, frames, layers, device, seed, cfg=None, mesh_device=None, model_config=None):
         from sparse4d_tt_b200 import DeformableFeatureAggregation, ops
         from sparse4d_tt_b200 import synthetic as syn
 
-        self.cfg = syn.DFAConfig(bs=frames)
+        self.cfg = syn.DFAConfig(bs=frames) if cfg is None else cfg
         cfg = self.cfg
+        mc = MODEL_CONFIG if model_config is None else model_config
         self.frames, self.layers, self.device = frames, layers, device
         gen = torch.Generator().manual_seed(seed)
         self.shape, self.start, self.num_feat = ops.level_tables(cfg.spatial_shapes, cfg.num_cams, device=device)
@@ -212,12 +215,14 @@ class Workload:
         self.packed = (self.feat, self.shape, self.start)
         self.inst0 = torch.randn(frames, cfg.num_anchor, cfg.embed_dims, generator=gen).to(device)
         a = syn.make_anchors(frames, cfg.num_anchor, gen)
-        self.anchors, self.embeds, self.mods = [], [], []
+        self.anchors, self.embeds, self.mods, self.params = [], [], [], []
         for layer in range(layers):
             self.anchors.append(a.to(device))
             self.embeds.append(torch.randn(frames, cfg.num_anchor, cfg.embed_dims, generator=gen).to(device))
             params = syn.make_params(cfg, torch.Generator().manual_seed(seed * 100 + layer))
-            self.mods.append(DeformableFeatureAggregation(device, params, MODEL_CONFIG, split_logits=True))
+            self.params.append(params)
+            self.mods.append(DeformableFeatureAggregation(device, params, mc, split_logits=True,
+                                                          mesh_device=mesh_device))
             a = syn.refine_anchors(a, gen)
         self.proj = syn.camera_ring(cfg.num_cams, cfg.image_wh)[None].expand(frames, -1, -1, -1).contiguous().to(device)
         self.wh = torch.tensor(cfg.image_wh, dtype=torch.float32).expand(frames, cfg.num_cams, 2).contiguous().to(device)
@@ -342,28 +347,69 @@ def time_steps(fn, steps, sync_barrier):
     return e0.elapsed_time(e1)
 
 
-def e2e_leg(w, stack, steps, warmup, sync_barrier):
-    """Same step through DFAStack.run with every input copied from pinned host memory inside
-    the timed region (into the graph's static buffers) and the final output read back to the
-    host."""
+def h2d_bandwidth(host, device, reps=3):
+    """Best-of-``reps`` GB/s of one plain copy of the pinned host tensor ``host`` to the device
+    (CUDA events on the current stream)."""
+    dst = torch.empty(host.shape, dtype=host.dtype, device=device)
+    best = None
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dst.copy_(host, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        best = ms if best is None else min(best, ms)
+    nbytes = host.numel() * host.element_size()
+    del dst
+    return nbytes / best / 1e6
+
+
+def gpu_numa_node(device):
+    """NUMA node of the GPU's PCI device (sysfs), or None."""
+    try:
+        p = torch.cuda.get_device_properties(device)
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/numa_node") as f:
+            return int(f.read().strip())
+    except Exception:
+        return None
+
+
+def e2e_leg(w, steps, warmup, sync_barrier):
+    """The step end to end through the library's public API: ``PipelinedDFAStack.submit`` with
+    every input copied from pinned host memory inside the timed region and the final output
+    read back into pinned host memory.  The two graphs of the pipeline let step k + 1's uploads
+    (on a copy stream) overlap step k's replay, so the step is bound by the host-to-device
+    copies; their floor is the bytes over the plain pinned-copy bandwidth measured here."""
+    from sparse4d_tt_b200 import PipelinedDFAStack
+
     host = {
-        "feat": w.feat.cpu().pin_memory(), "inst": w.inst0.cpu().pin_memory(),
-        "anchors": [a.cpu().pin_memory() for a in w.anchors], "embeds": [e.cpu().pin_memory() for e in w.embeds],
-        "proj": w.proj.cpu().pin_memory(), "wh": w.wh.cpu().pin_memory(),
+        "mc_ms_feat": w.feat.cpu().pin_memory(), "instance_feature": w.inst0.cpu().pin_memory(),
+        "anchors": [a.cpu().pin_memory() for a in w.anchors],
+        "anchor_embeds": [e.cpu().pin_memory() for e in w.embeds],
+        "projection_mat": w.proj.cpu().pin_memory(), "image_wh": w.wh.cpu().pin_memory(),
     }
-    out_host = torch.empty(w.frames, w.cfg.num_anchor, 2 * w.cfg.embed_dims, pin_memory=True)
-    h2d = (host["feat"].numel() * 2 + host["inst"].numel() * 4 + sum(a.numel() * 4 for a in host["anchors"])
-           + sum(e.numel() * 4 for e in host["embeds"]) + host["proj"].numel() * 4 + host["wh"].numel() * 4)
-    d2h = out_host.numel() * 4
+    outs = [torch.empty(w.frames, w.cfg.num_anchor, 2 * w.cfg.embed_dims, pin_memory=True) for _ in range(2)]
+    h2d = (host["mc_ms_feat"].numel() * 2 + host["instance_feature"].numel() * 4
+           + sum(a.numel() * 4 for a in host["anchors"]) + sum(e.numel() * 4 for e in host["anchor_embeds"])
+           + host["projection_mat"].numel() * 4 + host["image_wh"].numel() * 4)
+    d2h = outs[0].numel() * 4
+    pipe = PipelinedDFAStack(w.mods, w.frames, w.cfg.num_anchor, w.cfg.spatial_shapes)
+    count = [0]
 
     def step():
-        out = stack.run(host["inst"], host["anchors"], host["embeds"], host["feat"], host["proj"], host["wh"])
-        out_host.copy_(out, non_blocking=True)
+        pipe.submit(out=outs[count[0] % 2], **host)
+        count[0] += 1
 
     for _ in range(warmup):
         step()
+    pipe.synchronize()
     ms = time_steps(step, steps, sync_barrier)
-    return ms, h2d, d2h
+    gbs = h2d_bandwidth(host["mc_ms_feat"], w.device)
+    del pipe
+    torch.cuda.empty_cache()
+    return ms, h2d, d2h, gbs
 
 
 def bs1_leg(device, iters=200):
@@ -392,9 +438,26 @@ def bs1_leg(device, iters=200):
     flush = torch.empty(max(2 * l2, 256 << 20) // 4, dtype=torch.float32, device=device)
     touched = unique_tap_pixels(loc, cfg.spatial_shapes, packed[2], packed[0].shape[1])
     lpg = 4 * 13 * 8
-    alg = touched * 512 + 900 * lpg * 4 + 6 * lpg * 4 + loc.numel() * 4 + out.numel() * 4
+    alg_loc = touched * 512 + 900 * lpg * 4 + 6 * lpg * 4 + loc.numel() * 4 + out.numel() * 4
+    # the module's own gather at bs=1 (as DeformableFeatureAggregation.run launches it): the
+    # sample locations computed in the kernel from the anchors and keypoint logits, with the
+    # per-frame camera factors in the workspace
+    mod.reset_frame_cache()
+    mod.run(inst, anchor, embed, packed, proj, wh, cfg.spatial_shapes, 1, 900)
+    assert mod.fused_keypoints
+    ws, wc_mod = mod._cached_camera_factors, mod._cached_camera_logits
+    logits = torch.empty(1, 900, 4, 13, 8, device=device)
+    learn_tc = torch.empty(1, 900, 18, device=device)
+    ops.weights_fc_into(logits.view(900, -1), learn_tc.view(900, -1), ops.row_view(inst, 256),
+                        ops.row_view(embed, 256), mod.weights_fc_weight, mod.learnable_fc_weight, mod.learnable_fc_bias)
+    alg = (touched * 512 + 900 * lpg * 4 + 6 * lpg * 4 + (anchor.numel() + learn_tc.numel() + proj.numel()
+                                                          + wh.numel()) * 4 + out.numel() * 4)
 
     def gather():
+        ops.deformable_aggregation_anchors_into(out, packed[0], packed[1], packed[2], anchor, mod.fix_scale,
+                                                learn_tc.view(900, -1), proj, wh, logits, wc_mod, ws)
+
+    def gather_loc():
         ops.deformable_aggregation_into(out, packed[0], packed[1], packed[2], loc, wa, True, wc)
 
     def layer():
@@ -409,7 +472,7 @@ def bs1_leg(device, iters=200):
     stack.run(inst, [anchor], [embed], packed[0], proj, wh)
 
     res = {}
-    for name, fn in (("gather", gather), ("layer", layer), ("layer_graph", stack.replay)):
+    for name, fn in (("gather", gather), ("gather_loc", gather_loc), ("layer", layer), ("layer_graph", stack.replay)):
         for _ in range(20):  # warm-up
             fn()
         times = []
@@ -426,16 +489,87 @@ def bs1_leg(device, iters=200):
                      "p90_us": 1000 * ms[(9 * len(ms)) // 10]}
     peak, src = measured_hbm()
     g_s = res["gather"]["median_us"] * 1e-6
+    gl_s = res["gather_loc"]["median_us"] * 1e-6
+    rot = bs1_rotating(device, mod, cfg)
     return {
         "workload": "1 frame, 1 DFA layer, 900 anchors, bf16 maps (704x256 image); L2 written (>= 2x L2) "
                     "before every iteration",
+        "gather_kernel": "the module's gather: s4d_deformable_aggregation_anchors (keypoints + projection + "
+                         "softmax + gather in one launch, camera factors ready)",
         "gather_kernel_us": res["gather"], "layer_us": res["layer"], "layer_graph_us": res["layer_graph"],
         "layer_calls_per_s": 1e6 / res["layer"]["median_us"],
         "layer_graph_calls_per_s": 1e6 / res["layer_graph"]["median_us"],
         "algorithmic_bytes": alg, "unique_tap_pixels": touched,
         "gather_achieved_gbs": alg / g_s / 1e9, "gather_frac_of_hbm": alg / g_s / 1e9 / peak,
+        "gather_loc": {"kernel": "s4d_deformable_aggregation reading a sample-location buffer (CTA per anchor)",
+                       "us": res["gather_loc"], "algorithmic_bytes": alg_loc,
+                       "frac_of_hbm": alg_loc / gl_s / 1e9 / peak},
         "peak_gbs": peak, "peak_source": src,
+        "rotating": rot,
     }
+
+
+def bs1_rotating(device, mod, cfg, sets=16, replays=13):
+    """The module's bs = 1 gather back to back over ``sets`` independent single-frame inputs
+    (each its own 46 MB of bf16 maps, anchors and logits: 736 MB of maps in all, so a set's rows
+    are long gone from the 126 MB L2 when its turn comes again), the ``sets`` launches captured
+    as one CUDA graph and replayed ``replays`` times: per-call time of a stream of bs = 1 calls,
+    without the per-call event and L2-flush overhead of the flushed figure."""
+    from sparse4d_tt_b200 import ops
+    from sparse4d_tt_b200 import synthetic as syn
+
+    shape, start, num_feat = ops.level_tables(cfg.spatial_shapes, cfg.num_cams, device=device)
+    proj = syn.camera_ring(6, cfg.image_wh)[None].contiguous().to(device)
+    wh = torch.tensor(cfg.image_wh, dtype=torch.float32).expand(1, 6, 2).contiguous().to(device)
+    wc = mod._cached_camera_logits
+    calls, alg = [], []
+    dgen = torch.Generator(device=device).manual_seed(77)
+    for r in range(sets):
+        gen = torch.Generator().manual_seed(500 + r)
+        feat = torch.randn(1, num_feat, 256, device=device, generator=dgen, dtype=torch.bfloat16)
+        anchor = syn.make_anchors(1, 900, gen).to(device)
+        inst = torch.randn(900, 256, generator=gen).to(device)
+        embed = torch.randn(900, 256, generator=gen).to(device)
+        logits = torch.empty(1, 900, 4, 13, 8, device=device)
+        learn = torch.empty(900, 18, device=device)
+        ops.weights_fc_into(logits.view(900, -1), learn, inst, embed, mod.weights_fc_weight, mod.learnable_fc_weight,
+                            mod.learnable_fc_bias)
+        ws = ops.camera_factors_into(ops.dfa_workspace(1, 6, 4, 13, 8, device), wc)
+        out = torch.empty(1, 900, 256, device=device)
+        loc = torch.empty(1, 900, 6, 13, 2, device=device)
+        ops.kps_project_into(anchor, learn.view(1, 900, 18), mod.fix_scale, proj, wh, sample_location=loc)
+        touched = unique_tap_pixels(loc, cfg.spatial_shapes, start, num_feat)
+        alg.append(touched * 512 + 900 * 416 * 4 + 6 * 416 * 4 + (anchor.numel() + learn.numel() + proj.numel()
+                                                                  + wh.numel()) * 4 + out.numel() * 4)
+        calls.append((out, feat, anchor, learn, logits, ws))
+
+    def run_all():
+        for out, feat, anchor, learn, logits, ws in calls:
+            ops.deformable_aggregation_anchors_into(out, feat, shape, start, anchor, mod.fix_scale, learn, proj, wh,
+                                                    logits, wc, ws)
+
+    from sparse4d_tt_b200.graph import capture
+
+    g = capture(run_all, warmup=2)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(replays):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    per_call_us = e0.elapsed_time(e1) * 1e3 / (replays * sets)
+    peak, src = measured_hbm()
+    a = statistics.mean(alg)
+    res = {"workload": f"{sets} independent single-frame inputs (900 anchors, 704x256 bf16 maps, 46 MB each) "
+                       f"cycled: {sets} gather launches per CUDA graph replay, {replays} replays timed",
+           "per_call_us": per_call_us, "calls_per_s": 1e6 / per_call_us, "algorithmic_bytes": a,
+           "achieved_gbs": a / per_call_us / 1e3, "frac_of_hbm": a / per_call_us / 1e3 / peak}
+    del calls, g
+    torch.cuda.empty_cache()
+    return res
 
 
 def kps_leg(device, iters=200):
@@ -519,6 +653,103 @@ def pack_leg(device, frames=32, iters=10):
            "launches_per_call": len(maps)}
     del maps, out
     torch.cuda.empty_cache()
+    return res
+
+
+HIGHRES_FRAMES = 16  # global batch of the high-resolution stress case
+
+
+def highres_leg(rank, world, device, pg, steps, warmup):
+    """High-resolution stress case: one DFA layer over a global batch of 16 frames of 1600x640
+    images (maps 160x400, 80x200, 40x100, 20x50; 261 MB of bf16 maps per frame), 1800 anchors,
+    run two ways on the N GPUs.
+
+    * frame-sharded: each rank takes 16 / N frames, no collective (the layer as one CUDA graph,
+      and launched eagerly); the gather's roofline as in the main line;
+    * camera-sharded (N >= 2): ranks form a (N / 2 frame groups) x (2 camera halves) grid; the
+      two ranks of a camera group take the same 16 / (N / 2) frames, each samples 3 of the 6
+      cameras with the softmax over all 6, the fp32 partial sums meet by an NCCL
+      reduce-scatter over the flattened (frame, anchor) rows, and each rank projects its half
+      (launched eagerly).  Rank 0 checks its shard against the same layer on one GPU.
+
+    Every rank runs every step; the times are device times, max over ranks."""
+    import torch.distributed as dist
+
+    from sparse4d_tt_b200 import DeformableFeatureAggregation
+    from sparse4d_tt_b200 import camera_shard as cs
+    from sparse4d_tt_b200 import synthetic as syn
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    def max_ms(ms):
+        t = torch.tensor([ms], device=device)
+        if pg is not None:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    peak, src = measured_hbm()
+    res = {"workload": f"1 DFA layer over {HIGHRES_FRAMES} frames (global) of 1600x640 images (maps 160x400, 80x200, "
+                       "40x100, 20x50), 1800 anchors x 13 pts x 6 cams x 4 levels x 256 ch, bf16 maps",
+           "global_frames": HIGHRES_FRAMES, "steps": steps}
+    fpr = max(1, HIGHRES_FRAMES // world)
+    w = Workload(fpr, 1, device, seed=3000 + rank, cfg=syn.config_highres(fpr, 1800))
+    for _ in range(warmup):
+        w.step()
+    eager = max_ms(time_steps(w.step, steps, barrier))
+    stack = w.graph_stack()
+    for _ in range(warmup):
+        stack.replay()
+    graph = max_ms(time_steps(stack.replay, steps, barrier))
+    g_ms = stack.gather_times_ms()[0]
+    alg, touched, inb = w.algorithmic_bytes_per_layer()[0]
+    calls = fpr * world * steps
+    res["frame_sharded"] = {
+        "frames_per_gpu": fpr, "value": calls / (graph / 1e3), "unit": UNIT, "ms_per_step": graph / steps,
+        "eager": {"value": calls / (eager / 1e3), "ms_per_step": eager / steps},
+        "collective": None,
+        "roofline": {"kernel": "dfa_gather_warp_kernel<bf16> (keypoints + projection + gather), rank 0's launch",
+                     "achieved": alg / (g_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": alg / (g_ms / 1e3) / 1e9 / peak, "peak_source": src, "algorithmic_bytes": alg,
+                     "unique_tap_pixels": touched, "launch_us": g_ms * 1e3},
+    }
+    del stack, w
+    torch.cuda.empty_cache()
+    if world >= 2 and world % 2 == 0:
+        fgroup, cgroup = cs.make_groups(world, 2)
+        fpg = HIGHRES_FRAMES // (world // 2)
+        mc = dict(MODEL_CONFIG, CAMERA_REDUCE="reduce_scatter")
+        w = Workload(fpg, 1, device, seed=4000 + fgroup, cfg=syn.config_highres(fpg, 1800), mesh_device=cgroup,
+                     model_config=mc)
+        for _ in range(warmup):
+            w.step()
+        ms = max_ms(time_steps(w.step, steps, barrier))
+        # parity: this rank's shard against the same layer on this GPU alone
+        out = w.step()
+        b, e = w.mods[0].shard
+        single = DeformableFeatureAggregation(device, w.params[0], MODEL_CONFIG).run(
+            w.inst0, w.anchors[0], w.embeds[0], w.packed, w.proj, w.wh, w.cfg.spatial_shapes, fpg, 1800)
+        ref = single.reshape(-1, single.shape[-1])[b:e].double()
+        got = out.double()
+        err = float((got - ref).abs().max())
+        pcc = float(torch.corrcoef(torch.stack([got.flatten(), ref.flatten()]))[0, 1])
+        stats = torch.tensor([err, -pcc], device=device)
+        if pg is not None:
+            pg.all_reduce(stats, op=pg.ReduceOp.MAX)
+        rows = fpg * 1800
+        res["camera_sharded"] = {
+            "grid": f"{world // 2} frame groups x 2 camera halves (3 cameras per rank)", "frames_per_group": fpg,
+            "value": fpg * (world // 2) * steps / (ms / 1e3), "unit": UNIT, "ms_per_step": ms / steps,
+            "collective": "reduce_scatter", "collective_group_size": dist.get_world_size(cgroup),
+            "collective_bytes_per_rank": rows * 256 * 4,
+            "launch": "eager (DeformableFeatureAggregation.run per step)",
+            "parity": {"max_abs_err": float(stats[0]), "pcc_min": -float(stats[1]),
+                       "against": "the same layer on one GPU (all 6 cameras), each rank's reduce-scattered rows; "
+                                  "max over ranks"},
+        }
+        del w, single
+        torch.cuda.empty_cache()
     return res
 
 
@@ -733,13 +964,34 @@ def run_ours(args):
     e2e = None
     if not args.no_e2e:
         e_steps = max(3, args.steps // 4)
-        e_ms, h2d, d2h = e2e_leg(w, stack, e_steps, 1, barrier)
+        e_ms, h2d, d2h, h2d_gbs = e2e_leg(w, e_steps, 2, barrier)
         te = torch.tensor([e_ms], device=device)
         if pg is not None:
             pg.all_reduce(te, op=pg.ReduceOp.MAX)
-        e2e = {"value": args.frames * args.layers * e_steps * world / (float(te.item()) / 1e3), "unit": UNIT,
+        e_ms_max = float(te.item())
+        # per-rank host-to-device rates, gathered to rank 0
+        rates = torch.tensor([h2d / (e_ms / e_steps) / 1e6, h2d_gbs], device=device)
+        if pg is not None:
+            allr = [torch.zeros_like(rates) for _ in range(world)]
+            pg.all_gather(allr, rates)
+            rates_all = [r.tolist() for r in allr]
+        else:
+            rates_all = [rates.tolist()]
+        floor_ms = h2d / (h2d_gbs * 1e6)
+        e2e = {"value": args.frames * args.layers * e_steps * world / (e_ms_max / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e_steps,
-               "path": "DFAStack.run (the 6-layer CUDA graph), inputs from pinned host memory"}
+               "ms_per_step": e_ms_max / e_steps,
+               "h2d_gbs_per_rank": [round(r[0], 2) for r in rates_all],
+               "h2d_copy_gbs_per_rank": [round(r[1], 2) for r in rates_all],
+               "h2d_floor_ms": floor_ms, "frac_of_h2d_floor": floor_ms / (e_ms_max / e_steps),
+               "gpu_numa_node": gpu_numa_node(device),
+               "path": "PipelinedDFAStack.submit (two 6-layer CUDA graphs; step k+1's uploads on a copy stream "
+                       "overlap step k's replay), inputs from pinned host memory, output read back each step",
+               "floor": "h2d bytes / the plain pinned host-to-device copy rate of the maps measured on this rank"}
+
+    highres = None
+    if not args.no_highres:
+        highres = highres_leg(rank, world, device, pg, min(args.steps, 20), 3)
 
     bs1 = pack = kps = None
     if rank == 0 and not args.no_bs1:
@@ -792,6 +1044,7 @@ def run_ours(args):
             "bs1": bs1,
             "pack": pack,
             "kps": kps,
+            "highres": highres,
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()

@@ -67,8 +67,9 @@ enum { S4D_LAYOUT_CAM_MAJOR = 0, S4D_LAYOUT_PT_MAJOR = 1, S4D_LAYOUT_GRID = 2 };
 enum {
   S4D_FLAG_BAD_LEVEL = 1,   /* a (camera, level) spatial_shape / scale_start_index entry lies
                                outside mc_ms_feat; its samples were skipped */
-  S4D_FLAG_WAIT_TIMEOUT = 2 /* a tensor-core kernel gave up (after 2 s) waiting on one of its own
-                               pipeline barriers; its outputs were not written.  Never expected. */
+  S4D_FLAG_WAIT_TIMEOUT = 2 /* a tensor-core kernel gave up waiting on one of its own pipeline
+                               barriers (after 2 s, or the limit set by s4d_set_tc_wait_limit_ns);
+                               its outputs were not written.  Never expected at the default limit. */
 };
 
 /* Layouts of the per-level maps s4d_pack_feature_maps reads. */
@@ -85,6 +86,18 @@ S4D_API const char* s4d_last_error(void);
 
 /* Version of this ABI (major * 100 + minor). */
 S4D_API int s4d_abi_version(void);
+
+/*
+ * Failure detection of the tensor-core kernels (s4d_dfa_weights_fc, s4d_dfa_output_proj).  Their
+ * pipeline barrier waits (the TMA producer on a free stage, the MMA issuer on a loaded stage, the
+ * epilogue on the accumulator) give up after this many nanoseconds, set S4D_FLAG_WAIT_TIMEOUT in
+ * the call's error_flag and leave the outputs unwritten; the CTA still waits (up to 2 s) for the
+ * copies and MMAs it already issued before it frees tensor memory and exits, so the context stays
+ * usable.  Applies to launches from the calling host thread; default 2,000,000,000 (2 s).  A test
+ * sets it to 0 to make the waits run out.  Returns the previous limit.  No counterpart in the
+ * reference (its device waits have no limit).
+ */
+S4D_API uint64_t s4d_set_tc_wait_limit_ns(uint64_t limit_ns);
 
 /* Bytes of device workspace s4d_kps_project needs when it compacts visible indices
  * (visible_idx or visible_count non-NULL).  Host-only, launches nothing. */

@@ -48,6 +48,7 @@ SIGNATURES = {
                                _p, _p, _p, _p, _p, _p, _sz, _p]),
     "s4d_kps_project_linear": (_int, [_p, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _i64, _p, _p, _i64, _i64, _i64,
                                       _int, _p, _p, _p, _p, _p, _p, _sz, _p]),
+    "s4d_set_tc_wait_limit_ns": (C.c_uint64, [C.c_uint64]),
     "s4d_kps_project_noalloc": (_int, [_p, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _int,
                                        _p, _p, _p, _p, _p, _p]),
     "s4d_kps_project_fused": (_int, [_p, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _p]),
@@ -83,7 +84,7 @@ class S4DError(RuntimeError):
 
 
 # Version of include/s4d_dfa.h these bindings are written for (s4d_abi_version()).
-ABI_VERSION = 103
+ABI_VERSION = 104
 
 
 def lib():

@@ -11,6 +11,16 @@ single-GPU result up to summation order.
 With 6 cameras and 8 GPUs the split is 2-D: ``frame_groups x camera_groups`` ranks (e.g.
 4 x 2), frames sharded over the first axis, cameras over the second; ``make_groups`` builds
 the camera sub-communicators.
+
+Two ways to combine the partial sums (``DeformableFeatureAggregation``'s
+``model_config["CAMERA_REDUCE"]``):
+
+* ``"all_reduce"`` -- every rank of the camera group ends with all ``bs * A`` rows (the
+  reference's ``ttnn.all_reduce``);
+* ``"reduce_scatter"`` -- NCCL reduce-scatter over the flattened ``(frame, anchor)`` rows: rank
+  ``r`` of a group of ``n`` ends with rows ``[r * bs * A / n, (r + 1) * bs * A / n)`` (whole
+  frames when ``n`` divides ``bs``), half the bytes of the all-reduce on the wire, and runs
+  ``output_proj`` on its shard only (``shard_rows``).
 """
 from __future__ import annotations
 
@@ -57,17 +67,36 @@ def make_groups(world_size: int, camera_groups: int):
     return mine
 
 
+def shard_rows(rows: int, group: Optional[dist.ProcessGroup] = None) -> Tuple[int, int]:
+    """``[begin, end)`` of the flattened ``(frame, anchor)`` rows this rank holds after a
+    row reduce-scatter over ``group`` (``rows`` must divide by the group size)."""
+    n = dist.get_world_size(group)
+    if rows % n:
+        raise ValueError(f"reduce-scatter needs bs * num_anchor ({rows}) divisible by the camera group size ({n})")
+    r = dist.get_rank(group)
+    return r * (rows // n), (r + 1) * (rows // n)
+
+
 def reduce_partial_sums(partial: torch.Tensor, group: Optional[dist.ProcessGroup] = None,
                         scatter: bool = False) -> torch.Tensor:
-    """Combine per-camera-shard partial sums ``[bs, A, C]``.
+    """Combine per-camera-shard partial sums, ``[bs, A, C]`` or flattened rows ``[R, C]``.
 
-    ``scatter=False``: all-reduce, every rank gets the full ``[bs, A, C]``.
-    ``scatter=True``: reduce-scatter over anchors, rank r gets anchors
-    ``[r*A/n, (r+1)*A/n)`` as ``[bs, A/n, C]`` (A must divide by the group size)."""
+    ``scatter=False``: all-reduce in place, every rank gets the full tensor.
+    ``scatter=True`` on ``[R, C]``: reduce-scatter over the rows, rank r gets rows
+    ``shard_rows(R, group)`` as ``[R/n, C]`` (no copy before the collective).
+    ``scatter=True`` on ``[bs, A, C]``: reduce-scatter over anchors within every frame, rank r
+    gets anchors ``[r*A/n, (r+1)*A/n)`` of each frame as ``[bs, A/n, C]`` (A must divide by the
+    group size; the per-frame chunks are gathered into one buffer first)."""
     if not scatter:
         dist.all_reduce(partial, group=group)
         return partial
     n = dist.get_world_size(group)
+    if partial.dim() == 2:
+        rows, C = partial.shape
+        b, e = shard_rows(rows, group)
+        out = torch.empty(e - b, C, dtype=partial.dtype, device=partial.device)
+        dist.reduce_scatter_tensor(out, partial.contiguous(), group=group)
+        return out
     bs, A, C = partial.shape
     if A % n:
         raise ValueError("reduce-scatter needs num_anchor divisible by the camera group size")

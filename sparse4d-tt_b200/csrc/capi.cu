@@ -9,6 +9,9 @@
 namespace s4d {
 
 static thread_local char g_last_error[512] = "";
+static thread_local unsigned long long g_tc_wait_limit_ns = 2000000000ull;
+
+unsigned long long tc_wait_limit_ns() { return g_tc_wait_limit_ns; }
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -44,7 +47,13 @@ const char* s4d_status_string(int status) {
 
 const char* s4d_last_error(void) { return g_last_error; }
 
-int s4d_abi_version(void) { return 103; }
+int s4d_abi_version(void) { return 104; }
+
+uint64_t s4d_set_tc_wait_limit_ns(uint64_t limit_ns) {
+  const uint64_t prev = g_tc_wait_limit_ns;
+  g_tc_wait_limit_ns = limit_ns;
+  return prev;
+}
 
 size_t s4d_kps_workspace_bytes(int64_t bs, int64_t num_anchor, int64_t num_cams, int64_t num_pts) {
   int64_t total = 0;
@@ -413,6 +422,7 @@ int s4d_dfa_weights_fc(const float* instance_feature, int64_t instance_ld, const
   p.n_learn = (int)num_learnable;
   p.k = (int)embed_dims;
   p.error_flag = error_flag;
+  p.wait_limit_ns = tc_wait_limit_ns();
   return launch_weights_fc(p, static_cast<cudaStream_t>(stream));
 }
 
@@ -632,6 +642,7 @@ int s4d_dfa_output_proj(const float* features, int64_t rows, const float* weight
   p.rows = rows;
   p.k = (int)embed_dims;
   p.error_flag = error_flag;
+  p.wait_limit_ns = tc_wait_limit_ns();
   return launch_output_proj(p, static_cast<cudaStream_t>(stream));
 }
 

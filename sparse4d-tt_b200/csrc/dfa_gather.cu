@@ -690,10 +690,25 @@ struct SampleRec {
 #ifndef S4D_GATHER_KPS_MIN_BLOCKS_BF16
 #define S4D_GATHER_KPS_MIN_BLOCKS_BF16 32
 #endif
-template <typename T, int NC, int NL, int NP, int G, int MODE, int WARPS, bool KPS>
-__global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? (KPS ? S4D_GATHER_KPS_MIN_BLOCKS_BF16
-                                                                     : S4D_GATHER_MIN_BLOCKS_BF16)
-                                                              : 24)
+// Resident warps per SM the register allocator must allow, for a block of WARPS warps.  The
+// blocks that share an anchor (SPLIT) run launches of fewer anchors than warp slots, so they
+// trade a few warp slots for registers: 28 warps (72 registers) for bf16 maps, where 64
+// registers spill; 20 (96) for fp32.
+template <typename T, bool KPS, int WARPS, bool SPLIT>
+constexpr int warp_kernel_min_blocks() {
+  constexpr int warps = SPLIT ? (sizeof(T) == 2 ? 28 : 20)
+                              : sizeof(T) == 2 ? (KPS ? S4D_GATHER_KPS_MIN_BLOCKS_BF16 : S4D_GATHER_MIN_BLOCKS_BF16) : 24;
+  return warps / WARPS > 0 ? warps / WARPS : 1;
+}
+
+// SPLIT = false: each warp of the block takes its own anchors (WARPS anchors in flight per
+// block).  SPLIT = true (few anchors: fewer than the resident warp slots): the block's WARPS warps
+// share one anchor.  Every warp computes the anchor's keypoints, softmax statistics and sample
+// records itself (identical work, no extra latency on an SM that is mostly idle at such sizes)
+// and gathers every WARPS-th merged tap block of each sub-round; the WARPS unnormalised partial
+// sums meet in shared memory in warp order, so the result is deterministic.
+template <typename T, int NC, int NL, int NP, int G, int MODE, int WARPS, bool KPS, bool SPLIT = false>
+__global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WARPS, SPLIT>()))
     dfa_gather_warp_kernel(GatherParams p) {
   constexpr int NLP = NL * NP;
   constexpr int LPG = NLP * G;
@@ -712,6 +727,8 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? (KPS ? S4D_GATHER
   __shared__ uint32_t s_xm[WARPS][32];
   __shared__ __align__(16) float4 s_kpt[KPS ? WARPS : 1][KPS ? NP : 1];  // KPS: the anchor's keypoints
   __shared__ float s_kc[KPS ? WARPS : 1][KPS ? NP * 3 : 1];               // KPS: their scaled coordinates
+  __shared__ __align__(16) float4 s_part[SPLIT ? WARPS : 1][SPLIT ? 64 : 1];  // SPLIT: partial sums per warp
+  __shared__ unsigned s_ticket;                                                // SPLIT: the block's anchor
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < NC * NL; i += WARPS * 32) {
@@ -745,9 +762,16 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? (KPS ? S4D_GATHER
   const int64_t total_anchors = (int64_t)p.bs * p.num_anchor;
   for (;;) {
   unsigned ticket = 0;
-  if (lane == 0) ticket = atomicAdd(p.anchor_counter, 1u);
-  const int64_t anchor_lin = __shfl_sync(0xffffffffu, ticket, 0);
-  if (anchor_lin >= total_anchors) break;
+  if (SPLIT) {  // one anchor per block
+    if (tid == 0) s_ticket = atomicAdd(p.anchor_counter, 1u);
+    __syncthreads();  // the ticket is read below, before the barriers that end the anchor
+    ticket = s_ticket;
+  } else {
+    if (lane == 0) ticket = atomicAdd(p.anchor_counter, 1u);
+    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+  }
+  const int64_t anchor_lin = ticket;
+  if (anchor_lin >= total_anchors) break;  // block-uniform when SPLIT
   const int b = (int)p.div_anchor.div((uint32_t)anchor_lin);  // anchors < 2^31
   const int gch = lane / (D / 8);  // group of this lane's output channels
 
@@ -930,16 +954,17 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? (KPS ? S4D_GATHER
         // unrolled so that the next blocks' loads are scheduled among this block's FMAs (4 fits
         // the 64 registers of the variant that computes its sample locations without spilling)
         constexpr int kTapUnroll = KPS ? 4 : 2;
+        constexpr int kStep = SPLIT ? WARPS : 1;  // SPLIT: this warp's share of the blocks
 #pragma unroll kTapUnroll
-        for (int k = 0; k < nlead; ++k) {
+        for (int k = SPLIT ? warp : 0; k < nlead; k += kStep) {
           const int4 px = s_rec[warp][k].pix;
           V v0, v1, v2, v3;  // every tap row is in bounds (see the record): no tests
           TapFma<T>::load(fb, px.x, lane, v0);
           TapFma<T>::load(fb, px.y, lane, v1);
           TapFma<T>::load(fb, px.z, lane, v2);
           TapFma<T>::load(fb, px.w, lane, v3);
-          if (k + 1 < nlead) {  // the next block's rows towards L1 (no registers held)
-            const int4 pn = s_rec[warp][k + 1].pix;
+          if (k + kStep < nlead) {  // the next block's rows towards L1 (no registers held)
+            const int4 pn = s_rec[warp][k + kStep].pix;
             const T* r = fb + lane * (kChannels / 32);
             prefetch_l1(r + (int64_t)pn.x * kChannels);
             prefetch_l1(r + (int64_t)pn.y * kChannels);
@@ -980,10 +1005,29 @@ __global__ void __launch_bounds__(WARPS * 32, sizeof(T) == 2 ? (KPS ? S4D_GATHER
   }
 
   // ---- 3. normalise and store ------------------------------------------------------------------
-  float4* o = reinterpret_cast<float4*>(p.out + anchor_lin * kChannels + lane * 8);
-  o[0] = make_float4(acc[0].x * inv, acc[0].y * inv, acc[1].x * inv, acc[1].y * inv);
-  o[1] = make_float4(acc[2].x * inv, acc[2].y * inv, acc[3].x * inv, acc[3].y * inv);
-  __syncwarp();  // this anchor's shared-memory state is read before the next one writes it
+  if (SPLIT) {  // the block's partial sums, added in warp order by warp 0
+    s_part[warp][2 * lane] = make_float4(acc[0].x, acc[0].y, acc[1].x, acc[1].y);
+    s_part[warp][2 * lane + 1] = make_float4(acc[2].x, acc[2].y, acc[3].x, acc[3].y);
+    __syncthreads();
+    if (warp == 0) {
+      float4 a0 = s_part[0][2 * lane], a1 = s_part[0][2 * lane + 1];
+#pragma unroll
+      for (int w = 1; w < WARPS; ++w) {
+        const float4 b0 = s_part[w][2 * lane], b1 = s_part[w][2 * lane + 1];
+        a0 = make_float4(a0.x + b0.x, a0.y + b0.y, a0.z + b0.z, a0.w + b0.w);
+        a1 = make_float4(a1.x + b1.x, a1.y + b1.y, a1.z + b1.z, a1.w + b1.w);
+      }
+      float4* o = reinterpret_cast<float4*>(p.out + anchor_lin * kChannels + lane * 8);
+      o[0] = make_float4(a0.x * inv, a0.y * inv, a0.z * inv, a0.w * inv);
+      o[1] = make_float4(a1.x * inv, a1.y * inv, a1.z * inv, a1.w * inv);
+    }
+    __syncthreads();  // s_part and s_ticket are rewritten for the next anchor
+  } else {
+    float4* o = reinterpret_cast<float4*>(p.out + anchor_lin * kChannels + lane * 8);
+    o[0] = make_float4(acc[0].x * inv, acc[0].y * inv, acc[1].x * inv, acc[1].y * inv);
+    o[1] = make_float4(acc[2].x * inv, acc[2].y * inv, acc[3].x * inv, acc[3].y * inv);
+    __syncwarp();  // this anchor's shared-memory state is read before the next one writes it
+  }
   }
 }
 
@@ -1006,19 +1050,46 @@ size_t gather_workspace_bytes(int64_t bs, int ncam, int nl, int np, int G) {
 // One-warp blocks of the warp kernel that fit on the current device at once, cached per device
 // and feature type (index `which`).
 template <typename K>
-static int resident_warp_blocks(K kernel, int which) {
-  static int cache[4][64] = {};
+static int resident_warp_blocks(K kernel, int which, int warps_per_block = kWarpBlock) {
+  static int cache[16][64] = {};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148 * 28;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148 * 28 / warps_per_block;
   if (cache[which][dev] > 0) return cache[which][dev];
   int per_sm = 0, sms = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kWarpBlock * 32, 0) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, warps_per_block * 32, 0) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || per_sm <= 0 || sms <= 0) {
     cudaGetLastError();
-    return 148 * 28;
+    return 148 * 28 / warps_per_block;
   }
   cache[which][dev] = per_sm * sms;
   return cache[which][dev];
+}
+
+// Warps that share one anchor in the warp kernel for `anchors` anchors: the largest of 1, 2, 4, 8
+// (at most S4D_GATHER_MAX_SPLIT) that keeps anchors x warps within S4D_GATHER_SPLIT_SLOTS warps
+// per SM (28: the warp slots of the SPLIT instances), so that a launch of few anchors still fills
+// the SMs in one wave.  It depends only on the anchor count and the SM count, so every instance
+// family (feature type, keypoints in the kernel or not) sums a given anchor in the same order.
+#ifndef S4D_GATHER_SPLIT_SLOTS
+#define S4D_GATHER_SPLIT_SLOTS 28
+#endif
+#ifndef S4D_GATHER_MAX_SPLIT
+#define S4D_GATHER_MAX_SPLIT 8
+#endif
+int gather_split_warps(int64_t anchors) {
+  static int sms_cache[64] = {};
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) {
+    if (sms_cache[dev] == 0 && cudaDeviceGetAttribute(&sms_cache[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      cudaGetLastError();
+      sms_cache[dev] = 148;
+    }
+    sms = sms_cache[dev];
+  }
+  const int64_t slots = (int64_t)sms * S4D_GATHER_SPLIT_SLOTS;
+  int s = 1;
+  while (s < S4D_GATHER_MAX_SPLIT && s < 8 && anchors * (2 * s) <= slots) s *= 2;
+  return s;
 }
 
 static bool fast_path_ok(const GatherParams& p) {
@@ -1060,21 +1131,41 @@ int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream) {
     int st = cuda_check(cudaMemsetAsync(q.anchor_counter, 0, sizeof(unsigned), stream), "cudaMemsetAsync(counter)");
     if (st) return st;
     const int64_t anchors = (int64_t)p.bs * p.num_anchor;
-    auto launch = [&](auto kernel, int which) {
-      const int64_t fit = resident_warp_blocks(kernel, which);
-      kernel<<<(unsigned)(anchors < fit ? anchors : fit), kWarpBlock * 32, 0, stream>>>(q);
-    };
     const bool bf = feat_dtype == S4D_DTYPE_BF16;
+    const int which = (p.kps_anchor != nullptr ? 2 : 0) + (bf ? 0 : 1);  // index of the one-warp instance
+    // The instances of one (feature type, KPS) pair: one-warp blocks (S = 1) and blocks of S warps
+    // sharing an anchor (S = 2, 4, 8); `which` + 4 * log2(S) indexes the occupancy cache.
+    auto launch_family = [&](auto k1, auto k2, auto k4, auto k8) {
+      const int split = gather_split_warps(anchors);
+      auto go = [&](auto kernel, int warps, int slot) {
+        const int64_t fit = resident_warp_blocks(kernel, which + 4 * slot, warps);
+        kernel<<<(unsigned)(anchors < fit ? anchors : fit), warps * 32, 0, stream>>>(q);
+      };
+      if (split == 8)
+        go(k8, 8, 3);
+      else if (split == 4)
+        go(k4, 4, 2);
+      else if (split == 2)
+        go(k2, 2, 1);
+      else
+        go(k1, kWarpBlock, 0);
+    };
+#define S4D_WARP_FAMILY(T, KPS)                                                                     \
+  launch_family(dfa_gather_warp_kernel<T, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock, KPS>,     \
+                dfa_gather_warp_kernel<T, kFastNC, kFastNL, kFastNP, kFastG, 1, 2, KPS, true>,        \
+                dfa_gather_warp_kernel<T, kFastNC, kFastNL, kFastNP, kFastG, 1, 4, KPS, true>,        \
+                dfa_gather_warp_kernel<T, kFastNC, kFastNL, kFastNP, kFastG, 1, 8, KPS, true>)
     if (p.kps_anchor != nullptr) {
       if (bf)
-        launch(dfa_gather_warp_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock, true>, 2);
+        S4D_WARP_FAMILY(__nv_bfloat16, true);
       else
-        launch(dfa_gather_warp_kernel<float, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock, true>, 3);
+        S4D_WARP_FAMILY(float, true);
     } else if (bf) {
-      launch(dfa_gather_warp_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock, false>, 0);
+      S4D_WARP_FAMILY(__nv_bfloat16, false);
     } else {
-      launch(dfa_gather_warp_kernel<float, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock, false>, 1);
+      S4D_WARP_FAMILY(float, false);
     }
+#undef S4D_WARP_FAMILY
     return cuda_check(cudaGetLastError(), "dfa_gather_warp_kernel launch");
   }
   if (p.kps_anchor != nullptr)  // only the warp kernel computes sample locations; the others read p.loc

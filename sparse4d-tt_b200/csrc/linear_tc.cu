@@ -75,15 +75,24 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
 }
 
 // Waits until the phase with `parity` has completed.  Returns false without waiting further
-// once another role of the CTA has given up (abort_flag set), or after kWaitLimitNs, in which
-// case it sets abort_flag itself.  With abort_flag == nullptr only the time limit applies.
-__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+// once another role of the CTA has given up (abort_flag set), or after limit_ns, in which case it
+// sets abort_flag itself.  With abort_flag == nullptr only the time limit applies.
+//
+// Two kinds of waits use it.  The pipeline waits (TMA producer on an empty stage, MMA issuer on a
+// full stage, epilogue on the accumulator) pass the CTA's abort flag and the launch's limit
+// (WfcParams / OprojParams::wait_limit_ns, 2 s unless a caller lowered it through
+// s4d_set_tc_wait_limit_ns).  The teardown waits -- the producer's drain of the loads it issued
+// and the MMA issuer's wait for the MMAs it issued -- pass no flag and always kWaitLimitNs: they
+// are what guarantees that no copy is still landing in shared memory and no MMA still writing
+// tensor memory when the CTA frees it and exits, whatever the pipeline waits decided.
+__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_test(bar, parity)) return true;
   const unsigned long long t0 = now_ns();
   for (;;) {
     if (mbar_test(bar, parity)) return true;
     if (abort_flag != nullptr && *abort_flag) return false;
-    if (now_ns() - t0 > kWaitLimitNs) {
+    if (now_ns() - t0 > limit_ns) {
       if (abort_flag != nullptr) *abort_flag = 1;
       return false;
     }
@@ -288,8 +297,8 @@ __device__ __forceinline__ void drain_loads(uint32_t full0, int issued) {
 }
 
 // Warp-uniform wait for the accumulator (tcgen05.ld is warp-collective).
-__device__ __forceinline__ bool wait_accumulator(const Ctl& c, uint32_t acc_bar) {
-  const bool done = __all_sync(0xffffffffu, mbar_wait(acc_bar, 0, c.abort_flag));
+__device__ __forceinline__ bool wait_accumulator(const Ctl& c, uint32_t acc_bar, unsigned long long limit_ns) {
+  const bool done = __all_sync(0xffffffffu, mbar_wait(acc_bar, 0, c.abort_flag, limit_ns));
   const int aborted = __shfl_sync(0xffffffffu, *c.abort_flag, 0);
   tc_fence_after();
   return done && !aborted;
@@ -332,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       for (int kb = 0; kb < kbs; ++kb) {
         const int s = kb % kStages;
-        if (kb >= kStages && !mbar_wait(empty0 + 8 * s, ((kb / kStages) - 1) & 1, c.abort_flag)) break;
+        if (kb >= kStages && !mbar_wait(empty0 + 8 * s, ((kb / kStages) - 1) & 1, c.abort_flag, p.wait_limit_ns)) break;
         const uint32_t st = smem_u32(smem + s * S::kStage), fb = full0 + 8 * s;
         mbar_expect_tx(fb, S::kStage);
         tma_load_2d(st, &map_inst, fb, kb * kBK, int(row0));
@@ -349,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {  // MMA issuer
       for (int kb = 0; kb < kbs; ++kb) {
         const int s = kb % kStages;
-        if (!mbar_wait(full0 + 8 * s, (kb / kStages) & 1, c.abort_flag)) break;
+        if (!mbar_wait(full0 + 8 * s, (kb / kStages) & 1, c.abort_flag, p.wait_limit_ns)) break;
         tc_fence_after();
         const uint32_t st = smem_u32(smem + s * S::kStage);
         const uint64_t a_inst = sw64_desc(st), a_emb = sw64_desc(st + kATile);
@@ -373,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // Epilogue: logits through TMA stores, learnable columns (not 16-byte rows) by plain stores.
     const int q = warp & 3;
-    if (wait_accumulator(c, acc_bar)) {
+    if (wait_accumulator(c, acc_bar, p.wait_limit_ns)) {
       store_columns(tmem, q, lane, row0, NW, &map_logits, smem + q * 2 * kStageChunk, nullptr, nullptr, 0, p.rows);
       uint32_t v[32];
       tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(NW), v);
@@ -418,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       int issued = 0;
       for (int kb = 0; kb < kbs; ++kb) {
         const int s = kb % kStages;
-        if (kb >= kStages && !mbar_wait(empty0 + 8 * s, ((kb / kStages) - 1) & 1, c.abort_flag)) break;
+        if (kb >= kStages && !mbar_wait(empty0 + 8 * s, ((kb / kStages) - 1) & 1, c.abort_flag, p.wait_limit_ns)) break;
         const uint32_t st = smem_u32(smem + s * S::kStage), fb = full0 + 8 * s;
         mbar_expect_tx(fb, S::kStage);
         tma_load_2d(st, &map_feat, fb, kb * kBK, int(row0));
@@ -431,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       for (int kb = 0; kb < kbs; ++kb) {
         const int s = kb % kStages;
-        if (!mbar_wait(full0 + 8 * s, (kb / kStages) & 1, c.abort_flag)) break;
+        if (!mbar_wait(full0 + 8 * s, (kb / kStages) & 1, c.abort_flag, p.wait_limit_ns)) break;
         tc_fence_after();
         const uint32_t st = smem_u32(smem + s * S::kStage);
         const uint64_t a = sw64_desc(st), b = sw64_desc(st + kATile);
@@ -467,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
       }
     }
-    if (wait_accumulator(c, acc_bar))
+    if (wait_accumulator(c, acc_bar, p.wait_limit_ns))
       store_columns(tmem, q, lane, row0, S::kN, &map_out, smem + q * 2 * kStageChunk, p.bias,
                     p.res_mode == S4D_RESIDUAL_ADD ? p.res : nullptr, p.res_ld, p.rows);
   }

@@ -87,6 +87,7 @@ struct WfcParams {
   int64_t rows;
   int n_logits, n_learn, k;
   int32_t* error_flag;
+  unsigned long long wait_limit_ns;  // limit of the pipeline's barrier waits (tc_wait_limit_ns())
 };
 
 struct OprojParams {
@@ -101,6 +102,7 @@ struct OprojParams {
   int64_t rows;
   int k;
   int32_t* error_flag;
+  unsigned long long wait_limit_ns;  // limit of the pipeline's barrier waits (tc_wait_limit_ns())
 };
 
 // Camera encoder + per-camera logit term (camera_encoder.cu).
@@ -153,6 +155,10 @@ struct IbSelectParams {
   int32_t* out_idx;             // CACHE: [bs, num_temp]; UPDATE: [bs, A - num_temp]; or null
   int bs, num_anchor, num_cls, embed_dims, anchor_dim, num_temp, sort_size;
 };
+
+// Limit of the tensor-core kernels' pipeline waits for launches from this host thread (2 s
+// unless s4d_set_tc_wait_limit_ns changed it).
+unsigned long long tc_wait_limit_ns();
 
 int launch_ib_project(const IbProjectParams& p, cudaStream_t stream);
 int launch_ib_select(IbSelectParams p, bool cache, cudaStream_t stream);

@@ -15,8 +15,12 @@ way by the decoder head (``model/sparse4d_head.py:405-411``).  What runs:
 
 Camera sharding (the reference's ``mesh_device`` mode, ``:172-176,925-931``) is available by
 passing a ``torch.distributed`` process group as ``mesh_device``: each rank samples only its
-own cameras, with the softmax taken over ALL cameras, and the partial sums are all-reduced
-(the reference softmaxes over each device's cameras only; see ``camera_shard``).
+own cameras, with the softmax taken over ALL cameras (the reference softmaxes over each
+device's cameras only; see ``camera_shard``).  ``model_config["CAMERA_REDUCE"]`` chooses how
+the fp32 partial sums meet: ``"all_reduce"`` (default; every rank returns all ``[bs, A, 2C]``,
+as the reference's ``ttnn.all_reduce``) or ``"reduce_scatter"`` (NCCL reduce-scatter over the
+flattened ``(frame, anchor)`` rows; the rank runs ``output_proj`` on its shard only and
+returns ``[bs * A / n, 2C]``, rows ``self.shard`` of the flattened output).
 """
 from __future__ import annotations
 
@@ -67,6 +71,7 @@ def preprocess_dfa_parameters(pt_model) -> Dict[str, Tensor]:
 FeatureMaps = Union[List[Tensor], Tuple[Tensor, Tensor, Tensor]]
 
 MATMUL_PRECISIONS = {"fp32": "highest", "tf32": "high"}
+CAMERA_REDUCES = ("all_reduce", "reduce_scatter")
 
 
 @contextlib.contextmanager
@@ -124,6 +129,11 @@ class DeformableFeatureAggregation:
         self.process_group = mesh_device if _is_process_group(mesh_device) else None
         if mesh_device is not None and self.process_group is None:
             raise ValueError("mesh_device must be a torch.distributed ProcessGroup (camera sharding)")
+        self.camera_reduce = self.model_config.get("CAMERA_REDUCE", "all_reduce")
+        if self.camera_reduce not in CAMERA_REDUCES:
+            raise ValueError(f"CAMERA_REDUCE must be one of {CAMERA_REDUCES}")
+        # (begin, end) of the flattened (frame, anchor) rows the last run() returned
+        self.shard: Optional[Tuple[int, int]] = None
         missing = [k for k in PARAM_KEYS if k not in parameters and (use_camera_embed or not k.startswith("cam_"))]
         if missing:
             raise KeyError(f"parameters missing {missing}")
@@ -387,25 +397,38 @@ class DeformableFeatureAggregation:
             ev[1].record(self._timing)
             self._timing_pending = True
             log.append(ev)
+        self.shard = (0, rows)
+        out_shape = (bs, num_anchor)
+        feats2d = feats.view(rows, C)
+        inst_rows = instance_feature.reshape(rows, C)
         if self.process_group is not None:
-            import torch.distributed as dist
+            from .camera_shard import reduce_partial_sums, shard_rows
 
-            dist.all_reduce(feats, group=self.process_group)
+            if self.camera_reduce == "reduce_scatter":
+                # NCCL reduce-scatter over the flattened (frame, anchor) rows: this rank keeps its
+                # shard of the summed features and projects only those rows
+                self.shard = shard_rows(rows, self.process_group)
+                feats2d = reduce_partial_sums(feats2d, self.process_group, scatter=True)
+                inst_rows = inst_rows[self.shard[0]:self.shard[1]]
+                out_shape = (self.shard[1] - self.shard[0],)
+            else:
+                reduce_partial_sums(feats, self.process_group)
+        n_out = feats2d.shape[0]
 
         if self._tc:
             width = 2 * C if self.residual_mode == "cat" else C
-            out = torch.empty(bs, num_anchor, width, device=dev)
-            ops.output_proj_into(out.view(rows, width), feats.view(rows, C), self.output_proj_weight,
-                                 self.output_proj_bias, inst2d, self.residual_mode)
+            out = torch.empty(*out_shape, width, device=dev)
+            ops.output_proj_into(out.view(n_out, width), feats2d, self.output_proj_weight, self.output_proj_bias,
+                                 ops.row_view(inst_rows, C), self.residual_mode)
             return out
         with _matmul_precision(self.matmul_precision):
-            out = F.linear(feats, self.output_proj_weight, self.output_proj_bias)
-        inst = instance_feature.to(out.dtype)
+            out = F.linear(feats2d, self.output_proj_weight, self.output_proj_bias)
+        inst = inst_rows.to(out.dtype)
         if self.residual_mode == "add":
-            return out + inst
-        if self.residual_mode == "cat":
-            return torch.cat([out, inst], dim=-1)
-        return out
+            out = out + inst
+        elif self.residual_mode == "cat":
+            out = torch.cat([out, inst], dim=-1)
+        return out.reshape(*out_shape, out.shape[-1])
 
     __call__ = run
 

@@ -144,3 +144,73 @@ class DFAStack:
         put(self.projection_mat, projection_mat)
         put(self.image_wh, image_wh)
         return self.replay()
+
+
+class PipelinedDFAStack:
+    """Batches streamed from host memory through two ``DFAStack`` graphs of the same layers, so
+    that the upload of batch ``k + 1`` overlaps the replay of batch ``k``.
+
+    ``submit(...)`` takes one batch's inputs (pinned host tensors for asynchronous copies; the
+    argument meaning of ``DFAStack.run``) and returns at once.  Its copies run on a copy stream
+    into the static buffers of graph ``k % 2`` as soon as that graph's previous replay (batch
+    ``k - 2``) has read them; the replay runs on the current stream after the copies, and the
+    output is copied into ``out`` (a pinned host tensor, if given) behind it.  The host tensors of
+    a batch must stay unchanged until its copies are done: ``wait(k)`` (or ``synchronize()``)
+    returns when batch ``k`` is complete.  Graph ``k % 2``'s output tensor holds batch ``k``'s
+    result until batch ``k + 2`` replays."""
+
+    def __init__(self, layers: Sequence, bs: int, num_anchor: int, spatial_shapes: Sequence[Tuple[int, int]],
+                 feature_dtype: torch.dtype = torch.bfloat16, warmup: int = 2):
+        self.stacks = [DFAStack(layers, bs, num_anchor, spatial_shapes, feature_dtype, warmup) for _ in range(2)]
+        dev = layers[0].device
+        self.copy_stream = torch.cuda.Stream(dev)
+        self._freed = [torch.cuda.Event() for _ in range(2)]  # the graph's last replay has read its inputs
+        self._copied = [torch.cuda.Event() for _ in range(2)]
+        self._done: List[Optional[torch.cuda.Event]] = []
+        self._count = 0
+
+    def submit(self, instance_feature: Optional[Tensor] = None, anchors: Optional[List[Tensor]] = None,
+               anchor_embeds: Optional[List[Tensor]] = None, mc_ms_feat: Optional[Tensor] = None,
+               projection_mat: Optional[Tensor] = None, image_wh: Optional[Tensor] = None,
+               out: Optional[Tensor] = None) -> int:
+        k = self._count
+        j = k % 2
+        st = self.stacks[j]
+        cur = torch.cuda.current_stream()
+        if k >= 2:
+            self.copy_stream.wait_event(self._freed[j])
+        with torch.cuda.stream(self.copy_stream):
+            def put(dst, src):
+                if src is not None:
+                    dst.copy_(src, non_blocking=True)
+
+            put(st.instance_feature, instance_feature)
+            for d, s in zip(st.anchors, anchors or []):
+                put(d, s)
+            for d, s in zip(st.anchor_embeds, anchor_embeds or []):
+                put(d, s)
+            put(st.mc_ms_feat, mc_ms_feat)
+            put(st.projection_mat, projection_mat)
+            put(st.image_wh, image_wh)
+            self._copied[j].record(self.copy_stream)
+        cur.wait_event(self._copied[j])
+        st.replay()
+        self._freed[j].record(cur)
+        if out is not None:
+            out.copy_(st.output, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(cur)
+        self._done.append(done)
+        self._count += 1
+        return k
+
+    def output(self, k: int) -> Tensor:
+        """Device output of batch ``k`` (valid until batch ``k + 2`` replays)."""
+        return self.stacks[k % 2].output
+
+    def wait(self, k: int) -> None:
+        self._done[k].synchronize()
+
+    def synchronize(self) -> None:
+        if self._done:
+            self._done[-1].synchronize()

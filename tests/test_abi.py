@@ -33,7 +33,7 @@ def lib():
 
 def test_every_declared_symbol_is_exported(lib):
     names = declared_functions()
-    assert len(names) == 20, names
+    assert len(names) == 21, names
     for n in names:
         assert hasattr(lib, n), n
         assert n in L.SIGNATURES, f"{n} has no ctypes signature"
@@ -52,7 +52,7 @@ def test_status_strings_and_version(lib):
     assert L.status_string(0) == "S4D_OK"
     assert L.status_string(2) == "S4D_ERR_UNSUPPORTED_SHAPE"
     assert L.status_string(99) == "S4D_ERR_UNKNOWN"
-    assert lib.s4d_abi_version() == 103 == L.ABI_VERSION
+    assert lib.s4d_abi_version() == 104 == L.ABI_VERSION
 
 
 def test_dfa_workspace_bytes(lib):
@@ -395,3 +395,20 @@ def test_noalloc_limit_is_checked_on_the_host(lib):
     assert st == L.S4D_ERR_UNSUPPORTED_SHAPE and "scratch limit" in msg, msg
     st, msg = call(1, 1, 1, 1 << 62, 1 << 62)
     assert st == L.S4D_ERR_UNSUPPORTED_SHAPE, msg
+
+
+def test_tc_wait_limit_is_per_thread_and_restorable(lib):
+    import threading
+
+    prev = lib.s4d_set_tc_wait_limit_ns(12345)
+    assert prev == 2_000_000_000
+    seen = {}
+
+    def other():
+        seen["v"] = lib.s4d_set_tc_wait_limit_ns(7)
+
+    t = threading.Thread(target=other)
+    t.start()
+    t.join()
+    assert seen["v"] == 2_000_000_000  # another thread keeps its own default
+    assert lib.s4d_set_tc_wait_limit_ns(prev) == 12345

@@ -87,3 +87,75 @@ def test_gather_from_anchors_empty(cuda_device):
                                             torch.empty(1, 0, 4, 13, 8, device=d), torch.zeros(1, 6, 4, 13, 8, device=d),
                                             ws)
     torch.cuda.synchronize()
+
+
+def _anchors_gather(cfg, t, feat, shape, start):
+    d = torch.device("cuda:0")
+    ws = ops.camera_factors_into(ops.dfa_workspace(cfg.bs, 6, 4, 13, 8, d), t["wc"])
+    out = torch.full((cfg.bs, cfg.num_anchor, 256), float("nan"), device=d)
+    ops.deformable_aggregation_anchors_into(out, feat, shape, start, t["anchor"], t["fix"], t["learn"], t["proj"],
+                                            t["wh"], t["wa"], t["wc"], ws)
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.mark.parametrize("A", [100, 900, 1800])
+def test_split_anchor_blocks_match_one_warp_per_anchor(cuda_device, A):
+    """Launches of few anchors share each anchor between 8 (100 anchors), 4 (900) or 2 (1800)
+    warps of a block; the same frame repeated in a batch of at least 4,800 anchors (one warp per
+    anchor on a 148-SM B200) must give the same sums up to the order of the fp32 additions."""
+    cfg1 = syn.DFAConfig(bs=1, num_anchor=A)
+    ins = syn.make_inputs(cfg1, 70)
+    params = syn.make_params(cfg1, torch.Generator().manual_seed(71))
+    gen = torch.Generator().manual_seed(72)
+    d = torch.device("cuda:0")
+    learn = torch.randn(A, 18, generator=gen) * 2
+    wa = torch.randn(1, A, 4, 13, 8, generator=gen) * 2
+    wc = torch.randn(1, 6, 4, 13, 8, generator=gen) * 2
+    feat, shape, start = ops.pack_feature_maps([m.to(d) for m in ins.feature_maps], dtype=torch.bfloat16)
+    t1 = {k: v.contiguous().to(d) for k, v in dict(anchor=ins.anchor, learn=learn, wa=wa, wc=wc,
+                                                   proj=ins.projection_mat, wh=ins.image_wh,
+                                                   fix=params["kps_fix_scale"]).items()}
+    one = _anchors_gather(cfg1, t1, feat, shape, start)
+    n = max(3, -(-4800 // A))
+    cfgn = syn.DFAConfig(bs=n, num_anchor=A)
+    tn = dict(t1)
+    for k in ("anchor", "wa", "wc", "proj", "wh"):
+        tn[k] = t1[k].expand(n, *t1[k].shape[1:]).contiguous()
+    tn["learn"] = t1["learn"].repeat(n, 1)
+    many = _anchors_gather(cfgn, tn, feat.expand(n, -1, -1).contiguous(), shape, start)
+    assert torch.isfinite(one).all()
+    ref = many[0]
+    err = (one[0] - ref).abs().max().item()
+    assert err <= 1e-5 * max(1.0, ref.abs().max().item()), err
+    assert torch.equal(many[0], many[n - 1])  # deterministic
+
+
+def test_split_anchor_blocks_bs1_against_reference_rows(cuda_device):
+    """The module's bs = 1 gather (900 anchors, 4 warps per anchor) fed the oracle's keypoint
+    logits and split weight logits, against the reference's fused rows of the bf16 fixture and
+    the oracle, at the bf16 tolerance."""
+    from helpers import max_rel_err, mean_rel_err, pcc, regen
+    from oracle import dfa_torch as oto
+
+    g, cfg, ins, params = regen("standard_s1_bf16")
+    d = torch.device("cuda:0")
+    W, b = params["weights_fc_weight"].double(), params["weights_fc_bias"].double()
+    wa = ((ins.instance_feature + ins.anchor_embed).double() @ W.T).float().reshape(1, 900, 4, 13, 8)
+    cam = oto.camera_embed(ins.projection_mat, params).double()
+    wc = (cam @ W.T + b).float().reshape(1, 6, 4, 13, 8)
+    learn = oto.learnable_logits(ins.instance_feature, params).reshape(900, 18)
+    feat, shape, start = ops.pack_feature_maps([m.to(d) for m in ins.feature_maps], dtype=torch.bfloat16)
+    t = {k: v.contiguous().to(d) for k, v in dict(anchor=ins.anchor, learn=learn, wa=wa, wc=wc,
+                                                  proj=ins.projection_mat, wh=ins.image_wh,
+                                                  fix=params["kps_fix_scale"]).items()}
+    got = _anchors_gather(cfg, t, feat, shape, start).cpu().reshape(900, 256)
+    sel = got.numpy()[g["rows"]]
+    p, mre, xre = pcc(sel, g["fused_rows"]), mean_rel_err(sel, g["fused_rows"]), max_rel_err(sel, g["fused_rows"])
+    print(f"bs1 split gather vs reference rows: pcc={p:.7f} mean_rel={mre:.2e} max_rel={xre:.2e}")
+    assert p >= 0.9999 and mre <= 1e-2 and xre <= 1e-2
+    kps = oto.key_points(ins.anchor, ins.instance_feature, params)
+    uv, _ = oto.project_points_with_depth(kps, ins.projection_mat, ins.image_wh)
+    logits = oto.weight_logits(ins.instance_feature, ins.anchor_embed, ins.projection_mat, params, 4, 13, 8)
+    ref = oto.deformable_aggregation(ins.feature_maps, uv, logits).reshape(900, 256)
+    assert pcc(got, ref) >= 0.9999 and max_rel_err(got, ref) <= 1e-2

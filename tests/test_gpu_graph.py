@@ -106,3 +106,30 @@ def test_stack_timed_replays(cuda_device):
     assert all(m.event_log is None for m in layers)
     with pytest.raises(RuntimeError):
         plain.gather_times_ms()
+
+
+def test_pipelined_stack_matches_stack(cuda_device):
+    """PipelinedDFAStack: four batches streamed from pinned host memory through the two graphs
+    (uploads overlapping replays) give exactly what one DFAStack gives on each batch."""
+    from sparse4d_tt_b200 import PipelinedDFAStack
+
+    cfg = syn.DFAConfig(bs=2, num_anchor=900)
+    layers = _layers(cfg, 2, seed=320)
+    pipe = PipelinedDFAStack(layers, cfg.bs, cfg.num_anchor, cfg.spatial_shapes)
+    ref_stack = DFAStack(layers, cfg.bs, cfg.num_anchor, cfg.spatial_shapes)
+    batches, outs = [], []
+    for seed in (11, 12, 13, 14):
+        ins, anchors, embeds = _inputs(cfg, 2, seed)
+        packed = ops.pack_feature_maps([m.to("cuda:0") for m in ins.feature_maps], dtype=torch.bfloat16)
+        host = dict(instance_feature=ins.instance_feature.pin_memory(), anchors=[a.pin_memory() for a in anchors],
+                    anchor_embeds=[e.pin_memory() for e in embeds], mc_ms_feat=packed[0].cpu().pin_memory(),
+                    projection_mat=ins.projection_mat.pin_memory(), image_wh=ins.image_wh.pin_memory())
+        batches.append(host)
+        outs.append(torch.empty(cfg.bs, cfg.num_anchor, 512, pin_memory=True))
+    for host, out in zip(batches, outs):
+        pipe.submit(out=out, **host)
+    pipe.synchronize()
+    for host, out in zip(batches, outs):
+        ref = ref_stack.run(host["instance_feature"], host["anchors"], host["anchor_embeds"], host["mc_ms_feat"],
+                            host["projection_mat"], host["image_wh"]).cpu()
+        assert torch.equal(out, ref)

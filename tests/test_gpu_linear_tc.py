@@ -166,3 +166,45 @@ def test_linear_tc_in_cuda_graph(cuda_device):
     body()
     torch.cuda.synchronize()
     assert torch.equal(got_l, logits) and torch.equal(got_o, out)
+
+
+def test_wait_timeout_sets_flag_and_next_launch_is_clean(cuda_device):
+    """Failure detection of the tensor-core kernels: with the pipeline wait limit lowered to 0
+    (s4d_set_tc_wait_limit_ns) the barrier waits give up at once, the launch reports
+    S4D_FLAG_WAIT_TIMEOUT in its error_flag and still finishes (each CTA waits for the copies and
+    MMAs it issued before freeing tensor memory); with the limit restored, the next launches on
+    the same context are correct and report nothing."""
+    from sparse4d_tt_b200 import _lib as L
+
+    dev = torch.device("cuda:0")
+    gen = torch.Generator().manual_seed(11)
+    rows, n, m, c = 28800, 416, 18, 256
+    w_fc, w_kps, b_kps = _weights(n, m, c, gen, dev)
+    inst = torch.randn(rows, c, generator=gen).to(dev)
+    embed = torch.randn(rows, c, generator=gen).to(dev)
+    w_o = ((torch.rand(c, c, generator=gen) * 2 - 1) * (3 / c) ** 0.5).to(dev)
+    b_o = torch.randn(c, generator=gen).to(dev)
+    logits = torch.empty(rows, n, device=dev)
+    learn = torch.empty(rows, m, device=dev)
+    out = torch.empty(rows, 2 * c, device=dev)
+    lib = L.lib()
+    flags = torch.zeros(2, dtype=torch.int32, device=dev)
+    prev = lib.s4d_set_tc_wait_limit_ns(0)
+    try:
+        ops.weights_fc_into(logits, learn, inst, embed, w_fc, w_kps, b_kps, error_flag=flags[0:1])
+        ops.output_proj_into(out, inst, w_o, b_o, embed, "cat", error_flag=flags[1:2])
+    finally:
+        lib.s4d_set_tc_wait_limit_ns(prev)
+    torch.cuda.synchronize()
+    assert prev == 2_000_000_000
+    assert flags[0].item() & L.S4D_FLAG_WAIT_TIMEOUT and flags[1].item() & L.S4D_FLAG_WAIT_TIMEOUT
+    flags.zero_()
+    ops.weights_fc_into(logits, learn, inst, embed, w_fc, w_kps, b_kps, error_flag=flags[0:1])
+    ops.output_proj_into(out, inst, w_o, b_o, embed, "cat", error_flag=flags[1:2])
+    torch.cuda.synchronize()
+    assert flags.tolist() == [0, 0]
+    i64, e64, wf = inst.double(), embed.double(), w_fc.double()
+    _check(logits, (i64 + e64) @ wf.T, (i64.abs() + e64.abs()) @ wf.abs().T, "logits after a timed-out launch")
+    _check(out[:, :c], i64 @ w_o.double().T + b_o.double(), i64.abs() @ w_o.double().abs().T + 1e-6,
+           "output_proj after a timed-out launch")
+    assert torch.equal(out[:, c:], embed)

@@ -1,6 +1,7 @@
 """Camera-sharded DFA on 2 GPUs (NCCL): each rank samples 3 of the 6 cameras with the softmax
-taken over all 6, the partial sums are all-reduced, and the result equals the single-GPU
-layer.  Skipped unless 2 GPUs are visible."""
+taken over all 6, the partial sums are all-reduced (every rank gets every row) or
+reduce-scattered over the flattened (frame, anchor) rows (each rank projects its half), and the
+result equals the single-GPU layer's rows.  Skipped unless 2 GPUs are visible."""
 import os
 import socket
 import tempfile
@@ -45,8 +46,26 @@ def _worker(rank, world, port, out_dir):
         sharded = DeformableFeatureAggregation(dev, params, {"FEATURE_DTYPE": torch.float32},
                                                mesh_device=dist.group.WORLD).run(*args)
         single = DeformableFeatureAggregation(dev, params, {"FEATURE_DTYPE": torch.float32}).run(*args)
+        rs_mod = DeformableFeatureAggregation(dev, params, {"FEATURE_DTYPE": torch.float32,
+                                                           "CAMERA_REDUCE": "reduce_scatter"},
+                                              mesh_device=dist.group.WORLD)
+        rs = rs_mod.run(*args)
+        b, e = rs_mod.shard
+        # the benchmark configuration: bf16 maps, tensor-core linears, keypoints in the gather
+        packed_bf = ops.pack_feature_maps([m.to(dev) for m in ins.feature_maps], dtype=torch.bfloat16)
+        cfg_tc = {"FEATURE_DTYPE": torch.bfloat16, "MATMUL_PRECISION": "tf32"}
+        args_bf = args[:3] + (packed_bf,) + args[4:]
+        rs_tc_mod = DeformableFeatureAggregation(dev, params, dict(cfg_tc, CAMERA_REDUCE="reduce_scatter"),
+                                                 mesh_device=dist.group.WORLD)
+        rs_tc = rs_tc_mod.run(*args_bf)
+        single_tc = DeformableFeatureAggregation(dev, params, cfg_tc).run(*args_bf)
         torch.cuda.synchronize()
-        np.save(os.path.join(out_dir, f"err{rank}.npy"), np.array((sharded - single).abs().max().item()))
+        ref_tc = single_tc.reshape(-1, 512)[b:e]
+        np.savez(os.path.join(out_dir, f"err{rank}.npz"),
+                 all_reduce=np.array((sharded - single).abs().max().item()),
+                 reduce_scatter=np.array((rs - single.reshape(-1, 512)[b:e]).abs().max().item()),
+                 shard=np.array([b, e]), shape=np.array(rs.shape),
+                 tc_rel=np.array(((rs_tc - ref_tc).abs().max() / ref_tc.abs().max()).item()))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -57,4 +76,9 @@ def test_camera_sharded_layer_matches_single_gpu():
     out_dir = tempfile.mkdtemp()
     mp.start_processes(_worker, args=(2, _free_port(), out_dir), nprocs=2, start_method="spawn")
     for r in range(2):
-        assert float(np.load(os.path.join(out_dir, f"err{r}.npy"))) <= 1e-5
+        g = np.load(os.path.join(out_dir, f"err{r}.npz"))
+        assert float(g["all_reduce"]) <= 1e-5
+        assert float(g["reduce_scatter"]) <= 1e-5
+        assert g["shard"].tolist() == [r * 900, (r + 1) * 900] and g["shape"].tolist() == [900, 512]
+        # same kernels, partial sums added in another order: far inside the bf16 tolerance
+        assert float(g["tc_rel"]) <= 1e-4

@@ -49,11 +49,15 @@ def _worker(rank, world, port, out_dir):
         part = torch.from_numpy(onp.deformable_aggregation(feat, shape, start, uv, logits, cam_range=(cb, ce)))
         summed = cs.reduce_partial_sums(part.clone())
         scattered = cs.reduce_partial_sums(part.clone(), scatter=True)
+        rows = cs.reduce_partial_sums(part.reshape(-1, 256).clone(), scatter=True)
+        rb, re_ = cs.shard_rows(part.shape[0] * part.shape[1])
         grid = cs.make_groups(world, world)
         res = {
             "range": np.array([cb, ce]),
             "allreduce_err": np.array((summed.numpy() - full).__abs__().max()),
             "scatter_err": np.array((scattered.numpy() - full[:, rank * 12:(rank + 1) * 12]).__abs__().max()),
+            "rows": np.array([rb, re_]),
+            "rows_err": np.array((rows.numpy() - full.reshape(-1, 256)[rb:re_]).__abs__().max()),
             "grid": np.array([grid[0], dist.get_world_size(grid[1])]),
         }
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **res)
@@ -70,7 +74,53 @@ def test_camera_sharded_partial_sums_two_ranks():
     for r in (r0, r1):
         assert float(r["allreduce_err"]) <= 1e-5  # global softmax over all 6 cameras
         assert float(r["scatter_err"]) <= 1e-5
+        assert float(r["rows_err"]) <= 1e-5
         assert r["grid"].tolist() == [0, 2]
+    assert r0["rows"].tolist() == [0, 24] and r1["rows"].tolist() == [24, 48]  # whole frames (bs 2)
+
+
+def _grid_worker(rank, world, port, out_dir):
+    """4 ranks as 2 frame groups x 2 camera halves: each rank takes its frame group's frames
+    and its camera half, the partial sums meet by a row reduce-scatter inside the camera group."""
+    import datetime
+    import sys
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, repo)
+    import torch.distributed as dist
+
+    from oracle import dfa_numpy as onp
+    from sparse4d_tt_b200 import camera_shard as cs
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        maps, uv, logits = _case(seed=5, bs=4, A=10)
+        feat, shape, start = onp.pack_feature_maps(maps)
+        full = onp.deformable_aggregation(feat, shape, start, uv, logits).reshape(4, 10, 256)
+        fgroup, cgroup = cs.make_groups(world, 2)
+        frames = slice(2 * fgroup, 2 * fgroup + 2)
+        cb, ce = cs.rank_camera_range(6, cgroup)
+        part = onp.deformable_aggregation(feat[frames], shape, start, uv[frames], logits[frames], cam_range=(cb, ce))
+        rows = cs.reduce_partial_sums(torch.from_numpy(part).reshape(-1, 256).contiguous(), cgroup, scatter=True)
+        rb, re_ = cs.shard_rows(20, cgroup)
+        want = full[frames].reshape(-1, 256)[rb:re_]
+        np.savez(os.path.join(out_dir, f"grid{rank}.npz"), fgroup=np.array(fgroup), cams=np.array([cb, ce]),
+                 rows=np.array([rb, re_]), err=np.array(np.abs(rows.numpy() - want).max()))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_frame_by_camera_grid_four_ranks():
+    out_dir = tempfile.mkdtemp()
+    mp.start_processes(_grid_worker, args=(4, _free_port(), out_dir), nprocs=4, start_method="spawn")
+    got = [np.load(os.path.join(out_dir, f"grid{r}.npz")) for r in range(4)]
+    assert [int(g["fgroup"]) for g in got] == [0, 0, 1, 1]
+    assert [g["cams"].tolist() for g in got] == [[0, 3], [3, 6], [0, 3], [3, 6]]
+    assert [g["rows"].tolist() for g in got] == [[0, 10], [10, 20], [0, 10], [10, 20]]
+    for g in got:
+        assert float(g["err"]) <= 1e-5
 
 
 def test_camera_split_shapes():
