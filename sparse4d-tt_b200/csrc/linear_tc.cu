@@ -182,6 +182,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 // ---- shared pieces of the two kernels ------------------------------------------------------
 
+// First column of the kb-th K step a CTA loads.  Every CTA reads the same weight matrix; with
+// S4D_TC_STAGGER_K each starts its K loop at a different step (blockIdx.x mod kbs), so that the
+// CTAs of a wave do not all fetch the same weight tile from the same L2 lines at once.  The sum
+// over K is the same up to the order of the fp32 additions, which is fixed per tile.
+#ifndef S4D_TC_STAGGER_K
+#define S4D_TC_STAGGER_K 1
+#endif
+__device__ __forceinline__ int k_column(int kb, int kbs) {
+  if (!S4D_TC_STAGGER_K || kbs != 16) return kb * kBK;  // both kernels run K = 256: 16 steps
+  const int k = kb + int(blockIdx.x & 15u);
+  return (k >= 16 ? k - 16 : k) * kBK;
+}
+
 struct Ctl {
   uint64_t* bars;
   uint32_t* tmem_slot;
@@ -343,13 +356,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = kb % kStages;
         if (kb >= kStages && !mbar_wait(empty0 + 8 * s, ((kb / kStages) - 1) & 1, c.abort_flag, p.wait_limit_ns)) break;
         const uint32_t st = smem_u32(smem + s * S::kStage), fb = full0 + 8 * s;
+        const int kx = k_column(kb, kbs);
         mbar_expect_tx(fb, S::kStage);
-        tma_load_2d(st, &map_inst, fb, kb * kBK, int(row0));
-        tma_load_2d(st + kATile, &map_embed, fb, kb * kBK, int(row0));
+        tma_load_2d(st, &map_inst, fb, kx, int(row0));
+        tma_load_2d(st + kATile, &map_embed, fb, kx, int(row0));
 #pragma unroll
         for (int j = 0; j < S::kSplit; ++j)
-          tma_load_2d(st + 2 * kATile + j * S::kNmma * kBK * 4, &map_wfc, fb, kb * kBK, j * S::kNmma);
-        tma_load_2d(st + 2 * kATile + S::kBW, &map_wkps, fb, kb * kBK, 0);
+          tma_load_2d(st + 2 * kATile + j * S::kNmma * kBK * 4, &map_wfc, fb, kx, j * S::kNmma);
+        tma_load_2d(st + 2 * kATile + S::kBW, &map_wkps, fb, kx, 0);
         issued = kb + 1;
       }
       drain_loads(full0, issued);
@@ -429,9 +443,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int s = kb % kStages;
         if (kb >= kStages && !mbar_wait(empty0 + 8 * s, ((kb / kStages) - 1) & 1, c.abort_flag, p.wait_limit_ns)) break;
         const uint32_t st = smem_u32(smem + s * S::kStage), fb = full0 + 8 * s;
+        const int kx = k_column(kb, kbs);
         mbar_expect_tx(fb, S::kStage);
-        tma_load_2d(st, &map_feat, fb, kb * kBK, int(row0));
-        tma_load_2d(st + kATile, &map_w, fb, kb * kBK, 0);
+        tma_load_2d(st, &map_feat, fb, kx, int(row0));
+        tma_load_2d(st + kATile, &map_w, fb, kx, 0);
         issued = kb + 1;
       }
       drain_loads(full0, issued);
