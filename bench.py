@@ -656,6 +656,36 @@ def pack_leg(device, frames=32, iters=10):
     return res
 
 
+def decoder_leg(device, frames, steps, warmup):
+    """The decoder chain around the DFA: a whole single-frame Sparse4D v3 decoder pass (6 DFA
+    layers with the decoupled attention, FFN, LayerNorm, refinement and anchor re-encoding
+    between them, anchors kept on the device from layer to layer) over ``frames`` frames as one
+    CUDA graph (head.HeadGraph), bf16 maps, the dense layers in TF32.  Seeded synthetic
+    parameters (synthetic.make_head_params) and the bench's camera ring."""
+    from sparse4d_tt_b200 import synthetic as syn
+    from sparse4d_tt_b200.head import HeadGraph, Sparse4DHead
+
+    cfg = syn.DFAConfig(bs=frames)
+    head = Sparse4DHead(device, syn.make_head_params(cfg, torch.Generator().manual_seed(600)), MODEL_CONFIG)
+    g = HeadGraph(head, frames, cfg.spatial_shapes)
+    dgen = torch.Generator(device=device).manual_seed(601)
+    g.mc_ms_feat.copy_(torch.randn(g.mc_ms_feat.shape, device=device, generator=dgen, dtype=torch.bfloat16))
+    g.projection_mat.copy_(syn.camera_ring(6, cfg.image_wh)[None].expand(frames, -1, -1, -1))
+    g.image_wh.copy_(torch.tensor(cfg.image_wh, dtype=torch.float32).expand(frames, 6, 2))
+    for _ in range(warmup):
+        g.replay()
+    ms = time_steps(g.replay, steps, lambda: None)
+    out = g.output
+    moved = (out["prediction"][-1][..., :3] - g.anchor[..., :3]).norm(dim=-1).mean().item()
+    return {"workload": f"single-frame Sparse4D v3 decoder pass over {frames} frames: 6 DFA layers + 11 decoupled "
+                        "attentions, 6 FFNs, 12 LayerNorms, 6 refinements and 5 anchor re-encodings; 900 anchors, "
+                        "704x256 bf16 maps; one CUDA graph per pass",
+            "ms_per_pass": ms / steps, "frames_per_s": frames * steps / (ms / 1e3),
+            "dfa_calls_per_s": 6 * frames * steps / (ms / 1e3), "steps": steps,
+            "mean_anchor_move_m": moved,
+            "anchors": "refined on the device by each decoder's refinement and re-encoded for the next DFA layer"}
+
+
 HIGHRES_FRAMES = 16  # global batch of the high-resolution stress case
 
 
@@ -993,11 +1023,12 @@ def run_ours(args):
     if not args.no_highres:
         highres = highres_leg(rank, world, device, pg, min(args.steps, 20), 3)
 
-    bs1 = pack = kps = None
+    bs1 = pack = kps = decoder = None
     if rank == 0 and not args.no_bs1:
         bs1 = bs1_leg(device)
         pack = pack_leg(device)
         kps = kps_leg(device)
+        decoder = decoder_leg(device, args.frames, max(3, args.steps // 4), 2)
     barrier()
 
     if rank == 0:
@@ -1045,6 +1076,7 @@ def run_ours(args):
             "pack": pack,
             "kps": kps,
             "highres": highres,
+            "decoder": decoder,
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()

@@ -7,12 +7,14 @@ Public API:
   output_proj_into, camera_logits_into                      -- operators (ops.py)
   DFAStack, PipelinedDFAStack, capture                      -- CUDA-graph execution (graph.py)
   InstanceBank, project_anchors                             -- temporal instances (instance_bank.py)
+  Sparse4DHead, HeadGraph, preprocess_head_parameters       -- the decoder chain around the DFA (head.py)
 The operators run hand-written sm_100a CUDA kernels from lib/libs4d_dfa.so through the C ABI
 of include/s4d_dfa.h; the library is loaded on first use and its absence raises.
 """
 from . import synthetic  # noqa: F401
 from .dfa import DeformableFeatureAggregation, preprocess_dfa_parameters  # noqa: F401
 from .graph import DFAStack, PipelinedDFAStack, capture  # noqa: F401
+from .head import HeadGraph, Sparse4DHead, preprocess_head_parameters  # noqa: F401
 from .instance_bank import InstanceBank, preprocess_instance_bank_parameters, project_anchors  # noqa: F401
 from .ops import (  # noqa: F401
     deformable_aggregation,

@@ -232,3 +232,60 @@ def make_inputs(
                 fm = fm.to(feature_dtype).float()
             maps.append(fm)
     return DFAInputs(inst, anchor, embed, maps, proj, wh)
+
+
+def head_operation_order(num_decoder: int = 6, num_single_frame: int = 1) -> List[str]:
+    """Operation order of the Sparse4D v3 decoder (``model/sparse4d_head.py``): one single-frame
+    decoder ``deformable, ffn, norm, refine``, then ``temp_gnn, gnn, norm, deformable, ffn, norm,
+    refine`` per temporal decoder."""
+    return (["gnn", "norm", "deformable", "ffn", "norm", "refine"] * num_single_frame
+            + ["temp_gnn", "gnn", "norm", "deformable", "ffn", "norm", "refine"] * (num_decoder - num_single_frame))[2:]
+
+
+def make_head_params(cfg: DFAConfig, gen: torch.Generator, num_cls: int = 10, num_decoder: int = 6,
+                     refine_scale: float = 0.1) -> Dict:
+    """Parameters of a single-frame decoder head in the format of ``head.preprocess_head_parameters``:
+    Xavier-uniform weights, zero biases, unit LayerNorms; the DFA layers from ``make_params``.
+    The refinement's output scale is ``refine_scale`` (a trained head moves boxes by small
+    steps; Xavier-initialised layers at scale 1 would move them by metres per layer); the
+    instance bank's anchors are seeded scene anchors (``make_anchors``) and its features zeros."""
+    C = cfg.embed_dims
+
+    def xavier(out_f, in_f):
+        bound = math.sqrt(6.0 / (in_f + out_f))
+        return torch.rand(out_f, in_f, generator=gen) * (2 * bound) - bound
+
+    def mlp(dims_in, dims, in_loops, out_loops):
+        mods, d_in = [], dims_in
+        for _ in range(out_loops):
+            for _ in range(in_loops):
+                mods += [("linear", xavier(dims, d_in), torch.zeros(dims)), ("relu", None, None)]
+                d_in = dims
+            mods.append(("ln", torch.ones(dims), torch.zeros(dims)))
+        return mods
+
+    order = head_operation_order(num_decoder)
+    layers = []
+    for op in order:
+        if op in ("gnn", "temp_gnn"):
+            layers.append({"in_proj_weight": xavier(3 * 2 * C, 2 * C), "in_proj_bias": torch.zeros(3 * 2 * C),
+                           "out_proj_weight": xavier(2 * C, 2 * C), "out_proj_bias": torch.zeros(2 * C),
+                           "num_heads": cfg.num_groups})
+        elif op == "norm":
+            layers.append({"weight": torch.ones(C), "bias": torch.zeros(C)})
+        elif op == "deformable":
+            layers.append(make_params(cfg, gen))
+        elif op == "ffn":
+            layers.append({"pre_norm": (torch.ones(2 * C), torch.zeros(2 * C)),
+                           "fc1": (xavier(4 * C, 2 * C), torch.zeros(4 * C)), "fc2": (xavier(C, 4 * C), torch.zeros(C)),
+                           "identity_fc": (xavier(C, 2 * C), torch.zeros(C))})
+        else:  # refine
+            layers.append({"layers": mlp(C, C, 2, 2) + [("linear", xavier(11, C), torch.zeros(11)),
+                                                        ("scale", torch.full((11,), refine_scale), None)],
+                           "cls_layers": mlp(C, C, 1, 2) + [("linear", xavier(num_cls, C), torch.zeros(num_cls))],
+                           "quality_layers": mlp(C, C, 1, 2) + [("linear", xavier(2, C), torch.zeros(2))]})
+    encoder = {"pos_fc": mlp(3, 128, 1, 4), "size_fc": mlp(3, 32, 1, 4), "yaw_fc": mlp(2, 32, 1, 4),
+               "vel_fc": mlp(3, 64, 1, 4)}
+    return {"operation_order": order, "layers": layers, "anchor_encoder": encoder,
+            "anchor": make_anchors(1, cfg.num_anchor, gen)[0], "instance_feature": torch.zeros(cfg.num_anchor, C),
+            "fc_before": xavier(2 * C, C), "fc_after": xavier(C, 2 * C), "num_single_frame_decoder": 1}

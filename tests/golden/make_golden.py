@@ -218,6 +218,55 @@ def reference_dummy_kps_inputs(ref, name, batches=(1, 2)):
     print(f"{name}: {sorted(out)} -> {os.path.getsize(path)} bytes")
 
 
+def import_reference_head():
+    """The reference's head twin module ``test/sparse4d_head_pcc.py`` (its ttnn and TT model imports
+    stand in through the same stub as ``import_reference``)."""
+    import_reference()
+    import sparse4d_head_pcc  # noqa: E402
+
+    return sparse4d_head_pcc
+
+
+def head_twin(name, seed=42, bs=1):
+    """The reference's own single-frame head test case (``test/sparse4d_head_pcc.py:530-565``):
+    ``_PTSparse4DHead`` built under ``torch.manual_seed(42)``, maps and projections x0.1, the
+    forward with debug intermediates.  Stores checksums of every parameter (state-dict order) and
+    input, every decoder's prediction whole, the classification and quality of the decoders that
+    return them, and the instance feature after each step."""
+    hp = import_reference_head()
+    torch.manual_seed(seed)
+    head = hp._PTSparse4DHead(embed_dims=256, num_decoder=6, num_single_frame=1, num_anchor=900, num_temp=600,
+                              num_cls=10, num_groups=8, decouple_attn=True).eval()
+    maps = [torch.randn(bs, 6, 256, h, w) * 0.1 for h, w in ((64, 176), (32, 88), (16, 44), (8, 22))]
+    metas = {"projection_mat": torch.randn(bs, 6, 4, 4) * 0.1,
+             "image_wh": torch.tensor([[704.0, 256.0]]).unsqueeze(0).expand(bs, 6, 2).contiguous(),
+             "timestamp": torch.zeros(bs)}
+    with torch.no_grad():
+        out = head(maps, metas, bs=bs, debug=True)
+    d = {"seed": np.array(seed), "bs": np.array(bs), "torch_version": np.array(torch.__version__),
+         "operation_order": np.array(head.operation_order)}
+    d["param_names"] = np.array(list(head.state_dict().keys()))
+    d["param_ck"] = np.stack([fx.checksum(v) for v in head.state_dict().values()])
+    for i, m in enumerate(maps):
+        d[f"ck_map{i}"] = fx.checksum(m)
+    d["ck_projection_mat"] = fx.checksum(metas["projection_mat"])
+    for i, pr in enumerate(out["prediction"]):
+        d[f"prediction{i}"] = pr.numpy()
+    for i, c in enumerate(out["classification"]):
+        if c is not None:
+            d[f"classification{i}"] = c.numpy()
+    for i, q in enumerate(out["quality"]):
+        if q is not None:
+            d[f"quality{i}"] = q.numpy()
+    for k, v in out["debug"].items():
+        if k.startswith("step_") and not k.endswith("_anchor"):
+            d["ck_" + k] = fx.checksum(v)
+    path = os.path.join(HERE, name + ".npz")
+    np.savez_compressed(path, **d)
+    print(f"{name}: {len(d['param_names'])} parameters, {len(out['prediction'])} decoders -> "
+          f"{os.path.getsize(path)} bytes")
+
+
 def instance_bank_projection(name, seed=7, bs=2, num=600):
     """The reference's own InstanceBank._anchor_projection (model/instance_bank.py:322-369, plain
     torch) on seeded cached anchors, ego transforms and time gaps; inputs and outputs stored
@@ -262,6 +311,7 @@ def main():
         "refdummy_bs1": lambda: reference_dummy(ref, "refdummy_bs1", 1),
         "refdummy_bs2": lambda: reference_dummy(ref, "refdummy_bs2", 2),
         "refdummy_kps_inputs": lambda: reference_dummy_kps_inputs(ref, "refdummy_kps_inputs"),
+        "head_twin_s42": lambda: head_twin("head_twin_s42"),
         "instance_bank_projection": lambda: instance_bank_projection("instance_bank_projection"),
     }
     names = sys.argv[1:] or list(jobs)
