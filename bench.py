@@ -845,7 +845,7 @@ def _cpu_model():
     return "unknown"
 
 
-GATHER_SOURCES = ("dfa_gather.cu", "kps_math.cuh", "common.cuh", "params.cuh")
+GATHER_SOURCES = ("dfa_gather.cu", "kps_math.cuh", "common.cuh")
 
 
 def gather_source_sha16():

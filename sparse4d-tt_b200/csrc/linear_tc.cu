@@ -229,10 +229,11 @@ __device__ __forceinline__ void stage_row(unsigned char* box, int r, const float
         make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3]);
 }
 
-// The epilogue warp `q` streams accumulator columns [0, ncols) of its 32 rows to `map` (a
-// 32x32-box, 128-byte swizzle store map) through two 4 KiB staging boxes at `stage`,
-// adding bias[col] and, when res != null, res[row * res_ld + col].
-__device__ __forceinline__ void store_columns(uint32_t tmem, int q, int lane, int64_t tile_row0, int ncols,
+// The epilogue warp `q` streams accumulator columns [0, ncols) of its 32 rows to columns
+// [col0, col0 + ncols) of `map` (a 32x32-box, 128-byte swizzle store map) through two 4 KiB
+// staging boxes at `stage`, adding bias[col0 + col] and, when res != null,
+// res[row * res_ld + col0 + col].
+__device__ __forceinline__ void store_columns(uint32_t tmem, int q, int lane, int64_t tile_row0, int col0, int ncols,
                                               const CUtensorMap* map, unsigned char* stage, const float* bias,
                                               const float* res, int64_t res_ld, int64_t rows) {
   const int64_t row = tile_row0 + q * 32 + lane;
@@ -245,12 +246,12 @@ __device__ __forceinline__ void store_columns(uint32_t tmem, int q, int lane, in
     if (bias != nullptr) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float4 b = __ldg(reinterpret_cast<const float4*>(bias + c * 32) + i);
+        const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col0 + c * 32) + i);
         f[4 * i] += b.x, f[4 * i + 1] += b.y, f[4 * i + 2] += b.z, f[4 * i + 3] += b.w;
       }
     }
     if (res != nullptr && row < rows) {
-      const float4* r4 = reinterpret_cast<const float4*>(res + row * res_ld + c * 32);
+      const float4* r4 = reinterpret_cast<const float4*>(res + row * res_ld + col0 + c * 32);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float4 r = ldg_nc_f4(r4 + i);
@@ -264,7 +265,7 @@ __device__ __forceinline__ void store_columns(uint32_t tmem, int q, int lane, in
     fence_proxy_async();
     __syncwarp();
     if (lane == 0) {
-      tma_store_2d(map, smem_u32(box), c * 32, int(tile_row0 + q * 32));
+      tma_store_2d(map, smem_u32(box), col0 + c * 32, int(tile_row0 + q * 32));
       bulk_commit();
     }
   }
@@ -327,7 +328,8 @@ struct Wfc {
   static constexpr int kBW = NW * kBK * 4;
   static constexpr int kBL = kNL * kBK * 4;
   static constexpr int kStage = 2 * kATile + kBW + kBL;  // inst, embed, W_fc, W_kps
-  static constexpr uint32_t kCols = 512;
+  // tensor-memory columns: the logits and the learnable columns, rounded up to a power of 2
+  static constexpr uint32_t kCols = NW + kNL <= 64 ? 64 : NW + kNL <= 128 ? 128 : NW + kNL <= 256 ? 256 : 512;
   static constexpr size_t kSmem = smem_bytes(kStage);
   static_assert(NW % 32 == 0 && kNmma % 16 == 0 && kNmma <= 256 && NW + kNL <= 512, "logit columns");
   static_assert(kBW % 512 == 0 && kStage % 1024 == 0 && (kNmma * kBK * 4) % 512 == 0, "swizzle alignment");
@@ -347,6 +349,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kbs = p.k / kBK;
   const int64_t row0 = int64_t(blockIdx.x) * kBM;
+  // Column group: logits [col0, col0 + NW); the learnable columns ride with group 0.
+  const int col0 = int(blockIdx.y) * NW;
+  const bool learn = blockIdx.y == 0;
   const uint32_t tmem = prologue(c, S::kCols, 0);
 
   if (warp == 0) {
@@ -357,13 +362,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (kb >= kStages && !mbar_wait(empty0 + 8 * s, ((kb / kStages) - 1) & 1, c.abort_flag, p.wait_limit_ns)) break;
         const uint32_t st = smem_u32(smem + s * S::kStage), fb = full0 + 8 * s;
         const int kx = k_column(kb, kbs);
-        mbar_expect_tx(fb, S::kStage);
+        mbar_expect_tx(fb, learn ? S::kStage : S::kStage - S::kBL);
         tma_load_2d(st, &map_inst, fb, kx, int(row0));
         tma_load_2d(st + kATile, &map_embed, fb, kx, int(row0));
 #pragma unroll
         for (int j = 0; j < S::kSplit; ++j)
-          tma_load_2d(st + 2 * kATile + j * S::kNmma * kBK * 4, &map_wfc, fb, kx, j * S::kNmma);
-        tma_load_2d(st + 2 * kATile + S::kBW, &map_wkps, fb, kx, 0);
+          tma_load_2d(st + 2 * kATile + j * S::kNmma * kBK * 4, &map_wfc, fb, kx, col0 + j * S::kNmma);
+        if (learn) tma_load_2d(st + 2 * kATile + S::kBW, &map_wkps, fb, kx, 0);
         issued = kb + 1;
       }
       drain_loads(full0, issued);
@@ -386,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_tf32(tmem + j * S::kNmma, a_inst + 2 * k, b, tf32_idesc(S::kNmma), acc);
             mma_tf32(tmem + j * S::kNmma, a_emb + 2 * k, b, tf32_idesc(S::kNmma), 1);
           }
-          mma_tf32(tmem + NW, a_inst + 2 * k, b_kps + 2 * k, tf32_idesc(S::kNL), acc);
+          if (learn) mma_tf32(tmem + NW, a_inst + 2 * k, b_kps + 2 * k, tf32_idesc(S::kNL), acc);
         }
         mma_commit(empty0 + 8 * s);
       }
@@ -397,11 +402,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Epilogue: logits through TMA stores, learnable columns (not 16-byte rows) by plain stores.
     const int q = warp & 3;
     if (wait_accumulator(c, acc_bar, p.wait_limit_ns)) {
-      store_columns(tmem, q, lane, row0, NW, &map_logits, smem + q * 2 * kStageChunk, nullptr, nullptr, 0, p.rows);
+      store_columns(tmem, q, lane, row0, col0, NW, &map_logits, smem + q * 2 * kStageChunk, nullptr, nullptr, 0,
+                    p.rows);
       uint32_t v[32];
-      tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(NW), v);
+      if (learn) tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(NW), v);
       const int64_t row = row0 + q * 32 + lane;
-      if (row < p.rows && p.n_learn > 0) {
+      if (learn && row < p.rows && p.n_learn > 0) {
         float* dst = p.learnable + row * p.n_learn;
 #pragma unroll
         for (int i = 0; i < 32; ++i)
@@ -414,26 +420,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---- output_proj ----------------------------------------------------------------------------
 
+// A CTA computes output columns [col0, col0 + NO) of a 128-row tile (NO = 256: all of them;
+// fewer when a launch has few row tiles, so that more SMs share it).
+template <int NO>
 struct Oproj {
-  static constexpr int kN = 256;
+  static constexpr int kK = 256;  // input features (embed_dims)
+  static constexpr int kN = NO;
   static constexpr int kStage = kATile + kN * kBK * 4;  // feats tile, W_o tile
-  static constexpr uint32_t kCols = 256;
+  static constexpr uint32_t kCols = NO <= 32 ? 32 : NO <= 64 ? 64 : NO <= 128 ? 128 : 256;
   static constexpr size_t kSmem = smem_bytes(kStage);
-  static_assert(kStage % 1024 == 0, "swizzle alignment");
+  static_assert(NO % 32 == 0 && NO <= 256 && kStage % 1024 == 0, "swizzle alignment");
   static_assert(4 * 2 * kStageChunk <= kStages * kStage, "epilogue staging fits in the stages");
 };
 
+template <int NO>
 __global__ void __launch_bounds__(kThreads, 2)
     output_proj_kernel(const __grid_constant__ CUtensorMap map_feat, const __grid_constant__ CUtensorMap map_w,
                        const __grid_constant__ CUtensorMap map_out, const OprojParams p) {
-  using S = Oproj;
+  using S = Oproj<NO>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
   const Ctl c = carve<S::kStage>(smem);
   const uint32_t full0 = smem_u32(c.bars), empty0 = full0 + 16 * kStages, acc_bar = full0 + 24 * kStages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kbs = S::kN / kBK;
+  const int kbs = S::kK / kBK;
   const int64_t row0 = int64_t(blockIdx.x) * kBM;
+  const int col0 = int(blockIdx.y) * NO;
   const uint32_t tmem = prologue(c, S::kCols, 0);
 
   if (warp == 0) {
@@ -446,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int kx = k_column(kb, kbs);
         mbar_expect_tx(fb, S::kStage);
         tma_load_2d(st, &map_feat, fb, kx, int(row0));
-        tma_load_2d(st + kATile, &map_w, fb, kx, 0);
+        tma_load_2d(st + kATile, &map_w, fb, kx, col0);
         issued = kb + 1;
       }
       drain_loads(full0, issued);
@@ -469,30 +481,32 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else {
     const int q = warp & 3;
     if (p.res_mode == S4D_RESIDUAL_CAT) {
-      // The residual half of the output is a plain copy: done while the tensor cores run, 8
-      // rows (16 float4 per lane) in flight per step.
+      // The residual half of the output (this CTA's columns of it) is a plain copy: done while
+      // the tensor cores run, 8 float4 per lane in flight per step, consecutive lanes on
+      // consecutive 16-byte pieces of a row.
+      constexpr int kF4 = NO / 4;          // float4 per row of this CTA's columns
+      constexpr int kTotal = 32 * kF4;     // ... over the warp's 32 rows
       const int64_t r_begin = row0 + q * 32;
-      const int64_t r_end = min(r_begin + 32, p.rows);
-      for (int64_t r = r_begin; r < r_end; r += 8) {
-        float4 buf[8][2];
+      for (int base = 0; base < kTotal; base += 8 * 32) {
+        float4 buf[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          if (r + i < r_end) {
-            const float4* src = reinterpret_cast<const float4*>(p.res + (r + i) * p.res_ld);
-            buf[i][0] = ldg_nc_f4(src + lane);
-            buf[i][1] = ldg_nc_f4(src + 32 + lane);
-          }
+        for (int i = 0; i < 8; ++i) {
+          const int idx = base + i * 32 + lane;
+          const int64_t r = r_begin + idx / kF4;
+          if (idx < kTotal && r < p.rows)
+            buf[i] = ldg_nc_f4(reinterpret_cast<const float4*>(p.res + r * p.res_ld + col0) + idx % kF4);
+        }
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          if (r + i < r_end) {
-            float4* dst = reinterpret_cast<float4*>(p.out + (r + i) * p.out_ld + S::kN);
-            dst[lane] = buf[i][0];
-            dst[32 + lane] = buf[i][1];
-          }
+        for (int i = 0; i < 8; ++i) {
+          const int idx = base + i * 32 + lane;
+          const int64_t r = r_begin + idx / kF4;
+          if (idx < kTotal && r < p.rows)
+            reinterpret_cast<float4*>(p.out + r * p.out_ld + S::kK + col0)[idx % kF4] = buf[i];
+        }
       }
     }
     if (wait_accumulator(c, acc_bar, p.wait_limit_ns))
-      store_columns(tmem, q, lane, row0, S::kN, &map_out, smem + q * 2 * kStageChunk, p.bias,
+      store_columns(tmem, q, lane, row0, col0, NO, &map_out, smem + q * 2 * kStageChunk, p.bias,
                     p.res_mode == S4D_RESIDUAL_ADD ? p.res : nullptr, p.res_ld, p.rows);
   }
   epilogue_teardown(c, tmem, S::kCols, p.error_flag);
@@ -545,6 +559,63 @@ int set_smem(K kernel, size_t bytes, const char* what) {
   return cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)), what);
 }
 
+// Column groups for launches of few row tiles (1 = always whole rows per CTA).
+#ifndef S4D_TC_COLUMN_GROUPS
+#define S4D_TC_COLUMN_GROUPS 1
+#endif
+
+// SMs of the current device (148 on B200 if the query fails).
+int sm_count() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      sms <= 0) {
+    cudaGetLastError();
+    return 148;
+  }
+  return sms;
+}
+
+// Column groups per row tile of a launch with `tiles` row tiles: the most of `choices` (widest
+// first) that still fits the launch in one wave on the SMs, so that a launch of few rows (bs = 1:
+// 8 tiles) spreads over many SMs; launches of more tiles than SMs keep whole rows per CTA.
+int column_groups(int64_t tiles, std::initializer_list<int> choices) {
+  const int64_t sms = sm_count();
+  int best = 1;
+  for (int g : choices)
+    if (tiles * g <= sms && g > best) best = g;
+  return best;
+}
+
+template <int NW>
+int launch_weights_fc_cols(const WfcParams& p, cudaStream_t stream, int groups) {
+  using S = Wfc<NW>;
+  CUtensorMap mi, me, mw, mk, mo;
+  int st = make_map(&mi, p.inst, p.rows, p.k, p.inst_ld, kBM);
+  if (st == S4D_OK) st = make_map(&me, p.embed, p.rows, p.k, p.embed_ld, kBM);
+  if (st == S4D_OK) st = make_map(&mw, p.w_fc, p.n_logits, p.k, p.k, S::kNmma);
+  if (st == S4D_OK) st = make_map(&mk, p.w_kps, p.n_learn > 0 ? p.n_learn : 1, p.k, p.k, S::kNL);
+  if (st == S4D_OK) st = make_map(&mo, p.logits, p.rows, p.n_logits, p.n_logits, 32, true);
+  if (st == S4D_OK) st = set_smem(weights_fc_kernel<NW>, S::kSmem, "cudaFuncSetAttribute(weights_fc_kernel)");
+  if (st != S4D_OK) return st;
+  const dim3 grid(unsigned((p.rows + kBM - 1) / kBM), unsigned(groups));
+  weights_fc_kernel<NW><<<grid, kThreads, S::kSmem, stream>>>(mi, me, mw, mk, mo, p);
+  return cuda_check(cudaGetLastError(), "weights_fc_kernel launch");
+}
+
+template <int NO>
+int launch_output_proj_cols(const OprojParams& p, cudaStream_t stream, int groups) {
+  using S = Oproj<NO>;
+  CUtensorMap mf, mw, mo;
+  int st = make_map(&mf, p.feat, p.rows, p.k, p.k, kBM);
+  if (st == S4D_OK) st = make_map(&mw, p.w, p.k, p.k, p.k, NO);
+  if (st == S4D_OK) st = make_map(&mo, p.out, p.rows, p.k, p.out_ld, 32, true);
+  if (st == S4D_OK) st = set_smem(output_proj_kernel<NO>, S::kSmem, "cudaFuncSetAttribute(output_proj_kernel)");
+  if (st != S4D_OK) return st;
+  const dim3 grid(unsigned((p.rows + kBM - 1) / kBM), unsigned(groups));
+  output_proj_kernel<NO><<<grid, kThreads, S::kSmem, stream>>>(mf, mw, mo, p);
+  return cuda_check(cudaGetLastError(), "output_proj_kernel launch");
+}
+
 }  // namespace
 
 int launch_weights_fc(const WfcParams& p, cudaStream_t stream) {
@@ -552,31 +623,20 @@ int launch_weights_fc(const WfcParams& p, cudaStream_t stream) {
   if (p.n_logits != 416 || p.k != 256 || p.n_learn > 32)
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "weights_fc: implemented for 416 logit columns, embed_dims 256, "
                                            "<= 32 learnable columns");
-  using S = Wfc<416>;
-  CUtensorMap mi, me, mw, mk, mo;
-  int st = make_map(&mi, p.inst, p.rows, p.k, p.inst_ld, kBM);
-  if (st == S4D_OK) st = make_map(&me, p.embed, p.rows, p.k, p.embed_ld, kBM);
-  if (st == S4D_OK) st = make_map(&mw, p.w_fc, p.n_logits, p.k, p.k, S::kNmma);
-  if (st == S4D_OK) st = make_map(&mk, p.w_kps, p.n_learn > 0 ? p.n_learn : 1, p.k, p.k, S::kNL);
-  if (st == S4D_OK) st = make_map(&mo, p.logits, p.rows, p.n_logits, p.n_logits, 32, true);
-  if (st == S4D_OK) st = set_smem(weights_fc_kernel<416>, S::kSmem, "cudaFuncSetAttribute(weights_fc_kernel)");
-  if (st != S4D_OK) return st;
-  weights_fc_kernel<416><<<unsigned((p.rows + kBM - 1) / kBM), kThreads, S::kSmem, stream>>>(mi, me, mw, mk, mo, p);
-  return cuda_check(cudaGetLastError(), "weights_fc_kernel launch");
+  // 416 logit columns in 1 or 13 groups (the epilogue stores 32-column boxes: 416 = 13 x 32)
+  const int groups = S4D_TC_COLUMN_GROUPS ? column_groups((p.rows + kBM - 1) / kBM, {13}) : 1;
+  if (groups == 13) return launch_weights_fc_cols<32>(p, stream, 13);
+  return launch_weights_fc_cols<416>(p, stream, 1);
 }
 
 int launch_output_proj(const OprojParams& p, cudaStream_t stream) {
   if (p.rows <= 0) return S4D_OK;
   if (p.k != 256) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "output_proj: implemented for embed_dims 256");
-  using S = Oproj;
-  CUtensorMap mf, mw, mo;
-  int st = make_map(&mf, p.feat, p.rows, p.k, p.k, kBM);
-  if (st == S4D_OK) st = make_map(&mw, p.w, S::kN, p.k, p.k, S::kN);
-  if (st == S4D_OK) st = make_map(&mo, p.out, p.rows, S::kN, p.out_ld, 32, true);
-  if (st == S4D_OK) st = set_smem(output_proj_kernel, S::kSmem, "cudaFuncSetAttribute(output_proj_kernel)");
-  if (st != S4D_OK) return st;
-  output_proj_kernel<<<unsigned((p.rows + kBM - 1) / kBM), kThreads, S::kSmem, stream>>>(mf, mw, mo, p);
-  return cuda_check(cudaGetLastError(), "output_proj_kernel launch");
+  // 256 output columns in 1, 2 (128 each) or 8 (32 each) groups
+  const int groups = S4D_TC_COLUMN_GROUPS ? column_groups((p.rows + kBM - 1) / kBM, {2, 8}) : 1;
+  if (groups == 8) return launch_output_proj_cols<32>(p, stream, 8);
+  if (groups == 2) return launch_output_proj_cols<128>(p, stream, 2);
+  return launch_output_proj_cols<256>(p, stream, 1);
 }
 
 }  // namespace s4d

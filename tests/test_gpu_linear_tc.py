@@ -95,7 +95,7 @@ def test_weights_fc_learnable_widths(cuda_device, m):
 
 
 @pytest.mark.parametrize("mode", ["cat", "add", "none"])
-@pytest.mark.parametrize("rows", [1, 129, 900, 28800])
+@pytest.mark.parametrize("rows", [1, 129, 900, 7200, 28800])
 def test_output_proj_residual_modes(cuda_device, mode, rows):
     dev = torch.device("cuda:0")
     gen = torch.Generator().manual_seed(rows + len(mode))
