@@ -99,7 +99,7 @@ def workload_config(frames, layers, world):
 # ---------------------------------------------------------------------------------------------
 class ClockSampler:
     """SM clock and clock-event reasons sampled during the timed region: NVML polled every
-    20 ms from a thread (read-only queries), or nvidia-smi at 200 ms when NVML is missing."""
+    2 ms from a thread (read-only queries), or nvidia-smi at 200 ms when NVML is missing."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -152,7 +152,7 @@ class ClockSampler:
                                      pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), int(reasons(h))))
             except Exception:
                 pass
-            self.stop_flag.wait(0.02)
+            self.stop_flag.wait(0.002)
 
     def stop(self):
         if self.nvml is not None:
@@ -163,7 +163,7 @@ class ClockSampler:
             found = sorted({n for _, _, r in self.samples for n, bit in self.REASON_BITS.items() if r & bit})
             return {"sm_mhz": statistics.median(s for s, _, _ in self.samples),
                     "sm_max_mhz": max(m for _, m, _ in self.samples), "reasons": found,
-                    "samples": len(self.samples), "source": "nvml, 20 ms"}
+                    "samples": len(self.samples), "source": "nvml, polled every 2 ms"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()

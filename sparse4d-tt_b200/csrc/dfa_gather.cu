@@ -775,6 +775,22 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
   const int b = (int)p.div_anchor.div((uint32_t)anchor_lin);  // anchors < 2^31
   const int gch = lane / (D / 8);  // group of this lane's output channels
 
+  const float* wrow = p.weights + anchor_lin * (MODE == 0 ? NW : LPG);
+  const float* wcam = MODE == 0 ? nullptr : p.weights_cam + (int64_t)b * NW;
+  const float* ec_tab = MODE == 1 ? p.cam_ws + (int64_t)b * (NC + 1) * LPG : nullptr;
+  float* ea = s_ea + (MODE == 1 ? warp * LPG : 0);
+  // SPLIT (few anchors, latency-bound): the softmax's loads are issued before the keypoint work,
+  // so their DRAM latency overlaps that of the anchor rows instead of following it
+  constexpr bool kEarly = SPLIT && MODE == 1;
+  float x[LPG / 32], ecs[LPG / 32];
+  if (kEarly) {
+#pragma unroll
+    for (int k = 0; k < LPG / 32; ++k) {
+      x[k] = __ldg(wrow + lane + 32 * k);
+      ecs[k] = __ldg(ec_tab + NW + lane + 32 * k);
+    }
+  }
+
   if (KPS) {  // the anchor's keypoints (kps_project's arithmetic)
     const float* a = p.kps_anchor + anchor_lin * p.kps_anchor_dim;
     const int nf = p.kps_num_fix, nlc = (NP - nf) * 3;
@@ -797,18 +813,15 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
     }
     __syncwarp();
   }
-  const float* wrow = p.weights + anchor_lin * (MODE == 0 ? NW : LPG);
-  const float* wcam = MODE == 0 ? nullptr : p.weights_cam + (int64_t)b * NW;
-  const float* ec_tab = MODE == 1 ? p.cam_ws + (int64_t)b * (NC + 1) * LPG : nullptr;
-  float* ea = s_ea + (MODE == 1 ? warp * LPG : 0);
 
   // ---- 1. softmax statistics of group lane % G ----------------------------------------------
   float m_l = -INFINITY, s_l = 0.0f;
   bool exact = MODE != 1;
   if (MODE == 1) {
-    float x[LPG / 32];
+    if (!kEarly) {
 #pragma unroll
-    for (int k = 0; k < LPG / 32; ++k) x[k] = __ldg(wrow + lane + 32 * k);
+      for (int k = 0; k < LPG / 32; ++k) x[k] = __ldg(wrow + lane + 32 * k);
+    }
 #pragma unroll
     for (int k = 0; k < LPG / 32; ++k) m_l = fmaxf(m_l, x[k]);
 #pragma unroll
@@ -818,7 +831,7 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
     for (int k = 0; k < LPG / 32; ++k) {
       const float e = ex2_approx(fmaf(x[k], kLog2e, -ml));
       ea[lane + 32 * k] = e;
-      s_l = fmaf(e, __ldg(ec_tab + NW + lane + 32 * k), s_l);
+      s_l = fmaf(e, kEarly ? ecs[k] : __ldg(ec_tab + NW + lane + 32 * k), s_l);
     }
 #pragma unroll
     for (int o = G; o < 32; o <<= 1) s_l += __shfl_xor_sync(0xffffffffu, s_l, o);
