@@ -700,7 +700,10 @@ def highres_leg(rank, world, device, pg, steps, warmup):
       two ranks of a camera group take the same 16 / (N / 2) frames, each samples 3 of the 6
       cameras with the softmax over all 6, the fp32 partial sums meet by an NCCL
       reduce-scatter over the flattened (frame, anchor) rows, and each rank projects its half
-      (launched eagerly).  Rank 0 checks its shard against the same layer on one GPU.
+      (launched eagerly).  Rank 0 checks its shard against the same layer on one GPU;
+    * camera-sharded p2p (N >= 2): the same grid and rows with no collective kernel: each
+      rank's output_proj reads the other GPU's partial sums over NVLink after a bounded flag
+      exchange and adds them in its accumulator.
 
     Every rank runs every step; the times are device times, max over ranks."""
     import torch.distributed as dist
@@ -749,37 +752,54 @@ def highres_leg(rank, world, device, pg, steps, warmup):
     if world >= 2 and world % 2 == 0:
         fgroup, cgroup = cs.make_groups(world, 2)
         fpg = HIGHRES_FRAMES // (world // 2)
-        mc = dict(MODEL_CONFIG, CAMERA_REDUCE="reduce_scatter")
-        w = Workload(fpg, 1, device, seed=4000 + fgroup, cfg=syn.config_highres(fpg, 1800), mesh_device=cgroup,
-                     model_config=mc)
-        for _ in range(warmup):
-            w.step()
-        ms = max_ms(time_steps(w.step, steps, barrier))
-        # parity: this rank's shard against the same layer on this GPU alone
-        out = w.step()
-        b, e = w.mods[0].shard
-        single = DeformableFeatureAggregation(device, w.params[0], MODEL_CONFIG).run(
-            w.inst0, w.anchors[0], w.embeds[0], w.packed, w.proj, w.wh, w.cfg.spatial_shapes, fpg, 1800)
-        ref = single.reshape(-1, single.shape[-1])[b:e].double()
-        got = out.double()
-        err = float((got - ref).abs().max())
-        pcc = float(torch.corrcoef(torch.stack([got.flatten(), ref.flatten()]))[0, 1])
-        stats = torch.tensor([err, -pcc], device=device)
-        if pg is not None:
-            pg.all_reduce(stats, op=pg.ReduceOp.MAX)
         rows = fpg * 1800
-        res["camera_sharded"] = {
-            "grid": f"{world // 2} frame groups x 2 camera halves (3 cameras per rank)", "frames_per_group": fpg,
-            "value": fpg * (world // 2) * steps / (ms / 1e3), "unit": UNIT, "ms_per_step": ms / steps,
-            "collective": "reduce_scatter", "collective_group_size": dist.get_world_size(cgroup),
-            "collective_bytes_per_rank": rows * 256 * 4,
-            "launch": "eager (DeformableFeatureAggregation.run per step)",
-            "parity": {"max_abs_err": float(stats[0]), "pcc_min": -float(stats[1]),
-                       "against": "the same layer on one GPU (all 6 cameras), each rank's reduce-scattered rows; "
-                                  "max over ranks"},
+        modes = {
+            "camera_sharded": ("reduce_scatter", {
+                "collective": "reduce_scatter",
+                "combine": "NCCL reduce-scatter of the fp32 partial sums over the flattened (frame, anchor) rows, "
+                           "then output_proj on this rank's rows"}),
+            "camera_sharded_p2p": ("p2p", {
+                "collective": None,
+                "combine": "no collective kernel: a bounded flag exchange over NVLink, then output_proj reads this "
+                           "rank's rows of its own partial sums and of the other GPU's (over NVLink, CUDA IPC "
+                           "mapping) and adds them in the tensor-core accumulator (s4d_dfa_output_proj_sum)"}),
         }
-        del w, single
-        torch.cuda.empty_cache()
+        for key, (reduce, extra) in modes.items():
+            mc = dict(MODEL_CONFIG, CAMERA_REDUCE=reduce)
+            w = Workload(fpg, 1, device, seed=4000 + fgroup, cfg=syn.config_highres(fpg, 1800), mesh_device=cgroup,
+                         model_config=mc)
+            for _ in range(warmup):
+                w.step()
+            ms = max_ms(time_steps(w.step, steps, barrier))
+            # parity: this rank's shard against the same layer on this GPU alone
+            out = w.step()
+            b, e = w.mods[0].shard
+            single = DeformableFeatureAggregation(device, w.params[0], MODEL_CONFIG).run(
+                w.inst0, w.anchors[0], w.embeds[0], w.packed, w.proj, w.wh, w.cfg.spatial_shapes, fpg, 1800)
+            ref = single.reshape(-1, single.shape[-1])[b:e].double()
+            got = out.double()
+            err = float((got - ref).abs().max())
+            pcc = float(torch.corrcoef(torch.stack([got.flatten(), ref.flatten()]))[0, 1])
+            peer = w.mods[0]._peer
+            flag = 0 if peer is None else int(peer.error_flag.item())
+            stats = torch.tensor([err, -pcc, flag], device=device)
+            if pg is not None:
+                pg.all_reduce(stats, op=pg.ReduceOp.MAX)
+            res[key] = {
+                "grid": f"{world // 2} frame groups x 2 camera halves (3 cameras per rank)", "frames_per_group": fpg,
+                "value": fpg * (world // 2) * steps / (ms / 1e3), "unit": UNIT, "ms_per_step": ms / steps,
+                **extra, "group_size": dist.get_world_size(cgroup),
+                "bytes_to_peer_per_rank": rows // 2 * 256 * 4,
+                "launch": "eager (DeformableFeatureAggregation.run per step)",
+                "parity": {"max_abs_err": float(stats[0]), "pcc_min": -float(stats[1]),
+                           "against": "the same layer on one GPU (all 6 cameras), each rank's rows of the output; "
+                                      "max over ranks"},
+            }
+            if peer is not None:
+                res[key]["peer_timeout_flag"] = int(stats[2])
+                peer.close()
+            del w, single
+            torch.cuda.empty_cache()
     return res
 
 

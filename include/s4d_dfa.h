@@ -67,9 +67,11 @@ enum { S4D_LAYOUT_CAM_MAJOR = 0, S4D_LAYOUT_PT_MAJOR = 1, S4D_LAYOUT_GRID = 2 };
 enum {
   S4D_FLAG_BAD_LEVEL = 1,   /* a (camera, level) spatial_shape / scale_start_index entry lies
                                outside mc_ms_feat; its samples were skipped */
-  S4D_FLAG_WAIT_TIMEOUT = 2 /* a tensor-core kernel gave up waiting on one of its own pipeline
+  S4D_FLAG_WAIT_TIMEOUT = 2, /* a tensor-core kernel gave up waiting on one of its own pipeline
                                barriers (after 2 s, or the limit set by s4d_set_tc_wait_limit_ns);
                                its outputs were not written.  Never expected at the default limit. */
+  S4D_FLAG_PEER_TIMEOUT = 4  /* s4d_peer_signal_wait gave up waiting for a peer's epoch; what the
+                               launches after it read from that peer is not that epoch's data */
 };
 
 /* Layouts of the per-level maps s4d_pack_feature_maps reads. */
@@ -410,6 +412,48 @@ S4D_API size_t s4d_dfa_camera_workspace_bytes(int64_t bs, int64_t num_cams, int6
 S4D_API int s4d_dfa_output_proj(const float* features, int64_t rows, const float* weight, const float* bias,
                                 const float* instance_feature, int64_t instance_ld, int residual_mode, float* out,
                                 int64_t out_ld, int64_t embed_dims, int32_t* error_flag, void* stream);
+
+/* output_proj of the sum of two partial-feature sources (the two camera halves of a camera-
+ * sharded layer), rows row0 .. row0 + rows - 1 of each:
+ *   out[:, :C] = (features + features2)[row0 : row0 + rows] . weight^T + bias  (+ residual)
+ * Both sources are [feature_rows, C] contiguous; features2 may be a peer GPU's buffer mapped by
+ * s4d_ipc_open (read over NVLink by the kernel's tensor-memory-access loads).  The sum is formed
+ * in the tensor-core accumulator, never in memory.  instance_feature (ADD / CAT), out and the
+ * residual modes are those of s4d_dfa_output_proj, for the `rows` output rows.  Replaces the
+ * mesh all-reduce of the partial sums plus output_proj
+ * (model/deformable_feature_aggregation.py:925-950). */
+S4D_API int s4d_dfa_output_proj_sum(const float* features, const float* features2, int64_t feature_rows,
+                                    int64_t row0, int64_t rows, const float* weight, const float* bias,
+                                    const float* instance_feature, int64_t instance_ld, int residual_mode,
+                                    float* out, int64_t out_ld, int64_t embed_dims, int32_t* error_flag,
+                                    void* stream);
+
+/*
+ * Peer memory between the GPUs of a camera group (one process per GPU).  No counterpart in the
+ * reference, whose mesh all-reduce hides the transfer (ttnn.all_reduce).
+ *
+ * s4d_ipc_handle_bytes   size of the opaque handle s4d_ipc_export writes (64).
+ * s4d_ipc_export         handle of the cudaMalloc allocation holding the device pointer `ptr`,
+ *                        and the byte offset of `ptr` in it.  Host-only.
+ * s4d_ipc_open           maps a handle exported by ANOTHER process into this one; *base is the
+ *                        allocation's base (add the exporter's offset).  Host-only.
+ * s4d_ipc_close          unmaps a base returned by s4d_ipc_open.
+ * s4d_peer_signal_wait   one launch: publishes `epoch` in slot `rank` of every peer's slot
+ *                        array (peer_slots[r], a mapped device pointer; entry `rank` unused) and
+ *                        waits until every peer r has published an epoch >= `epoch` (modulo
+ *                        2^32) in own_slots[r].  Work of earlier launches on `stream` is visible
+ *                        to the peers' later launches; the peers' earlier work is visible to
+ *                        this stream's later launches.  The wait gives up after limit_ns, ORs
+ *                        S4D_FLAG_PEER_TIMEOUT into error_flag and returns.  1 <= world <= 8.
+ *                        Every rank must call it with the same epoch sequence; the ranks must be
+ *                        on different GPUs (waiting launches on one GPU may never run together).
+ */
+S4D_API size_t s4d_ipc_handle_bytes(void);
+S4D_API int s4d_ipc_export(const void* ptr, void* handle, uint64_t* offset);
+S4D_API int s4d_ipc_open(const void* handle, void** base);
+S4D_API int s4d_ipc_close(void* base);
+S4D_API int s4d_peer_signal_wait(uint32_t* own_slots, uint32_t* const* peer_slots, int rank, int world,
+                                 uint32_t epoch, uint64_t limit_ns, int32_t* error_flag, void* stream);
 
 #ifdef __cplusplus
 }

@@ -28,6 +28,7 @@ S4D_LAYOUT_GRID = 2
 
 S4D_FLAG_BAD_LEVEL = 1
 S4D_FLAG_WAIT_TIMEOUT = 2
+S4D_FLAG_PEER_TIMEOUT = 4
 
 S4D_MAPS_NCHW = 0
 S4D_MAPS_NHWC = 1
@@ -69,6 +70,12 @@ SIGNATURES = {
     "s4d_instance_bank_cache": (_int, [_p, _p, _p, _p, C.c_float, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p]),
     "s4d_instance_bank_update": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
     "s4d_dfa_output_proj": (_int, [_p, _i64, _p, _p, _p, _i64, _int, _p, _i64, _i64, _p, _p]),
+    "s4d_dfa_output_proj_sum": (_int, [_p, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _int, _p, _i64, _i64, _p, _p]),
+    "s4d_ipc_handle_bytes": (_sz, []),
+    "s4d_ipc_export": (_int, [_p, _p, C.POINTER(C.c_uint64)]),
+    "s4d_ipc_open": (_int, [_p, C.POINTER(C.c_void_p)]),
+    "s4d_ipc_close": (_int, [_p]),
+    "s4d_peer_signal_wait": (_int, [_p, _p, _int, _int, C.c_uint32, C.c_uint64, _p, _p]),
 }
 
 _lib = None
@@ -84,7 +91,7 @@ class S4DError(RuntimeError):
 
 
 # Version of include/s4d_dfa.h these bindings are written for (s4d_abi_version()).
-ABI_VERSION = 104
+ABI_VERSION = 105
 
 
 def lib():

@@ -18,7 +18,8 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(REPO, "include")
 LIB_DIR = os.path.join(PKG, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libs4d_dfa.so")
-SOURCES = ["capi.cu", "kps_project.cu", "dfa_gather.cu", "kps_noalloc.cu", "linear_tc.cu", "camera_encoder.cu", "pack_maps.cu", "instance_bank.cu"]
+SOURCES = ["capi.cu", "kps_project.cu", "dfa_gather.cu", "kps_noalloc.cu", "linear_tc.cu", "camera_encoder.cu", "pack_maps.cu",
+           "instance_bank.cu", "peer.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -30,6 +30,13 @@ constexpr int64_t kMaxElems = (int64_t)1 << 31;
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Shared checks and launch of s4d_dfa_output_proj and s4d_dfa_output_proj_sum (fn names the
+// entry point in the error text); rows row0 .. row0 + rows - 1 of [feature_rows, C] sources.
+int output_proj_checked(const char* fn, const float* features, const float* features2, int64_t feature_rows,
+                        int64_t row0, int64_t rows, const float* weight, const float* bias,
+                        const float* instance_feature, int64_t instance_ld, int residual_mode, float* out,
+                        int64_t out_ld, int64_t embed_dims, int32_t* error_flag, void* stream);
+
 }  // namespace
 
 extern "C" {
@@ -47,7 +54,7 @@ const char* s4d_status_string(int status) {
 
 const char* s4d_last_error(void) { return g_last_error; }
 
-int s4d_abi_version(void) { return 104; }
+int s4d_abi_version(void) { return 105; }
 
 uint64_t s4d_set_tc_wait_limit_ns(uint64_t limit_ns) {
   const uint64_t prev = g_tc_wait_limit_ns;
@@ -615,23 +622,59 @@ int s4d_dfa_output_proj(const float* features, int64_t rows, const float* weight
                         int64_t out_ld, int64_t embed_dims, int32_t* error_flag, void* stream) {
   set_error("%s", "");
   if (rows < 0) return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj: negative rows");
+  return output_proj_checked("s4d_dfa_output_proj", features, nullptr, rows, 0, rows, weight, bias, instance_feature,
+                             instance_ld, residual_mode, out, out_ld, embed_dims, error_flag, stream);
+}
+
+int s4d_dfa_output_proj_sum(const float* features, const float* features2, int64_t feature_rows, int64_t row0,
+                            int64_t rows, const float* weight, const float* bias, const float* instance_feature,
+                            int64_t instance_ld, int residual_mode, float* out, int64_t out_ld, int64_t embed_dims,
+                            int32_t* error_flag, void* stream) {
+  set_error("%s", "");
+  if (rows < 0 || row0 < 0 || feature_rows < 0)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj_sum: negative rows, row0 or feature_rows");
+  if (feature_rows >= kMaxElems) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_output_proj_sum: feature_rows must be < 2^31");
+  if (row0 > feature_rows || rows > feature_rows - row0)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj_sum: rows row0 .. row0 + rows - 1 outside the sources");
+  if (rows > 0 && (features2 == nullptr || !aligned(features2, 16)))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj_sum: null or misaligned features2");
+  return output_proj_checked("s4d_dfa_output_proj_sum", features, features2, feature_rows, row0, rows, weight, bias,
+                             instance_feature, instance_ld, residual_mode, out, out_ld, embed_dims, error_flag, stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+int output_proj_checked(const char* fn, const float* features, const float* features2, int64_t feature_rows,
+                        int64_t row0, int64_t rows, const float* weight, const float* bias,
+                        const float* instance_feature, int64_t instance_ld, int residual_mode, float* out,
+                        int64_t out_ld, int64_t embed_dims, int32_t* error_flag, void* stream) {
+  char msg[160];
+  auto bad = [&](int status, const char* what) {
+    snprintf(msg, sizeof(msg), "%s: %s", fn, what);
+    return fail(status, msg);
+  };
   if (residual_mode != S4D_RESIDUAL_NONE && residual_mode != S4D_RESIDUAL_ADD && residual_mode != S4D_RESIDUAL_CAT)
-    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj: unknown residual_mode");
-  if (embed_dims != 256) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_output_proj: embed_dims must be 256");
-  if (rows >= kMaxElems) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_output_proj: rows must be < 2^31");
+    return bad(S4D_ERR_INVALID_ARG, "unknown residual_mode");
+  if (embed_dims != 256) return bad(S4D_ERR_UNSUPPORTED_SHAPE, "embed_dims must be 256");
+  if (rows >= kMaxElems) return bad(S4D_ERR_UNSUPPORTED_SHAPE, "rows must be < 2^31");
   const bool res = residual_mode != S4D_RESIDUAL_NONE;
   if (out_ld < (residual_mode == S4D_RESIDUAL_CAT ? 2 : 1) * embed_dims || out_ld % 4 != 0)
-    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj: out_ld too small or not a multiple of 4");
+    return bad(S4D_ERR_INVALID_ARG, "out_ld too small or not a multiple of 4");
   if (res && (instance_ld < embed_dims || instance_ld % 4 != 0))
-    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj: instance_ld must be >= embed_dims and a multiple of 4");
+    return bad(S4D_ERR_INVALID_ARG, "instance_ld must be >= embed_dims and a multiple of 4");
   if (rows == 0) return S4D_OK;
   if (features == nullptr || weight == nullptr || out == nullptr || (res && instance_feature == nullptr))
-    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj: null pointer");
+    return bad(S4D_ERR_INVALID_ARG, "null pointer");
   if (!aligned(features, 16) || !aligned(weight, 16) || !aligned(out, 16) || (bias != nullptr && !aligned(bias, 16)) ||
       (res && !aligned(instance_feature, 16)))
-    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj: misaligned pointer");
+    return bad(S4D_ERR_INVALID_ARG, "misaligned pointer");
   OprojParams p{};
   p.feat = features;
+  p.feat2 = features2;
+  p.feat_rows = feature_rows;
+  p.feat_row0 = row0;
   p.w = weight;
   p.bias = bias;
   p.res = res ? instance_feature : nullptr;
@@ -646,4 +689,4 @@ int s4d_dfa_output_proj(const float* features, int64_t rows, const float* weight
   return launch_output_proj(p, static_cast<cudaStream_t>(stream));
 }
 
-}  // extern "C"
+}  // namespace

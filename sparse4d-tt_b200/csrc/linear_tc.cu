@@ -422,22 +422,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // A CTA computes output columns [col0, col0 + NO) of a 128-row tile (NO = 256: all of them;
 // fewer when a launch has few row tiles, so that more SMs share it).
-template <int NO>
+template <int NO, bool TWO = false>
 struct Oproj {
   static constexpr int kK = 256;  // input features (embed_dims)
   static constexpr int kN = NO;
-  static constexpr int kStage = kATile + kN * kBK * 4;  // feats tile, W_o tile
+  static constexpr int kA = TWO ? 2 : 1;                     // feature sources summed by the MMAs
+  static constexpr int kStage = kA * kATile + kN * kBK * 4;  // feats tile(s), W_o tile
   static constexpr uint32_t kCols = NO <= 32 ? 32 : NO <= 64 ? 64 : NO <= 128 ? 128 : 256;
   static constexpr size_t kSmem = smem_bytes(kStage);
   static_assert(NO % 32 == 0 && NO <= 256 && kStage % 1024 == 0, "swizzle alignment");
   static_assert(4 * 2 * kStageChunk <= kStages * kStage, "epilogue staging fits in the stages");
 };
 
-template <int NO>
+// TWO: out = (feat + feat2) . W^T + ... with feat2 another [rows, k] source (the other camera
+// half's partial sums, which may live on a peer GPU): both tiles of a K step are multiplied by the
+// same W tile into one accumulator, so the sum is never formed in memory.
+template <int NO, bool TWO = false>
 __global__ void __launch_bounds__(kThreads, 2)
-    output_proj_kernel(const __grid_constant__ CUtensorMap map_feat, const __grid_constant__ CUtensorMap map_w,
-                       const __grid_constant__ CUtensorMap map_out, const OprojParams p) {
-  using S = Oproj<NO>;
+    output_proj_kernel(const __grid_constant__ CUtensorMap map_feat, const __grid_constant__ CUtensorMap map_feat2,
+                       const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_out,
+                       const OprojParams p) {
+  using S = Oproj<NO, TWO>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
   const Ctl c = carve<S::kStage>(smem);
@@ -457,8 +462,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t st = smem_u32(smem + s * S::kStage), fb = full0 + 8 * s;
         const int kx = k_column(kb, kbs);
         mbar_expect_tx(fb, S::kStage);
-        tma_load_2d(st, &map_feat, fb, kx, int(row0));
-        tma_load_2d(st + kATile, &map_w, fb, kx, col0);
+        tma_load_2d(st, &map_feat, fb, kx, int(p.feat_row0 + row0));
+        if (TWO) tma_load_2d(st + kATile, &map_feat2, fb, kx, int(p.feat_row0 + row0));
+        tma_load_2d(st + S::kA * kATile, &map_w, fb, kx, col0);
         issued = kb + 1;
       }
       drain_loads(full0, issued);
@@ -470,9 +476,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (!mbar_wait(full0 + 8 * s, (kb / kStages) & 1, c.abort_flag, p.wait_limit_ns)) break;
         tc_fence_after();
         const uint32_t st = smem_u32(smem + s * S::kStage);
-        const uint64_t a = sw64_desc(st), b = sw64_desc(st + kATile);
+        const uint64_t a = sw64_desc(st), a2 = sw64_desc(st + kATile), b = sw64_desc(st + S::kA * kATile);
 #pragma unroll
-        for (int k = 0; k < kBK / 8; ++k) mma_tf32(tmem, a + 2 * k, b + 2 * k, tf32_idesc(S::kN), (kb | k) != 0);
+        for (int k = 0; k < kBK / 8; ++k) {
+          mma_tf32(tmem, a + 2 * k, b + 2 * k, tf32_idesc(S::kN), (kb | k) != 0);
+          if (TWO) mma_tf32(tmem, a2 + 2 * k, b + 2 * k, tf32_idesc(S::kN), 1);
+        }
         mma_commit(empty0 + 8 * s);
       }
       mma_commit(acc_bar);
@@ -602,17 +611,19 @@ int launch_weights_fc_cols(const WfcParams& p, cudaStream_t stream, int groups) 
   return cuda_check(cudaGetLastError(), "weights_fc_kernel launch");
 }
 
-template <int NO>
+template <int NO, bool TWO>
 int launch_output_proj_cols(const OprojParams& p, cudaStream_t stream, int groups) {
-  using S = Oproj<NO>;
-  CUtensorMap mf, mw, mo;
-  int st = make_map(&mf, p.feat, p.rows, p.k, p.k, kBM);
+  using S = Oproj<NO, TWO>;
+  CUtensorMap mf, mf2, mw, mo;
+  const int64_t feat_rows = p.feat_rows > 0 ? p.feat_rows : p.rows;
+  int st = make_map(&mf, p.feat, feat_rows, p.k, p.k, kBM);
+  if (st == S4D_OK) st = TWO ? make_map(&mf2, p.feat2, feat_rows, p.k, p.k, kBM) : make_map(&mf2, p.feat, feat_rows, p.k, p.k, kBM);
   if (st == S4D_OK) st = make_map(&mw, p.w, p.k, p.k, p.k, NO);
   if (st == S4D_OK) st = make_map(&mo, p.out, p.rows, p.k, p.out_ld, 32, true);
-  if (st == S4D_OK) st = set_smem(output_proj_kernel<NO>, S::kSmem, "cudaFuncSetAttribute(output_proj_kernel)");
+  if (st == S4D_OK) st = set_smem(output_proj_kernel<NO, TWO>, S::kSmem, "cudaFuncSetAttribute(output_proj_kernel)");
   if (st != S4D_OK) return st;
   const dim3 grid(unsigned((p.rows + kBM - 1) / kBM), unsigned(groups));
-  output_proj_kernel<NO><<<grid, kThreads, S::kSmem, stream>>>(mf, mw, mo, p);
+  output_proj_kernel<NO, TWO><<<grid, kThreads, S::kSmem, stream>>>(mf, mf2, mw, mo, p);
   return cuda_check(cudaGetLastError(), "output_proj_kernel launch");
 }
 
@@ -634,9 +645,14 @@ int launch_output_proj(const OprojParams& p, cudaStream_t stream) {
   if (p.k != 256) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "output_proj: implemented for embed_dims 256");
   // 256 output columns in 1, 2 (128 each) or 8 (32 each) groups
   const int groups = S4D_TC_COLUMN_GROUPS ? column_groups((p.rows + kBM - 1) / kBM, {2, 8}) : 1;
-  if (groups == 8) return launch_output_proj_cols<32>(p, stream, 8);
-  if (groups == 2) return launch_output_proj_cols<128>(p, stream, 2);
-  return launch_output_proj_cols<256>(p, stream, 1);
+  if (p.feat2 != nullptr) {
+    if (groups == 8) return launch_output_proj_cols<32, true>(p, stream, 8);
+    if (groups == 2) return launch_output_proj_cols<128, true>(p, stream, 2);
+    return launch_output_proj_cols<256, true>(p, stream, 1);
+  }
+  if (groups == 8) return launch_output_proj_cols<32, false>(p, stream, 8);
+  if (groups == 2) return launch_output_proj_cols<128, false>(p, stream, 2);
+  return launch_output_proj_cols<256, false>(p, stream, 1);
 }
 
 }  // namespace s4d

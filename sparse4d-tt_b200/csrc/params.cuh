@@ -91,7 +91,10 @@ struct WfcParams {
 };
 
 struct OprojParams {
-  const float* feat;  // [rows, k]
+  const float* feat;   // [feat_rows, k]: rows feat_row0 ... feat_row0 + rows - 1 are used
+  const float* feat2;  // null, or a second [feat_rows, k] source added to feat (may be a peer's memory)
+  int64_t feat_rows;   // rows of the feature sources (0: rows)
+  int64_t feat_row0;
   const float* w;     // [k, k]
   const float* bias;  // [k] or null
   const float* res;   // residual rows, row stride res_ld (add / cat)

@@ -18,9 +18,11 @@ passing a ``torch.distributed`` process group as ``mesh_device``: each rank samp
 own cameras, with the softmax taken over ALL cameras (the reference softmaxes over each
 device's cameras only; see ``camera_shard``).  ``model_config["CAMERA_REDUCE"]`` chooses how
 the fp32 partial sums meet: ``"all_reduce"`` (default; every rank returns all ``[bs, A, 2C]``,
-as the reference's ``ttnn.all_reduce``) or ``"reduce_scatter"`` (NCCL reduce-scatter over the
+as the reference's ``ttnn.all_reduce``), ``"reduce_scatter"`` (NCCL reduce-scatter over the
 flattened ``(frame, anchor)`` rows; the rank runs ``output_proj`` on its shard only and
-returns ``[bs * A / n, 2C]``, rows ``self.shard`` of the flattened output).
+returns ``[bs * A / n, 2C]``, rows ``self.shard`` of the flattened output) or ``"p2p"`` (groups
+of 2 GPUs: the same shards with no collective kernel -- ``output_proj`` reads the other GPU's
+partial sums over NVLink and adds them in its accumulator; see ``camera_shard``).
 """
 from __future__ import annotations
 
@@ -71,7 +73,7 @@ def preprocess_dfa_parameters(pt_model) -> Dict[str, Tensor]:
 FeatureMaps = Union[List[Tensor], Tuple[Tensor, Tensor, Tensor]]
 
 MATMUL_PRECISIONS = {"fp32": "highest", "tf32": "high"}
-CAMERA_REDUCES = ("all_reduce", "reduce_scatter")
+CAMERA_REDUCES = ("all_reduce", "reduce_scatter", "p2p")
 
 
 @contextlib.contextmanager
@@ -174,6 +176,13 @@ class DeformableFeatureAggregation:
         # ... and for the gather that computes its own sample locations from the anchors
         # (s4d_deformable_aggregation_anchors): no keypoint launch, no location buffer.
         self.fused_keypoints = self._tc and self._factors_ok and num_learnable_pts > 0
+        if self.camera_reduce == "p2p" and self.process_group is not None:
+            import torch.distributed as dist
+
+            if dist.get_world_size(self.process_group) != 2 or not self._tc:
+                raise ValueError("CAMERA_REDUCE='p2p' needs a camera group of 2 ranks and the tensor-core linears "
+                                 "(MATMUL_PRECISION 'tf32', residual_mode 'cat', 'add' or 'none')")
+        self._peer = None  # camera_shard.PeerPartialSums of the p2p mode, made at the first run
         self._side: Optional[torch.cuda.Stream] = None
         self._side_kps: Optional[torch.cuda.Stream] = None
         self._side_pending = False
@@ -364,7 +373,18 @@ class DeformableFeatureAggregation:
             from .camera_shard import rank_camera_range
 
             cam_begin, cam_end = rank_camera_range(self.num_cams, self.process_group)
-        feats = torch.empty(bs, num_anchor, self.embed_dims, dtype=torch.float32, device=dev)
+        p2p = self.process_group is not None and self.camera_reduce == "p2p"
+        if p2p:
+            # the gather writes straight into the buffer the other rank reads over NVLink
+            if self._peer is None or self._peer.capacity < rows:
+                from .camera_shard import PeerPartialSums
+
+                if self._peer is not None:
+                    self._peer.close()
+                self._peer = PeerPartialSums(rows, self.embed_dims, self.process_group, dev)
+            feats = self._peer.current(rows).view(bs, num_anchor, self.embed_dims)
+        else:
+            feats = torch.empty(bs, num_anchor, self.embed_dims, dtype=torch.float32, device=dev)
         logits = logits.contiguous()
         logits_cam = None if logits_cam is None else logits_cam.contiguous()
         log = self.event_log
@@ -401,6 +421,19 @@ class DeformableFeatureAggregation:
         out_shape = (bs, num_anchor)
         feats2d = feats.view(rows, C)
         inst_rows = instance_feature.reshape(rows, C)
+        if p2p:
+            from .camera_shard import shard_rows
+
+            # this rank's rows of (own partial sums + the other rank's, read over NVLink), summed
+            # in output_proj's tensor-core accumulator
+            self.shard = b, e = shard_rows(rows, self.process_group)
+            peer = self._peer.exchange()
+            width = 2 * C if self.residual_mode == "cat" else C
+            out = torch.empty(e - b, width, device=dev)
+            ops.output_proj_sum_into(out, feats2d, peer, b, e - b, self.output_proj_weight, self.output_proj_bias,
+                                     ops.row_view(inst_rows[b:e], C), self.residual_mode,
+                                     error_flag=self._peer.error_flag)
+            return out
         if self.process_group is not None:
             from .camera_shard import reduce_partial_sums, shard_rows
 

@@ -202,6 +202,35 @@ def output_proj_into(out: Tensor, features: Tensor, weight: Tensor, bias: Option
     return out
 
 
+def output_proj_sum_into(out: Tensor, features: Tensor, features2_ptr: int, row0: int, rows: int, weight: Tensor,
+                         bias: Optional[Tensor], instance_feature: Optional[Tensor] = None,
+                         residual_mode: str = "cat", error_flag: Optional[Tensor] = None) -> Tensor:
+    """``output_proj_into`` of ``(features + features2)[row0 : row0 + rows]``: both sources are
+    ``[R, C]`` contiguous fp32; ``features2_ptr`` is the device address of the second one, which
+    may be a peer GPU's buffer (``PeerPartialSums``), read by the kernel over NVLink.  ``out`` and
+    ``instance_feature`` hold the ``rows`` output rows."""
+    name = "output_proj_sum"
+    mode = RESIDUAL_MODES[residual_mode]
+    dev = _require_cuda(name, out, features, weight, bias, instance_feature, error_flag)
+    _check_contig(name, features=features, weight=weight, bias=bias)
+    for k, t in (("out", out), ("features", features), ("weight", weight), ("bias", bias),
+                 ("instance_feature", instance_feature)):
+        _check_dtype(name, t, (torch.float32,), k)
+    _check_dtype(name, error_flag, (torch.int32,), "error_flag")
+    total, c = features.shape
+    _require(tuple(weight.shape) == (c, c), f"weight must be [{c}, {c}]")
+    _require(out.dim() == 2 and out.shape[0] == rows and out.stride(1) == 1, f"out must be a [{rows}, n] row view")
+    if mode != L.S4D_RESIDUAL_NONE:
+        _require(instance_feature is not None and tuple(instance_feature.shape) == (rows, c)
+                 and instance_feature.stride(1) == 1, f"instance_feature must be a [{rows}, {c}] row view")
+    st = L.lib().s4d_dfa_output_proj_sum(features.data_ptr(), int(features2_ptr), total, row0, rows,
+                                         weight.data_ptr(), _ptr(bias), _ptr(instance_feature),
+                                         0 if instance_feature is None else instance_feature.stride(0), mode,
+                                         out.data_ptr(), out.stride(0), c, _ptr(error_flag), _stream_ptr(dev))
+    L.check(name, st)
+    return out
+
+
 # ---------------------------------------------------------------------------------------------
 # deformable_aggregation
 # ---------------------------------------------------------------------------------------------

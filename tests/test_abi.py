@@ -33,7 +33,7 @@ def lib():
 
 def test_every_declared_symbol_is_exported(lib):
     names = declared_functions()
-    assert len(names) == 21, names
+    assert len(names) == 27, names
     for n in names:
         assert hasattr(lib, n), n
         assert n in L.SIGNATURES, f"{n} has no ctypes signature"
@@ -52,7 +52,7 @@ def test_status_strings_and_version(lib):
     assert L.status_string(0) == "S4D_OK"
     assert L.status_string(2) == "S4D_ERR_UNSUPPORTED_SHAPE"
     assert L.status_string(99) == "S4D_ERR_UNKNOWN"
-    assert lib.s4d_abi_version() == 104 == L.ABI_VERSION
+    assert lib.s4d_abi_version() == 105 == L.ABI_VERSION
 
 
 def test_dfa_workspace_bytes(lib):
@@ -412,3 +412,56 @@ def test_tc_wait_limit_is_per_thread_and_restorable(lib):
     t.join()
     assert seen["v"] == 2_000_000_000  # another thread keeps its own default
     assert lib.s4d_set_tc_wait_limit_ns(prev) == 12345
+
+
+def _oproj_sum(lib, **kw):
+    a = dict(feat=16, feat2=16, total=1800, row0=900, rows=900, w=16, b=16, inst=16, ild=512, mode=2, out=16,
+             old=512, C=256)
+    a.update(kw)
+    st = lib.s4d_dfa_output_proj_sum(a["feat"], a["feat2"], a["total"], a["row0"], a["rows"], a["w"], a["b"],
+                                     a["inst"], a["ild"], a["mode"], a["out"], a["old"], a["C"], None, None)
+    return st, lib.s4d_last_error().decode()
+
+
+@pytest.mark.parametrize("kw,status,text", [
+    (dict(row0=901), L.S4D_ERR_INVALID_ARG, "outside the sources"),
+    (dict(row0=-1), L.S4D_ERR_INVALID_ARG, "negative"),
+    (dict(rows=-1), L.S4D_ERR_INVALID_ARG, "negative"),
+    (dict(total=1 << 31, row0=0), L.S4D_ERR_UNSUPPORTED_SHAPE, "feature_rows"),
+    (dict(feat2=None), L.S4D_ERR_INVALID_ARG, "features2"),
+    (dict(feat2=8), L.S4D_ERR_INVALID_ARG, "features2"),
+    (dict(feat=8), L.S4D_ERR_INVALID_ARG, "s4d_dfa_output_proj_sum: misaligned"),
+    (dict(C=512), L.S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_output_proj_sum: embed_dims"),
+    (dict(old=256), L.S4D_ERR_INVALID_ARG, "out_ld"),
+    (dict(mode=3), L.S4D_ERR_INVALID_ARG, "residual_mode"),
+])
+def test_output_proj_sum_rejects(lib, kw, status, text):
+    st, msg = _oproj_sum(lib, **kw)
+    assert st == status and text in msg, msg
+
+
+def test_output_proj_sum_zero_rows_is_ok(lib):
+    assert _oproj_sum(lib, rows=0, row0=1800, feat2=None)[0] == L.S4D_OK
+
+
+def test_peer_entry_points_reject_on_host(lib):
+    assert lib.s4d_ipc_handle_bytes() == 64
+    slots = (C.c_void_p * 8)(16, 32)
+    arr = C.cast(slots, C.c_void_p)
+    for world, rank, text in ((0, 0, "world"), (9, 0, "world"), (2, 2, "rank"), (2, -1, "rank")):
+        st = lib.s4d_peer_signal_wait(64, arr, rank, world, 1, 1000, None, None)
+        assert st != L.S4D_OK and text in lib.s4d_last_error().decode()
+    assert lib.s4d_peer_signal_wait(None, arr, 0, 2, 1, 1000, None, None) == L.S4D_ERR_INVALID_ARG
+    assert lib.s4d_peer_signal_wait(64, None, 0, 2, 1, 1000, None, None) == L.S4D_ERR_INVALID_ARG
+    assert lib.s4d_peer_signal_wait(66, arr, 0, 2, 1, 1000, None, None) == L.S4D_ERR_INVALID_ARG
+    bad = (C.c_void_p * 8)(16, 0)  # rank 0's peer (rank 1) has no slots
+    st = lib.s4d_peer_signal_wait(64, C.cast(bad, C.c_void_p), 0, 2, 1, 1000, None, None)
+    assert st == L.S4D_ERR_INVALID_ARG and "peer slots" in lib.s4d_last_error().decode()
+    # one rank alone has nobody to wait for: nothing is launched
+    assert lib.s4d_peer_signal_wait(64, arr, 0, 1, 1, 1000, None, None) == L.S4D_OK
+    off = C.c_uint64(0)
+    handle = C.create_string_buffer(64)
+    assert lib.s4d_ipc_export(None, handle, C.byref(off)) == L.S4D_ERR_INVALID_ARG
+    base = C.c_void_p()
+    assert lib.s4d_ipc_open(None, C.byref(base)) == L.S4D_ERR_INVALID_ARG
+    assert lib.s4d_ipc_close(None) == L.S4D_ERR_INVALID_ARG

@@ -208,3 +208,57 @@ def test_wait_timeout_sets_flag_and_next_launch_is_clean(cuda_device):
     _check(out[:, :c], i64 @ w_o.double().T + b_o.double(), i64.abs() @ w_o.double().abs().T + 1e-6,
            "output_proj after a timed-out launch")
     assert torch.equal(out[:, c:], embed)
+
+
+@pytest.mark.parametrize("mode", ["cat", "add", "none"])
+@pytest.mark.parametrize("rows,row0,total", [(1, 0, 1), (129, 7, 300), (900, 900, 1800), (7200, 7200, 14400),
+                                             (14400, 0, 28800)])
+def test_output_proj_sum_of_two_sources(cuda_device, mode, rows, row0, total):
+    """s4d_dfa_output_proj_sum: rows row0 .. row0 + rows - 1 of (features + features2), the sum
+    formed by two MMAs per K step into one accumulator (here both sources are on this GPU; the
+    camera-sharded mode passes a peer GPU's buffer as the second)."""
+    dev = torch.device("cuda:0")
+    gen = torch.Generator().manual_seed(rows + row0 + len(mode))
+    c = 256
+    w = ((torch.rand(c, c, generator=gen) * 2 - 1) * (3 / c) ** 0.5).to(dev)
+    b = torch.randn(c, generator=gen).to(dev)
+    f1 = torch.randn(total, c, generator=gen).to(dev)
+    f2 = torch.randn(total, c, generator=gen).to(dev)
+    inst_wide = torch.randn(rows, 2 * c, generator=gen).to(dev)
+    inst = inst_wide[:, :c]
+    width = 2 * c if mode == "cat" else c + 8
+    out = torch.full((rows, width), -7.0, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops.output_proj_sum_into(out, f1, f2.data_ptr(), row0, rows, w, b, None if mode == "none" else inst, mode,
+                             error_flag=flag)
+    torch.cuda.synchronize()
+    assert flag.item() == 0
+    a64, b64, w64 = f1[row0:row0 + rows].double(), f2[row0:row0 + rows].double(), w.double()
+    ref = (a64 + b64) @ w64.T + b.double()
+    scale = (a64.abs() + b64.abs()) @ w64.abs().T + 1e-6
+    if mode == "add":
+        ref = ref + inst.double()
+    _check(out[:, :c], ref, scale, f"output_proj_sum {mode} rows={rows} row0={row0}")
+    if mode == "cat":
+        assert torch.equal(out[:, c:], inst)
+    else:
+        assert torch.all(out[:, c:] == -7.0)
+
+
+def test_output_proj_sum_with_zero_second_source_equals_output_proj(cuda_device):
+    """With features2 all zeros the sum kernel gives output_proj's result bit for bit (adding
+    exact zeros to the accumulator changes nothing)."""
+    dev = torch.device("cuda:0")
+    gen = torch.Generator().manual_seed(5)
+    rows, c = 2700, 256
+    w = ((torch.rand(c, c, generator=gen) * 2 - 1) * (3 / c) ** 0.5).to(dev)
+    b = torch.randn(c, generator=gen).to(dev)
+    f1 = torch.randn(2 * rows, c, generator=gen).to(dev)
+    zeros = torch.zeros(2 * rows, c, device=dev)
+    inst = torch.randn(rows, c, generator=gen).to(dev)
+    got = torch.empty(rows, 2 * c, device=dev)
+    ref = torch.empty(rows, 2 * c, device=dev)
+    ops.output_proj_sum_into(got, f1, zeros.data_ptr(), rows, rows, w, b, inst, "cat")
+    ops.output_proj_into(ref, f1[rows:].contiguous(), w, b, inst, "cat")
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)

@@ -1,7 +1,8 @@
 """Camera-sharded DFA on 2 GPUs (NCCL): each rank samples 3 of the 6 cameras with the softmax
-taken over all 6, the partial sums are all-reduced (every rank gets every row) or
-reduce-scattered over the flattened (frame, anchor) rows (each rank projects its half), and the
-result equals the single-GPU layer's rows.  Skipped unless 2 GPUs are visible."""
+taken over all 6, the partial sums are all-reduced (every rank gets every row),
+reduce-scattered over the flattened (frame, anchor) rows (each rank projects its half), or
+read by each rank's output_proj from the other GPU's memory (p2p), and the result equals the
+single-GPU layer's rows.  Skipped unless 2 GPUs are visible."""
 import os
 import socket
 import tempfile
@@ -82,3 +83,68 @@ def test_camera_sharded_layer_matches_single_gpu():
         assert g["shard"].tolist() == [r * 900, (r + 1) * 900] and g["shape"].tolist() == [900, 512]
         # same kernels, partial sums added in another order: far inside the bf16 tolerance
         assert float(g["tc_rel"]) <= 1e-4
+
+
+def _p2p_worker(rank, world, port, out_dir):
+    import datetime
+    import sys
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, repo)
+    import torch.distributed as dist
+
+    from sparse4d_tt_b200 import DeformableFeatureAggregation, ops
+    from sparse4d_tt_b200 import synthetic as syn
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device(f"cuda:{rank}")
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        cfg = syn.DFAConfig(bs=2, num_anchor=900)
+        params = syn.make_params(cfg, torch.Generator().manual_seed(42))
+        cfg_tc = {"FEATURE_DTYPE": torch.bfloat16, "MATMUL_PRECISION": "tf32"}
+        p2p = DeformableFeatureAggregation(dev, params, dict(cfg_tc, CAMERA_REDUCE="p2p"),
+                                           mesh_device=dist.group.WORLD)
+        rs = DeformableFeatureAggregation(dev, params, dict(cfg_tc, CAMERA_REDUCE="reduce_scatter"),
+                                          mesh_device=dist.group.WORLD)
+        single = DeformableFeatureAggregation(dev, params, cfg_tc)
+        errs, rs_errs = [], []
+        # five calls with new inputs each: both buffers of the double-buffered exchange, reused
+        for call in range(5):
+            ins = syn.make_inputs(cfg, 60 + call, feature_dtype=torch.bfloat16)
+            packed = ops.pack_feature_maps([m.to(dev) for m in ins.feature_maps], dtype=torch.bfloat16)
+            args = (ins.instance_feature.to(dev), ins.anchor.to(dev), ins.anchor_embed.to(dev), packed,
+                    ins.projection_mat.to(dev), ins.image_wh.to(dev), cfg.spatial_shapes, 2, 900)
+            for m in (p2p, rs, single):
+                m._cached_camera_embed = m._cached_camera_logits = None
+                m._cached_camera_ws = m._cached_camera_factors = None
+            got = p2p.run(*args)
+            b, e = p2p.shard
+            ref = single.run(*args).reshape(-1, 512)[b:e]
+            other = rs.run(*args)
+            torch.cuda.synchronize()
+            errs.append(((got - ref).abs().max() / ref.abs().max()).item())
+            rs_errs.append(((got - other).abs().max() / other.abs().max()).item())
+        p2p._peer.check()
+        np.savez(os.path.join(out_dir, f"p2p{rank}.npz"), rel=np.array(errs), rel_rs=np.array(rs_errs),
+                 shard=np.array(p2p.shard), shape=np.array(got.shape), epoch=np.array(p2p._peer.epoch),
+                 flag=np.array(p2p._peer.error_flag.item()))
+        p2p._peer.close()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_camera_sharded_p2p_matches_single_gpu():
+    out_dir = tempfile.mkdtemp()
+    mp.start_processes(_p2p_worker, args=(2, _free_port(), out_dir), nprocs=2, start_method="spawn")
+    for r in range(2):
+        g = np.load(os.path.join(out_dir, f"p2p{r}.npz"))
+        assert int(g["flag"]) == 0 and int(g["epoch"]) == 5
+        assert g["shard"].tolist() == [r * 900, (r + 1) * 900] and g["shape"].tolist() == [900, 512]
+        # the same partial sums, added inside the accumulator instead of before it
+        assert float(np.max(g["rel"])) <= 1e-4, g["rel"]
+        assert float(np.max(g["rel_rs"])) <= 1e-4, g["rel_rs"]
