@@ -14,6 +14,8 @@
 //   dfa_gather_warp_kernel   Sparse4D v3 shape (6 cams, 4 levels, 13 points, 8 groups), split
 //                            logits with the per-frame camera factors (cam_softmax_prep_kernel)
 //                            in the workspace: one warp per anchor, factorised softmax.
+//   dfa_gather_coop_kernel   the same with fewer anchors than warp slots (a single frame): 2, 4
+//                            or 8 warps per anchor, the anchor's work divided between them.
 //   dfa_gather_fast_kernel   Sparse4D v3 shape, cam-major logits (full or split, no workspace):
 //                            one CTA per anchor with compile-time dimensions.
 //   dfa_gather_kernel        every other shape / layout (generic, described below).
@@ -690,25 +692,18 @@ struct SampleRec {
 #ifndef S4D_GATHER_KPS_MIN_BLOCKS_BF16
 #define S4D_GATHER_KPS_MIN_BLOCKS_BF16 32
 #endif
-// Resident warps per SM the register allocator must allow, for a block of WARPS warps.  The
-// blocks that share an anchor (SPLIT) run launches of fewer anchors than warp slots, so they
-// trade a few warp slots for registers: 28 warps (72 registers) for bf16 maps, where 64
-// registers spill; 20 (96) for fp32.
-template <typename T, bool KPS, int WARPS, bool SPLIT>
+// Resident warps per SM the register allocator must allow, for a block of WARPS warps.
+template <typename T, bool KPS, int WARPS>
 constexpr int warp_kernel_min_blocks() {
-  constexpr int warps = SPLIT ? (sizeof(T) == 2 ? 28 : 20)
-                              : sizeof(T) == 2 ? (KPS ? S4D_GATHER_KPS_MIN_BLOCKS_BF16 : S4D_GATHER_MIN_BLOCKS_BF16) : 24;
+  constexpr int warps =
+      sizeof(T) == 2 ? (KPS ? S4D_GATHER_KPS_MIN_BLOCKS_BF16 : S4D_GATHER_MIN_BLOCKS_BF16) : 24;
   return warps / WARPS > 0 ? warps / WARPS : 1;
 }
 
-// SPLIT = false: each warp of the block takes its own anchors (WARPS anchors in flight per
-// block).  SPLIT = true (few anchors: fewer than the resident warp slots): the block's WARPS warps
-// share one anchor.  Every warp computes the anchor's keypoints, softmax statistics and sample
-// records itself (identical work, no extra latency on an SM that is mostly idle at such sizes)
-// and gathers every WARPS-th merged tap block of each sub-round; the WARPS unnormalised partial
-// sums meet in shared memory in warp order, so the result is deterministic.
-template <typename T, int NC, int NL, int NP, int G, int MODE, int WARPS, bool KPS, bool SPLIT = false>
-__global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WARPS, SPLIT>()))
+// Each warp of the block takes its own anchors (WARPS anchors in flight per block).  Launches of
+// fewer anchors than warp slots use dfa_gather_coop_kernel instead (several warps per anchor).
+template <typename T, int NC, int NL, int NP, int G, int MODE, int WARPS, bool KPS>
+__global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WARPS>()))
     dfa_gather_warp_kernel(GatherParams p) {
   constexpr int NLP = NL * NP;
   constexpr int LPG = NLP * G;
@@ -727,8 +722,6 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
   __shared__ uint32_t s_xm[WARPS][32];
   __shared__ __align__(16) float4 s_kpt[KPS ? WARPS : 1][KPS ? NP : 1];  // KPS: the anchor's keypoints
   __shared__ float s_kc[KPS ? WARPS : 1][KPS ? NP * 3 : 1];               // KPS: their scaled coordinates
-  __shared__ __align__(16) float4 s_part[SPLIT ? WARPS : 1][SPLIT ? 64 : 1];  // SPLIT: partial sums per warp
-  __shared__ unsigned s_ticket;                                                // SPLIT: the block's anchor
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < NC * NL; i += WARPS * 32) {
@@ -762,16 +755,10 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
   const int64_t total_anchors = (int64_t)p.bs * p.num_anchor;
   for (;;) {
   unsigned ticket = 0;
-  if (SPLIT) {  // one anchor per block
-    if (tid == 0) s_ticket = atomicAdd(p.anchor_counter, 1u);
-    __syncthreads();  // the ticket is read below, before the barriers that end the anchor
-    ticket = s_ticket;
-  } else {
-    if (lane == 0) ticket = atomicAdd(p.anchor_counter, 1u);
-    ticket = __shfl_sync(0xffffffffu, ticket, 0);
-  }
+  if (lane == 0) ticket = atomicAdd(p.anchor_counter, 1u);
+  ticket = __shfl_sync(0xffffffffu, ticket, 0);
   const int64_t anchor_lin = ticket;
-  if (anchor_lin >= total_anchors) break;  // block-uniform when SPLIT
+  if (anchor_lin >= total_anchors) break;
   const int b = (int)p.div_anchor.div((uint32_t)anchor_lin);  // anchors < 2^31
   const int gch = lane / (D / 8);  // group of this lane's output channels
 
@@ -779,17 +766,6 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
   const float* wcam = MODE == 0 ? nullptr : p.weights_cam + (int64_t)b * NW;
   const float* ec_tab = MODE == 1 ? p.cam_ws + (int64_t)b * (NC + 1) * LPG : nullptr;
   float* ea = s_ea + (MODE == 1 ? warp * LPG : 0);
-  // SPLIT (few anchors, latency-bound): the softmax's loads are issued before the keypoint work,
-  // so their DRAM latency overlaps that of the anchor rows instead of following it
-  constexpr bool kEarly = SPLIT && MODE == 1;
-  float x[LPG / 32], ecs[LPG / 32];
-  if (kEarly) {
-#pragma unroll
-    for (int k = 0; k < LPG / 32; ++k) {
-      x[k] = __ldg(wrow + lane + 32 * k);
-      ecs[k] = __ldg(ec_tab + NW + lane + 32 * k);
-    }
-  }
 
   if (KPS) {  // the anchor's keypoints (kps_project's arithmetic)
     const float* a = p.kps_anchor + anchor_lin * p.kps_anchor_dim;
@@ -818,10 +794,9 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
   float m_l = -INFINITY, s_l = 0.0f;
   bool exact = MODE != 1;
   if (MODE == 1) {
-    if (!kEarly) {
+    float x[LPG / 32];
 #pragma unroll
-      for (int k = 0; k < LPG / 32; ++k) x[k] = __ldg(wrow + lane + 32 * k);
-    }
+    for (int k = 0; k < LPG / 32; ++k) x[k] = __ldg(wrow + lane + 32 * k);
 #pragma unroll
     for (int k = 0; k < LPG / 32; ++k) m_l = fmaxf(m_l, x[k]);
 #pragma unroll
@@ -831,7 +806,7 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
     for (int k = 0; k < LPG / 32; ++k) {
       const float e = ex2_approx(fmaf(x[k], kLog2e, -ml));
       ea[lane + 32 * k] = e;
-      s_l = fmaf(e, kEarly ? ecs[k] : __ldg(ec_tab + NW + lane + 32 * k), s_l);
+      s_l = fmaf(e, __ldg(ec_tab + NW + lane + 32 * k), s_l);
     }
 #pragma unroll
     for (int o = G; o < 32; o <<= 1) s_l += __shfl_xor_sync(0xffffffffu, s_l, o);
@@ -967,17 +942,16 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
         // unrolled so that the next blocks' loads are scheduled among this block's FMAs (4 fits
         // the 64 registers of the variant that computes its sample locations without spilling)
         constexpr int kTapUnroll = KPS ? 4 : 2;
-        constexpr int kStep = SPLIT ? WARPS : 1;  // SPLIT: this warp's share of the blocks
 #pragma unroll kTapUnroll
-        for (int k = SPLIT ? warp : 0; k < nlead; k += kStep) {
+        for (int k = 0; k < nlead; ++k) {
           const int4 px = s_rec[warp][k].pix;
           V v0, v1, v2, v3;  // every tap row is in bounds (see the record): no tests
           TapFma<T>::load(fb, px.x, lane, v0);
           TapFma<T>::load(fb, px.y, lane, v1);
           TapFma<T>::load(fb, px.z, lane, v2);
           TapFma<T>::load(fb, px.w, lane, v3);
-          if (k + kStep < nlead) {  // the next block's rows towards L1 (no registers held)
-            const int4 pn = s_rec[warp][k + kStep].pix;
+          if (k + 1 < nlead) {  // the next block's rows towards L1 (no registers held)
+            const int4 pn = s_rec[warp][k + 1].pix;
             const T* r = fb + lane * (kChannels / 32);
             prefetch_l1(r + (int64_t)pn.x * kChannels);
             prefetch_l1(r + (int64_t)pn.y * kChannels);
@@ -1018,10 +992,353 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
   }
 
   // ---- 3. normalise and store ------------------------------------------------------------------
-  if (SPLIT) {  // the block's partial sums, added in warp order by warp 0
+  float4* o = reinterpret_cast<float4*>(p.out + anchor_lin * kChannels + lane * 8);
+  o[0] = make_float4(acc[0].x * inv, acc[0].y * inv, acc[1].x * inv, acc[1].y * inv);
+  o[1] = make_float4(acc[2].x * inv, acc[2].y * inv, acc[3].x * inv, acc[3].y * inv);
+  __syncwarp();  // this anchor's shared-memory state is read before the next one writes it
+  }
+}
+
+// -----------------------------------------------------------------------------------------------
+// Few anchors (fewer than the resident warp slots, e.g. a single frame): a block of WARPS warps
+// per anchor, the anchor's work divided between the warps instead of repeated by each of them.
+//   phase 1  warp 0: the softmax statistics (factorised, or the exact fallback) and the anchor's
+//            exp table; warp 1: the anchor's keypoints (KPS); the remaining warps (warp 1 as
+//            well when WARPS is 2) stage the frame's camera factors, and (KPS) its projection
+//            matrices and image sizes, in shared memory.
+//   phase 2  the (camera, point) pairs in chunks of CHUNK (<= 32), chunk c to warp c % WARPS:
+//            projection (or the stored location), survivor test and the records of the chunk's
+//            (survivor, level) candidates with coinciding 2x2 tap blocks merged, 32 candidates
+//            per round; after each round every warp gathers every WARPS-th merged block of each
+//            warp's records.
+//   phase 3  warp 0 adds the WARPS partial sums in warp order, normalises and stores.
+// Block barriers (all in uniform control flow): 3 per anchor plus 2 per round after the first.  Every sample's location,
+// bilinear weights and softmax weight come from the same arithmetic as in
+// dfa_gather_warp_kernel; only the grouping of samples into merged blocks and the order of the
+// final sum differ (the result is deterministic).
+// -----------------------------------------------------------------------------------------------
+template <typename T, int NC, int NL, int NP, int G, int WARPS, bool KPS>
+__global__ void __launch_bounds__(WARPS * 32, (sizeof(T) == 2 ? 28 : 20) / WARPS)
+    dfa_gather_coop_kernel(GatherParams p) {
+  constexpr int NLP = NL * NP;
+  constexpr int LPG = NLP * G;
+  constexpr int NW = NC * LPG;
+  constexpr int NPAIR = NC * NP;
+  constexpr int D = kChannels / G;
+  constexpr int CHUNK = (NPAIR + WARPS - 1) / WARPS < 32 ? (NPAIR + WARPS - 1) / WARPS : 32;
+  constexpr int NCHUNK = (NPAIR + CHUNK - 1) / CHUNK;
+  constexpr int STAGER0 = WARPS > 2 ? 2 : 1;  // first warp that stages the frame's tables
+  constexpr float kLog2e = 1.4426950408889634f;
+  static_assert(WARPS >= 2 && WARPS <= 8, "coop gather: 2 to 8 warps per anchor");
+  static_assert(LPG % 32 == 0 && 32 % G == 0 && G >= 4 && (G & (G - 1)) == 0 && NW % 4 == 0, "coop gather shape");
+  __shared__ __align__(16) int4 s_lvl[NC * NL];  // (H, W, start, ok)
+  __shared__ __align__(16) float4 s_win[NC];     // per camera: (u_lo, u_hi, v_lo, v_hi)
+  __shared__ __align__(16) float s_ea[LPG];      // the anchor's exp(wa - M1) per (level, point, group)
+  __shared__ __align__(16) float s_ec[NW];       // the frame's camera factors exp(wc - M2)
+  __shared__ __align__(16) float4 s_proj[KPS ? NC * 3 : 1];  // KPS: rows 0..2 of each camera's matrix
+  __shared__ __align__(16) float2 s_wh[KPS ? NC : 1];
+  __shared__ __align__(16) float4 s_kpt[KPS ? NP : 1];
+  __shared__ float s_kc[KPS ? NP * 3 : 1];
+  __shared__ float s_stat[2][G];  // per group: max x log2(e) (exact mode) and 1 / sum
+  __shared__ int s_exact;
+  __shared__ unsigned char s_surv[WARPS][32];
+  __shared__ __align__(16) SampleRec<G> s_rec[WARPS][32];
+  __shared__ uint32_t s_xm[WARPS][32];
+  __shared__ __align__(16) float4 s_part[WARPS][64];
+  __shared__ int s_nlead[WARPS];       // per round: the warp's merged blocks,
+  __shared__ uint32_t s_extras[WARPS];  // the lanes of their other member samples,
+  __shared__ int s_more[WARPS];         // whether the warp has candidates left
+  __shared__ unsigned s_ticket;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < NC * NL; i += WARPS * 32) {
+    const int H = p.spatial_shape[2 * i], W = p.spatial_shape[2 * i + 1], st = p.scale_start[i];
+    const bool ok = H > 0 && W > 0 && st >= 0 && (int64_t)st + (int64_t)H * W <= p.num_feat;
+    const int c = i / NL;
+    if (!ok && c >= p.cam_begin && c < p.cam_end && p.error_flag != nullptr && blockIdx.x == 0)
+      atomicOr(p.error_flag, S4D_FLAG_BAD_LEVEL);
+    s_lvl[i] = make_int4(H, W, st, ok ? 1 : 0);
+    if (i % NL == NL - 1) {  // the camera's survivor window: that of its narrowest valid level
+      int wmin = 0, hmin = 0;
+      for (int l = 0; l < NL; ++l) {
+        const int j = c * NL + l;
+        const int Hl = p.spatial_shape[2 * j], Wl = p.spatial_shape[2 * j + 1], sl = p.scale_start[j];
+        if (Hl > 0 && Wl > 0 && sl >= 0 && (int64_t)sl + (int64_t)Hl * Wl <= p.num_feat) {
+          wmin = wmin == 0 || Wl < wmin ? Wl : wmin;
+          hmin = hmin == 0 || Hl < hmin ? Hl : hmin;
+        }
+      }
+      s_win[c] = wmin == 0 ? make_float4(1.0f, 0.0f, 1.0f, 0.0f)
+                           : make_float4(-0.5f / wmin - 1e-3f, 1.0f + 0.5f / wmin + 1e-3f, -0.5f / hmin - 1e-3f,
+                                         1.0f + 0.5f / hmin + 1e-3f);
+    }
+  }
+  const int64_t total_anchors = (int64_t)p.bs * p.num_anchor;
+  const int gch = lane / (D / 8);  // group of this lane's output channels
+  const uint32_t lt = (1u << lane) - 1u;
+  using V = typename TapVec<T>::type;
+  for (;;) {
+    if (tid == 0) s_ticket = atomicAdd(p.anchor_counter, 1u);
+    // (A) the ticket and the level tables are visible; the previous anchor is finished
+    __syncthreads();
+    const int64_t anchor_lin = s_ticket;
+    if (anchor_lin >= total_anchors) break;  // block-uniform
+    const int b = (int)p.div_anchor.div((uint32_t)anchor_lin);
+    const float* wrow = p.weights + anchor_lin * LPG;
+    const float* wcam = p.weights_cam + (int64_t)b * NW;
+    const float* ec_tab = p.cam_ws + (int64_t)b * (NC + 1) * LPG;
+
+    // ---- phase 1 ------------------------------------------------------------------------------
+    if (warp == 0) {  // softmax statistics of group lane % G, the warp kernel's arithmetic
+      float x[LPG / 32];
+#pragma unroll
+      for (int k = 0; k < LPG / 32; ++k) x[k] = __ldg(wrow + lane + 32 * k);
+      float m_l = -INFINITY, s_l = 0.0f;
+#pragma unroll
+      for (int k = 0; k < LPG / 32; ++k) m_l = fmaxf(m_l, x[k]);
+#pragma unroll
+      for (int o = G; o < 32; o <<= 1) m_l = fmaxf(m_l, __shfl_xor_sync(0xffffffffu, m_l, o));
+      const float ml = m_l * kLog2e;
+#pragma unroll
+      for (int k = 0; k < LPG / 32; ++k) {
+        const float e = ex2_approx(fmaf(x[k], kLog2e, -ml));
+        s_ea[lane + 32 * k] = e;
+        s_l = fmaf(e, __ldg(ec_tab + NW + lane + 32 * k), s_l);
+      }
+#pragma unroll
+      for (int o = G; o < 32; o <<= 1) s_l += __shfl_xor_sync(0xffffffffu, s_l, o);
+      const bool exact = __any_sync(0xffffffffu, !(s_l >= 1e-20f));
+      if (exact) {  // the factorised sum underflowed: exact two-pass max / sum over all logits
+        auto logit = [&](int e) { return __ldg(wrow + e % LPG) + __ldg(wcam + e); };
+        m_l = -INFINITY;
+        for (int e = lane; e < NW; e += 32) m_l = fmaxf(m_l, logit(e));
+#pragma unroll
+        for (int o = G; o < 32; o <<= 1) m_l = fmaxf(m_l, __shfl_xor_sync(0xffffffffu, m_l, o));
+        const float ml2 = m_l * kLog2e;
+        s_l = 0.0f;
+        for (int e = lane; e < NW; e += 32) s_l += ex2_approx(fmaf(logit(e), kLog2e, -ml2));
+#pragma unroll
+        for (int o = G; o < 32; o <<= 1) s_l += __shfl_xor_sync(0xffffffffu, s_l, o);
+      }
+      if (lane < G) {
+        s_stat[0][lane] = m_l * kLog2e;
+        s_stat[1][lane] = 1.0f / s_l;
+      }
+      if (lane == 0) s_exact = exact ? 1 : 0;
+    } else if (KPS && warp == 1) {  // the anchor's keypoints (kps_project's arithmetic)
+      const float* a = p.kps_anchor + anchor_lin * p.kps_anchor_dim;
+      const int nf = p.kps_num_fix, nlc = (NP - nf) * 3;
+      const float* lg = p.kps_learnable + anchor_lin * nlc;
+      for (int t = lane; t < NP * 3; t += 32) {
+        const bool learn = t < nlc;
+        const int u = learn ? t : t - nlc;
+        const int pt = (learn ? nf : 0) + u / 3, ax = u - (u / 3) * 3;
+        const float sc = expf(a[3 + ax]);
+        s_kc[3 * pt + ax] = learn ? __fmul_rn(__fsub_rn(kps_sigmoid_rn(lg[u]), 0.5f), sc)
+                                  : __fmul_rn(p.kps_fix_scale[u], sc);
+      }
+      __syncwarp();
+      if (lane < NP) {
+        float px, py, pz;
+        kps_place(a, s_kc[3 * lane], s_kc[3 * lane + 1], s_kc[3 * lane + 2], px, py, pz);
+        s_kpt[lane] = make_float4(px, py, pz, 0.0f);
+      }
+    }
+    if (warp >= STAGER0) {  // the frame's tables
+      const int t0 = tid - STAGER0 * 32, nt = (WARPS - STAGER0) * 32;
+      const float4* ec4 = reinterpret_cast<const float4*>(ec_tab);
+      for (int i = t0; i < NW / 4; i += nt) reinterpret_cast<float4*>(s_ec)[i] = __ldg(ec4 + i);
+      if (KPS) {
+        for (int i = t0; i < NC * 3; i += nt)
+          s_proj[i] = __ldg(reinterpret_cast<const float4*>(p.kps_proj) + ((int64_t)b * NC + i / 3) * 4 + i % 3);
+        for (int i = t0; i < NC; i += nt)
+          s_wh[i] = __ldg(reinterpret_cast<const float2*>(p.kps_wh) + (int64_t)b * NC + i);
+      }
+    }
+    __syncthreads();  // (B) phase 1's tables are visible
+
+    // ---- phase 2 ------------------------------------------------------------------------------
+    // Rounds: every warp builds the records of its next sub-round (up to 32 candidates of its
+    // current chunk), then all warps gather the merged blocks of every warp's sub-round, warp w
+    // taking every WARPS-th block of each, so the tap work is shared out evenly whichever cameras
+    // see the anchor.
+    const bool exact = s_exact != 0;
+    const float inv = s_stat[1][gch];
+    const float mlg = s_stat[0][gch];
+    const float2* locp = reinterpret_cast<const float2*>(p.loc) + anchor_lin * NPAIR;
+    const T* fb = static_cast<const T*>(p.feat) + (int64_t)b * p.num_feat * kChannels;
+    float2 acc[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.f, 0.f);
+
+    // this warp's candidate stream over its chunks (warp-uniform state)
+    int chunk = warp - WARPS, base = 0, sub = 0, n = 0, nsurv = 1;
+    uint32_t inv_surv = 1;
+    float2 uv = make_float2(-4.0f, -4.0f);
+    auto next_chunk = [&]() -> bool {  // the warp's next chunk with survivors, if any
+      for (chunk += WARPS; chunk < NCHUNK; chunk += WARPS) {
+        base = chunk * CHUNK;
+        const int q = base + lane;
+        const int cq = q / NP;
+        uv = make_float2(-4.0f, -4.0f);
+        bool maybe = false;
+        if (lane < CHUNK && q < NPAIR) {
+          if (KPS) {  // project keypoint q % NP into camera cq
+            const float4 kp = s_kpt[q - cq * NP];
+            const float2 wh = s_wh[cq];
+            bool front;
+            kps_uv(s_proj[3 * cq], s_proj[3 * cq + 1], s_proj[3 * cq + 2], wh.x, wh.y, kp.x, kp.y, kp.z, uv.x,
+                   uv.y, front);
+          } else {
+            uv = __ldg(locp + q);
+          }
+          const float4 wn = s_win[cq];
+          maybe = cq >= p.cam_begin && cq < p.cam_end && uv.x > wn.x && uv.x < wn.y && uv.y > wn.z && uv.y < wn.w;
+        }
+        const uint32_t keep = __ballot_sync(0xffffffffu, maybe);
+        if (keep == 0u) continue;  // warp-uniform
+        __syncwarp();              // the previous chunk's survivor list has been read
+        if (maybe) s_surv[warp][__popc(keep & lt)] = (unsigned char)lane;
+        __syncwarp();
+        nsurv = __popc(keep);
+        n = nsurv * NL;  // candidates (survivor, level), level-major, as in the warp kernel
+        inv_surv = (65536u + nsurv - 1) / (uint32_t)nsurv;
+        sub = 0;
+        return true;
+      }
+      return false;
+    };
+    bool have = next_chunk();
+#pragma unroll 1
+    for (;;) {
+      int my_nlead = 0;
+      uint32_t my_extras = 0u;
+      if (have) {  // the records of candidates sub .. sub + 31 of the current chunk
+        const int idx = sub + lane;
+        const int l = (int)(((uint32_t)idx * inv_surv) >> 16), k = idx - l * nsurv;
+        const int src = idx < n ? s_surv[warp][k] : 0;
+        const float2 uvs = make_float2(__shfl_sync(0xffffffffu, uv.x, src), __shfl_sync(0xffffffffu, uv.y, src));
+        const int qs = base + src;
+        const int cs = qs / NP, ps = qs - (qs / NP) * NP;
+        uint64_t key = 0xffffffff00000000ull | (uint32_t)lane;  // invalid lanes only match themselves
+        bool valid = false;
+        SampleRec<G> rec;
+        if (idx < n) {
+          const int4 lv = s_lvl[cs * NL + l];
+          const float Wf = (float)lv.y, Hf = (float)lv.x;
+          const float ix = ((uvs.x * 2.0f - 1.0f + 1.0f) * Wf - 1.0f) * 0.5f;
+          const float iy = ((uvs.y * 2.0f - 1.0f + 1.0f) * Hf - 1.0f) * 0.5f;
+          if (lv.w && ix > -1.0f && ix < Wf && iy > -1.0f && iy < Hf) {
+            const float x0f = floorf(ix), y0f = floorf(iy);
+            const int x0 = (int)x0f, y0 = (int)y0f;
+            const float x1f = x0f + 1.0f, y1f = y0f + 1.0f;
+            const bool vx0 = x0 >= 0, vx1 = x0 + 1 < lv.y, vy0 = y0 >= 0, vy1 = y0 + 1 < lv.x;
+            const int p00 = lv.z + y0 * lv.y + x0;
+            const bool t00 = vx0 && vy0, t01 = vx1 && vy0, t10 = vx0 && vy1, t11 = vx1 && vy1;
+            const int any = t00 ? p00 : t01 ? p00 + 1 : t10 ? p00 + lv.y : p00 + lv.y + 1;
+            rec.pix = make_int4(t00 ? p00 : any, t01 ? p00 + 1 : any, t10 ? p00 + lv.y : any,
+                                t11 ? p00 + lv.y + 1 : any);
+            rec.bw = make_float4(t00 ? (x1f - ix) * (y1f - iy) : 0.0f, t01 ? (ix - x0f) * (y1f - iy) : 0.0f,
+                                 t10 ? (x1f - ix) * (iy - y0f) : 0.0f, t11 ? (ix - x0f) * (iy - y0f) : 0.0f);
+            const int lp = l * NP + ps;
+            const int e1 = lp * G, e2 = cs * LPG + lp * G;
+            if (!exact && G % 4 == 0) {
+#pragma unroll
+              for (int g = 0; g < G; g += 4) {
+                const float4 a = *reinterpret_cast<const float4*>(s_ea + e1 + g);
+                const float4 c = *reinterpret_cast<const float4*>(s_ec + e2 + g);
+                rec.sw[g] = a.x * c.x, rec.sw[g + 1] = a.y * c.y, rec.sw[g + 2] = a.z * c.z, rec.sw[g + 3] = a.w * c.w;
+              }
+            } else {
+#pragma unroll
+              for (int g = 0; g < G; ++g)
+                rec.sw[g] = exact ? __ldg(wrow + e1 + g) + __ldg(wcam + e2 + g) : s_ea[e1 + g] * s_ec[e2 + g];
+            }
+            key = ((uint64_t)(cs * NL + l) << 32) | (uint32_t)((y0 + 1) * (lv.y + 1) + (x0 + 1));
+            valid = true;
+          }
+        }
+        const uint32_t grp = __match_any_sync(0xffffffffu, key);
+        const bool lead = valid && lane == __ffs(grp) - 1;
+        const uint32_t leaders = __ballot_sync(0xffffffffu, lead);
+        my_extras = __ballot_sync(0xffffffffu, valid && !lead);
+        my_nlead = __popc(leaders);
+        if (valid) {
+          const int slot = lead ? __popc(leaders & lt) : my_nlead + __popc(my_extras & lt);
+          s_rec[warp][slot] = rec;
+          if (lead) s_xm[warp][slot] = grp & ~(1u << lane);
+        }
+        sub += 32;
+        if (sub >= n) have = next_chunk();
+      }
+      if (lane == 0) {
+        s_nlead[warp] = my_nlead;
+        s_extras[warp] = my_extras;
+        s_more[warp] = have ? 1 : 0;
+      }
+      __syncthreads();  // (R) every warp's records of this round are visible
+      int more = 0;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) more |= s_more[w];
+      auto tap_loop = [&](auto ex) {
+        constexpr bool EX = decltype(ex)::value;
+        constexpr int kTapUnroll = KPS ? 4 : 2;
+#pragma unroll 1
+        for (int w = 0; w < WARPS; ++w) {
+          const int nlead = s_nlead[w];
+          const uint32_t extras = s_extras[w];
+#pragma unroll kTapUnroll
+          for (int k = warp; k < nlead; k += WARPS) {
+            const int4 px = s_rec[w][k].pix;
+            V v0, v1, v2, v3;  // every tap row is in bounds (see the record): no tests
+            TapFma<T>::load(fb, px.x, lane, v0);
+            TapFma<T>::load(fb, px.y, lane, v1);
+            TapFma<T>::load(fb, px.z, lane, v2);
+            TapFma<T>::load(fb, px.w, lane, v3);
+            if (k + WARPS < nlead) {  // this warp's next block of the same records towards L1
+              const int4 pn = s_rec[w][k + WARPS].pix;
+              const T* r = fb + lane * (kChannels / 32);
+              prefetch_l1(r + (int64_t)pn.x * kChannels);
+              prefetch_l1(r + (int64_t)pn.y * kChannels);
+              prefetch_l1(r + (int64_t)pn.z * kChannels);
+              prefetch_l1(r + (int64_t)pn.w * kChannels);
+            }
+            const float4 bw = s_rec[w][k].bw;
+            float sw = s_rec[w][k].sw[gch];
+            if (EX) sw = ex2_approx(fmaf(sw, kLog2e, -mlg));
+            float4 w4 = make_float4(bw.x * sw, bw.y * sw, bw.z * sw, bw.w * sw);
+            uint32_t xm = s_xm[w][k];
+            while (xm != 0u) {  // warp-uniform: most blocks have a single sample
+              const int j = __ffs(xm) - 1;
+              xm &= xm - 1u;
+              const int e = nlead + __popc(extras & ((1u << j) - 1u));
+              const float4 bwe = s_rec[w][e].bw;
+              float swe = s_rec[w][e].sw[gch];
+              if (EX) swe = ex2_approx(fmaf(swe, kLog2e, -mlg));
+              w4.x = fmaf(bwe.x, swe, w4.x);
+              w4.y = fmaf(bwe.y, swe, w4.y);
+              w4.z = fmaf(bwe.z, swe, w4.z);
+              w4.w = fmaf(bwe.w, swe, w4.w);
+            }
+            TapFma<T>::fma(v0, w4.x, acc);
+            TapFma<T>::fma(v1, w4.y, acc);
+            TapFma<T>::fma(v2, w4.z, acc);
+            TapFma<T>::fma(v3, w4.w, acc);
+          }
+        }
+      };
+      if (exact)
+        tap_loop(std::true_type{});
+      else
+        tap_loop(std::false_type{});
+      if (!more) break;  // block-uniform
+      __syncthreads();   // this round's records are read before the next round writes its own
+    }
+
+    // ---- phase 3 ------------------------------------------------------------------------------
     s_part[warp][2 * lane] = make_float4(acc[0].x, acc[0].y, acc[1].x, acc[1].y);
     s_part[warp][2 * lane + 1] = make_float4(acc[2].x, acc[2].y, acc[3].x, acc[3].y);
-    __syncthreads();
+    __syncthreads();  // (C) every warp's partial sum is in shared memory
     if (warp == 0) {
       float4 a0 = s_part[0][2 * lane], a1 = s_part[0][2 * lane + 1];
 #pragma unroll
@@ -1034,15 +1351,9 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
       o[0] = make_float4(a0.x * inv, a0.y * inv, a0.z * inv, a0.w * inv);
       o[1] = make_float4(a1.x * inv, a1.y * inv, a1.z * inv, a1.w * inv);
     }
-    __syncthreads();  // s_part and s_ticket are rewritten for the next anchor
-  } else {
-    float4* o = reinterpret_cast<float4*>(p.out + anchor_lin * kChannels + lane * 8);
-    o[0] = make_float4(acc[0].x * inv, acc[0].y * inv, acc[1].x * inv, acc[1].y * inv);
-    o[1] = make_float4(acc[2].x * inv, acc[2].y * inv, acc[3].x * inv, acc[3].y * inv);
-    __syncwarp();  // this anchor's shared-memory state is read before the next one writes it
-  }
   }
 }
+
 
 // The Sparse4D v3 shape the fast kernels are compiled for.
 constexpr int kFastNC = 6, kFastNL = 4, kFastNP = 13, kFastG = 8;
@@ -1080,7 +1391,7 @@ static int resident_warp_blocks(K kernel, int which, int warps_per_block = kWarp
 
 // Warps that share one anchor in the warp kernel for `anchors` anchors: the largest of 1, 2, 4, 8
 // (at most S4D_GATHER_MAX_SPLIT) that keeps anchors x warps within S4D_GATHER_SPLIT_SLOTS warps
-// per SM (28: the warp slots of the SPLIT instances), so that a launch of few anchors still fills
+// per SM (28: the warp slots of the cooperative instances), so that a launch of few anchors still fills
 // the SMs in one wave.  It depends only on the anchor count and the SM count, so every instance
 // family (feature type, keypoints in the kernel or not) sums a given anchor in the same order.
 #ifndef S4D_GATHER_SPLIT_SLOTS
@@ -1163,11 +1474,11 @@ int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream) {
       else
         go(k1, kWarpBlock, 0);
     };
-#define S4D_WARP_FAMILY(T, KPS)                                                                     \
-  launch_family(dfa_gather_warp_kernel<T, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock, KPS>,     \
-                dfa_gather_warp_kernel<T, kFastNC, kFastNL, kFastNP, kFastG, 1, 2, KPS, true>,        \
-                dfa_gather_warp_kernel<T, kFastNC, kFastNL, kFastNP, kFastG, 1, 4, KPS, true>,        \
-                dfa_gather_warp_kernel<T, kFastNC, kFastNL, kFastNP, kFastG, 1, 8, KPS, true>)
+#define S4D_WARP_FAMILY(T, KPS)                                                                 \
+  launch_family(dfa_gather_warp_kernel<T, kFastNC, kFastNL, kFastNP, kFastG, 1, kWarpBlock, KPS>, \
+                dfa_gather_coop_kernel<T, kFastNC, kFastNL, kFastNP, kFastG, 2, KPS>,             \
+                dfa_gather_coop_kernel<T, kFastNC, kFastNL, kFastNP, kFastG, 4, KPS>,             \
+                dfa_gather_coop_kernel<T, kFastNC, kFastNL, kFastNP, kFastG, 8, KPS>)
     if (p.kps_anchor != nullptr) {
       if (bf)
         S4D_WARP_FAMILY(__nv_bfloat16, true);
