@@ -8,9 +8,10 @@ One step = six stacked DFA layers (different weights, anchors refined between la
 layer's output feeding the next) over a batch of 32 frames per GPU at the Sparse4D v3 R50
 shape: 900 anchors x 13 keypoints x 6 cameras x 4 levels x 256 channels, bf16 channels-last
 maps of a 704x256 image, fp32 accumulation.  Each layer runs through the drop-in
-``DeformableFeatureAggregation.run`` (cuBLAS linears + the keypoint kernel + the fused
-softmax/gather kernel).  Frames shard across GPUs with no collective in the timed region
-(weak scaling: 32 frames per GPU).
+``DeformableFeatureAggregation.run`` (this library's tensor-core weights_fc and output_proj,
+the camera kernels and the fused keypoint + softmax + gather kernel), the 6 layers captured
+as one CUDA graph.  Frames shard across GPUs with no collective in the timed region (weak
+scaling: 32 frames per GPU).
 
 Printed (rank 0, one JSON line): DFA calls/s for the whole job (calls = frames x layers),
 the gather kernel's roofline (algorithmic bytes per launch over its CUDA-event duration,
@@ -703,7 +704,7 @@ def highres_leg(rank, world, device, pg, steps, warmup):
       (launched eagerly).  Rank 0 checks its shard against the same layer on one GPU;
     * camera-sharded p2p (N >= 2): the same grid and rows with no collective kernel: each
       rank's output_proj reads the other GPU's partial sums over NVLink after a bounded flag
-      exchange and adds them in its accumulator.
+      exchange and adds them in its accumulator; launched eagerly and as one CUDA graph.
 
     Every rank runs every step; the times are device times, max over ranks."""
     import torch.distributed as dist
@@ -771,6 +772,13 @@ def highres_leg(rank, world, device, pg, steps, warmup):
             for _ in range(warmup):
                 w.step()
             ms = max_ms(time_steps(w.step, steps, barrier))
+            graph_ms = None
+            if reduce == "p2p":  # no collective kernel in the call: it can be captured in a CUDA graph
+                stack = w.graph_stack()
+                for _ in range(warmup):
+                    stack.replay()
+                graph_ms = max_ms(time_steps(stack.replay, steps, barrier))
+                del stack
             # parity: this rank's shard against the same layer on this GPU alone
             out = w.step()
             b, e = w.mods[0].shard
@@ -785,9 +793,10 @@ def highres_leg(rank, world, device, pg, steps, warmup):
             stats = torch.tensor([err, -pcc, flag], device=device)
             if pg is not None:
                 pg.all_reduce(stats, op=pg.ReduceOp.MAX)
+            calls = fpg * (world // 2) * steps
             res[key] = {
                 "grid": f"{world // 2} frame groups x 2 camera halves (3 cameras per rank)", "frames_per_group": fpg,
-                "value": fpg * (world // 2) * steps / (ms / 1e3), "unit": UNIT, "ms_per_step": ms / steps,
+                "value": calls / (ms / 1e3), "unit": UNIT, "ms_per_step": ms / steps,
                 **extra, "group_size": dist.get_world_size(cgroup),
                 "bytes_to_peer_per_rank": rows // 2 * 256 * 4,
                 "launch": "eager (DeformableFeatureAggregation.run per step)",
@@ -795,6 +804,10 @@ def highres_leg(rank, world, device, pg, steps, warmup):
                            "against": "the same layer on one GPU (all 6 cameras), each rank's rows of the output; "
                                       "max over ranks"},
             }
+            if graph_ms is not None:
+                res[key]["graph"] = {"value": calls / (graph_ms / 1e3), "ms_per_step": graph_ms / steps,
+                                     "launch": "the layer as one CUDA graph (DFAStack) per step, both exchanges and "
+                                               "output_proj_sum inside it"}
             if peer is not None:
                 res[key]["peer_timeout_flag"] = int(stats[2])
                 peer.close()

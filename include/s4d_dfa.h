@@ -447,6 +447,12 @@ S4D_API int s4d_dfa_output_proj_sum(const float* features, const float* features
  *                        S4D_FLAG_PEER_TIMEOUT into error_flag and returns.  1 <= world <= 8.
  *                        Every rank must call it with the same epoch sequence; the ranks must be
  *                        on different GPUs (waiting launches on one GPU may never run together).
+ * s4d_peer_signal_wait_counter
+ *                        the same with the epoch kept on the device: epoch = *epoch_counter +
+ *                        advance (advance 0 or 1), read when the launch runs, and stored back in
+ *                        *epoch_counter when advance is 1; so a CUDA graph that captured the call
+ *                        moves to the next epoch at every replay.  epoch_counter is a device u32
+ *                        of this rank, zero before the first call.
  */
 S4D_API size_t s4d_ipc_handle_bytes(void);
 S4D_API int s4d_ipc_export(const void* ptr, void* handle, uint64_t* offset);
@@ -454,6 +460,9 @@ S4D_API int s4d_ipc_open(const void* handle, void** base);
 S4D_API int s4d_ipc_close(void* base);
 S4D_API int s4d_peer_signal_wait(uint32_t* own_slots, uint32_t* const* peer_slots, int rank, int world,
                                  uint32_t epoch, uint64_t limit_ns, int32_t* error_flag, void* stream);
+S4D_API int s4d_peer_signal_wait_counter(uint32_t* own_slots, uint32_t* const* peer_slots, int rank, int world,
+                                         uint32_t* epoch_counter, int advance, uint64_t limit_ns,
+                                         int32_t* error_flag, void* stream);
 
 #ifdef __cplusplus
 }

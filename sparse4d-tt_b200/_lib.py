@@ -76,6 +76,7 @@ SIGNATURES = {
     "s4d_ipc_open": (_int, [_p, C.POINTER(C.c_void_p)]),
     "s4d_ipc_close": (_int, [_p]),
     "s4d_peer_signal_wait": (_int, [_p, _p, _int, _int, C.c_uint32, C.c_uint64, _p, _p]),
+    "s4d_peer_signal_wait_counter": (_int, [_p, _p, _int, _int, _p, _int, C.c_uint64, _p, _p]),
 }
 
 _lib = None
@@ -91,7 +92,7 @@ class S4DError(RuntimeError):
 
 
 # Version of include/s4d_dfa.h these bindings are written for (s4d_abi_version()).
-ABI_VERSION = 105
+ABI_VERSION = 106
 
 
 def lib():

@@ -124,17 +124,20 @@ def _export(t: torch.Tensor) -> Tuple[bytes, int]:
 
 
 class PeerPartialSums:
-    """Partial-sum buffers of a 2-rank camera group, shared over CUDA IPC (``CAMERA_REDUCE="p2p"``).
+    """Partial-sum buffer of a 2-rank camera group, shared over CUDA IPC (``CAMERA_REDUCE="p2p"``).
 
-    Each rank owns two ``[capacity, C]`` fp32 buffers -- alternate calls use alternate buffers,
-    so a rank's next gather never overwrites what the other rank may still be reading -- and a
-    slot array in which the other rank publishes its epoch.  Per call: the gather writes
-    ``current()``; ``exchange()`` launches the bounded flag exchange on the current stream and
-    returns the device address of the other rank's buffer of the same call, for
-    ``ops.output_proj_sum_into``.  Construction and ``close()`` are collective over the group;
-    the two ranks must be on different GPUs (their waits must run at the same time).  A wait
-    that gives up after ``limit_ns`` sets ``S4D_FLAG_PEER_TIMEOUT`` in ``error_flag``
-    (``check()`` reads it)."""
+    Each rank owns one ``[capacity, C]`` fp32 buffer, two slot arrays in which the other rank
+    publishes its epochs (partial sums ready; the other rank's buffer consumed) and a device
+    epoch counter.  Per call: ``begin()`` launches the "consumed" exchange (this rank has
+    finished reading the other's buffer of the previous call, and waits until the other rank
+    has finished reading this one's) and returns the buffer view the gather writes; after the
+    gather, ``exchange()`` launches the "ready" exchange and returns the device address of the
+    other rank's buffer, for ``ops.output_proj_sum_into``.  The epochs live on the device
+    (``s4d_peer_signal_wait_counter``), so a CUDA graph that captured a call replays correctly,
+    and eager calls and replays may be mixed, as long as both ranks make the same sequence of
+    calls.  Construction and ``close()`` are collective over the group; the two ranks must be on
+    different GPUs (their waits must run at the same time).  A wait that gives up after
+    ``limit_ns`` sets ``S4D_FLAG_PEER_TIMEOUT`` in ``error_flag`` (``check()`` reads it)."""
 
     def __init__(self, capacity: int, channels: int, group: dist.ProcessGroup, device: torch.device,
                  limit_ns: int = 2_000_000_000) -> None:
@@ -147,13 +150,14 @@ class PeerPartialSums:
         self.peer = 1 - self.rank
         self.capacity, self.channels = int(capacity), int(channels)
         self.limit_ns = int(limit_ns)
-        self.bufs = [torch.empty(self.capacity, channels, dtype=torch.float32, device=self.device) for _ in range(2)]
-        self.slots = torch.zeros(8, dtype=torch.int32, device=self.device)
+        self.buf = torch.empty(self.capacity, channels, dtype=torch.float32, device=self.device)
+        # slots [0:8] ready epochs, [8:16] consumed epochs (slot r written by rank r), [16] the
+        # epoch counter (calls whose ready exchange has run)
+        self.slots = torch.zeros(24, dtype=torch.int32, device=self.device)
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self.epoch = 0
         torch.cuda.synchronize(self.device)  # the zeroed slots are in place before the peer can write them
         uuid = str(torch.cuda.get_device_properties(self.device).uuid)
-        mine = (uuid, [_export(t) for t in (*self.bufs, self.slots)])
+        mine = (uuid, [_export(t) for t in (self.buf, self.slots)])
         everyone: List = [None, None]
         dist.all_gather_object(everyone, mine, group=group)
         peer_uuid, peer_entries = everyone[self.peer]
@@ -167,28 +171,35 @@ class PeerPartialSums:
                 L.check("ipc_open", L.lib().s4d_ipc_open(handle, ctypes.byref(base)))
                 self._bases[handle] = int(base.value)
             ptrs.append(self._bases[handle] + offset)
-        self.peer_bufs, self.peer_slots = ptrs[:2], ptrs[2]
-        self._slot_array = (ctypes.c_void_p * 8)()
-        self._slot_array[self.peer] = self.peer_slots
+        self.peer_buf, peer_slots = ptrs
+        self._ready = (ctypes.c_void_p * 8)()
+        self._ready[self.peer] = peer_slots
+        self._consumed = (ctypes.c_void_p * 8)()
+        self._consumed[self.peer] = peer_slots + 8 * 4
 
-    def current(self, rows: int) -> torch.Tensor:
-        """``[rows, C]`` view of this call's buffer (the gather's output)."""
-        if rows > self.capacity:
-            raise ValueError(f"{rows} rows exceed the shared buffers' {self.capacity}")
-        return self.bufs[self.epoch & 1][:rows]
-
-    def exchange(self) -> int:
-        """Launch the flag exchange of this call on the current stream; returns the address of the
-        other rank's buffer of the same call."""
+    def _signal(self, own_offset: int, peers, advance: int) -> None:
         from . import _lib as L
 
-        idx = self.epoch & 1
-        self.epoch += 1
-        st = L.lib().s4d_peer_signal_wait(self.slots.data_ptr(), ctypes.cast(self._slot_array, ctypes.c_void_p),
-                                          self.rank, 2, self.epoch & 0xFFFFFFFF, self.limit_ns,
-                                          self.error_flag.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
-        L.check("peer_signal_wait", st)
-        return self.peer_bufs[idx]
+        base = self.slots.data_ptr()
+        st = L.lib().s4d_peer_signal_wait_counter(base + own_offset * 4, ctypes.cast(peers, ctypes.c_void_p),
+                                                  self.rank, 2, base + 16 * 4, advance, self.limit_ns,
+                                                  self.error_flag.data_ptr(),
+                                                  torch.cuda.current_stream(self.device).cuda_stream)
+        L.check("peer_signal_wait_counter", st)
+
+    def begin(self, rows: int) -> torch.Tensor:
+        """Launch this call's "consumed" exchange; returns the ``[rows, C]`` view of the buffer
+        the gather may now overwrite."""
+        if rows > self.capacity:
+            raise ValueError(f"{rows} rows exceed the shared buffer's {self.capacity}")
+        self._signal(8, self._consumed, 0)
+        return self.buf[:rows]
+
+    def exchange(self) -> int:
+        """Launch this call's "ready" exchange (after the gather) on the current stream; returns
+        the address of the other rank's buffer."""
+        self._signal(0, self._ready, 1)
+        return self.peer_buf
 
     def check(self) -> None:
         """Raise if a wait gave up (synchronises with the device)."""
@@ -196,6 +207,10 @@ class PeerPartialSums:
 
         if int(self.error_flag.item()) & L.S4D_FLAG_PEER_TIMEOUT:
             raise RuntimeError("peer_signal_wait gave up waiting for the other rank of the camera group")
+
+    def epochs(self) -> int:
+        """Calls whose ready exchange has run on this rank (synchronises with the device)."""
+        return int(self.slots[16].item())
 
     def close(self) -> None:
         """Collective: both ranks finish their work, then unmap the other's buffers."""

@@ -11,6 +11,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 
@@ -42,7 +43,9 @@ struct SignalParams {
   uint32_t* own;               // [world] slots of this GPU, slot r written by rank r
   uint32_t* peer[kMaxPeers];   // rank r's slot array (mapped from its GPU); this rank's entry unused
   int rank, world;
-  uint32_t epoch;
+  uint32_t epoch;              // used when counter is null
+  uint32_t* counter;           // or: epoch = *counter + advance, read when the launch runs
+  int advance;                 // 0 or 1; with 1 the launch stores the new epoch back in *counter
   unsigned long long limit_ns;
   int32_t* error_flag;
 };
@@ -70,11 +73,15 @@ __device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
 // epoch.  The wait gives up after limit_ns, sets S4D_FLAG_PEER_TIMEOUT and returns.
 __global__ void peer_signal_wait_kernel(const SignalParams p) {
   const int r = int(threadIdx.x);
+  // a device-side epoch (counter) lets a CUDA graph replay the launch: every replay advances it
+  const uint32_t epoch = p.counter != nullptr ? *p.counter + uint32_t(p.advance) : p.epoch;
+  __syncthreads();  // every thread has read the counter
+  if (r == 0 && p.counter != nullptr && p.advance) *p.counter = epoch;
   if (r >= p.world || r == p.rank) return;
   asm volatile("fence.acq_rel.sys;" ::: "memory");
-  store_release_sys(p.peer[r] + p.rank, p.epoch);
+  store_release_sys(p.peer[r] + p.rank, epoch);
   const unsigned long long t0 = timer_ns();
-  while (int32_t(load_acquire_sys(p.own + r) - p.epoch) < 0) {
+  while (int32_t(load_acquire_sys(p.own + r) - epoch) < 0) {
     if (timer_ns() - t0 > p.limit_ns) {
       if (p.error_flag != nullptr) atomicOr(p.error_flag, S4D_FLAG_PEER_TIMEOUT);
       return;
@@ -128,29 +135,61 @@ int s4d_ipc_close(void* base) {
   return cuda_check(cudaIpcCloseMemHandle(base), "s4d_ipc_close: cudaIpcCloseMemHandle");
 }
 
-int s4d_peer_signal_wait(uint32_t* own_slots, uint32_t* const* peer_slots, int rank, int world, uint32_t epoch,
-                         uint64_t limit_ns, int32_t* error_flag, void* stream) {
-  set_error("%s", "");
-  if (world < 1 || world > kMaxPeers) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_peer_signal_wait: world must be 1..8");
-  if (rank < 0 || rank >= world) return fail(S4D_ERR_INVALID_ARG, "s4d_peer_signal_wait: rank outside [0, world)");
-  if (own_slots == nullptr || peer_slots == nullptr) return fail(S4D_ERR_INVALID_ARG, "s4d_peer_signal_wait: null pointer");
-  if (!aligned(own_slots, 4)) return fail(S4D_ERR_INVALID_ARG, "s4d_peer_signal_wait: misaligned slots");
+}  // extern "C"
+
+namespace {
+
+int signal_wait(const char* fn, uint32_t* own_slots, uint32_t* const* peer_slots, int rank, int world, uint32_t epoch,
+                uint32_t* counter, int advance, uint64_t limit_ns, int32_t* error_flag, void* stream) {
+  char msg[128];
+  auto bad = [&](int status, const char* what) {
+    snprintf(msg, sizeof(msg), "%s: %s", fn, what);
+    return fail(status, msg);
+  };
+  if (world < 1 || world > kMaxPeers) return bad(S4D_ERR_UNSUPPORTED_SHAPE, "world must be 1..8");
+  if (rank < 0 || rank >= world) return bad(S4D_ERR_INVALID_ARG, "rank outside [0, world)");
+  if (own_slots == nullptr || peer_slots == nullptr) return bad(S4D_ERR_INVALID_ARG, "null pointer");
+  if (!aligned(own_slots, 4)) return bad(S4D_ERR_INVALID_ARG, "misaligned slots");
+  if (advance != 0 && advance != 1) return bad(S4D_ERR_INVALID_ARG, "advance must be 0 or 1");
+  if (counter != nullptr && !aligned(counter, 4)) return bad(S4D_ERR_INVALID_ARG, "misaligned epoch counter");
   SignalParams p{};
   p.own = own_slots;
   for (int r = 0; r < world; ++r) {
     if (r == rank) continue;
     if (peer_slots[r] == nullptr || !aligned(peer_slots[r], 4))
-      return fail(S4D_ERR_INVALID_ARG, "s4d_peer_signal_wait: null or misaligned peer slots");
+      return bad(S4D_ERR_INVALID_ARG, "null or misaligned peer slots");
     p.peer[r] = peer_slots[r];
   }
-  if (world == 1) return S4D_OK;
+  if (world == 1 && (counter == nullptr || !advance)) return S4D_OK;
   p.rank = rank;
   p.world = world;
   p.epoch = epoch;
+  p.counter = counter;
+  p.advance = advance;
   p.limit_ns = limit_ns;
   p.error_flag = error_flag;
   peer_signal_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return cuda_check(cudaGetLastError(), "peer_signal_wait_kernel launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+int s4d_peer_signal_wait(uint32_t* own_slots, uint32_t* const* peer_slots, int rank, int world, uint32_t epoch,
+                         uint64_t limit_ns, int32_t* error_flag, void* stream) {
+  set_error("%s", "");
+  return signal_wait("s4d_peer_signal_wait", own_slots, peer_slots, rank, world, epoch, nullptr, 0, limit_ns,
+                     error_flag, stream);
+}
+
+int s4d_peer_signal_wait_counter(uint32_t* own_slots, uint32_t* const* peer_slots, int rank, int world,
+                                 uint32_t* epoch_counter, int advance, uint64_t limit_ns, int32_t* error_flag,
+                                 void* stream) {
+  set_error("%s", "");
+  if (epoch_counter == nullptr) return fail(S4D_ERR_INVALID_ARG, "s4d_peer_signal_wait_counter: null epoch counter");
+  return signal_wait("s4d_peer_signal_wait_counter", own_slots, peer_slots, rank, world, 0, epoch_counter, advance,
+                     limit_ns, error_flag, stream);
 }
 
 }  // extern "C"

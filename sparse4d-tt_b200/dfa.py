@@ -375,14 +375,20 @@ class DeformableFeatureAggregation:
             cam_begin, cam_end = rank_camera_range(self.num_cams, self.process_group)
         p2p = self.process_group is not None and self.camera_reduce == "p2p"
         if p2p:
-            # the gather writes straight into the buffer the other rank reads over NVLink
+            # the gather writes straight into the buffer the other rank reads over NVLink, once the
+            # other rank has finished reading it (begin); the exchanges keep their epochs on the
+            # device, so the call can be captured in a CUDA graph
             if self._peer is None or self._peer.capacity < rows:
                 from .camera_shard import PeerPartialSums
+
+                if torch.cuda.is_current_stream_capturing():
+                    raise RuntimeError("CAMERA_REDUCE='p2p': run the module once eagerly (on both ranks, with "
+                                       "this batch size or larger) before capturing it in a CUDA graph")
 
                 if self._peer is not None:
                     self._peer.close()
                 self._peer = PeerPartialSums(rows, self.embed_dims, self.process_group, dev)
-            feats = self._peer.current(rows).view(bs, num_anchor, self.embed_dims)
+            feats = self._peer.begin(rows).view(bs, num_anchor, self.embed_dims)
         else:
             feats = torch.empty(bs, num_anchor, self.embed_dims, dtype=torch.float32, device=dev)
         logits = logits.contiguous()

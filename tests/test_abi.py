@@ -33,7 +33,7 @@ def lib():
 
 def test_every_declared_symbol_is_exported(lib):
     names = declared_functions()
-    assert len(names) == 27, names
+    assert len(names) == 28, names
     for n in names:
         assert hasattr(lib, n), n
         assert n in L.SIGNATURES, f"{n} has no ctypes signature"
@@ -52,7 +52,7 @@ def test_status_strings_and_version(lib):
     assert L.status_string(0) == "S4D_OK"
     assert L.status_string(2) == "S4D_ERR_UNSUPPORTED_SHAPE"
     assert L.status_string(99) == "S4D_ERR_UNKNOWN"
-    assert lib.s4d_abi_version() == 105 == L.ABI_VERSION
+    assert lib.s4d_abi_version() == 106 == L.ABI_VERSION
 
 
 def test_dfa_workspace_bytes(lib):
@@ -465,3 +465,14 @@ def test_peer_entry_points_reject_on_host(lib):
     base = C.c_void_p()
     assert lib.s4d_ipc_open(None, C.byref(base)) == L.S4D_ERR_INVALID_ARG
     assert lib.s4d_ipc_close(None) == L.S4D_ERR_INVALID_ARG
+    # the device-epoch variant
+    st = lib.s4d_peer_signal_wait_counter(64, arr, 0, 2, None, 1, 1000, None, None)
+    assert st == L.S4D_ERR_INVALID_ARG and "epoch counter" in lib.s4d_last_error().decode()
+    st = lib.s4d_peer_signal_wait_counter(64, arr, 0, 2, 66, 1, 1000, None, None)
+    assert st == L.S4D_ERR_INVALID_ARG and "misaligned epoch counter" in lib.s4d_last_error().decode()
+    st = lib.s4d_peer_signal_wait_counter(64, arr, 0, 2, 128, 2, 1000, None, None)
+    assert st == L.S4D_ERR_INVALID_ARG and "advance" in lib.s4d_last_error().decode()
+    st = lib.s4d_peer_signal_wait_counter(64, arr, 3, 2, 128, 1, 1000, None, None)
+    assert st == L.S4D_ERR_INVALID_ARG and "s4d_peer_signal_wait_counter: rank" in lib.s4d_last_error().decode()
+    # one rank, no advance: nothing to publish, wait for or count
+    assert lib.s4d_peer_signal_wait_counter(64, arr, 0, 1, 128, 0, 1000, None, None) == L.S4D_OK

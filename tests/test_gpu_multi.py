@@ -95,6 +95,7 @@ def _p2p_worker(rank, world, port, out_dir):
 
     from sparse4d_tt_b200 import DeformableFeatureAggregation, ops
     from sparse4d_tt_b200 import synthetic as syn
+    from sparse4d_tt_b200.graph import capture
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dev = torch.device(f"cuda:{rank}")
@@ -110,27 +111,57 @@ def _p2p_worker(rank, world, port, out_dir):
         rs = DeformableFeatureAggregation(dev, params, dict(cfg_tc, CAMERA_REDUCE="reduce_scatter"),
                                           mesh_device=dist.group.WORLD)
         single = DeformableFeatureAggregation(dev, params, cfg_tc)
-        errs, rs_errs = [], []
-        # five calls with new inputs each: both buffers of the double-buffered exchange, reused
-        for call in range(5):
-            ins = syn.make_inputs(cfg, 60 + call, feature_dtype=torch.bfloat16)
+
+        def inputs(seed):
+            ins = syn.make_inputs(cfg, seed, feature_dtype=torch.bfloat16)
             packed = ops.pack_feature_maps([m.to(dev) for m in ins.feature_maps], dtype=torch.bfloat16)
-            args = (ins.instance_feature.to(dev), ins.anchor.to(dev), ins.anchor_embed.to(dev), packed,
-                    ins.projection_mat.to(dev), ins.image_wh.to(dev), cfg.spatial_shapes, 2, 900)
-            for m in (p2p, rs, single):
-                m._cached_camera_embed = m._cached_camera_logits = None
-                m._cached_camera_ws = m._cached_camera_factors = None
-            got = p2p.run(*args)
+            return [ins.instance_feature.to(dev), ins.anchor.to(dev), ins.anchor_embed.to(dev), packed,
+                    ins.projection_mat.to(dev), ins.image_wh.to(dev)]
+
+        def reference(args):
+            single.reset_frame_cache()
+            rs.reset_frame_cache()
+            ref = single.run(*args, cfg.spatial_shapes, 2, 900).reshape(-1, 512)
+            other = rs.run(*args, cfg.spatial_shapes, 2, 900)
+            return ref, other
+
+        errs, rs_errs = [], []
+        # eager calls with new inputs each: the single buffer rewritten call after call
+        for call in range(3):
+            args = inputs(60 + call)
+            p2p.reset_frame_cache()
+            got = p2p.run(*args, cfg.spatial_shapes, 2, 900)
             b, e = p2p.shard
-            ref = single.run(*args).reshape(-1, 512)[b:e]
-            other = rs.run(*args)
+            ref, other = reference(args)
             torch.cuda.synchronize()
-            errs.append(((got - ref).abs().max() / ref.abs().max()).item())
+            errs.append(((got - ref[b:e]).abs().max() / ref[b:e].abs().max()).item())
+            rs_errs.append(((got - other).abs().max() / other.abs().max()).item())
+        # the same call captured in a CUDA graph and replayed with new inputs copied in
+        static = inputs(70)
+
+        def fn():
+            p2p.reset_frame_cache()
+            return p2p.run(*static, cfg.spatial_shapes, 2, 900)
+
+        call = capture(fn, warmup=2)
+        for rep in range(3):
+            fresh = inputs(80 + rep)
+            for dst, src in zip(static, fresh):
+                if isinstance(dst, tuple):
+                    dst[0].copy_(src[0])
+                else:
+                    dst.copy_(src)
+            got = call.replay()
+            b, e = p2p.shard
+            ref, other = reference(fresh)
+            torch.cuda.synchronize()
+            errs.append(((got - ref[b:e]).abs().max() / ref[b:e].abs().max()).item())
             rs_errs.append(((got - other).abs().max() / other.abs().max()).item())
         p2p._peer.check()
         np.savez(os.path.join(out_dir, f"p2p{rank}.npz"), rel=np.array(errs), rel_rs=np.array(rs_errs),
-                 shard=np.array(p2p.shard), shape=np.array(got.shape), epoch=np.array(p2p._peer.epoch),
+                 shard=np.array(p2p.shard), shape=np.array(got.shape), epoch=np.array(p2p._peer.epochs()),
                  flag=np.array(p2p._peer.error_flag.item()))
+        del call
         p2p._peer.close()
         dist.barrier()
     finally:
@@ -139,11 +170,14 @@ def _p2p_worker(rank, world, port, out_dir):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_camera_sharded_p2p_matches_single_gpu():
+    """Three eager calls, then the call captured in a CUDA graph (two warm-up calls) and replayed
+    three times with new inputs: every result equals the single-GPU layer's rows of this rank."""
     out_dir = tempfile.mkdtemp()
     mp.start_processes(_p2p_worker, args=(2, _free_port(), out_dir), nprocs=2, start_method="spawn")
     for r in range(2):
         g = np.load(os.path.join(out_dir, f"p2p{r}.npz"))
-        assert int(g["flag"]) == 0 and int(g["epoch"]) == 5
+        # 3 eager calls + 2 warm-up calls + 3 replays, one ready exchange each
+        assert int(g["flag"]) == 0 and int(g["epoch"]) == 8
         assert g["shard"].tolist() == [r * 900, (r + 1) * 900] and g["shape"].tolist() == [900, 512]
         # the same partial sums, added inside the accumulator instead of before it
         assert float(np.max(g["rel"])) <= 1e-4, g["rel"]
