@@ -703,8 +703,9 @@ def highres_leg(rank, world, device, pg, steps, warmup):
       reduce-scatter over the flattened (frame, anchor) rows, and each rank projects its half
       (launched eagerly).  Rank 0 checks its shard against the same layer on one GPU;
     * camera-sharded p2p (N >= 2): the same grid and rows with no collective kernel: each
-      rank's output_proj reads the other GPU's partial sums over NVLink after a bounded flag
-      exchange and adds them in its accumulator; launched eagerly and as one CUDA graph.
+      rank's gather writes the other rank's rows straight into that GPU's memory over NVLink,
+      and after a bounded flag exchange output_proj adds the two partial sums in its
+      accumulator; launched eagerly and as one CUDA graph.
 
     Every rank runs every step; the times are device times, max over ranks."""
     import torch.distributed as dist
@@ -761,9 +762,10 @@ def highres_leg(rank, world, device, pg, steps, warmup):
                            "then output_proj on this rank's rows"}),
             "camera_sharded_p2p": ("p2p", {
                 "collective": None,
-                "combine": "no collective kernel: a bounded flag exchange over NVLink, then output_proj reads this "
-                           "rank's rows of its own partial sums and of the other GPU's (over NVLink, CUDA IPC "
-                           "mapping) and adds them in the tensor-core accumulator (s4d_dfa_output_proj_sum)"}),
+                "combine": "no collective kernel: each rank's gather writes the other rank's rows of its partial "
+                           "sums straight into that rank's memory over NVLink (CUDA IPC mapping) as it produces "
+                           "them; after a bounded flag exchange, output_proj sums this rank's own and received "
+                           "partial sums, both local, in the tensor-core accumulator (s4d_dfa_output_proj_sum)"}),
         }
         for key, (reduce, extra) in modes.items():
             mc = dict(MODEL_CONFIG, CAMERA_REDUCE=reduce)

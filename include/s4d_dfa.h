@@ -329,6 +329,29 @@ S4D_API int s4d_deformable_aggregation_anchors(const void* mc_ms_feat, int feat_
                                                int64_t cam_begin, int64_t cam_end, float* out, int32_t* error_flag,
                                                void* workspace, size_t workspace_bytes, void* stream);
 
+/* s4d_deformable_aggregation_anchors with its output rows routed: the flattened (frame, anchor)
+ * rows in [peer_row_begin, peer_row_end) are written to out_peer + row * C (the other GPU's
+ * receive buffer of a camera-sharded pair, mapped by s4d_ipc_open, [bs * A, C] rows with the
+ * same indexing as out), the others to out.  So the partial sums the other GPU projects cross
+ * NVLink as the gather produces them, and that GPU's s4d_dfa_output_proj_sum reads both of its
+ * sources from its own memory.  Every block fences its stores at system scope before it exits;
+ * the flag exchange that follows (s4d_peer_signal_wait*) orders them before the other GPU's
+ * reads.  out and out_peer 16-byte aligned when rows are routed; an empty range routes nothing.
+ * Replaces the mesh all_reduce of the partial sums (model/deformable_feature_aggregation.py:
+ * 925-931) for the transfer half. */
+S4D_API int s4d_deformable_aggregation_anchors_peer(const void* mc_ms_feat, int feat_dtype, int64_t num_feat,
+                                                    const int32_t* spatial_shape, const int32_t* scale_start_index,
+                                                    const float* anchor, int64_t anchor_dim, const float* fix_scale,
+                                                    int64_t num_fix, const float* learnable,
+                                                    const float* projection_mat, const float* image_wh,
+                                                    const float* weights, const float* weights_cam, int64_t bs,
+                                                    int64_t num_anchor, int64_t num_cams, int64_t num_levels,
+                                                    int64_t num_pts, int64_t num_groups, int64_t embed_dims,
+                                                    int64_t cam_begin, int64_t cam_end, float* out, float* out_peer,
+                                                    int64_t peer_row_begin, int64_t peer_row_end,
+                                                    int32_t* error_flag, void* workspace, size_t workspace_bytes,
+                                                    void* stream);
+
 /* Bytes of the optional workspace of s4d_deformable_aggregation (split logits only: the
  * per-frame camera softmax factors, bs * (Ncam + 1) * L * P * G floats rounded up to 16 bytes,
  * then 16 bytes for the gather's anchor counter; 0 otherwise).  Host-only, launches nothing. */

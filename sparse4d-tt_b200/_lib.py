@@ -59,6 +59,9 @@ SIGNATURES = {
     "s4d_deformable_aggregation_anchors": (_int, [_p, _int, _i64, _p, _p, _p, _i64, _p, _i64, _p, _p, _p, _p, _p,
                                                   _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                                   _p, _p, _p, _sz, _p]),
+    "s4d_deformable_aggregation_anchors_peer": (_int, [_p, _int, _i64, _p, _p, _p, _i64, _p, _i64, _p, _p, _p, _p,
+                                                       _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                                       _p, _p, _i64, _i64, _p, _p, _sz, _p]),
     "s4d_dfa_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _int]),
     "s4d_dfa_camera_factors": (_int, [_p, _i64, _i64, _i64, _i64, _i64, _p, _sz, _p]),
     "s4d_dfa_weights_fc": (_int, [_p, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _p]),
@@ -92,7 +95,7 @@ class S4DError(RuntimeError):
 
 
 # Version of include/s4d_dfa.h these bindings are written for (s4d_abi_version()).
-ABI_VERSION = 106
+ABI_VERSION = 107
 
 
 def lib():

@@ -22,10 +22,11 @@ Two ways to combine the partial sums (``DeformableFeatureAggregation``'s
   frames when ``n`` divides ``bs``), half the bytes of the all-reduce on the wire, and runs
   ``output_proj`` on its shard only (``shard_rows``);
 * ``"p2p"`` (groups of 2 GPUs, tensor-core linears) -- the same row shards without a collective
-  kernel: each rank's gather writes its partial sums into a buffer the other rank has mapped
-  (``PeerPartialSums``, CUDA IPC), a bounded flag exchange over NVLink orders the two GPUs, and
-  ``output_proj`` reads its rows of both partial sums -- the peer's over NVLink -- and adds them
-  in the tensor-core accumulator (``s4d_dfa_output_proj_sum``).
+  kernel: each rank's gather writes the other rank's rows of its partial sums straight into that
+  rank's receive buffer over NVLink (``PeerPartialSums``, CUDA IPC; the transfer overlaps the
+  gather), a bounded flag exchange orders the two GPUs, and ``output_proj`` sums its own partial
+  sums and the received ones, both in local memory, in the tensor-core accumulator
+  (``s4d_dfa_output_proj_sum``).
 """
 from __future__ import annotations
 
@@ -124,20 +125,23 @@ def _export(t: torch.Tensor) -> Tuple[bytes, int]:
 
 
 class PeerPartialSums:
-    """Partial-sum buffer of a 2-rank camera group, shared over CUDA IPC (``CAMERA_REDUCE="p2p"``).
+    """Partial-sum buffers of a 2-rank camera group, shared over CUDA IPC (``CAMERA_REDUCE="p2p"``).
 
-    Each rank owns one ``[capacity, C]`` fp32 buffer, two slot arrays in which the other rank
-    publishes its epochs (partial sums ready; the other rank's buffer consumed) and a device
-    epoch counter.  Per call: ``begin()`` launches the "consumed" exchange (this rank has
-    finished reading the other's buffer of the previous call, and waits until the other rank
-    has finished reading this one's) and returns the buffer view the gather writes; after the
-    gather, ``exchange()`` launches the "ready" exchange and returns the device address of the
-    other rank's buffer, for ``ops.output_proj_sum_into``.  The epochs live on the device
-    (``s4d_peer_signal_wait_counter``), so a CUDA graph that captured a call replays correctly,
-    and eager calls and replays may be mixed, as long as both ranks make the same sequence of
-    calls.  Construction and ``close()`` are collective over the group; the two ranks must be on
-    different GPUs (their waits must run at the same time).  A wait that gives up after
-    ``limit_ns`` sets ``S4D_FLAG_PEER_TIMEOUT`` in ``error_flag`` (``check()`` reads it)."""
+    Each rank owns ``part`` (its own partial sums of its own rows) and ``recv`` (the other
+    rank's partial sums of this rank's rows, written by the other rank's gather over NVLink),
+    both ``[capacity, C]`` fp32 rows with the flattened (frame, anchor) indexing; two slot arrays
+    in which the other rank publishes its epochs (partial sums sent; receive buffer free again);
+    and a device epoch counter.  Per call: ``begin()`` launches the "consumed" exchange (this
+    rank has finished reading its ``recv`` of the previous call, and waits until the other rank
+    has finished reading its own, which this call's gather is about to overwrite) and returns the
+    ``part`` view; the gather writes this rank's rows to ``part`` and the other rank's rows to
+    ``peer_recv``; ``exchange()`` launches the "ready" exchange; then ``output_proj`` sums ``part``
+    and ``recv``, both local.  The epochs live on the device (``s4d_peer_signal_wait_counter``),
+    so a CUDA graph that captured a call replays correctly, and eager calls and replays may be
+    mixed, as long as both ranks make the same sequence of calls.  Construction and ``close()``
+    are collective over the group; the two ranks must be on different GPUs (their waits must run
+    at the same time).  A wait that gives up after ``limit_ns`` sets ``S4D_FLAG_PEER_TIMEOUT``
+    in ``error_flag`` (``check()`` reads it)."""
 
     def __init__(self, capacity: int, channels: int, group: dist.ProcessGroup, device: torch.device,
                  limit_ns: int = 2_000_000_000) -> None:
@@ -150,14 +154,15 @@ class PeerPartialSums:
         self.peer = 1 - self.rank
         self.capacity, self.channels = int(capacity), int(channels)
         self.limit_ns = int(limit_ns)
-        self.buf = torch.empty(self.capacity, channels, dtype=torch.float32, device=self.device)
+        self.part = torch.empty(self.capacity, channels, dtype=torch.float32, device=self.device)
+        self.recv = torch.empty(self.capacity, channels, dtype=torch.float32, device=self.device)
         # slots [0:8] ready epochs, [8:16] consumed epochs (slot r written by rank r), [16] the
         # epoch counter (calls whose ready exchange has run)
         self.slots = torch.zeros(24, dtype=torch.int32, device=self.device)
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         torch.cuda.synchronize(self.device)  # the zeroed slots are in place before the peer can write them
         uuid = str(torch.cuda.get_device_properties(self.device).uuid)
-        mine = (uuid, [_export(t) for t in (self.buf, self.slots)])
+        mine = (uuid, [_export(t) for t in (self.recv, self.slots)])
         everyone: List = [None, None]
         dist.all_gather_object(everyone, mine, group=group)
         peer_uuid, peer_entries = everyone[self.peer]
@@ -171,7 +176,7 @@ class PeerPartialSums:
                 L.check("ipc_open", L.lib().s4d_ipc_open(handle, ctypes.byref(base)))
                 self._bases[handle] = int(base.value)
             ptrs.append(self._bases[handle] + offset)
-        self.peer_buf, peer_slots = ptrs
+        self.peer_recv, peer_slots = ptrs
         self._ready = (ctypes.c_void_p * 8)()
         self._ready[self.peer] = peer_slots
         self._consumed = (ctypes.c_void_p * 8)()
@@ -188,18 +193,17 @@ class PeerPartialSums:
         L.check("peer_signal_wait_counter", st)
 
     def begin(self, rows: int) -> torch.Tensor:
-        """Launch this call's "consumed" exchange; returns the ``[rows, C]`` view of the buffer
-        the gather may now overwrite."""
+        """Launch this call's "consumed" exchange; returns the ``[rows, C]`` view of ``part``."""
         if rows > self.capacity:
-            raise ValueError(f"{rows} rows exceed the shared buffer's {self.capacity}")
+            raise ValueError(f"{rows} rows exceed the shared buffers' {self.capacity}")
         self._signal(8, self._consumed, 0)
-        return self.buf[:rows]
+        return self.part[:rows]
 
-    def exchange(self) -> int:
+    def exchange(self) -> torch.Tensor:
         """Launch this call's "ready" exchange (after the gather) on the current stream; returns
-        the address of the other rank's buffer."""
+        ``recv``, which then holds the other rank's partial sums of this rank's rows."""
         self._signal(0, self._ready, 1)
-        return self.peer_buf
+        return self.recv
 
     def check(self) -> None:
         """Raise if a wait gave up (synchronises with the device)."""

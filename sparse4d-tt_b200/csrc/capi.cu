@@ -54,7 +54,7 @@ const char* s4d_status_string(int status) {
 
 const char* s4d_last_error(void) { return g_last_error; }
 
-int s4d_abi_version(void) { return 106; }
+int s4d_abi_version(void) { return 107; }
 
 uint64_t s4d_set_tc_wait_limit_ns(uint64_t limit_ns) {
   const uint64_t prev = g_tc_wait_limit_ns;
@@ -263,7 +263,8 @@ static int gather_entry(const void* mc_ms_feat, int feat_dtype, int64_t num_feat
                         const float* weights, const float* weights_cam, int weights_are_logits, int layout, int64_t bs,
                         int64_t num_anchor, int64_t num_cams, int64_t num_levels, int64_t num_pts,
                         int64_t num_groups, int64_t embed_dims, int64_t cam_begin, int64_t cam_end, float* out,
-                        int32_t* error_flag, void* workspace, size_t workspace_bytes, void* stream) {
+                        int32_t* error_flag, void* workspace, size_t workspace_bytes, void* stream,
+                        float* out_peer = nullptr, int64_t peer_row_begin = 0, int64_t peer_row_end = 0) {
   if (bs < 0 || num_anchor < 0 || num_cams <= 0 || num_levels <= 0 || num_pts <= 0 || num_groups <= 0 ||
       embed_dims <= 0 || num_feat < 0)
     return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: sizes must be positive");
@@ -303,6 +304,10 @@ static int gather_entry(const void* mc_ms_feat, int feat_dtype, int64_t num_feat
     return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: null pointer");
   if (!aligned(mc_ms_feat, 16))
     return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: mc_ms_feat must be 16-byte aligned");
+  if (peer_row_begin < 0 || peer_row_end < peer_row_begin || peer_row_end > anchors)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: need 0 <= peer_row_begin <= peer_row_end <= bs*A");
+  if (peer_row_end > peer_row_begin && (out_peer == nullptr || !aligned(out_peer, 16) || !aligned(out, 16)))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: out_peer null, or out / out_peer not 16-byte aligned");
   if ((kps == nullptr && !aligned(sample_location, 8)) || !aligned(weights, 4) || !aligned(out, 4))
     return fail(S4D_ERR_INVALID_ARG, "s4d_deformable_aggregation: misaligned sample_location/weights/out");
   GatherParams p{};
@@ -314,6 +319,11 @@ static int gather_entry(const void* mc_ms_feat, int feat_dtype, int64_t num_feat
   p.weights = weights;
   p.weights_cam = weights_cam;
   p.out = out;
+  if (peer_row_end > peer_row_begin) {
+    p.out_peer = out_peer;
+    p.peer_row_begin = peer_row_begin;
+    p.peer_row_end = peer_row_end;
+  }
   p.error_flag = error_flag;
   p.bs = (int)bs;
   p.num_anchor = (int)num_anchor;
@@ -361,15 +371,16 @@ int s4d_deformable_aggregation(const void* mc_ms_feat, int feat_dtype, int64_t n
                       num_groups, embed_dims, cam_begin, cam_end, out, error_flag, workspace, workspace_bytes, stream);
 }
 
-int s4d_deformable_aggregation_anchors(const void* mc_ms_feat, int feat_dtype, int64_t num_feat,
-                                       const int32_t* spatial_shape, const int32_t* scale_start_index,
-                                       const float* anchor, int64_t anchor_dim, const float* fix_scale,
-                                       int64_t num_fix, const float* learnable, const float* projection_mat,
-                                       const float* image_wh, const float* weights, const float* weights_cam,
-                                       int64_t bs, int64_t num_anchor, int64_t num_cams, int64_t num_levels,
-                                       int64_t num_pts, int64_t num_groups, int64_t embed_dims, int64_t cam_begin,
-                                       int64_t cam_end, float* out, int32_t* error_flag, void* workspace,
-                                       size_t workspace_bytes, void* stream) {
+int s4d_deformable_aggregation_anchors_peer(const void* mc_ms_feat, int feat_dtype, int64_t num_feat,
+                                            const int32_t* spatial_shape, const int32_t* scale_start_index,
+                                            const float* anchor, int64_t anchor_dim, const float* fix_scale,
+                                            int64_t num_fix, const float* learnable, const float* projection_mat,
+                                            const float* image_wh, const float* weights, const float* weights_cam,
+                                            int64_t bs, int64_t num_anchor, int64_t num_cams, int64_t num_levels,
+                                            int64_t num_pts, int64_t num_groups, int64_t embed_dims,
+                                            int64_t cam_begin, int64_t cam_end, float* out, float* out_peer,
+                                            int64_t peer_row_begin, int64_t peer_row_end, int32_t* error_flag,
+                                            void* workspace, size_t workspace_bytes, void* stream) {
   set_error("%s", "");
   if (!(num_cams == 6 && num_levels == 4 && num_pts == 13 && num_groups == 8))
     return fail(S4D_ERR_UNSUPPORTED_SHAPE,
@@ -389,7 +400,24 @@ int s4d_deformable_aggregation_anchors(const void* mc_ms_feat, int feat_dtype, i
   const GatherAnchors kps{anchor, anchor_dim, fix_scale, num_fix, learnable, projection_mat, image_wh};
   return gather_entry(mc_ms_feat, feat_dtype, num_feat, spatial_shape, scale_start_index, nullptr, &kps, weights,
                       weights_cam, 2, S4D_LAYOUT_CAM_MAJOR, bs, num_anchor, num_cams, num_levels, num_pts,
-                      num_groups, embed_dims, cam_begin, cam_end, out, error_flag, workspace, workspace_bytes, stream);
+                      num_groups, embed_dims, cam_begin, cam_end, out, error_flag, workspace, workspace_bytes, stream,
+                      out_peer, peer_row_begin, peer_row_end);
+}
+
+int s4d_deformable_aggregation_anchors(const void* mc_ms_feat, int feat_dtype, int64_t num_feat,
+                                       const int32_t* spatial_shape, const int32_t* scale_start_index,
+                                       const float* anchor, int64_t anchor_dim, const float* fix_scale,
+                                       int64_t num_fix, const float* learnable, const float* projection_mat,
+                                       const float* image_wh, const float* weights, const float* weights_cam,
+                                       int64_t bs, int64_t num_anchor, int64_t num_cams, int64_t num_levels,
+                                       int64_t num_pts, int64_t num_groups, int64_t embed_dims, int64_t cam_begin,
+                                       int64_t cam_end, float* out, int32_t* error_flag, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  return s4d_deformable_aggregation_anchors_peer(mc_ms_feat, feat_dtype, num_feat, spatial_shape, scale_start_index,
+                                                 anchor, anchor_dim, fix_scale, num_fix, learnable, projection_mat,
+                                                 image_wh, weights, weights_cam, bs, num_anchor, num_cams, num_levels,
+                                                 num_pts, num_groups, embed_dims, cam_begin, cam_end, out, nullptr, 0,
+                                                 0, error_flag, workspace, workspace_bytes, stream);
 }
 
 int s4d_dfa_weights_fc(const float* instance_feature, int64_t instance_ld, const float* anchor_embed,

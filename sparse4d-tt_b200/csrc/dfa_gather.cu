@@ -992,11 +992,13 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
   }
 
   // ---- 3. normalise and store ------------------------------------------------------------------
-  float4* o = reinterpret_cast<float4*>(p.out + anchor_lin * kChannels + lane * 8);
+  float* dst = anchor_lin >= p.peer_row_begin && anchor_lin < p.peer_row_end ? p.out_peer : p.out;
+  float4* o = reinterpret_cast<float4*>(dst + anchor_lin * kChannels + lane * 8);
   o[0] = make_float4(acc[0].x * inv, acc[0].y * inv, acc[1].x * inv, acc[1].y * inv);
   o[1] = make_float4(acc[2].x * inv, acc[2].y * inv, acc[3].x * inv, acc[3].y * inv);
   __syncwarp();  // this anchor's shared-memory state is read before the next one writes it
   }
+  if (p.out_peer != nullptr) __threadfence_system();  // the rows stored to the other GPU are performed
 }
 
 // -----------------------------------------------------------------------------------------------
@@ -1347,11 +1349,13 @@ __global__ void __launch_bounds__(WARPS * 32, (sizeof(T) == 2 ? 28 : 20) / WARPS
         a0 = make_float4(a0.x + b0.x, a0.y + b0.y, a0.z + b0.z, a0.w + b0.w);
         a1 = make_float4(a1.x + b1.x, a1.y + b1.y, a1.z + b1.z, a1.w + b1.w);
       }
-      float4* o = reinterpret_cast<float4*>(p.out + anchor_lin * kChannels + lane * 8);
+      float* dst = anchor_lin >= p.peer_row_begin && anchor_lin < p.peer_row_end ? p.out_peer : p.out;
+      float4* o = reinterpret_cast<float4*>(dst + anchor_lin * kChannels + lane * 8);
       o[0] = make_float4(a0.x * inv, a0.y * inv, a0.z * inv, a0.w * inv);
       o[1] = make_float4(a1.x * inv, a1.y * inv, a1.z * inv, a1.w * inv);
     }
   }
+  if (p.out_peer != nullptr) __threadfence_system();  // the rows stored to the other GPU are performed
 }
 
 
@@ -1494,6 +1498,8 @@ int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream) {
   }
   if (p.kps_anchor != nullptr)  // only the warp kernel computes sample locations; the others read p.loc
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "gather from anchors: needs the split-logit warp path");
+  if (p.out_peer != nullptr)  // output routing exists in the warp kernels only
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "gather output routing: needs the split-logit warp path");
   if (fast_path_ok(p)) {
     if (feat_dtype == S4D_DTYPE_BF16)
       dfa_gather_fast_kernel<__nv_bfloat16, kFastNC, kFastNL, kFastNP, kFastG><<<grid, kGatherThreads, 0, stream>>>(p);

@@ -71,6 +71,11 @@ struct GatherParams {
   const float* kps_learnable;  // [bs * A, (P - kps_num_fix) * 3] logits
   const float* kps_proj;
   const float* kps_wh;
+  // Output routing (warp and cooperative kernels): the rows (flattened anchors) in
+  // [peer_row_begin, peer_row_end) go to out_peer + row * 256 (another GPU's buffer, mapped)
+  // instead of out + row * 256.
+  float* out_peer;
+  int64_t peer_row_begin, peer_row_end;
 };
 
 // Tensor-core linears (linear_tc.cu).  Row strides are in floats.

@@ -179,9 +179,10 @@ class DeformableFeatureAggregation:
         if self.camera_reduce == "p2p" and self.process_group is not None:
             import torch.distributed as dist
 
-            if dist.get_world_size(self.process_group) != 2 or not self._tc:
-                raise ValueError("CAMERA_REDUCE='p2p' needs a camera group of 2 ranks and the tensor-core linears "
-                                 "(MATMUL_PRECISION 'tf32', residual_mode 'cat', 'add' or 'none')")
+            if dist.get_world_size(self.process_group) != 2 or not self._tc or not self.fused_keypoints:
+                raise ValueError("CAMERA_REDUCE='p2p' needs a camera group of 2 ranks, the tensor-core linears "
+                                 "(MATMUL_PRECISION 'tf32', residual_mode 'cat', 'add' or 'none') and the gather "
+                                 "from anchors (6 cameras, 4 levels, 13 points, 8 groups, learnable keypoints)")
         self._peer = None  # camera_shard.PeerPartialSums of the p2p mode, made at the first run
         self._side: Optional[torch.cuda.Stream] = None
         self._side_kps: Optional[torch.cuda.Stream] = None
@@ -375,9 +376,10 @@ class DeformableFeatureAggregation:
             cam_begin, cam_end = rank_camera_range(self.num_cams, self.process_group)
         p2p = self.process_group is not None and self.camera_reduce == "p2p"
         if p2p:
-            # the gather writes straight into the buffer the other rank reads over NVLink, once the
-            # other rank has finished reading it (begin); the exchanges keep their epochs on the
-            # device, so the call can be captured in a CUDA graph
+            # the gather writes this rank's rows into its own buffer and the other rank's rows
+            # straight into that rank's receive buffer over NVLink, once the other rank has
+            # finished reading it (begin); the exchanges keep their epochs on the device, so the
+            # call can be captured in a CUDA graph
             if self._peer is None or self._peer.capacity < rows:
                 from .camera_shard import PeerPartialSums
 
@@ -412,9 +414,15 @@ class DeformableFeatureAggregation:
         if loc is None:  # the camera factors are prepared whenever the shape has the kernel for them
             if not ready:
                 raise RuntimeError("DeformableFeatureAggregation: camera factors missing for the gather from anchors")
+            route = {}
+            if p2p:  # the other rank's rows go straight to its receive buffer
+                from .camera_shard import shard_rows
+
+                mb, me = shard_rows(rows, self.process_group)
+                route = dict(out_peer=self._peer.peer_recv, peer_rows=(me, rows) if mb == 0 else (0, mb))
             ops.deformable_aggregation_anchors_into(feats, mc_ms_feat, spatial_shape, scale_start, anchor,
                                                     self.fix_scale, learn.view(rows, -1), projection_mat, image_wh,
-                                                    logits, logits_cam, ws, cam_begin, cam_end)
+                                                    logits, logits_cam, ws, cam_begin, cam_end, **route)
         else:
             ops.deformable_aggregation_into(feats, mc_ms_feat, spatial_shape, scale_start, loc, logits, True,
                                             logits_cam, cam_begin, cam_end, workspace=ws, factors_ready=ready)
@@ -430,14 +438,14 @@ class DeformableFeatureAggregation:
         if p2p:
             from .camera_shard import shard_rows
 
-            # this rank's rows of (own partial sums + the other rank's, read over NVLink), summed
-            # in output_proj's tensor-core accumulator
+            # this rank's rows of (own partial sums + the other rank's, received during its
+            # gather), summed in output_proj's tensor-core accumulator
             self.shard = b, e = shard_rows(rows, self.process_group)
-            peer = self._peer.exchange()
+            recv = self._peer.exchange()
             width = 2 * C if self.residual_mode == "cat" else C
             out = torch.empty(e - b, width, device=dev)
-            ops.output_proj_sum_into(out, feats2d, peer, b, e - b, self.output_proj_weight, self.output_proj_bias,
-                                     ops.row_view(inst_rows[b:e], C), self.residual_mode,
+            ops.output_proj_sum_into(out, feats2d, recv.data_ptr(), b, e - b, self.output_proj_weight,
+                                     self.output_proj_bias, ops.row_view(inst_rows[b:e], C), self.residual_mode,
                                      error_flag=self._peer.error_flag)
             return out
         if self.process_group is not None:

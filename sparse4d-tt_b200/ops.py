@@ -307,12 +307,18 @@ def deformable_aggregation_anchors_into(out: Tensor, mc_ms_feat: Tensor, spatial
                                         scale_start_index: Tensor, anchor: Tensor, fix_scale: Tensor,
                                         learnable: Optional[Tensor], projection_mat: Tensor, image_wh: Tensor,
                                         weights: Tensor, weights_cam: Tensor, workspace: Tensor, cam_begin: int = 0,
-                                        cam_end: int = -1, error_flag: Optional[Tensor] = None) -> Tensor:
+                                        cam_end: int = -1, error_flag: Optional[Tensor] = None,
+                                        out_peer: Optional[int] = None,
+                                        peer_rows: Tuple[int, int] = (0, 0)) -> Tensor:
     """``deformable_aggregation_into`` with the sample locations computed inside the gather from
     ``anchor [bs, A, D]``, ``fix_scale [num_fix, 3]``, the keypoint logits ``learnable [bs*A,
     (P - num_fix)*3]``, ``projection_mat [bs, Ncam, 4, 4]`` and ``image_wh [bs, Ncam, 2]``
     (the same (u, v) as ``kps_project_into``), for split logits whose camera factors
-    ``camera_factors_into`` already wrote into ``workspace``."""
+    ``camera_factors_into`` already wrote into ``workspace``.
+
+    ``out_peer`` (a device address, e.g. another GPU's buffer mapped by ``PeerPartialSums``) and
+    ``peer_rows = (begin, end)``: the flattened rows in ``[begin, end)`` are written to
+    ``out_peer`` (``[bs*A, C]`` rows, the same indexing as ``out``) instead of ``out``."""
     name = "deformable_aggregation_anchors"
     dev = _require_cuda(name, out, mc_ms_feat, spatial_shape, scale_start_index, anchor, fix_scale, learnable,
                         projection_mat, image_wh, weights, weights_cam, workspace, error_flag)
@@ -342,13 +348,14 @@ def deformable_aggregation_anchors_into(out: Tensor, mc_ms_feat: Tensor, spatial
     _require(learnable is None or learnable.numel() == bs * A * (P - num_fix) * 3,
              f"learnable must hold {(P - num_fix) * 3} logits per anchor")
     ce = nc if cam_end is None or cam_end < 0 else int(cam_end)
-    st = L.lib().s4d_deformable_aggregation_anchors(
+    pb, pe = (int(v) for v in peer_rows)
+    st = L.lib().s4d_deformable_aggregation_anchors_peer(
         mc_ms_feat.data_ptr(), L.S4D_DTYPE_BF16 if mc_ms_feat.dtype == torch.bfloat16 else L.S4D_DTYPE_F32,
         int(mc_ms_feat.shape[1]), spatial_shape.data_ptr(), scale_start_index.data_ptr(), anchor.data_ptr(),
         int(anchor.shape[-1]), fix_scale.data_ptr(), num_fix, _ptr(learnable), projection_mat.data_ptr(),
         image_wh.data_ptr(), weights.data_ptr(), weights_cam.data_ptr(), bs, A, nc, nl, P, G, C, int(cam_begin), ce,
-        out.data_ptr(), _ptr(error_flag), workspace.data_ptr(), workspace.numel() * workspace.element_size(),
-        _stream_ptr(dev))
+        out.data_ptr(), None if out_peer is None else int(out_peer), pb, pe, _ptr(error_flag), workspace.data_ptr(),
+        workspace.numel() * workspace.element_size(), _stream_ptr(dev))
     L.check(name, st)
     return out
 

@@ -33,7 +33,7 @@ def lib():
 
 def test_every_declared_symbol_is_exported(lib):
     names = declared_functions()
-    assert len(names) == 28, names
+    assert len(names) == 29, names
     for n in names:
         assert hasattr(lib, n), n
         assert n in L.SIGNATURES, f"{n} has no ctypes signature"
@@ -52,7 +52,7 @@ def test_status_strings_and_version(lib):
     assert L.status_string(0) == "S4D_OK"
     assert L.status_string(2) == "S4D_ERR_UNSUPPORTED_SHAPE"
     assert L.status_string(99) == "S4D_ERR_UNKNOWN"
-    assert lib.s4d_abi_version() == 106 == L.ABI_VERSION
+    assert lib.s4d_abi_version() == 107 == L.ABI_VERSION
 
 
 def test_dfa_workspace_bytes(lib):
@@ -476,3 +476,21 @@ def test_peer_entry_points_reject_on_host(lib):
     assert st == L.S4D_ERR_INVALID_ARG and "s4d_peer_signal_wait_counter: rank" in lib.s4d_last_error().decode()
     # one rank, no advance: nothing to publish, wait for or count
     assert lib.s4d_peer_signal_wait_counter(64, arr, 0, 1, 128, 0, 1000, None, None) == L.S4D_OK
+
+
+def test_gather_routing_rejects_on_host(lib):
+    """s4d_deformable_aggregation_anchors_peer: the routed row range and out_peer are checked
+    before anything launches."""
+    def call(out_peer, begin, end, out=16):
+        return lib.s4d_deformable_aggregation_anchors_peer(
+            16, 1, 100, 16, 16, 16, 11, 16, 7, 16, 16, 16, 16, 16, 2, 900, 6, 4, 13, 8, 256, 0, 6, out, out_peer,
+            begin, end, None, 64, 1 << 20, None), lib.s4d_last_error().decode()
+    for begin, end in ((-1, 5), (10, 5), (0, 1801)):
+        st, msg = call(32, begin, end)
+        assert st == L.S4D_ERR_INVALID_ARG and "peer_row_begin" in msg, msg
+    st, msg = call(None, 900, 1800)
+    assert st == L.S4D_ERR_INVALID_ARG and "out_peer" in msg, msg
+    st, msg = call(40, 900, 1800)
+    assert st == L.S4D_ERR_INVALID_ARG and "out_peer" in msg, msg
+    st, msg = call(32, 900, 1800, out=20)
+    assert st == L.S4D_ERR_INVALID_ARG and "16-byte" in msg, msg

@@ -159,3 +159,32 @@ def test_split_anchor_blocks_bs1_against_reference_rows(cuda_device):
     logits = oto.weight_logits(ins.instance_feature, ins.anchor_embed, ins.projection_mat, params, 4, 13, 8)
     ref = oto.deformable_aggregation(ins.feature_maps, uv, logits).reshape(900, 256)
     assert pcc(got, ref) >= 0.9999 and max_rel_err(got, ref) <= 1e-2
+
+
+@pytest.mark.parametrize("bs,rows", [(1, (450, 900)), (1, (0, 450)), (3, (900, 2700)), (3, (0, 0))])
+def test_gather_output_routing(cuda_device, bs, rows):
+    """s4d_deformable_aggregation_anchors_peer: rows [begin, end) go to out_peer (here a second
+    buffer on the same GPU), the others to out, each bit for bit the unrouted result; neither
+    buffer is written outside its rows (the cooperative kernel at bs = 1, the warp kernel at
+    bs = 3)."""
+    cfg, t, feat32, shape, start = _case(bs, 90 + bs)
+    feat = feat32.to(torch.bfloat16)
+    d = torch.device("cuda:0")
+    A = cfg.num_anchor
+    ws = ops.camera_factors_into(ops.dfa_workspace(bs, 6, 4, 13, 8, d), t["wc"])
+    args = (feat, shape, start, t["anchor"], t["fix"], t["learn"], t["proj"], t["wh"], t["wa"], t["wc"], ws)
+    ref = torch.empty(bs, A, 256, device=d)
+    ops.deformable_aggregation_anchors_into(ref, *args)
+    out = torch.full((bs, A, 256), float("nan"), device=d)
+    peer = torch.full((bs * A, 256), float("nan"), device=d)
+    flag = torch.zeros(1, dtype=torch.int32, device=d)
+    ops.deformable_aggregation_anchors_into(out, *args, error_flag=flag, out_peer=peer.data_ptr(), peer_rows=rows)
+    torch.cuda.synchronize()
+    assert flag.item() == 0
+    b, e = rows
+    ref2, out2 = ref.view(-1, 256), out.view(-1, 256)
+    inside = torch.zeros(bs * A, dtype=torch.bool, device=d)
+    inside[b:e] = True
+    assert torch.equal(peer[inside], ref2[inside])
+    assert torch.equal(out2[~inside], ref2[~inside])
+    assert torch.isnan(out2[inside]).all() and torch.isnan(peer[~inside]).all()
