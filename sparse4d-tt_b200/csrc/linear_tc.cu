@@ -563,9 +563,16 @@ int make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, in
   return S4D_OK;
 }
 
+// The dynamic shared-memory limit of `kernel`, set once per device (the attribute persists in the
+// context); `done` is the caller's per-instantiation record of the devices already set.
 template <typename K>
-int set_smem(K kernel, size_t bytes, const char* what) {
-  return cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)), what);
+int set_smem(K kernel, size_t bytes, const char* what, bool (&done)[64]) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  if (dev >= 0 && dev < 64 && done[dev]) return S4D_OK;
+  const int st = cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)), what);
+  if (st == S4D_OK && dev >= 0 && dev < 64) done[dev] = true;
+  return st;
 }
 
 // Column groups for launches of few row tiles (1 = always whole rows per CTA).
@@ -573,14 +580,20 @@ int set_smem(K kernel, size_t bytes, const char* what) {
 #define S4D_TC_COLUMN_GROUPS 1
 #endif
 
-// SMs of the current device (148 on B200 if the query fails).
+// SMs of the current device (148 on B200 if the query fails), cached per device.
 int sm_count() {
+  static int cache[64] = {};
   int dev = 0, sms = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-      sms <= 0) {
+  if (cudaGetDevice(&dev) != cudaSuccess) {
     cudaGetLastError();
     return 148;
   }
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+    cudaGetLastError();
+    return 148;
+  }
+  if (dev >= 0 && dev < 64) cache[dev] = sms;
   return sms;
 }
 
@@ -604,7 +617,8 @@ int launch_weights_fc_cols(const WfcParams& p, cudaStream_t stream, int groups) 
   if (st == S4D_OK) st = make_map(&mw, p.w_fc, p.n_logits, p.k, p.k, S::kNmma);
   if (st == S4D_OK) st = make_map(&mk, p.w_kps, p.n_learn > 0 ? p.n_learn : 1, p.k, p.k, S::kNL);
   if (st == S4D_OK) st = make_map(&mo, p.logits, p.rows, p.n_logits, p.n_logits, 32, true);
-  if (st == S4D_OK) st = set_smem(weights_fc_kernel<NW>, S::kSmem, "cudaFuncSetAttribute(weights_fc_kernel)");
+  static bool smem_set[64] = {};
+  if (st == S4D_OK) st = set_smem(weights_fc_kernel<NW>, S::kSmem, "cudaFuncSetAttribute(weights_fc_kernel)", smem_set);
   if (st != S4D_OK) return st;
   const dim3 grid(unsigned((p.rows + kBM - 1) / kBM), unsigned(groups));
   weights_fc_kernel<NW><<<grid, kThreads, S::kSmem, stream>>>(mi, me, mw, mk, mo, p);
@@ -620,7 +634,9 @@ int launch_output_proj_cols(const OprojParams& p, cudaStream_t stream, int group
   if (st == S4D_OK) st = TWO ? make_map(&mf2, p.feat2, feat_rows, p.k, p.k, kBM) : make_map(&mf2, p.feat, feat_rows, p.k, p.k, kBM);
   if (st == S4D_OK) st = make_map(&mw, p.w, p.k, p.k, p.k, NO);
   if (st == S4D_OK) st = make_map(&mo, p.out, p.rows, p.k, p.out_ld, 32, true);
-  if (st == S4D_OK) st = set_smem(output_proj_kernel<NO, TWO>, S::kSmem, "cudaFuncSetAttribute(output_proj_kernel)");
+  static bool smem_set[64] = {};
+  if (st == S4D_OK)
+    st = set_smem(output_proj_kernel<NO, TWO>, S::kSmem, "cudaFuncSetAttribute(output_proj_kernel)", smem_set);
   if (st != S4D_OK) return st;
   const dim3 grid(unsigned((p.rows + kBM - 1) / kBM), unsigned(groups));
   output_proj_kernel<NO, TWO><<<grid, kThreads, S::kSmem, stream>>>(mf, mf2, mw, mo, p);

@@ -41,27 +41,37 @@ def _ptr(t: Optional[Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+# torch's current-stream handle of a device index, without building a Stream object (a
+# measurable share of an eager small-batch call); the public call where it is missing
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream_ptr(device: torch.device) -> int:
+    if _raw_stream is not None and device.index is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream
 
 
 def _require_cuda(name: str, *ts: Optional[Tensor]) -> torch.device:
-    dev = None
+    idx = None
     for t in ts:
         if t is None:
             continue
-        if not t.is_cuda:
+        i = t.get_device()
+        if i < 0:
             raise ValueError(f"{name}: every tensor must be on a CUDA device (got {t.device}); no CPU path exists")
-        if dev is None:
-            dev = t.device
-        elif t.device != dev:
-            raise ValueError(f"{name}: tensors on different devices ({dev} and {t.device})")
-    return dev
+        if idx is None:
+            idx = i
+        elif i != idx:
+            raise ValueError(f"{name}: tensors on different devices (cuda:{idx} and cuda:{i})")
+    return None if idx is None else torch.device("cuda", idx)
 
 
-def _require(cond: bool, msg: str) -> None:
+def _require(cond: bool, msg) -> None:
+    """Raise ValueError(msg) unless cond; msg may be a callable that builds the text (so that
+    the checks of a successful call format nothing)."""
     if not cond:
-        raise ValueError(msg)
+        raise ValueError(msg() if callable(msg) else msg)
 
 
 def _check_contig(name: str, **ts: Optional[Tensor]) -> None:
@@ -86,7 +96,7 @@ def row_view(t: Tensor, cols: int) -> Tensor:
     """``t [..., cols]`` as a 2-D ``[rows, cols]`` fp32 view the tensor-core kernels can read
     in place (unit column stride, row stride a multiple of 4 floats, 16-byte aligned base);
     a contiguous copy when the strides do not allow that."""
-    _require(t.shape[-1] == cols, f"expected a last dimension of {cols}, got {tuple(t.shape)}")
+    _require(t.shape[-1] == cols, lambda: f"expected a last dimension of {cols}, got {tuple(t.shape)}")
     v = t.reshape(-1, cols)
     if v.stride(1) != 1 or v.stride(0) % 4 != 0 or v.stride(0) < cols or v.data_ptr() % 16 != 0:
         v = v.contiguous()
@@ -118,13 +128,13 @@ def weights_fc_into(logits: Tensor, learnable: Optional[Tensor], instance_featur
     _require(tuple(anchor_embed.shape) == (rows, c), "anchor_embed must match instance_feature")
     _require(instance_feature.stride(1) == 1 and anchor_embed.stride(1) == 1, "inputs need a unit column stride")
     n = int(weights_fc_weight.shape[0])
-    _require(tuple(weights_fc_weight.shape) == (n, c), f"weights_fc_weight must be [n, {c}]")
-    _require(tuple(logits.shape) == (rows, n), f"logits must be [{rows}, {n}]")
+    _require(tuple(weights_fc_weight.shape) == (n, c), lambda: f"weights_fc_weight must be [n, {c}]")
+    _require(tuple(logits.shape) == (rows, n), lambda: f"logits must be [{rows}, {n}]")
     m = 0 if learnable is None else int(learnable.shape[1])
-    _require(learnable is None or tuple(learnable.shape) == (rows, m), f"learnable must be [{rows}, m]")
+    _require(learnable is None or tuple(learnable.shape) == (rows, m), lambda: f"learnable must be [{rows}, m]")
     _require(m == 0 or (learnable_fc_weight is not None and tuple(learnable_fc_weight.shape) == (m, c)),
              f"learnable_fc_weight must be [{m}, {c}]")
-    _require(learnable_bias is None or tuple(learnable_bias.shape) == (m,), f"learnable_bias must be [{m}]")
+    _require(learnable_bias is None or tuple(learnable_bias.shape) == (m,), lambda: f"learnable_bias must be [{m}]")
     st = L.lib().s4d_dfa_weights_fc(instance_feature.data_ptr(), instance_feature.stride(0), anchor_embed.data_ptr(),
                                     anchor_embed.stride(0), rows, weights_fc_weight.data_ptr(),
                                     _ptr(learnable_fc_weight), _ptr(learnable_bias), n, m, c, logits.data_ptr(),
@@ -158,10 +168,11 @@ def camera_logits_into(camera_logits: Tensor, projection_mat: Tensor, cam_linear
              f"camera encoder weights must be [{c}, 12] and [{c}, {c}]")
     for k in ("cam_linear1_bias", "cam_ln1_weight", "cam_ln1_bias", "cam_linear2_bias", "cam_ln2_weight",
               "cam_ln2_bias"):
-        _require(tuple(ts[k].shape) == (c,), f"{k} must be [{c}]")
-    _require(tuple(weights_fc_bias.shape) == (n,), f"weights_fc_bias must be [{n}]")
-    _require(camera_logits.numel() == bs * nc * n, f"camera_logits must hold [{bs}, {nc}, {n}]")
-    _require(camera_embed is None or camera_embed.numel() == bs * nc * c, f"camera_embed must hold [{bs}, {nc}, {c}]")
+        _require(tuple(ts[k].shape) == (c,), lambda: f"{k} must be [{c}]")
+    _require(tuple(weights_fc_bias.shape) == (n,), lambda: f"weights_fc_bias must be [{n}]")
+    _require(camera_logits.numel() == bs * nc * n, lambda: f"camera_logits must hold [{bs}, {nc}, {n}]")
+    _require(camera_embed is None or camera_embed.numel() == bs * nc * c,
+             lambda: f"camera_embed must hold [{bs}, {nc}, {c}]")
     if workspace is None:
         workspace = torch.empty(bs * nc * c, dtype=torch.float32, device=dev)
     _require_cuda(name, workspace)
@@ -190,8 +201,9 @@ def output_proj_into(out: Tensor, features: Tensor, weight: Tensor, bias: Option
         _check_dtype(name, t, (torch.float32,), k)
     _check_dtype(name, error_flag, (torch.int32,), "error_flag")
     rows, c = features.shape
-    _require(tuple(weight.shape) == (c, c), f"weight must be [{c}, {c}]")
-    _require(out.dim() == 2 and out.shape[0] == rows and out.stride(1) == 1, f"out must be a [{rows}, n] row view")
+    _require(tuple(weight.shape) == (c, c), lambda: f"weight must be [{c}, {c}]")
+    _require(out.dim() == 2 and out.shape[0] == rows and out.stride(1) == 1,
+             lambda: f"out must be a [{rows}, n] row view")
     if mode != L.S4D_RESIDUAL_NONE:
         _require(instance_feature is not None and tuple(instance_feature.shape) == (rows, c)
                  and instance_feature.stride(1) == 1, f"instance_feature must be a [{rows}, {c}] row view")
@@ -218,8 +230,9 @@ def output_proj_sum_into(out: Tensor, features: Tensor, features2_ptr: int, row0
         _check_dtype(name, t, (torch.float32,), k)
     _check_dtype(name, error_flag, (torch.int32,), "error_flag")
     total, c = features.shape
-    _require(tuple(weight.shape) == (c, c), f"weight must be [{c}, {c}]")
-    _require(out.dim() == 2 and out.shape[0] == rows and out.stride(1) == 1, f"out must be a [{rows}, n] row view")
+    _require(tuple(weight.shape) == (c, c), lambda: f"weight must be [{c}, {c}]")
+    _require(out.dim() == 2 and out.shape[0] == rows and out.stride(1) == 1,
+             lambda: f"out must be a [{rows}, n] row view")
     if mode != L.S4D_RESIDUAL_NONE:
         _require(instance_feature is not None and tuple(instance_feature.shape) == (rows, c)
                  and instance_feature.stride(1) == 1, f"instance_feature must be a [{rows}, {c}] row view")
@@ -286,9 +299,9 @@ def deformable_aggregation_into(out: Tensor, mc_ms_feat: Tensor, spatial_shape: 
     bs, A, nc, nl, P, G = _dfa_dims(sample_location, weights, weights_cam, lay)
     C = int(mc_ms_feat.shape[2])
     _require(int(mc_ms_feat.shape[0]) == bs, "mc_ms_feat batch must match sample_location")
-    _require(tuple(spatial_shape.shape) == (nc, nl, 2), f"spatial_shape must be [{nc}, {nl}, 2]")
-    _require(tuple(scale_start_index.shape) == (nc, nl), f"scale_start_index must be [{nc}, {nl}]")
-    _require(tuple(out.shape) == (bs, A, C), f"out must be [{bs}, {A}, {C}]")
+    _require(tuple(spatial_shape.shape) == (nc, nl, 2), lambda: f"spatial_shape must be [{nc}, {nl}, 2]")
+    _require(tuple(scale_start_index.shape) == (nc, nl), lambda: f"scale_start_index must be [{nc}, {nl}]")
+    _require(tuple(out.shape) == (bs, A, C), lambda: f"out must be [{bs}, {A}, {C}]")
     ce = nc if cam_end is None or cam_end < 0 else int(cam_end)
     _require_cuda(name, workspace)
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
@@ -339,11 +352,11 @@ def deformable_aggregation_anchors_into(out: Tensor, mc_ms_feat: Tensor, spatial
     bs, nc, nl, P, G = (int(v) for v in weights_cam.shape)
     A = int(out.shape[1])
     C = int(mc_ms_feat.shape[2])
-    _require(tuple(out.shape) == (bs, A, C), f"out must be [{bs}, A, {C}]")
+    _require(tuple(out.shape) == (bs, A, C), lambda: f"out must be [{bs}, A, {C}]")
     _require(anchor.numel() == bs * A * int(anchor.shape[-1]), "anchor must be [bs, A, D]")
     _require(tuple(projection_mat.shape[-2:]) == (4, 4) and projection_mat.numel() == bs * nc * 16,
              f"projection_mat must be [{bs}, {nc}, 4, 4]")
-    _require(image_wh.numel() == bs * nc * 2, f"image_wh must be [{bs}, {nc}, 2]")
+    _require(image_wh.numel() == bs * nc * 2, lambda: f"image_wh must be [{bs}, {nc}, 2]")
     num_fix = int(fix_scale.shape[0])
     _require(learnable is None or learnable.numel() == bs * A * (P - num_fix) * 3,
              f"learnable must hold {(P - num_fix) * 3} logits per anchor")
@@ -463,11 +476,11 @@ def kps_project_into(anchor: Tensor, learnable_logits: Optional[Tensor], fix_sca
     P = n_fix + n_learn
     if sample_location is not None:
         exp = (bs, A, nc, P, 2) if lay == L.S4D_LAYOUT_CAM_MAJOR else (bs, A, P, nc, 2)
-        _require(tuple(sample_location.shape) == exp, f"sample_location must be {list(exp)}")
+        _require(tuple(sample_location.shape) == exp, lambda: f"sample_location must be {list(exp)}")
     if depth_mask is not None:
-        _require(tuple(depth_mask.shape) == (bs, A, nc, P), f"depth_mask must be [{bs}, {A}, {nc}, {P}]")
+        _require(tuple(depth_mask.shape) == (bs, A, nc, P), lambda: f"depth_mask must be [{bs}, {A}, {nc}, {P}]")
     if key_points is not None:
-        _require(tuple(key_points.shape) == (bs, A, P, 3), f"key_points must be [{bs}, {A}, {P}, 3]")
+        _require(tuple(key_points.shape) == (bs, A, P, 3), lambda: f"key_points must be [{bs}, {A}, {P}, 3]")
     if visible_idx is not None:
         _require(tuple(visible_idx.shape) == (bs * A * nc * P, 4), "visible_idx must be [bs*A*Ncam*P, 4]")
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
@@ -519,11 +532,11 @@ def kps_project_linear_into(anchor: Tensor, instance_feature: Tensor, learnable_
     P = n_fix + m3 // 3
     if sample_location is not None:
         exp = (bs, A, nc, P, 2) if lay == L.S4D_LAYOUT_CAM_MAJOR else (bs, A, P, nc, 2)
-        _require(tuple(sample_location.shape) == exp, f"sample_location must be {list(exp)}")
+        _require(tuple(sample_location.shape) == exp, lambda: f"sample_location must be {list(exp)}")
     if depth_mask is not None:
-        _require(tuple(depth_mask.shape) == (bs, A, nc, P), f"depth_mask must be [{bs}, {A}, {nc}, {P}]")
+        _require(tuple(depth_mask.shape) == (bs, A, nc, P), lambda: f"depth_mask must be [{bs}, {A}, {nc}, {P}]")
     if key_points is not None:
-        _require(tuple(key_points.shape) == (bs, A, P, 3), f"key_points must be [{bs}, {A}, {P}, 3]")
+        _require(tuple(key_points.shape) == (bs, A, P, 3), lambda: f"key_points must be [{bs}, {A}, {P}, 3]")
     if visible_idx is not None:
         _require(tuple(visible_idx.shape) == (bs * A * nc * P, 4), "visible_idx must be [bs*A*Ncam*P, 4]")
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
@@ -633,19 +646,20 @@ def pack_feature_maps(feature_maps: List[Tensor], dtype: Optional[torch.dtype] =
     name = "pack_feature_maps"
     maps = [f if f.is_contiguous() else f.contiguous() for f in feature_maps]
     dev = _require_cuda(name, *maps, out)
-    _require(len(maps) > 0, f"{name}: no maps")
+    _require(len(maps) > 0, lambda: f"{name}: no maps")
     for f in maps:
         _check_dtype(name, f, (torch.float32, torch.bfloat16), "feature map")
-        _require(f.dtype == maps[0].dtype and f.dim() == 5, f"{name}: maps must be 5-D and share one dtype")
+        _require(f.dtype == maps[0].dtype and f.dim() == 5, lambda: f"{name}: maps must be 5-D and share one dtype")
     bs, nc = int(maps[0].shape[0]), int(maps[0].shape[1])
     if channels_last:
         shapes = [(int(f.shape[2]), int(f.shape[3])) for f in maps]
         c = int(maps[0].shape[4])
-        _require(all(tuple(f.shape[:2]) == (bs, nc) and f.shape[4] == c for f in maps), f"{name}: inconsistent maps")
+        _require(all(tuple(f.shape[:2]) == (bs, nc) and f.shape[4] == c for f in maps),
+                 lambda: f"{name}: inconsistent maps")
     else:
         shapes = [(int(f.shape[3]), int(f.shape[4])) for f in maps]
         c = int(maps[0].shape[2])
-        _require(all(tuple(f.shape[:3]) == (bs, nc, c) for f in maps), f"{name}: inconsistent maps")
+        _require(all(tuple(f.shape[:3]) == (bs, nc, c) for f in maps), lambda: f"{name}: inconsistent maps")
     dtype = dtype or maps[0].dtype
     _check_dtype(name, torch.empty(0, dtype=dtype), (torch.float32, torch.bfloat16), "dtype")
     rows = nc * sum(h * w for h, w in shapes)
