@@ -32,8 +32,10 @@ def _weights(n, m, c, gen, dev):
     return w_fc.to(dev), w_kps.to(dev), b_kps.to(dev)
 
 
-@pytest.mark.parametrize("rows", [1, 4, 127, 128, 129, 900, 1800, 7200])
+@pytest.mark.parametrize("rows", [1, 4, 127, 128, 129, 900, 1800, 7200, 18945, 20000, 28800])
 def test_weights_fc_matches_float64(cuda_device, rows):
+    """Column groups for few row tiles, whole tiles per CTA otherwise, up to the two waves of
+    tiles of the 32-frame layer (28,800 rows)."""
     dev = torch.device("cuda:0")
     gen = torch.Generator().manual_seed(rows)
     n, m, c = 416, 18, 256
