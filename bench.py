@@ -1099,6 +1099,10 @@ def run_ours(args):
                 "launch_timing": "CUDA events of the graph's event-record nodes around each layer's gather, "
                                  "last replay of the timed region",
                 "share_of_step": sum(g_ms) / (ms / args.steps),
+                # the L2-side tap traffic (not the roofline numerator): 4 taps x 512 B per
+                # in-bounds sample, over the same average launch time
+                "tap_bytes_per_launch": inb_per_call * args.frames * 4 * 512,
+                "tap_gbs": inb_per_call * args.frames * 4 * 512 / (g_avg_ms / 1e3) / 1e9,
             },
             "gpu_launches": launches_per_layer(w) * args.layers * args.steps,
             "step": "one replay of the 6-layer DFAStack CUDA graph per step",
