@@ -110,7 +110,11 @@ class Sparse4DHead:
     """The single-frame decoder of ``model/sparse4d_head.py`` on ``device``, from
     ``preprocess_head_parameters``.  ``model_config`` goes to every DFA layer
     (``FEATURE_DTYPE``, ``MATMUL_PRECISION``); ``MATMUL_PRECISION`` also sets torch's fp32 matmul
-    precision for the dense layers around them."""
+    precision for the dense layers around them.  ``model_config["ATTENTION_DTYPE"]``
+    (``torch.float32`` by default, or ``torch.bfloat16``) is the type the attention's softmax(QK^T)V
+    runs in: bf16 (the reference's TT-NN attention runs in bf16) uses the flash kernels, about 9x
+    faster than the fp32 kernel at 900 tokens, with q, k, v rounded to bf16 and the result
+    returned as fp32."""
 
     def __init__(self, device, parameters: Dict, model_config: Optional[Dict] = None, embed_dims: int = 256,
                  num_groups: int = 8, num_levels: int = 4, num_cams: int = 6, num_learnable_pts: int = 6):
@@ -120,6 +124,10 @@ class Sparse4DHead:
         self.num_single_frame_decoder = parameters.get("num_single_frame_decoder", 1)
         cfg = dict(model_config or {})
         self.matmul_precision = MATMUL_PRECISIONS[cfg.get("MATMUL_PRECISION", "fp32")]
+        self.attention_dtype = cfg.get("ATTENTION_DTYPE", torch.float32)
+        if self.attention_dtype not in (torch.float32, torch.bfloat16, torch.float16):
+            raise ValueError("ATTENTION_DTYPE must be torch.float32, torch.bfloat16 or torch.float16")
+        cfg.pop("ATTENTION_DTYPE", None)  # a head option, not a DFA one
         dev = self.device
         self.layers = []
         for op, p in zip(self.operation_order, parameters["layers"]):
@@ -164,7 +172,12 @@ class Sparse4DHead:
         q = F.linear(query, wq, bq).view(bs, n, heads, e // heads).transpose(1, 2)
         k = F.linear(query, wk, bk).view(bs, n, heads, e // heads).transpose(1, 2)
         v = F.linear(v_in, wv, bv).view(bs, n, heads, e // heads).transpose(1, 2)
-        o = F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(bs, n, e)
+        dt = self.attention_dtype
+        if dt == torch.float32:
+            o = F.scaled_dot_product_attention(q, k, v)
+        else:
+            o = F.scaled_dot_product_attention(q.to(dt), k.to(dt), v.to(dt)).float()
+        o = o.transpose(1, 2).reshape(bs, n, e)
         out = query + F.linear(o, p["out_proj_weight"], p["out_proj_bias"])
         return F.linear(out, self.fc_after)
 

@@ -58,16 +58,19 @@ def _ring_case(bs=2, seed=9):
     return cfg, ins
 
 
-def test_head_graph_replay_equals_eager_and_oracle(cuda_device, twin):
-    """The benchmark configuration (bf16 maps, TF32 linears) on the synthetic camera ring with
-    anchors spread over the scene: one CUDA-graph replay of the whole decoder equals the eager
-    pass bit for bit, and both follow the fp32 oracle head within the bf16/TF32 tolerance."""
+@pytest.mark.parametrize("attention", [torch.float32, torch.bfloat16])
+def test_head_graph_replay_equals_eager_and_oracle(cuda_device, twin, attention):
+    """The benchmark configuration (bf16 maps, TF32 linears; attention in fp32 or bf16) on the
+    synthetic camera ring with anchors spread over the scene: one CUDA-graph replay of the whole
+    decoder equals the eager pass bit for bit, and both follow the fp32 oracle head within the
+    bf16/TF32 tolerance."""
     _, head, _, _, _ = twin
     d = torch.device("cuda:0")
     cfg, ins = _ring_case()
     anchor = ins.anchor
     gh = Sparse4DHead(d, preprocess_head_parameters(head), {"FEATURE_DTYPE": torch.bfloat16,
-                                                             "MATMUL_PRECISION": "tf32"})
+                                                             "MATMUL_PRECISION": "tf32",
+                                                             "ATTENTION_DTYPE": attention})
     from sparse4d_tt_b200 import ops
 
     packed = ops.pack_feature_maps([m.to(d) for m in ins.feature_maps], dtype=torch.bfloat16)
