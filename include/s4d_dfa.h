@@ -487,6 +487,18 @@ S4D_API int s4d_peer_signal_wait_counter(uint32_t* own_slots, uint32_t* const* p
                                          uint32_t* epoch_counter, int advance, uint64_t limit_ns,
                                          int32_t* error_flag, void* stream);
 
+/* LayerNorm over the last dimension for the decoder layers around the DFA (nn.LayerNorm of the
+ * head's "norm" operations, the asymmetric FFN's pre-norm and the linear_relu_ln blocks of the
+ * refinement and anchor-encoder MLPs: model/sparse4d_head.py, model/asymmetric_ffn.py,
+ * model/refinement_module.py):
+ *   y[r, :] = (x[r, :] - mean) / sqrt(var + eps) * weight + bias   (biased variance)
+ *   x, y      [rows, width] f32 contiguous, not overlapping
+ *   weight    [width] or NULL (no affine); bias [width] or NULL
+ * One warp per row.  Implemented: width 32, 64, 128, 256 or 512.  No reference counterpart as
+ * a separate op (the reference calls ttnn / torch LayerNorm). */
+S4D_API int s4d_layer_norm(const float* x, const float* weight, const float* bias, float* y, int64_t rows,
+                           int64_t width, float eps, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -80,6 +80,7 @@ SIGNATURES = {
     "s4d_ipc_close": (_int, [_p]),
     "s4d_peer_signal_wait": (_int, [_p, _p, _int, _int, C.c_uint32, C.c_uint64, _p, _p]),
     "s4d_peer_signal_wait_counter": (_int, [_p, _p, _int, _int, _p, _int, C.c_uint64, _p, _p]),
+    "s4d_layer_norm": (_int, [_p, _p, _p, _p, _i64, _i64, C.c_float, _p]),
 }
 
 _lib = None
@@ -95,7 +96,7 @@ class S4DError(RuntimeError):
 
 
 # Version of include/s4d_dfa.h these bindings are written for (s4d_abi_version()).
-ABI_VERSION = 107
+ABI_VERSION = 108
 
 
 def lib():

@@ -19,7 +19,7 @@ INCLUDE = os.path.join(REPO, "include")
 LIB_DIR = os.path.join(PKG, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libs4d_dfa.so")
 SOURCES = ["capi.cu", "kps_project.cu", "dfa_gather.cu", "kps_noalloc.cu", "linear_tc.cu", "camera_encoder.cu", "pack_maps.cu",
-           "instance_bank.cu", "peer.cu"]
+           "instance_bank.cu", "peer.cu", "layer_norm.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -54,7 +54,7 @@ const char* s4d_status_string(int status) {
 
 const char* s4d_last_error(void) { return g_last_error; }
 
-int s4d_abi_version(void) { return 107; }
+int s4d_abi_version(void) { return 108; }
 
 uint64_t s4d_set_tc_wait_limit_ns(uint64_t limit_ns) {
   const uint64_t prev = g_tc_wait_limit_ns;

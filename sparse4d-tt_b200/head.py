@@ -93,6 +93,14 @@ def _to(dev, t):
     return None if t is None else t.detach().to(dev, torch.float32).contiguous()
 
 
+def _layer_norm(x: Tensor, w: Tensor, b: Tensor) -> Tensor:
+    """nn.LayerNorm (eps 1e-5) over the last dimension: this library's warp-per-row kernel for
+    the decoder's contiguous fp32 rows of 32 to 512 features, torch's kernel otherwise."""
+    if x.dtype == torch.float32 and x.shape[-1] in ops.LAYER_NORM_WIDTHS and x.is_contiguous():
+        return ops.layer_norm(x, w, b, 1e-5)
+    return F.layer_norm(x, (w.shape[0],), w, b, 1e-5)
+
+
 def _run_mlp(x: Tensor, mods) -> Tensor:
     for kind, w, b in mods:
         if kind == "linear":
@@ -100,7 +108,7 @@ def _run_mlp(x: Tensor, mods) -> Tensor:
         elif kind == "relu":
             x = F.relu(x)
         elif kind == "ln":
-            x = F.layer_norm(x, (w.shape[0],), w, b, 1e-5)
+            x = _layer_norm(x, w, b)
         else:  # scale
             x = x * w
     return x
@@ -183,7 +191,7 @@ class Sparse4DHead:
 
     def _ffn(self, p, x: Tensor) -> Tensor:
         """Asymmetric FFN 2C -> C with pre-norm (``model/asymmetric_ffn.py``)."""
-        x = F.layer_norm(x, (x.shape[-1],), *p["pre_norm"], 1e-5)
+        x = _layer_norm(x, *p["pre_norm"])
         return F.linear(x, *p["identity_fc"]) + F.linear(F.relu(F.linear(x, *p["fc1"])), *p["fc2"])
 
     def _refine(self, p, inst: Tensor, anchor: Tensor, embed: Tensor, time_interval: Tensor, return_cls: bool):
@@ -233,7 +241,7 @@ class Sparse4DHead:
                 elif op == "gnn":
                     inst = self._attention(p, torch.cat([inst, embed], dim=-1), F.linear(inst, self.fc_before))
                 elif op == "norm":
-                    inst = F.layer_norm(inst, (self.embed_dims,), p[0], p[1], 1e-5)
+                    inst = _layer_norm(inst, p[0], p[1])
                 elif op == "ffn":
                     inst = self._ffn(p, inst)
                 elif op == "deformable":

@@ -244,6 +244,29 @@ def output_proj_sum_into(out: Tensor, features: Tensor, features2_ptr: int, row0
     return out
 
 
+LAYER_NORM_WIDTHS = (32, 64, 128, 256, 512)
+
+
+def layer_norm(x: Tensor, weight: Optional[Tensor], bias: Optional[Tensor], eps: float = 1e-5,
+               out: Optional[Tensor] = None) -> Tensor:
+    """LayerNorm of ``x [..., width]`` (fp32, contiguous) over its last dimension on this library's
+    warp-per-row kernel (``s4d_layer_norm``); ``width`` in ``LAYER_NORM_WIDTHS``."""
+    name = "layer_norm"
+    dev = _require_cuda(name, x, weight, bias, out)
+    width = int(x.shape[-1])
+    _require(width in LAYER_NORM_WIDTHS, lambda: f"{name}: width must be one of {LAYER_NORM_WIDTHS}, got {width}")
+    _check_contig(name, x=x, weight=weight, bias=bias, out=out)
+    for k, t in (("x", x), ("weight", weight), ("bias", bias), ("out", out)):
+        _check_dtype(name, t, (torch.float32,), k)
+    if out is None:
+        out = torch.empty_like(x)
+    _require(out.shape == x.shape, lambda: f"{name}: out must be {tuple(x.shape)}")
+    st = L.lib().s4d_layer_norm(x.data_ptr(), _ptr(weight), _ptr(bias), out.data_ptr(), x.numel() // width, width,
+                                float(eps), _stream_ptr(dev))
+    L.check(name, st)
+    return out
+
+
 # ---------------------------------------------------------------------------------------------
 # deformable_aggregation
 # ---------------------------------------------------------------------------------------------

@@ -33,7 +33,7 @@ def lib():
 
 def test_every_declared_symbol_is_exported(lib):
     names = declared_functions()
-    assert len(names) == 29, names
+    assert len(names) == 30, names
     for n in names:
         assert hasattr(lib, n), n
         assert n in L.SIGNATURES, f"{n} has no ctypes signature"
@@ -52,7 +52,7 @@ def test_status_strings_and_version(lib):
     assert L.status_string(0) == "S4D_OK"
     assert L.status_string(2) == "S4D_ERR_UNSUPPORTED_SHAPE"
     assert L.status_string(99) == "S4D_ERR_UNKNOWN"
-    assert lib.s4d_abi_version() == 107 == L.ABI_VERSION
+    assert lib.s4d_abi_version() == 108 == L.ABI_VERSION
 
 
 def test_dfa_workspace_bytes(lib):
@@ -494,3 +494,18 @@ def test_gather_routing_rejects_on_host(lib):
     assert st == L.S4D_ERR_INVALID_ARG and "out_peer" in msg, msg
     st, msg = call(32, 900, 1800, out=20)
     assert st == L.S4D_ERR_INVALID_ARG and "16-byte" in msg, msg
+
+
+def test_layer_norm_rejects_on_host(lib):
+    def call(x=16, w=16, b=16, y=32, rows=10, width=256, eps=1e-5):
+        return lib.s4d_layer_norm(x, w, b, y, rows, width, eps, None), lib.s4d_last_error().decode()
+    for kw, status, text in ((dict(width=48), L.S4D_ERR_UNSUPPORTED_SHAPE, "width"),
+                             (dict(rows=-1), L.S4D_ERR_INVALID_ARG, "negative"),
+                             (dict(eps=-1.0), L.S4D_ERR_INVALID_ARG, "eps"),
+                             (dict(x=None), L.S4D_ERR_INVALID_ARG, "null"),
+                             (dict(w=None), L.S4D_ERR_INVALID_ARG, "bias needs a weight"),
+                             (dict(y=18), L.S4D_ERR_INVALID_ARG, "misaligned"),
+                             (dict(rows=1 << 40), L.S4D_ERR_UNSUPPORTED_SHAPE, "too many")):
+        st, msg = call(**kw)
+        assert st == status and text in msg, (kw, msg)
+    assert call(rows=0)[0] == L.S4D_OK
