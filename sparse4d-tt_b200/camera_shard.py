@@ -181,10 +181,13 @@ class PeerPartialSums:
         self._ready[self.peer] = peer_slots
         self._consumed = (ctypes.c_void_p * 8)()
         self._consumed[self.peer] = peer_slots + 8 * 4
+        self.closed = False
 
     def _signal(self, own_offset: int, peers, advance: int) -> None:
         from . import _lib as L
 
+        if self.closed:
+            raise RuntimeError("PeerPartialSums: used after close() (the other rank's buffers are unmapped)")
         base = self.slots.data_ptr()
         st = L.lib().s4d_peer_signal_wait_counter(base + own_offset * 4, ctypes.cast(peers, ctypes.c_void_p),
                                                   self.rank, 2, base + 16 * 4, advance, self.limit_ns,
@@ -194,6 +197,8 @@ class PeerPartialSums:
 
     def begin(self, rows: int) -> torch.Tensor:
         """Launch this call's "consumed" exchange; returns the ``[rows, C]`` view of ``part``."""
+        if self.closed:
+            raise RuntimeError("PeerPartialSums: used after close() (the other rank's buffers are unmapped)")
         if rows > self.capacity:
             raise ValueError(f"{rows} rows exceed the shared buffers' {self.capacity}")
         self._signal(8, self._consumed, 0)
@@ -220,11 +225,13 @@ class PeerPartialSums:
         """Collective: both ranks finish their work, then unmap the other's buffers."""
         from . import _lib as L
 
-        if not self._bases:
+        if self.closed:
             return
+        self.closed = True
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
         for base in self._bases.values():
             L.check("ipc_close", L.lib().s4d_ipc_close(base))
         self._bases = {}
+        self.peer_recv = None
         dist.barrier(group=self.group)  # neither rank frees its buffers while the other maps them

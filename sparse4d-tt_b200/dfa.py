@@ -380,15 +380,14 @@ class DeformableFeatureAggregation:
             # straight into that rank's receive buffer over NVLink, once the other rank has
             # finished reading it (begin); the exchanges keep their epochs on the device, so the
             # call can be captured in a CUDA graph
-            if self._peer is None or self._peer.capacity < rows:
+            if self._peer is None or self._peer.closed or self._peer.capacity < rows:
                 from .camera_shard import PeerPartialSums
 
                 if torch.cuda.is_current_stream_capturing():
                     raise RuntimeError("CAMERA_REDUCE='p2p': run the module once eagerly (on both ranks, with "
                                        "this batch size or larger) before capturing it in a CUDA graph")
-
                 if self._peer is not None:
-                    self._peer.close()
+                    self._peer.close()  # collective; a no-op when already closed
                 self._peer = PeerPartialSums(rows, self.embed_dims, self.process_group, dev)
             feats = self._peer.begin(rows).view(bs, num_anchor, self.embed_dims)
         else:

@@ -163,6 +163,16 @@ def _p2p_worker(rank, world, port, out_dir):
                  flag=np.array(p2p._peer.error_flag.item()))
         del call
         p2p._peer.close()
+        # a call after close() maps a fresh pair of buffers (collectively) and is correct again
+        args = inputs(90)
+        p2p.reset_frame_cache()
+        got = p2p.run(*args, cfg.spatial_shapes, 2, 900)
+        b, e = p2p.shard
+        ref, _ = reference(args)
+        torch.cuda.synchronize()
+        after_close = ((got - ref[b:e]).abs().max() / ref[b:e].abs().max()).item()
+        np.savez(os.path.join(out_dir, f"p2p_reopen{rank}.npz"), rel=np.array(after_close))
+        p2p._peer.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -182,3 +192,4 @@ def test_camera_sharded_p2p_matches_single_gpu():
         # the same partial sums, added inside the accumulator instead of before it
         assert float(np.max(g["rel"])) <= 1e-4, g["rel"]
         assert float(np.max(g["rel_rs"])) <= 1e-4, g["rel_rs"]
+        assert float(np.load(os.path.join(out_dir, f"p2p_reopen{r}.npz"))["rel"]) <= 1e-4
