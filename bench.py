@@ -657,6 +657,71 @@ def pack_leg(device, frames=32, iters=10):
     return res
 
 
+def bank_metas(frames, step):
+    """Synthetic per-frame ego poses and timestamps of one step of the InstanceBank workload:
+    frame f at time 0.5 * step, yawed and shifted a little more every step."""
+    import numpy as np
+
+    img = []
+    for f in range(frames):
+        yaw, sx, sy = 0.01 * (f + 3 * step), 0.4 * step + 0.01 * f, 0.1 * step
+        c, s_ = np.cos(yaw), np.sin(yaw)
+        tg = np.array([[c, -s_, 0, sx], [s_, c, 0, sy], [0, 0, 1, 0], [0, 0, 0, 1]], dtype=np.float64)
+        img.append({"T_global": tg, "T_global_inv": np.linalg.inv(tg)})
+    return {"timestamp": torch.full((frames,), 0.5 * step, dtype=torch.float64), "img_metas": img}
+
+
+def bank_inputs(frames, seed=700):
+    """The learnable anchors and features of the bank, and one set of decoder outputs (new
+    features, anchors, class scores) per frame, seeded."""
+    from sparse4d_tt_b200 import synthetic as syn
+
+    g = torch.Generator().manual_seed(seed)
+    anchor_data = syn.make_anchors(1, 900, g)[0]
+    feat_data = torch.randn(900, 256, generator=g)
+    new = (torch.randn(frames, 900, 256, generator=g), syn.make_anchors(frames, 900, g),
+           torch.randn(frames, 900, 10, generator=g))
+    return anchor_data, feat_data, new
+
+
+def instance_bank_leg(device, frames, steps=40, warmup=3):
+    """The temporal InstanceBank around the decoder (model/instance_bank.py get / update / cache)
+    for a batch of ``frames`` frames: each step moves the 600 cached anchors to the frame (get),
+    merges the top 300 of the 900 new instances with them (update) and keeps the 600 most
+    confident for the next frame (cache), eagerly, with the host's per-frame pose products; CUDA
+    events around the timed steps."""
+    from sparse4d_tt_b200.instance_bank import InstanceBank
+
+    anchor_data, feat_data, (nf, na, nc) = bank_inputs(frames)
+    bank = InstanceBank(device, anchor_data, feat_data)
+    nf, na, nc = nf.to(device), na.to(device), nc.to(device)
+
+    metas = [bank_metas(frames, k) for k in range(warmup + 1 + steps)]  # the data loader's part
+
+    def step(k):
+        bank.get(frames, metas[k])
+        f, a = bank.update(nf, na, nc)
+        bank.cache(f, a, nc, metas[k])
+
+    k = 0
+    for _ in range(warmup + 1):
+        step(k)
+        k += 1
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step(k)
+        k += 1
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"workload": f"InstanceBank get + update + cache over {frames} frames: 600 cached of 900 anchors, "
+                        "256 ch, 10 classes; eager, per-frame ego poses from the host",
+            "ms_per_step": ms, "frames_per_s": frames / (ms / 1e3), "steps": steps,
+            "launches_per_step": 3}
+
+
 def decoder_leg(device, frames, steps, warmup):
     """The decoder chain around the DFA: a whole single-frame Sparse4D v3 decoder pass (6 DFA
     layers with the decoupled attention, FFN, LayerNorm, refinement and anchor re-encoding
@@ -874,12 +939,31 @@ def cpu_baseline(seconds=12.0, max_calls=40):
         kps_call()
         k_times.append(time.perf_counter() - t0)
     k_med = statistics.median(k_times)
+
+    # the InstanceBank step of the GPU leg (32 frames) on the oracle's port of the reference class
+    from oracle import instance_bank_torch as oib
+
+    anchor_data, feat_data, (nf, na, nc) = bank_inputs(32)
+    bank = oib.InstanceBankOracle(anchor_data, feat_data)
+    b_times = []
+    metas = [bank_metas(32, k) for k in range(6)]
+    for k in range(6):
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            bank.get(32, metas[k])
+            f, a = bank.update(nf, na, nc)
+            bank.cache(f, a, nc, metas[k])
+        b_times.append(time.perf_counter() - t0)
+    b_med = statistics.median(b_times[2:])
     return {"value": 1.0 / med, "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"{len(times)} single-frame DFA layer calls (900 anchors, 704x256 maps as fp32, all linears "
                       f"included) after 2 warm-ups; median {med * 1e3:.1f} ms/call; torch {torch.__version__} CPU",
             "median_ms": med * 1e3, "cpu": _cpu_model(),
             "kps": {"median_ms": k_med * 1e3, "calls_per_s": 1.0 / k_med,
-                    "sample": "50 keypoint-only calls (1 frame, 900 anchors, learnable_fc included) after 3 warm-ups"}}
+                    "sample": "50 keypoint-only calls (1 frame, 900 anchors, learnable_fc included) after 3 warm-ups"},
+            "instance_bank": {"median_ms": b_med * 1e3, "frames_per_s": 32 / b_med,
+                              "sample": "4 InstanceBank get + update + cache steps over 32 frames (the GPU leg's "
+                                        "workload) after 2, on the oracle's port of the reference class"}}
 
 
 def _cpu_model():
@@ -1071,11 +1155,12 @@ def run_ours(args):
     if not args.no_highres:
         highres = highres_leg(rank, world, device, pg, min(args.steps, 20), 3)
 
-    bs1 = pack = kps = decoder = None
+    bs1 = pack = kps = decoder = bank = None
     if rank == 0 and not args.no_bs1:
         bs1 = bs1_leg(device)
         pack = pack_leg(device)
         kps = kps_leg(device)
+        bank = instance_bank_leg(device, args.frames)
         decoder = decoder_leg(device, args.frames, max(3, args.steps // 4), 2)
     barrier()
 
@@ -1129,6 +1214,7 @@ def run_ours(args):
             "kps": kps,
             "highres": highres,
             "decoder": decoder,
+            "instance_bank": bank,
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
