@@ -295,7 +295,8 @@ S4D_API int s4d_instance_bank_update(const float* feature, const float* anchor, 
  * s4d_deformable_aggregation then reads with weights_are_logits = 2: per frame and (level, point,
  * group) column, exp(weights_cam - M2[group]) for every camera and their sum over cameras
  * (M2 = the frame's per-group maximum).  They depend only on the per-camera term, so they can be
- * computed once per frame, e.g. next to s4d_dfa_camera_logits on another stream.
+ * computed once per frame, e.g. next to s4d_dfa_camera_logits on another stream.  The launch
+ * also zeroes the workspace's anchor counter (see s4d_dfa_workspace_bytes).
  *   weights_cam [bs, Ncam, L, P, G]; workspace >= s4d_dfa_workspace_bytes(..., split_logits=1)
  *   bytes, 16-byte aligned.  Implemented: Ncam 6, L 4, P 13, G 8. */
 S4D_API int s4d_dfa_camera_factors(const float* weights_cam, int64_t bs, int64_t num_cams, int64_t num_levels,
@@ -354,7 +355,11 @@ S4D_API int s4d_deformable_aggregation_anchors_peer(const void* mc_ms_feat, int 
 
 /* Bytes of the optional workspace of s4d_deformable_aggregation (split logits only: the
  * per-frame camera softmax factors, bs * (Ncam + 1) * L * P * G floats rounded up to 16 bytes,
- * then 16 bytes for the gather's anchor counter; 0 otherwise).  Host-only, launches nothing. */
+ * then 16 bytes for the gather's anchor counter; 0 otherwise).  Host-only, launches nothing.
+ * The counter is zeroed when the factors are written (s4d_dfa_camera_factors, or the gather
+ * itself with weights_are_logits = 1) and every gather launch leaves it at zero, so a prepared
+ * workspace serves any number of calls in stream order; calls that share one workspace must not
+ * overlap on the GPU. */
 S4D_API size_t s4d_dfa_workspace_bytes(int64_t bs, int64_t num_cams, int64_t num_levels, int64_t num_pts,
                                        int64_t num_groups, int split_logits);
 

@@ -386,6 +386,19 @@ struct TapFma<float> {
   }
 };
 
+// End of a gather launch that took anchors from `counter` (counter[0]: next ticket, counter[1]:
+// blocks done): called once per block by one thread after the block has taken its last ticket.
+// The last block to get here resets both words, so the next launch on the same workspace starts
+// from zero without a memset.  The fence orders this block's ticket atomics before its done
+// count, so the last block sees every other block's tickets taken before it resets.
+__device__ __forceinline__ void release_anchor_counter(unsigned* counter) {
+  __threadfence();
+  if (atomicAdd(counter + 1, 1u) == gridDim.x - 1) {
+    atomicExch(counter, 0u);
+    atomicExch(counter + 1, 0u);
+  }
+}
+
 // A hint to bring the line holding p into L1; no register is written.
 __device__ __forceinline__ void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
 
@@ -629,14 +642,21 @@ __global__ void __launch_bounds__(kGatherThreads, 4) dfa_gather_fast_kernel(Gath
 // sum falls below 1e-20 (the largest logit sits > ~46 below M1 + M2, where factors could
 // underflow) the anchor switches to the exact two-pass softmax over wa + wc.
 // -----------------------------------------------------------------------------------------------
+// cam_softmax_prep_kernel also resets the workspace's anchor counter pair (ticket, blocks done)
+// that the warp and cooperative gather kernels take anchors from, so that a freshly prepared workspace starts at
+// zero; every gather launch then leaves the pair at zero again when its last block exits
+// (release_anchor_counter), and no memset has to run between the join of this kernel's stream
+// and the gather.
 template <int NC, int LPG, int G>
 __global__ void __launch_bounds__(kGatherThreads) cam_softmax_prep_kernel(const float* __restrict__ wc,
-                                                                          float* __restrict__ ws) {
+                                                                          float* __restrict__ ws,
+                                                                          unsigned* __restrict__ anchor_counter) {
   constexpr float kLog2e = 1.4426950408889634f;
   static_assert(kGatherThreads % G == 0, "thread t only sees group t % G");
   __shared__ float s_tmp[kGatherWarps * 32];
   __shared__ float s_m[32];
   const int b = blockIdx.x, tid = threadIdx.x;
+  if (b == 0 && tid < 2) anchor_counter[tid] = 0u;
   const float* w = wc + (int64_t)b * NC * LPG;
   float* ec = ws + (int64_t)b * (NC + 1) * LPG;
   float m = -INFINITY;
@@ -999,6 +1019,12 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
   __syncwarp();  // this anchor's shared-memory state is read before the next one writes it
   }
   if (p.out_peer != nullptr) __threadfence_system();  // the rows stored to the other GPU are performed
+  if (WARPS == 1) {
+    if (lane == 0) release_anchor_counter(p.anchor_counter);
+  } else {
+    __syncthreads();  // every warp of the block has taken its last ticket
+    if (tid == 0) release_anchor_counter(p.anchor_counter);
+  }
 }
 
 // -----------------------------------------------------------------------------------------------
@@ -1356,6 +1382,7 @@ __global__ void __launch_bounds__(WARPS * 32, (sizeof(T) == 2 ? 28 : 20) / WARPS
     }
   }
   if (p.out_peer != nullptr) __threadfence_system();  // the rows stored to the other GPU are performed
+  if (tid == 0) release_anchor_counter(p.anchor_counter);
 }
 
 
@@ -1437,7 +1464,9 @@ int launch_cam_factors(const float* weights_cam, float* cam_ws, int bs, int ncam
     return fail(S4D_ERR_UNSUPPORTED_SHAPE, "camera factors: implemented for 6 cameras, 4 levels, 13 points, 8 groups");
   if (bs <= 0) return S4D_OK;
   constexpr int LPG = kFastNL * kFastNP * kFastG;
-  cam_softmax_prep_kernel<kFastNC, LPG, kFastG><<<(unsigned)bs, kGatherThreads, 0, stream>>>(weights_cam, cam_ws);
+  unsigned* counter = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(cam_ws) + factor_bytes(bs, ncam, nl, np, G));
+  cam_softmax_prep_kernel<kFastNC, LPG, kFastG><<<(unsigned)bs, kGatherThreads, 0, stream>>>(weights_cam, cam_ws,
+                                                                                           counter);
   return cuda_check(cudaGetLastError(), "cam_softmax_prep_kernel launch");
 }
 
@@ -1454,10 +1483,10 @@ int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream) {
     }
     GatherParams q = p;
     q.div_anchor = FastDiv((uint32_t)p.num_anchor);
+    // the counter pair is zero: reset by cam_softmax_prep_kernel when the workspace was prepared,
+    // and by the last block of every gather launch on it since
     q.anchor_counter = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(p.cam_ws) +
                                                    factor_bytes(p.bs, p.num_cams, p.num_levels, p.num_pts, p.num_groups));
-    int st = cuda_check(cudaMemsetAsync(q.anchor_counter, 0, sizeof(unsigned), stream), "cudaMemsetAsync(counter)");
-    if (st) return st;
     const int64_t anchors = (int64_t)p.bs * p.num_anchor;
     const bool bf = feat_dtype == S4D_DTYPE_BF16;
     const int which = (p.kps_anchor != nullptr ? 2 : 0) + (bf ? 0 : 1);  // index of the one-warp instance

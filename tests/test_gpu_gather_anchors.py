@@ -188,3 +188,37 @@ def test_gather_output_routing(cuda_device, bs, rows):
     assert torch.equal(peer[inside], ref2[inside])
     assert torch.equal(out2[~inside], ref2[~inside])
     assert torch.isnan(out2[inside]).all() and torch.isnan(peer[~inside]).all()
+
+
+@pytest.mark.parametrize("bs", [1, 3])
+def test_prepared_workspace_serves_repeated_calls(cuda_device, bs):
+    """The gather takes anchors from a counter in the workspace: s4d_dfa_camera_factors zeroes it
+    (here over memory filled with garbage first) and every gather launch leaves it at zero, so one
+    prepared workspace serves call after call with no reset in between, for the cooperative
+    kernel (bs = 1) and the warp kernel (bs = 3), from anchors and from locations alike."""
+    cfg, t, feat32, shape, start = _case(bs, 120 + bs)
+    feat = feat32.to(torch.bfloat16)
+    d = torch.device("cuda:0")
+    A = cfg.num_anchor
+    ws = ops.dfa_workspace(bs, 6, 4, 13, 8, d)
+    ws.view(torch.int32).fill_(-12345)  # whatever the allocator handed out
+    ops.camera_factors_into(ws, t["wc"])
+    loc = torch.empty(bs, A, 6, 13, 2, device=d)
+    ops.kps_project_into(t["anchor"], t["learn"].view(bs, A, 18), t["fix"], t["proj"], t["wh"], sample_location=loc)
+    outs = []
+    for i in range(5):
+        out = torch.full((bs, A, 256), float("nan"), device=d)
+        if i % 2 == 0:
+            ops.deformable_aggregation_anchors_into(out, feat, shape, start, t["anchor"], t["fix"], t["learn"],
+                                                    t["proj"], t["wh"], t["wa"], t["wc"], ws)
+        else:
+            ops.deformable_aggregation_into(out, feat, shape, start, loc, t["wa"], True, t["wc"], workspace=ws,
+                                            factors_ready=True)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert not torch.isnan(outs[0]).any()
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    # the counter pair is back at zero after the last call
+    tail = ws.view(torch.int32)[-4:]
+    assert tail[0].item() == 0 and tail[1].item() == 0
