@@ -288,12 +288,14 @@ class Workload:
 
 
 def launches_per_layer(w):
-    """This library's kernels per DFA layer: camera softmax factors and gather, plus the
-    keypoints unless the gather computes them; the two camera-encoder launches (split logits);
-    the two tensor-core linears (weights_fc + learnable_fc, output_proj + residual) when the
-    layer runs them."""
+    """This library's kernels per DFA layer: the gather, plus the keypoints unless the gather
+    computes them; with split logits the camera terms (one launch with the softmax factors for
+    the Sparse4D v3 shape, else the two camera-encoder launches); the two tensor-core linears
+    (weights_fc + learnable_fc, output_proj + residual) when the layer runs them."""
     m = w.mods[0]
-    return 2 + (0 if m.fused_keypoints else 1) + (2 if m.split_logits else 0) + (2 if m._tc else 0)
+    one_launch = m._factors_ok and w.frames <= m.camera_terms_max_frames
+    camera = (1 if one_launch else 2 + (1 if m._factors_ok else 0)) if m.split_logits else 0
+    return 1 + (0 if m.fused_keypoints else 1) + camera + (2 if m._tc else 0)
 
 
 def inbounds_samples(loc, spatial_shapes):

@@ -425,6 +425,25 @@ S4D_API int s4d_dfa_camera_logits(const float* projection_mat, int64_t bs, int64
 /* Bytes of the workspace of s4d_dfa_camera_logits (bs * Ncam * C floats).  Host-only. */
 S4D_API size_t s4d_dfa_camera_workspace_bytes(int64_t bs, int64_t num_cams, int64_t embed_dims);
 
+/* The per-frame camera terms in one launch: the outputs of s4d_dfa_camera_logits and, when a
+ * workspace is given, the softmax factors of s4d_dfa_camera_factors (with the anchor counter
+ * zeroed), bitwise equal to those two calls.  One cluster of 8 CTAs per frame exchanges the
+ * hidden layer through distributed shared memory, so no scratch is needed.  Replaces the camera
+ * encoder of model/deformable_feature_aggregation.py:679-717, weights_fc on its output (:719-798)
+ * and the camera part of the softmax over the weights (:800-805).
+ *   arguments as s4d_dfa_camera_logits, with
+ *   workspace  NULL (no factors), or the gather workspace of s4d_dfa_workspace_bytes(bs, Ncam,
+ *              L, P, G, 1) with L * P * G == num_logits and G == 8, 16-byte aligned
+ * Implemented: 1 <= Ncam <= 8, C == 256, num_logits <= 512 (a multiple of 8 with a workspace). */
+S4D_API int s4d_dfa_camera_terms(const float* projection_mat, int64_t bs, int64_t num_cams,
+                                 const float* cam_linear1_weight, const float* cam_linear1_bias,
+                                 const float* cam_ln1_weight, const float* cam_ln1_bias,
+                                 const float* cam_linear2_weight, const float* cam_linear2_bias,
+                                 const float* cam_ln2_weight, const float* cam_ln2_bias,
+                                 const float* weights_fc_weight, const float* weights_fc_bias, int64_t num_logits,
+                                 int64_t embed_dims, float* camera_embed, float* camera_logits, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* output_proj with the residual fused into its epilogue:
  *   out[:, :C] = features . weight^T + bias                        (residual_mode NONE)
  *   out[:, :C] = features . weight^T + bias + instance_feature     (ADD)

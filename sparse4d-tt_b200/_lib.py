@@ -68,6 +68,8 @@ SIGNATURES = {
     "s4d_dfa_camera_logits": (_int, [_p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p, _p,
                                      _p, _sz, _p]),
     "s4d_dfa_camera_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "s4d_dfa_camera_terms": (_int, [_p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p, _p,
+                                    _p, _sz, _p]),
     "s4d_pack_feature_maps": (_int, [_p, _int, _int, _i64, _i64, _i64, _p, _i64, _int, _p, _p]),
     "s4d_instance_bank_project": (_int, [_p, _p, _p, _i64, _i64, _p, _p]),
     "s4d_instance_bank_cache": (_int, [_p, _p, _p, _p, C.c_float, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p]),
@@ -96,7 +98,7 @@ class S4DError(RuntimeError):
 
 
 # Version of include/s4d_dfa.h these bindings are written for (s4d_abi_version()).
-ABI_VERSION = 108
+ABI_VERSION = 109
 
 
 def lib():

@@ -54,7 +54,7 @@ const char* s4d_status_string(int status) {
 
 const char* s4d_last_error(void) { return g_last_error; }
 
-int s4d_abi_version(void) { return 108; }
+int s4d_abi_version(void) { return 109; }
 
 uint64_t s4d_set_tc_wait_limit_ns(uint64_t limit_ns) {
   const uint64_t prev = g_tc_wait_limit_ns;
@@ -643,6 +643,60 @@ int s4d_dfa_camera_logits(const float* projection_mat, int64_t bs, int64_t num_c
   p.num_logits = (int)num_logits;
   p.embed_dims = (int)embed_dims;
   return launch_camera_logits(p, static_cast<cudaStream_t>(stream));
+}
+
+int s4d_dfa_camera_terms(const float* projection_mat, int64_t bs, int64_t num_cams, const float* cam_linear1_weight,
+                         const float* cam_linear1_bias, const float* cam_ln1_weight, const float* cam_ln1_bias,
+                         const float* cam_linear2_weight, const float* cam_linear2_bias, const float* cam_ln2_weight,
+                         const float* cam_ln2_bias, const float* weights_fc_weight, const float* weights_fc_bias,
+                         int64_t num_logits, int64_t embed_dims, float* camera_embed, float* camera_logits,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  set_error("%s", "");
+  if (bs < 0 || num_cams <= 0 || num_logits <= 0) return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_camera_terms: bad sizes");
+  if (num_cams > 8 || embed_dims != 256 || num_logits > 512)
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE,
+                "s4d_dfa_camera_terms: implemented for 1..8 cameras, embed_dims 256 and at most 512 logits");
+  if (bs >= (1 << 30)) return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_camera_terms: too many frames");
+  if (workspace != nullptr && num_logits % 8 != 0)
+    return fail(S4D_ERR_UNSUPPORTED_SHAPE, "s4d_dfa_camera_terms: the softmax factors need 8 groups "
+                                           "(num_logits a multiple of 8)");
+  if (bs == 0) return S4D_OK;
+  if (projection_mat == nullptr || cam_linear1_weight == nullptr || cam_linear1_bias == nullptr ||
+      cam_ln1_weight == nullptr || cam_ln1_bias == nullptr || cam_linear2_weight == nullptr ||
+      cam_linear2_bias == nullptr || cam_ln2_weight == nullptr || cam_ln2_bias == nullptr ||
+      weights_fc_weight == nullptr || weights_fc_bias == nullptr || camera_logits == nullptr)
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_camera_terms: null pointer");
+  if (!aligned(cam_linear2_weight, 16) || !aligned(weights_fc_weight, 16))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_camera_terms: the C x C and weights_fc matrices must be 16-byte aligned");
+  // the factors and the anchor counter pair sit where the gather expects them: the workspace of
+  // s4d_dfa_workspace_bytes(bs, num_cams, L, P, 8, 1) for any L * P * 8 == num_logits
+  const size_t need = gather_workspace_bytes(bs, (int)num_cams, 1, 1, (int)num_logits);
+  if (workspace != nullptr && (!aligned(workspace, 16) || workspace_bytes < need))
+    return fail(S4D_ERR_INVALID_ARG, "s4d_dfa_camera_terms: workspace misaligned or smaller than "
+                                     "s4d_dfa_workspace_bytes()");
+  CamEncParams p{};
+  p.proj = projection_mat;
+  p.w1 = cam_linear1_weight;
+  p.b1 = cam_linear1_bias;
+  p.ln1_w = cam_ln1_weight;
+  p.ln1_b = cam_ln1_bias;
+  p.w2 = cam_linear2_weight;
+  p.b2 = cam_linear2_bias;
+  p.ln2_w = cam_ln2_weight;
+  p.ln2_b = cam_ln2_bias;
+  p.w_fc = weights_fc_weight;
+  p.b_fc = weights_fc_bias;
+  p.camera_embed = camera_embed;
+  p.logits = camera_logits;
+  if (workspace != nullptr) {
+    p.factors = static_cast<float*>(workspace);
+    p.anchor_counter = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + need - 16);
+  }
+  p.bs = (int)bs;
+  p.num_cams = (int)num_cams;
+  p.num_logits = (int)num_logits;
+  p.embed_dims = (int)embed_dims;
+  return launch_camera_terms(p, static_cast<cudaStream_t>(stream));
 }
 
 int s4d_dfa_output_proj(const float* features, int64_t rows, const float* weight, const float* bias,

@@ -121,11 +121,14 @@ struct CamEncParams {
   const float *w_fc, *b_fc;              // weights_fc [num_logits, C], [num_logits]
   float* camera_embed;                   // [bs, num_cams, C] or null
   float* logits;                         // [bs, num_cams, num_logits]
-  float* hidden;                         // [bs, num_cams, C] scratch (workspace)
+  float* hidden;                         // [bs, num_cams, C] scratch (workspace); unused by camera_terms
+  float* factors;                        // camera_terms: softmax factors [bs, num_cams + 1, num_logits] or null
+  unsigned* anchor_counter;              // camera_terms: the gather's anchor counter pair, zeroed with factors
   int bs, num_cams, num_logits, embed_dims;
 };
 
 int launch_camera_logits(const CamEncParams& p, cudaStream_t stream);
+int launch_camera_terms(const CamEncParams& p, cudaStream_t stream);
 
 // Packing of per-level feature maps (pack_maps.cu).
 constexpr int kMaxPackLevels = 8;

@@ -105,6 +105,11 @@ class DeformableFeatureAggregation:
     kernel instead of materialising the ``[bs, A, Ncam, L*P*G]`` logits (same result up to
     fp32 rounding); ``split_logits=False`` evaluates the linear exactly as the reference does."""
 
+    # Up to this many frames per call the per-frame camera terms (encoder, per-camera logits,
+    # softmax factors) run as one cluster launch; above it as three shorter launches, whose
+    # short-lived CTAs leave room sooner for the concurrent tensor-core weights_fc.
+    camera_terms_max_frames = 8
+
     def __init__(self, device, parameters: Dict[str, Tensor], model_config: Optional[Dict] = None,
                  embed_dims: int = 256, num_groups: int = 8, num_levels: int = 4, num_cams: int = 6,
                  num_pts: int = 13, num_learnable_pts: int = 6, use_camera_embed: bool = True,
@@ -220,8 +225,10 @@ class DeformableFeatureAggregation:
 
     def _camera_logits(self, projection_mat: Tensor, bs: int, side: bool = False) -> Tensor:
         """Per-camera term of the split logits, ``weights_fc(camera_embed)`` with the bias:
-        ``[bs, Ncam, L, P, G]``, cached per frame.  Two kernels compute the camera encoder and
-        this term together (``ops.camera_logits_into``).  With ``side=True`` they run on this
+        ``[bs, Ncam, L, P, G]``, cached per frame.  For the Sparse4D v3 shape one launch computes
+        the camera encoder, this term and the gather's per-frame softmax factors
+        (``ops.camera_terms_into``); otherwise two kernels compute the encoder and this term
+        (``ops.camera_logits_into``).  With ``side=True`` they run on this
         module's side stream, forked from the current stream, so that they overlap the
         per-anchor work; ``_join_side()`` makes the current stream wait for them.  Their
         outputs and workspace stay in the per-frame cache, so no buffer the side stream writes
@@ -231,7 +238,8 @@ class DeformableFeatureAggregation:
             lpg = (self.num_levels, self.num_pts, self.num_groups)
             wc = torch.empty(bs, self.num_cams, *lpg, device=self.device)
             emb = torch.empty(bs, self.num_cams, self.embed_dims, device=self.device)
-            ws = torch.empty(bs * self.num_cams * self.embed_dims, device=self.device)
+            one_launch = self._factors_ok and bs <= self.camera_terms_max_frames
+            ws = None if one_launch else torch.empty(bs * self.num_cams * self.embed_dims, device=self.device)
             ctx = contextlib.nullcontext()
             if side:
                 if self._side is None:
@@ -244,13 +252,20 @@ class DeformableFeatureAggregation:
                 factors = ops.dfa_workspace(bs, self.num_cams, self.num_levels, self.num_pts, self.num_groups,
                                             self.device)
             with ctx:
-                ops.camera_logits_into(wc, projection_mat, self.cam_linear1_weight, self.cam_linear1_bias,
-                                       self.cam_ln1_weight, self.cam_ln1_bias, self.cam_linear2_weight,
-                                       self.cam_linear2_bias, self.cam_ln2_weight, self.cam_ln2_bias,
-                                       self.weights_fc_weight, self.weights_fc_bias, camera_embed=emb,
-                                       workspace=ws)
-                if factors is not None:  # the softmax's per-frame camera factors, off the gather's path
-                    ops.camera_factors_into(factors, wc)
+                if one_launch:  # with the softmax's per-frame camera factors, one launch
+                    ops.camera_terms_into(wc, projection_mat, self.cam_linear1_weight, self.cam_linear1_bias,
+                                          self.cam_ln1_weight, self.cam_ln1_bias, self.cam_linear2_weight,
+                                          self.cam_linear2_bias, self.cam_ln2_weight, self.cam_ln2_bias,
+                                          self.weights_fc_weight, self.weights_fc_bias, camera_embed=emb,
+                                          factors=factors)
+                else:
+                    ops.camera_logits_into(wc, projection_mat, self.cam_linear1_weight, self.cam_linear1_bias,
+                                           self.cam_ln1_weight, self.cam_ln1_bias, self.cam_linear2_weight,
+                                           self.cam_linear2_bias, self.cam_ln2_weight, self.cam_ln2_bias,
+                                           self.weights_fc_weight, self.weights_fc_bias, camera_embed=emb,
+                                           workspace=ws)
+                    if factors is not None:  # the softmax's per-frame camera factors, off the gather's path
+                        ops.camera_factors_into(factors, wc)
             self._cached_camera_embed, self._cached_camera_logits, self._cam_key = emb, wc, key
             self._cached_camera_ws, self._cached_camera_factors = ws, factors
         return self._cached_camera_logits

@@ -186,6 +186,47 @@ def camera_logits_into(camera_logits: Tensor, projection_mat: Tensor, cam_linear
     return camera_logits
 
 
+def camera_terms_into(camera_logits: Tensor, projection_mat: Tensor, cam_linear1_weight: Tensor,
+                      cam_linear1_bias: Tensor, cam_ln1_weight: Tensor, cam_ln1_bias: Tensor,
+                      cam_linear2_weight: Tensor, cam_linear2_bias: Tensor, cam_ln2_weight: Tensor,
+                      cam_ln2_bias: Tensor, weights_fc_weight: Tensor, weights_fc_bias: Tensor,
+                      camera_embed: Optional[Tensor] = None, factors: Optional[Tensor] = None) -> Tensor:
+    """``camera_logits_into`` and, with ``factors`` (a workspace from ``dfa_workspace``),
+    ``camera_factors_into`` in one launch of 8-CTA clusters, bitwise equal to the two calls
+    (``model/deformable_feature_aggregation.py:679-805``).  Needs no scratch workspace."""
+    name = "camera_terms"
+    ts = dict(camera_logits=camera_logits, projection_mat=projection_mat, cam_linear1_weight=cam_linear1_weight,
+              cam_linear1_bias=cam_linear1_bias, cam_ln1_weight=cam_ln1_weight, cam_ln1_bias=cam_ln1_bias,
+              cam_linear2_weight=cam_linear2_weight, cam_linear2_bias=cam_linear2_bias,
+              cam_ln2_weight=cam_ln2_weight, cam_ln2_bias=cam_ln2_bias, weights_fc_weight=weights_fc_weight,
+              weights_fc_bias=weights_fc_bias, camera_embed=camera_embed, factors=factors)
+    dev = _require_cuda(name, *ts.values())
+    _check_contig(name, **ts)
+    for k, t in ts.items():
+        _check_dtype(name, t, (torch.float32,), k)
+    _require(projection_mat.dim() == 4 and tuple(projection_mat.shape[2:]) == (4, 4),
+             "projection_mat must be [bs, Ncam, 4, 4]")
+    bs, nc = int(projection_mat.shape[0]), int(projection_mat.shape[1])
+    n, c = weights_fc_weight.shape
+    _require(tuple(cam_linear1_weight.shape) == (c, 12) and tuple(cam_linear2_weight.shape) == (c, c),
+             f"camera encoder weights must be [{c}, 12] and [{c}, {c}]")
+    for k in ("cam_linear1_bias", "cam_ln1_weight", "cam_ln1_bias", "cam_linear2_bias", "cam_ln2_weight",
+              "cam_ln2_bias"):
+        _require(tuple(ts[k].shape) == (c,), lambda: f"{k} must be [{c}]")
+    _require(tuple(weights_fc_bias.shape) == (n,), lambda: f"weights_fc_bias must be [{n}]")
+    _require(camera_logits.numel() == bs * nc * n, lambda: f"camera_logits must hold [{bs}, {nc}, {n}]")
+    _require(camera_embed is None or camera_embed.numel() == bs * nc * c,
+             lambda: f"camera_embed must hold [{bs}, {nc}, {c}]")
+    fb = 0 if factors is None else factors.numel() * factors.element_size()
+    st = L.lib().s4d_dfa_camera_terms(
+        projection_mat.data_ptr(), bs, nc, cam_linear1_weight.data_ptr(), cam_linear1_bias.data_ptr(),
+        cam_ln1_weight.data_ptr(), cam_ln1_bias.data_ptr(), cam_linear2_weight.data_ptr(), cam_linear2_bias.data_ptr(),
+        cam_ln2_weight.data_ptr(), cam_ln2_bias.data_ptr(), weights_fc_weight.data_ptr(), weights_fc_bias.data_ptr(),
+        n, c, _ptr(camera_embed), camera_logits.data_ptr(), _ptr(factors), fb, _stream_ptr(dev))
+    L.check(name, st)
+    return camera_logits
+
+
 def output_proj_into(out: Tensor, features: Tensor, weight: Tensor, bias: Optional[Tensor],
                      instance_feature: Optional[Tensor] = None, residual_mode: str = "cat",
                      error_flag: Optional[Tensor] = None) -> Tensor:

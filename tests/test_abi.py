@@ -33,7 +33,7 @@ def lib():
 
 def test_every_declared_symbol_is_exported(lib):
     names = declared_functions()
-    assert len(names) == 30, names
+    assert len(names) == 31, names
     for n in names:
         assert hasattr(lib, n), n
         assert n in L.SIGNATURES, f"{n} has no ctypes signature"
@@ -52,7 +52,7 @@ def test_status_strings_and_version(lib):
     assert L.status_string(0) == "S4D_OK"
     assert L.status_string(2) == "S4D_ERR_UNSUPPORTED_SHAPE"
     assert L.status_string(99) == "S4D_ERR_UNKNOWN"
-    assert lib.s4d_abi_version() == 108 == L.ABI_VERSION
+    assert lib.s4d_abi_version() == 109 == L.ABI_VERSION
 
 
 def test_dfa_workspace_bytes(lib):
@@ -269,6 +269,39 @@ def test_camera_logits_zero_frames_is_ok(lib):
 def test_camera_workspace_bytes(lib):
     assert lib.s4d_dfa_camera_workspace_bytes(32, 6, 256) == 32 * 6 * 256 * 4
     assert lib.s4d_dfa_camera_workspace_bytes(0, 6, 256) == 0
+
+
+def _terms(lib, **kw):
+    a = dict(proj=16, bs=32, nc=6, w=16, n=416, C=256, emb=None, out=16, ws=16,
+             wsb=lib.s4d_dfa_workspace_bytes(32, 6, 4, 13, 8, 1))
+    a.update(kw)
+    w = a["w"]
+    st = lib.s4d_dfa_camera_terms(a["proj"], a["bs"], a["nc"], w, w, w, w, w, w, w, w, w, w, a["n"], a["C"], a["emb"],
+                                  a["out"], a["ws"], a["wsb"], None)
+    return st, lib.s4d_last_error().decode()
+
+
+@pytest.mark.parametrize("kw,status,text", [
+    (dict(nc=9), L.S4D_ERR_UNSUPPORTED_SHAPE, "1..8 cameras"),
+    (dict(C=128), L.S4D_ERR_UNSUPPORTED_SHAPE, "embed_dims 256"),
+    (dict(n=520), L.S4D_ERR_UNSUPPORTED_SHAPE, "512 logits"),
+    (dict(n=412), L.S4D_ERR_UNSUPPORTED_SHAPE, "8 groups"),
+    (dict(nc=0), L.S4D_ERR_INVALID_ARG, "bad sizes"),
+    (dict(bs=-1), L.S4D_ERR_INVALID_ARG, "bad sizes"),
+    (dict(out=None), L.S4D_ERR_INVALID_ARG, "null"),
+    (dict(w=8), L.S4D_ERR_INVALID_ARG, "16-byte aligned"),
+    (dict(ws=8), L.S4D_ERR_INVALID_ARG, "workspace"),
+    (dict(wsb=1000), L.S4D_ERR_INVALID_ARG, "workspace"),
+])
+def test_camera_terms_rejects_on_host(lib, kw, status, text):
+    """Every argument check of the one-launch camera terms runs before a launch (no GPU here)."""
+    st, msg = _terms(lib, **kw)
+    assert st == status and text in msg, msg
+
+
+def test_camera_terms_zero_frames_is_ok(lib):
+    assert _terms(lib, bs=0)[0] == L.S4D_OK
+    assert _terms(lib, bs=0, ws=None, n=412)[0] == L.S4D_OK
 
 
 def _pack(lib, **kw):
