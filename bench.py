@@ -87,7 +87,7 @@ def workload_config(frames, layers, world):
         "frames_per_gpu": frames, "layers": layers, "global_batch": frames * world,
         "anchors": 900, "num_pts": 13, "num_cams": 6, "num_levels": 4, "embed_dims": 256, "num_groups": 8,
         "accumulate": "f32", "logits": "split (per-anchor + per-camera terms, summed in the gather kernel)",
-        "linears": "TF32 operands, fp32 accumulation: weights_fc + learnable_fc (embed add folded in) and "
+        "linears": "TF32 operands, fp32 accumulation: weights_fc + learnable_fc (embed add fused) and "
                    "output_proj (residual cat fused) on this library's tcgen05 kernels; the per-frame "
                    "camera encoder + per-camera logits on this library's fp32 kernels, recomputed every step",
         "parallelism": f"dp{world} (frames)",

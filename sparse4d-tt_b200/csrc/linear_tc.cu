@@ -3,8 +3,9 @@
 //
 //   weights_fc   logits = (inst + embed) . W_fc^T and learnable = inst . W_kps^T + b_kps in one
 //                pass over 128-row tiles (model/deformable_feature_aggregation.py:651-677,719-798;
-//                test/dfa_pcc.py:231-233,306-320).  The sum is never formed: inst . W_fc^T and
-//                embed . W_fc^T accumulate into the same tensor-memory columns from one W tile.
+//                test/dfa_pcc.py:231-233,306-320).  The sum is formed in shared memory, stage by
+//                stage, by the epilogue warps (idle during the K loop): one MMA per K step reads
+//                it, instead of one for inst and one for embed.
 //   output_proj  feats . W_o^T + b_o written straight into the residual output, the instance
 //                feature copied beside it (cat) or added to it (add)
 //                (model/deformable_feature_aggregation.py:934-950; test/dfa_pcc.py:299-304).
@@ -15,8 +16,9 @@
 //   warp 1     allocates the tensor-memory accumulator (128 lanes x N fp32 columns); one thread
 //              issues tcgen05.mma (M 128, K 8, N <= 256 per instruction) and commits each stage
 //              back to the producer;
-//   warps 2-5  during the main loop: output_proj copies the instance rows for the residual cat
-//              (weights_fc has nothing for them to do).  After it: tcgen05.ld of their 32 TMEM lanes (warp
+//   warps 2-5  during the main loop: weights_fc adds each stage's inst tile into its embed tile
+//              (the MMA issuer waits for that); output_proj copies the instance rows for the
+//              residual cat.  After it: tcgen05.ld of their 32 TMEM lanes (warp
 //              index mod 4), bias / residual in registers, the tile staged in shared memory
 //              with the 128-byte swizzle and written by TMA bulk-tensor stores.
 // Every barrier wait is bounded: after 2 s the CTA raises S4D_FLAG_WAIT_TIMEOUT, lets its copies
@@ -201,7 +203,7 @@ struct Ctl {
   volatile int* abort_flag;
 };
 
-// Barrier block after the stages: full[S], aux[S] (unused slots), empty[S], acc, then the TMEM slot and the
+// Barrier block after the stages: full[S], aux[S] (weights_fc: stage summed), empty[S], acc, then the TMEM slot and the
 // abort flag.
 template <int STAGE_BYTES>
 __device__ __forceinline__ Ctl carve(unsigned char* smem) {
@@ -280,7 +282,7 @@ __device__ __forceinline__ uint32_t prologue(const Ctl& c, uint32_t cols, int au
     const uint32_t b0 = smem_u32(c.bars);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(b0 + 8 * s, 1);                                    // full: TMA bytes landed
-      mbar_init(b0 + 8 * (kStages + s), aux_count > 0 ? aux_count : 1);  // aux: not waited on by these kernels
+      mbar_init(b0 + 8 * (kStages + s), aux_count > 0 ? aux_count : 1);  // aux: aux_count arrivals (0: unused)
       mbar_init(b0 + 8 * (2 * kStages + s), 1);                    // empty: MMAs of the stage done
     }
     mbar_init(b0 + 8 * (3 * kStages), 1);  // acc: accumulator complete
@@ -345,14 +347,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
   const Ctl c = carve<S::kStage>(smem);
-  const uint32_t full0 = smem_u32(c.bars), empty0 = full0 + 16 * kStages, acc_bar = full0 + 24 * kStages;
+  // full[s]: the stage's TMA bytes landed; summed[s] (the aux slots): the 128 epilogue threads have
+  // added its inst tile into its embed tile; empty[s]: its MMAs are done
+  const uint32_t full0 = smem_u32(c.bars), summed0 = full0 + 8 * kStages, empty0 = full0 + 16 * kStages,
+                 acc_bar = full0 + 24 * kStages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kbs = p.k / kBK;
   const int64_t row0 = int64_t(blockIdx.x) * kBM;
   // Column group: logits [col0, col0 + NW); the learnable columns ride with group 0.
   const int col0 = int(blockIdx.y) * NW;
   const bool learn = blockIdx.y == 0;
-  const uint32_t tmem = prologue(c, S::kCols, 0);
+  const uint32_t tmem = prologue(c, S::kCols, kThreads - 64);
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer
@@ -377,10 +382,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {  // MMA issuer
       for (int kb = 0; kb < kbs; ++kb) {
         const int s = kb % kStages;
-        if (!mbar_wait(full0 + 8 * s, (kb / kStages) & 1, c.abort_flag, p.wait_limit_ns)) break;
+        if (!mbar_wait(summed0 + 8 * s, (kb / kStages) & 1, c.abort_flag, p.wait_limit_ns)) break;
         tc_fence_after();
         const uint32_t st = smem_u32(smem + s * S::kStage);
-        const uint64_t a_inst = sw64_desc(st), a_emb = sw64_desc(st + kATile);
+        const uint64_t a_inst = sw64_desc(st), a_sum = sw64_desc(st + kATile);
         const uint64_t b_kps = sw64_desc(st + 2 * kATile + S::kBW);
 #pragma unroll
         for (int k = 0; k < kBK / 8; ++k) {
@@ -388,8 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < S::kSplit; ++j) {
             const uint64_t b = sw64_desc(st + 2 * kATile + j * S::kNmma * kBK * 4) + 2 * k;
-            mma_tf32(tmem + j * S::kNmma, a_inst + 2 * k, b, tf32_idesc(S::kNmma), acc);
-            mma_tf32(tmem + j * S::kNmma, a_emb + 2 * k, b, tf32_idesc(S::kNmma), 1);
+            mma_tf32(tmem + j * S::kNmma, a_sum + 2 * k, b, tf32_idesc(S::kNmma), acc);
           }
           if (learn) mma_tf32(tmem + NW, a_inst + 2 * k, b_kps + 2 * k, tf32_idesc(S::kNL), acc);
         }
@@ -399,6 +403,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(acc_bar, 0, nullptr);
     }
   } else {
+    // K loop: (inst + embed) of every stage, in place in its embed tile.  The two tiles come from
+    // the same kind of tensor map (box, swizzle, zero fill), so element i of one lies at the
+    // same byte offset as element i of the other and a flat add over the bytes pairs them up.
+    const int et = threadIdx.x - 64;
+    for (int kb = 0; kb < kbs; ++kb) {
+      const int s = kb % kStages;
+      if (!mbar_wait(full0 + 8 * s, (kb / kStages) & 1, c.abort_flag, p.wait_limit_ns)) break;
+      const float4* a4 = reinterpret_cast<const float4*>(smem + s * S::kStage);
+      float4* e4 = reinterpret_cast<float4*>(smem + s * S::kStage + kATile);
+#pragma unroll
+      for (int j = 0; j < kATile / 16 / (kThreads - 64); ++j) {
+        const int x = et + j * (kThreads - 64);
+        const float4 a = a4[x];
+        float4 e = e4[x];
+        e.x = a.x + e.x, e.y = a.y + e.y, e.z = a.z + e.z, e.w = a.w + e.w;
+        e4[x] = e;
+      }
+      fence_proxy_async();  // the tensor cores read the sum through the async proxy
+      mbar_arrive(summed0 + 8 * s);
+    }
     // Epilogue: logits through TMA stores, learnable columns (not 16-byte rows) by plain stores.
     const int q = warp & 3;
     if (wait_accumulator(c, acc_bar, p.wait_limit_ns)) {

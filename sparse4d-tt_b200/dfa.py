@@ -164,7 +164,7 @@ class DeformableFeatureAggregation:
         self.output_proj_weight = t("output_proj_weight")
         self.output_proj_bias = t("output_proj_bias")
         # TF32 linears run on this library's tensor-core kernels: weights_fc + learnable_fc
-        # in one pass (embed add folded in) and output_proj with the residual fused.
+        # in one pass (embed add fused) and output_proj with the residual fused.
         lpg = num_levels * num_pts * num_groups
         self._tc = (self.matmul_precision == "high" and self.split_logits
                     and ops.weights_fc_supported(lpg, 3 * num_learnable_pts, embed_dims)

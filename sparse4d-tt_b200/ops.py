@@ -13,7 +13,7 @@
   (``tt-metal/ops/kps_project_fused/kps_project_fused_nanobind.cpp:69-91``).
 * ``weights_fc_into`` / ``output_proj_into`` -- the layer's linears on the tensor cores
   (tcgen05, TF32 operands, fp32 accumulation): ``weights_fc`` (per-anchor logits) + the
-  keypoint ``learnable_fc`` in one pass with the embed add folded in, and ``output_proj`` with
+  keypoint ``learnable_fc`` in one pass with the embed add fused, and ``output_proj`` with
   the residual cat/add fused (``model/deformable_feature_aggregation.py:651-677,719-798,934-950``).
 * ``pack_feature_maps(feature_maps)`` -- per-level maps to the packed channels-last
   ``mc_ms_feat`` layout.
