@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <initializer_list>
+#include <utility>
 
 #include "s4d_dfa.h"
 
@@ -78,6 +79,39 @@ __device__ __forceinline__ float4 ldg_nc_f4(const void* p) {
                : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
                : "l"(p));
   return r;
+}
+
+// Programmatic dependent launch.  The DFA layer's chain weights_fc -> gather -> output_proj is
+// serial and, for one frame, short; launched with programmatic stream serialisation, a kernel's
+// CTAs may start (barrier init, tensor-memory allocation) while the kernel ahead of it in the
+// stream is still finishing.  griddep_wait() returns once every kernel this one depends on has
+// completed and its memory operations are visible, so each kernel calls it before its first
+// global-memory access; griddep_launch_dependents() lets the kernel behind this one be scheduled
+// (once every CTA of this launch has called it or exited).  For a launch without the attribute
+// both are no-ops.
+#ifndef S4D_PDL
+#define S4D_PDL 1
+#endif
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launches `kernel` on `stream`, with programmatic stream serialisation when `pdl` and S4D_PDL
+// are set.  The callers ask for it on the launches of one frame (one wave of CTAs, where CTA
+// start-up is a visible share of the kernel); a launch of many waves gains nothing from it.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = S4D_PDL && pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace s4d

@@ -744,6 +744,8 @@ __global__ void __launch_bounds__(WARPS * 32, (warp_kernel_min_blocks<T, KPS, WA
   __shared__ float s_kc[KPS ? WARPS : 1][KPS ? NP * 3 : 1];               // KPS: their scaled coordinates
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  griddep_wait();  // launched with programmatic serialisation: the kernels ahead of this one are done
+  griddep_launch_dependents();
   for (int i = tid; i < NC * NL; i += WARPS * 32) {
     const int H = p.spatial_shape[2 * i], W = p.spatial_shape[2 * i + 1], st = p.scale_start[i];
     const bool ok = H > 0 && W > 0 && st >= 0 && (int64_t)st + (int64_t)H * W <= p.num_feat;
@@ -1079,6 +1081,8 @@ __global__ void __launch_bounds__(WARPS * 32, (sizeof(T) == 2 ? 28 : 20) / WARPS
   __shared__ unsigned s_ticket;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  griddep_wait();  // launched with programmatic serialisation: the kernels ahead of this one are done
+  griddep_launch_dependents();
   for (int i = tid; i < NC * NL; i += WARPS * 32) {
     const int H = p.spatial_shape[2 * i], W = p.spatial_shape[2 * i + 1], st = p.scale_start[i];
     const bool ok = H > 0 && W > 0 && st >= 0 && (int64_t)st + (int64_t)H * W <= p.num_feat;
@@ -1496,7 +1500,8 @@ int launch_gather(const GatherParams& p, int feat_dtype, cudaStream_t stream) {
       const int split = gather_split_warps(anchors);
       auto go = [&](auto kernel, int warps, int slot) {
         const int64_t fit = resident_warp_blocks(kernel, which + 4 * slot, warps);
-        kernel<<<(unsigned)(anchors < fit ? anchors : fit), warps * 32, 0, stream>>>(q);
+        launch_pdl(warps > 1, kernel, dim3(static_cast<unsigned>(anchors < fit ? anchors : fit)), dim3(warps * 32), 0,
+                   stream, q);
       };
       if (split == 8)
         go(k8, 8, 3);

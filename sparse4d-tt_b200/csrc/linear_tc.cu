@@ -358,6 +358,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int col0 = int(blockIdx.y) * NW;
   const bool learn = blockIdx.y == 0;
   const uint32_t tmem = prologue(c, S::kCols, kThreads - 64);
+  griddep_wait();  // the kernels ahead of this one (which write inst, or read this launch's outputs) are done
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer
@@ -476,6 +478,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int64_t row0 = int64_t(blockIdx.x) * kBM;
   const int col0 = int(blockIdx.y) * NO;
   const uint32_t tmem = prologue(c, S::kCols, 0);
+  griddep_wait();  // the gather that wrote the features (and any reader of this launch's outputs) is done
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -645,8 +649,9 @@ int launch_weights_fc_cols(const WfcParams& p, cudaStream_t stream, int groups) 
   if (st == S4D_OK) st = set_smem(weights_fc_kernel<NW>, S::kSmem, "cudaFuncSetAttribute(weights_fc_kernel)", smem_set);
   if (st != S4D_OK) return st;
   const dim3 grid(unsigned((p.rows + kBM - 1) / kBM), unsigned(groups));
-  weights_fc_kernel<NW><<<grid, kThreads, S::kSmem, stream>>>(mi, me, mw, mk, mo, p);
-  return cuda_check(cudaGetLastError(), "weights_fc_kernel launch");
+  return cuda_check(
+      launch_pdl(groups > 1, weights_fc_kernel<NW>, grid, dim3(kThreads), S::kSmem, stream, mi, me, mw, mk, mo, p),
+      "weights_fc_kernel launch");
 }
 
 template <int NO, bool TWO>
@@ -663,8 +668,9 @@ int launch_output_proj_cols(const OprojParams& p, cudaStream_t stream, int group
     st = set_smem(output_proj_kernel<NO, TWO>, S::kSmem, "cudaFuncSetAttribute(output_proj_kernel)", smem_set);
   if (st != S4D_OK) return st;
   const dim3 grid(unsigned((p.rows + kBM - 1) / kBM), unsigned(groups));
-  output_proj_kernel<NO, TWO><<<grid, kThreads, S::kSmem, stream>>>(mf, mf2, mw, mo, p);
-  return cuda_check(cudaGetLastError(), "output_proj_kernel launch");
+  return cuda_check(
+      launch_pdl(groups > 1, output_proj_kernel<NO, TWO>, grid, dim3(kThreads), S::kSmem, stream, mf, mf2, mw, mo, p),
+      "output_proj_kernel launch");
 }
 
 }  // namespace
