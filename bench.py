@@ -229,6 +229,8 @@ class Workload:
         self.wh = torch.tensor(cfg.image_wh, dtype=torch.float32).expand(frames, cfg.num_cams, 2).contiguous().to(device)
 
     def step(self, inst=None, anchors=None, embeds=None, packed=None, proj=None, wh=None):
+        from sparse4d_tt_b200 import chained_camera_terms
+
         inst = self.inst0 if inst is None else inst
         anchors = self.anchors if anchors is None else anchors
         embeds = self.embeds if embeds is None else embeds
@@ -238,10 +240,11 @@ class Workload:
         out = None
         for mod in self.mods:  # a new batch of frames: per-frame camera caches start empty
             mod.reset_frame_cache()
-        for layer, mod in enumerate(self.mods):
-            out = mod.run(inst, anchors[layer], embeds[layer], packed, proj, wh, self.cfg.spatial_shapes,
-                          self.frames, self.cfg.num_anchor)
-            inst = out[..., : self.cfg.embed_dims]
+        with chained_camera_terms(self.mods):  # each layer starts the next one's camera terms
+            for layer, mod in enumerate(self.mods):
+                out = mod.run(inst, anchors[layer], embeds[layer], packed, proj, wh, self.cfg.spatial_shapes,
+                              self.frames, self.cfg.num_anchor)
+                inst = out[..., : self.cfg.embed_dims]
         return out
 
     def graph_stack(self):

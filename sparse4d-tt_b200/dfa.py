@@ -201,6 +201,11 @@ class DeformableFeatureAggregation:
         self.event_log: Optional[List[Tuple[TimingEvent, TimingEvent]]] = None
         self._timing: Optional[torch.cuda.Stream] = None
         self._timing_pending = False
+        # The layer that runs after this one on the same frames (set by DFAStack): its per-frame
+        # camera terms depend only on projection_mat, so run() starts them on that layer's side
+        # stream just before this layer's gather, where they fill the SMs the gather's last
+        # anchors leave idle instead of sharing them with the next layer's weights_fc.
+        self.next_layer: Optional["DeformableFeatureAggregation"] = None
 
     # ---- dense parts (cuBLAS through torch) -----------------------------------------------
     def _camera_encoder(self, projection_mat: Tensor, bs: int) -> Tensor:
@@ -383,6 +388,9 @@ class DeformableFeatureAggregation:
             loc = torch.empty(bs, num_anchor, self.num_cams, self.num_pts, 2, dtype=torch.float32, device=dev)
             ops.kps_project_into(anchor, learn, self.fix_scale, projection_mat, image_wh, sample_location=loc)
         self._join_side()  # the camera terms are needed from here on
+        nxt = self.next_layer
+        if nxt is not None and self._tc and nxt._tc and side:
+            nxt._camera_logits(projection_mat, bs, side=True)  # forked after weights_fc: beside the gather
 
         cam_begin, cam_end = 0, self.num_cams
         if self.process_group is not None:

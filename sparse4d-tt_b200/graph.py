@@ -15,6 +15,7 @@ per-frame camera encoder, runs on every replay.
 """
 from __future__ import annotations
 
+import contextlib
 from typing import Callable, List, Optional, Sequence, Tuple
 
 import torch
@@ -54,6 +55,21 @@ def capture(fn: Callable[[], object], warmup: int = 2, pool=None,
     with torch.cuda.graph(g, pool=pool):
         out = fn()
     return CapturedCall(g, out)
+
+
+@contextlib.contextmanager
+def chained_camera_terms(layers: Sequence):
+    """Within the block, each DFA layer of ``layers`` (run in this order on the same frames)
+    starts the next layer's per-frame camera terms just before its own gather
+    (``DeformableFeatureAggregation.next_layer``); the links are removed on exit."""
+    layers = list(layers)
+    for a, b in zip(layers[:-1], layers[1:]):
+        a.next_layer = b
+    try:
+        yield
+    finally:
+        for m in layers:
+            m.next_layer = None
 
 
 class DFAStack:
@@ -104,10 +120,11 @@ class DFAStack:
         C = self.layers[0].embed_dims
         for mod in self.layers:  # a new batch of frames: the camera terms are recomputed
             mod.reset_frame_cache()
-        for i, mod in enumerate(self.layers):
-            out = mod.run(inst, self.anchors[i], self.anchor_embeds[i], packed, self.projection_mat, self.image_wh,
-                          self.spatial_shapes, self.bs, self.num_anchor)
-            inst = out[..., :C]
+        with chained_camera_terms(self.layers):
+            for i, mod in enumerate(self.layers):
+                out = mod.run(inst, self.anchors[i], self.anchor_embeds[i], packed, self.projection_mat, self.image_wh,
+                              self.spatial_shapes, self.bs, self.num_anchor)
+                inst = out[..., :C]
         for mod in self.layers:
             mod.join_timing_stream()
         return out

@@ -26,7 +26,7 @@ import torch.nn.functional as F
 
 from . import ops
 from .dfa import MATMUL_PRECISIONS, DeformableFeatureAggregation, _matmul_precision, preprocess_dfa_parameters
-from .graph import capture
+from .graph import capture, chained_camera_terms
 
 Tensor = torch.Tensor
 
@@ -233,7 +233,8 @@ class Sparse4DHead:
                 mod.reset_frame_cache()  # a new frame: the per-frame camera terms are recomputed
         preds, clss, qts = [], [], []
         last = len(self.operation_order) - 1
-        with _matmul_precision(self.matmul_precision):
+        dfas = [p for op, p in zip(self.operation_order, self.layers) if op == "deformable"]
+        with _matmul_precision(self.matmul_precision), chained_camera_terms(dfas):
             embed = self.anchor_embed(anchor)
             for i, (op, p) in enumerate(zip(self.operation_order, self.layers)):
                 if op == "temp_gnn":

@@ -6,7 +6,7 @@ import torch
 
 from oracle import dfa_torch as oto
 from helpers import max_rel_err, pcc
-from sparse4d_tt_b200 import DFAStack, DeformableFeatureAggregation, ops
+from sparse4d_tt_b200 import DFAStack, DeformableFeatureAggregation, chained_camera_terms, ops
 from sparse4d_tt_b200 import synthetic as syn
 
 pytestmark = pytest.mark.gpu
@@ -55,6 +55,39 @@ def test_stack_replay_equals_eager(cuda_device, bs, n_layers):
         ref = _eager(layers, cfg, ins, anchors, embeds, packed)
         torch.cuda.synchronize()
         assert torch.equal(out, ref), (seed, (out - ref).abs().max().item())
+
+
+def test_chained_camera_terms_eager_equal_unchained(cuda_device):
+    """With the layers chained, each layer starts the next layer's camera terms on that layer's
+    side stream before its own gather (10 frames: 9,000 rows, where eager calls use the side
+    stream); the outputs are bitwise those of the unchained layers, and the links are gone
+    after the block."""
+    cfg = syn.DFAConfig(bs=10, num_anchor=900)
+    n = 3
+    layers = _layers(cfg, n)
+    d = torch.device("cuda:0")
+    ins, anchors, embeds = _inputs(cfg, n, 11)
+    packed = ops.pack_feature_maps([m.to(d) for m in ins.feature_maps], dtype=torch.bfloat16)
+    proj, wh = ins.projection_mat.to(d), ins.image_wh.to(d)
+    anchors, embeds = [a.to(d) for a in anchors], [e.to(d) for e in embeds]
+
+    def run(chain):
+        for mod in layers:
+            mod.reset_frame_cache()
+        inst, out = ins.instance_feature.to(d), None
+        with chained_camera_terms(layers if chain else []):
+            for i, mod in enumerate(layers):
+                out = mod.run(inst, anchors[i], embeds[i], packed, proj, wh, cfg.spatial_shapes, cfg.bs, cfg.num_anchor)
+                if chain and i + 1 < n:
+                    assert layers[i + 1]._cached_camera_logits is not None  # started by layer i
+                inst = out[..., :256]
+        return out.clone()
+
+    ref = run(False)
+    got = run(True)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref), (got - ref).abs().max().item()
+    assert all(m.next_layer is None for m in layers)
 
 
 def test_stack_single_layer_against_oracle(cuda_device):
