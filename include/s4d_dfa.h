@@ -19,7 +19,11 @@
  *     The library never allocates or frees: the caller owns every input, output and workspace.
  *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).  Calls are
  *     asynchronous and stream-ordered; nothing here synchronises the host.  Calls on different
- *     streams from different host threads are safe.
+ *     streams from different host threads are safe.  Small launches of s4d_dfa_weights_fc,
+ *     s4d_dfa_output_proj(_sum) and the gathers (one frame: one wave of CTAs) use programmatic
+ *     dependent launch.  Their CTAs may start before the preceding kernel in the stream ends,
+ *     but they touch no global memory until it has completed, so stream order still holds for
+ *     every read and write.
  *   - Every entry point returns an s4d_status; nothing throws and no kernel traps.  Shapes are
  *     checked on the host before any launch.  The text of the last failure on the calling
  *     thread is returned by s4d_last_error().
