@@ -130,3 +130,22 @@ def test_fastdiv_is_exact_below_2_31(d):
     ns += [k * d + r for k in (1, 2, 1000, ((1 << 31) - 1) // d) for r in (-1, 0, 1) if 0 <= k * d + r < (1 << 31)]
     for n in ns:
         assert q(n) == n // d, (n, d)
+
+
+def test_chained_camera_terms_links_and_unlinks():
+    """Within the block each layer points at the one after it (the last at nothing); the links
+    are removed on exit, also when the block raises."""
+    from types import SimpleNamespace
+
+    from sparse4d_tt_b200 import chained_camera_terms
+
+    layers = [SimpleNamespace(next_layer=None) for _ in range(4)]
+    with chained_camera_terms(layers):
+        assert [m.next_layer for m in layers] == layers[1:] + [None]
+    assert all(m.next_layer is None for m in layers)
+    with pytest.raises(RuntimeError):
+        with chained_camera_terms(layers):
+            raise RuntimeError("a layer failed")
+    assert all(m.next_layer is None for m in layers)
+    with chained_camera_terms([]):
+        pass
