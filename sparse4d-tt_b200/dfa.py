@@ -4,11 +4,15 @@ Same constructor arguments, parameter-dictionary keys and ``run`` signature as t
 module (``model/deformable_feature_aggregation.py:42-57,800-811,954-995``), called the same
 way by the decoder head (``model/sparse4d_head.py:405-411``).  What runs:
 
-* the dense layers stay on cuBLAS through torch: camera encoder
-  (``model/deformable_feature_aggregation.py:679-717``), ``weights_fc``, the keypoint
-  ``learnable_fc`` and ``output_proj`` (``:934-950``);
+* the camera encoder and the per-camera term of the weight logits
+  (``model/deformable_feature_aggregation.py:679-717``) on this library's fp32 kernels (with
+  split logits, the default);
+* ``weights_fc`` + the keypoint ``learnable_fc`` and ``output_proj`` (``:934-950``) on this
+  library's tcgen05 kernels with ``MATMUL_PRECISION "tf32"``, on cuBLAS fp32 through torch with
+  ``"fp32"`` (the default);
 * kernel (a) ``s4d_kps_project`` replaces ``_kps_generator_pre_rotation`` +
-  ``ttnn.kps_project_fused`` (``:651-677,855-860``);
+  ``ttnn.kps_project_fused`` (``:651-677,855-860``); with the tcgen05 linears the gather
+  computes the keypoints itself;
 * kernel (b)+(c) ``s4d_deformable_aggregation`` replaces the softmax, the per-level
   ``ttnn.grid_sample`` + ``ttnn.transposed_s2i`` loop and ``ttnn.grouped_weighted_sum``
   (``:791-796,864-899``).
