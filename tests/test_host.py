@@ -149,3 +149,19 @@ def test_chained_camera_terms_links_and_unlinks():
     assert all(m.next_layer is None for m in layers)
     with chained_camera_terms([]):
         pass
+
+
+def test_camera_operators_have_no_cpu_path():
+    """The camera encoder operators (two launches, and the one-launch camera terms with the
+    softmax factors) run on the GPU only; CPU tensors are rejected before any library call."""
+    cfg = syn.DFAConfig(bs=1)
+    params = syn.make_params(cfg, torch.Generator().manual_seed(3))
+    w = [params[k] for k in ("cam_linear1_weight", "cam_linear1_bias", "cam_ln1_weight", "cam_ln1_bias",
+                             "cam_linear2_weight", "cam_linear2_bias", "cam_ln2_weight", "cam_ln2_bias",
+                             "weights_fc_weight", "weights_fc_bias")]
+    proj = torch.eye(4).expand(1, 6, 4, 4).contiguous()
+    logits = torch.empty(1, 6, 416)
+    with pytest.raises(ValueError, match="no CPU path"):
+        ops.camera_logits_into(logits, proj, *w)
+    with pytest.raises(ValueError, match="no CPU path"):
+        ops.camera_terms_into(logits, proj, *w, factors=torch.empty(16))
