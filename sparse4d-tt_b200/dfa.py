@@ -205,7 +205,8 @@ class DeformableFeatureAggregation:
         self.event_log: Optional[List[Tuple[TimingEvent, TimingEvent]]] = None
         self._timing: Optional[torch.cuda.Stream] = None
         self._timing_pending = False
-        # The layer that runs after this one on the same frames (set by DFAStack): its per-frame
+        # The layer that runs after this one on the same frames (set for the length of a forward
+        # by DFAStack, the head and graph.chained_camera_terms): its per-frame
         # camera terms depend only on projection_mat, so run() starts them on that layer's side
         # stream just before this layer's gather, where they fill the SMs the gather's last
         # anchors leave idle instead of sharing them with the next layer's weights_fc.
@@ -234,10 +235,11 @@ class DeformableFeatureAggregation:
 
     def _camera_logits(self, projection_mat: Tensor, bs: int, side: bool = False) -> Tensor:
         """Per-camera term of the split logits, ``weights_fc(camera_embed)`` with the bias:
-        ``[bs, Ncam, L, P, G]``, cached per frame.  For the Sparse4D v3 shape one launch computes
-        the camera encoder, this term and the gather's per-frame softmax factors
-        (``ops.camera_terms_into``); otherwise two kernels compute the encoder and this term
-        (``ops.camera_logits_into``).  With ``side=True`` they run on this
+        ``[bs, Ncam, L, P, G]``, cached per frame.  For the Sparse4D v3 shape and at most
+        ``camera_terms_max_frames`` frames one launch computes the camera encoder, this term and
+        the gather's per-frame softmax factors (``ops.camera_terms_into``); otherwise two kernels
+        compute the encoder and this term (``ops.camera_logits_into``), followed for the v3 shape
+        by the factor kernel.  With ``side=True`` they run on this
         module's side stream, forked from the current stream, so that they overlap the
         per-anchor work; ``_join_side()`` makes the current stream wait for them.  Their
         outputs and workspace stay in the per-frame cache, so no buffer the side stream writes
